@@ -1,0 +1,134 @@
+/* Drop-in replacement for the reference engine's GPU ABI.
+ *
+ * Same symbols, struct layouts, argument meaning and status convention as
+ * native/cuda/orbit_wars_cuda.h:9-92 of TryDotAtwo/Orbit-Wars-2D-Transformer,
+ * so the engine's dlopen binding (crates/orbit-wars-trainer/src/cuda_true2d.rs:
+ * 360-451, RTLD_NOW, five symbols) loads this library unchanged through
+ * ORBIT_WARS_CUDA_LIB_PATH. Implementation: sm_100a kernels in
+ * orbit-wars-2d-transformer_b200/csrc/orbit_wars_true2d.cu.
+ *
+ * Status: code 0 OK, 1 BAD_ARGUMENT, 2 RUNTIME_ERROR; message is a static
+ * string the caller does not free. All buffers are host buffers unless noted;
+ * calls are synchronous and use device 0, like the reference.
+ */
+#pragma once
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* orbit_wars_cuda.h:9-12 */
+typedef struct OrbitWarsCudaStatus {
+  int code;
+  const char* message;
+} OrbitWarsCudaStatus;
+
+/* orbit_wars_cuda.h:14-19: legacy TrainableTransformer shape */
+typedef struct OrbitWarsCudaTransformerShape {
+  size_t layer_count;
+  size_t d_model;
+  size_t head_count;
+  size_t row_count;
+} OrbitWarsCudaTransformerShape;
+
+/* orbit_wars_cuda.h:21-25: True2D shape */
+typedef struct OrbitWarsCudaTrue2DShape {
+  size_t layer_count;
+  size_t row_count;
+  size_t head_count;
+} OrbitWarsCudaTrue2DShape;
+
+/* orbit_wars_cuda.h:27-35 */
+typedef struct OrbitWarsCudaTrue2DTrainingConfig {
+  size_t batch_sample_count;
+  float learning_rate;
+  float reward_normalizer;
+  float send_threshold;
+  float owner_class_own;
+  float owner_class_empty;
+  float owner_class_absent_on_map;
+} OrbitWarsCudaTrue2DTrainingConfig;
+
+/* orbit_wars_cuda.h:37; .cu:2438-2448 -- OK when a CUDA device is visible. */
+OrbitWarsCudaStatus orbit_wars_cuda_status(void);
+
+/* orbit_wars_cuda.h:39-44; .cu:2450-2466 -- device-pointer copy of
+ * games x rows x features floats. */
+OrbitWarsCudaStatus orbit_wars_cuda_encode_identity_batch(
+    const float* input_rows,
+    float* output_rows,
+    size_t game_count,
+    size_t row_count,
+    size_t feature_count);
+
+/* orbit_wars_cuda.h:46-51; .cu:2468-2582 -- legacy TrainableTransformer
+ * (crates/orbit-wars-core/src/model.rs:210-301). Input games x rows x 2,
+ * output games x rows x 2 (target, send). The reference copied back 24
+ * floats per row into a 2-per-row buffer; this one writes exactly 2. */
+OrbitWarsCudaStatus orbit_wars_cuda_trainable_forward(
+    const float* input_rows,
+    const float* weights,
+    float* output_rows,
+    size_t game_count,
+    OrbitWarsCudaTransformerShape shape);
+
+/* orbit_wars_cuda.h:53-58; .cu:3332-3483 -- one True2D model
+ * (true2d_model.rs:197-283). Input games x rows x 7, output games x rows x 24. */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward(
+    const float* input_rows,
+    const float* weights,
+    float* output_rows,
+    size_t game_count,
+    OrbitWarsCudaTrue2DShape shape);
+
+/* orbit_wars_cuda.h:60-67; .cu:2738-2770 -- request r uses model
+ * model_indices[r] of all_weights (models back to back). Leaves the
+ * population resident for ..._forward_many_resident. */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_many(
+    const float* input_rows,
+    const size_t* model_indices,
+    const float* all_weights,
+    float* output_rows,
+    size_t request_count,
+    size_t model_count,
+    OrbitWarsCudaTrue2DShape shape);
+
+/* orbit_wars_cuda.h:69-73; .cu:2772-2800 -- uploads a population into the
+ * persistent device workspace sized for request_capacity requests. */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_upload_population(
+    const float* all_weights,
+    size_t model_count,
+    size_t request_capacity,
+    OrbitWarsCudaTrue2DShape shape);
+
+/* orbit_wars_cuda.h:75-80; .cu:2802-2821 -- forward on the resident
+ * population (errors when none is loaded, the shape differs or the request
+ * count exceeds the uploaded capacity). */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_many_resident(
+    const float* input_rows,
+    const size_t* model_indices,
+    float* output_rows,
+    size_t request_count,
+    OrbitWarsCudaTrue2DShape shape);
+
+/* orbit_wars_cuda.h:82-92; .cu:2823-3330 -- training is not part of the
+ * policy forward. The call is forwarded to the library named by
+ * ORBIT_WARS_CUDA_TRAIN_LIB_PATH (for example the reference's own build),
+ * else it returns RUNTIME_ERROR "training not provided". */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
+    const float* input_rows,
+    const float* output_rows,
+    const int* rewards,
+    const float* target_action_rewards,
+    const size_t* model_indices,
+    float* all_weights,
+    size_t sample_count,
+    size_t model_count,
+    OrbitWarsCudaTrue2DShape shape,
+    OrbitWarsCudaTrue2DTrainingConfig training_config);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,115 @@
+/* Orbit Wars entity-encoder policy forward on NVIDIA B200 (sm_100a): C ABI.
+ *
+ * A batch of game states, each a padded set of N entity tokens of F
+ * features plus a per-state valid count, runs through an entity embedding,
+ * L pre-LN encoder blocks (masked multi-head attention + GELU FFN), per-entity
+ * policy logits, a mean-pooled value head and greedy or Gumbel-max actions.
+ * The math and the weight-blob layout are frozen in SPEC.md.
+ *
+ * Conventions follow the reference engine's GPU ABI
+ * (native/cuda/orbit_wars_cuda.h:9-12, native/cuda/orbit_wars_cuda.cu:12-14):
+ * every call returns {code, message}; code 0 = OK, 1 = BAD_ARGUMENT,
+ * 2 = RUNTIME_ERROR; message is a static string the caller does not free.
+ * Buffers are contiguous row-major, request x rows x features, like the
+ * packed f32 batches of crates/orbit-wars-trainer/src/cuda_true2d.rs:469-487.
+ *
+ * The reference has no encoder policy: these symbols are new, added beside
+ * the reference's orbit_wars_cuda_* symbols (orbit_wars_cuda.h) in the same
+ * library. A handle is bound to one device and one stream; separate handles
+ * may be used from separate threads.
+ */
+#ifndef OW_POLICY_H_
+#define OW_POLICY_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct OwStatus {
+  int code;
+  const char* message;
+} OwStatus;
+
+enum { OW_STATUS_OK = 0, OW_STATUS_BAD_ARGUMENT = 1, OW_STATUS_RUNTIME_ERROR = 2 };
+enum { OW_PRECISION_F32 = 0, OW_PRECISION_BF16 = 1, OW_PRECISION_FP8 = 2 };
+enum { OW_DTYPE_F32 = 0, OW_DTYPE_BF16 = 1 };
+enum { OW_IO_HOST = 0, OW_IO_DEVICE = 1 };
+
+typedef struct OwPolicyConfig {
+  int32_t batch_capacity; /* max states per forward call */
+  int32_t n_entities;     /* N, padded entity slots per state, 1..128 */
+  int32_t features;       /* F, 1..32 */
+  int32_t d_model;        /* d, multiple of 32 (head_dim 32), 128..512 */
+  int32_t heads;          /* d / 32 */
+  int32_t ffn;            /* f, multiple of 128 */
+  int32_t layers;         /* L >= 1 */
+  int32_t actions;        /* P, 1..32 */
+  int32_t precision;      /* OW_PRECISION_* */
+  int32_t sample_actions; /* 0 greedy argmax, 1 Gumbel-max (Philox4x32-10) */
+  int32_t logits_dtype;   /* OW_DTYPE_* */
+  int32_t value_dtype;    /* OW_DTYPE_* */
+  int32_t io;             /* OW_IO_HOST: host buffers, synchronous; OW_IO_DEVICE: device buffers, async on the stream */
+} OwPolicyConfig;
+
+typedef struct OwPolicy OwPolicy;
+
+/* Fills *config with preset 1..5 (the five documented workloads). */
+OwStatus ow_policy_preset(int preset, OwPolicyConfig* config);
+
+/* Number of f32 weights the blob for this config holds. */
+OwStatus ow_policy_weight_count(const OwPolicyConfig* config, size_t* count);
+
+/* Creates a handle on `device`: validates the config, converts and uploads
+ * the f32 weight blob (to bf16 / e4m3 + per-channel scales as the precision
+ * asks), allocates the batch_capacity workspace. `stream` may be NULL (a
+ * handle-owned stream is created). */
+OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, size_t weight_count, int device,
+                          void* stream, OwPolicy** out);
+
+/* Replaces the weights of an existing handle (same config). */
+OwStatus ow_policy_set_weights(OwPolicy* policy, const float* weights, size_t weight_count);
+
+/* One forward of `batch` states (batch <= batch_capacity).
+ *   features f32 [batch, N, F]; counts int32 [batch], each in [0, N]
+ *   logits [batch, N, P] (logits_dtype), value [batch] (value_dtype),
+ *   actions int32 [batch, N]; any output pointer may be NULL to skip it.
+ * OW_IO_HOST: host pointers; returns after the outputs are on the host.
+ * OW_IO_DEVICE: device pointers; enqueued on the handle's stream, returns
+ * at once (call ow_policy_synchronize to collect device-side errors). */
+OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_t* counts, int32_t batch,
+                           void* logits, void* value, int32_t* actions, uint64_t seed);
+
+/* Waits for the handle's stream and reports any device-side error
+ * (a bad count, a bounded wait that expired). */
+OwStatus ow_policy_synchronize(OwPolicy* policy);
+
+/* Device pointer and byte size of the handle's packed device weights (the
+ * tensor a weight broadcast moves), for callers that run their own NCCL. */
+OwStatus ow_policy_device_weights(OwPolicy* policy, void** ptr, size_t* bytes);
+
+/* Per-kernel device timing. ow_policy_profile_begin arms CUDA events around
+ * every launch of the next `max_forwards` forwards (events only, no host
+ * synchronisation); ow_policy_profile_end synchronises and returns, per
+ * kernel name, the launches and the summed event-to-event milliseconds. */
+typedef struct OwKernelTiming {
+  const char* name;
+  int32_t launches;
+  float total_ms;
+} OwKernelTiming;
+
+OwStatus ow_policy_profile_begin(OwPolicy* policy, int32_t max_forwards);
+OwStatus ow_policy_profile_end(OwPolicy* policy, OwKernelTiming* out, int32_t capacity, int32_t* count);
+
+/* Kernel launches one forward issues (for launch accounting). */
+OwStatus ow_policy_launches_per_forward(const OwPolicy* policy, int32_t* launches);
+
+void ow_policy_destroy(OwPolicy* policy);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OW_POLICY_H_ */

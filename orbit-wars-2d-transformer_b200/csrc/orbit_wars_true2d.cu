@@ -1,0 +1,693 @@
+// sm_100a implementation of the reference engine's GPU ABI
+// (include/orbit_wars_cuda.h): the True2D self-play policy forward, the
+// legacy TrainableTransformer forward and the identity copy.
+//
+// True2D forward per request (true2d_model.rs:197-283), three kernels:
+//   1. t2_expand_pre:  thread per (request, cell): expand (true2d_model.rs:321-366)
+//                      then the pre-attention matrix layers (:419-461) with the
+//                      cell value held in a register; weights of request r's
+//                      model streamed from L2/HBM (12 floats per layer per cell,
+//                      three 16-byte loads).
+//   2. t2_attention:   CTA per request: full scalar self-attention over all
+//                      cells (:463-544). Keys/values of the request sit in shared
+//                      memory; the row max is closed-form because scores are
+//                      rank-1 (max_j q*k_j = q*kmax for q >= 0, q*kmin otherwise),
+//                      so softmax and weighted sum take ONE pass over the keys
+//                      (the reference takes two). Attention FFN fused.
+//   3. t2_post_collapse: CTA per 4 rows of a request: post-attention matrix layers,
+//                      then the 12-action collapse (:546-647) from shared memory.
+// The model population stays resident in HBM between calls (upload_population);
+// all buffers live in one process-global workspace like the reference's
+// (orbit_wars_cuda.cu:421-441), guarded by a mutex.
+
+#include "orbit_wars_cuda.h"
+
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "ow_common.cuh"
+
+namespace {
+
+constexpr int kOk = 0, kBad = 1, kRt = 2;  // orbit_wars_cuda.cu:12-14
+constexpr size_t kFeatures = 7;
+constexpr size_t kTargets = 12;
+constexpr size_t kOutPerRow = 24;
+constexpr size_t kCellWeights = 12;
+constexpr size_t kHeadWeights = 7;
+constexpr size_t kSharedWeights = 6;
+constexpr size_t kOutScalars = 5;
+constexpr size_t kMinRows = 2, kMaxRows = 128, kMaxHeads = 16;
+
+OrbitWarsCudaStatus ok() { return {kOk, "ok"}; }
+OrbitWarsCudaStatus bad(const char* m) { return {kBad, m}; }
+OrbitWarsCudaStatus rt(const char* m) { return {kRt, m}; }
+OrbitWarsCudaStatus from_cuda(cudaError_t e) { return e == cudaSuccess ? ok() : rt(cudaGetErrorString(e)); }
+
+#define T2_TRY(expr)                               \
+  do {                                             \
+    const cudaError_t e_ = (expr);                 \
+    if (e_ != cudaSuccess) return from_cuda(e_);   \
+  } while (0)
+
+struct T2Layout {
+  size_t rows, cells, layers, heads;
+  size_t pair, src_emb, tgt_emb, pair_emb, bias, matrix, attn, tbias, sbias, scalars, total;
+};
+
+// Weight-vector layout, true2d_model.rs:111-126 (order of the slices in :216-246).
+T2Layout t2_layout(size_t layers, size_t rows, size_t heads) {
+  T2Layout o{};
+  o.rows = rows;
+  o.cells = rows * rows;
+  o.layers = layers;
+  o.heads = heads;
+  size_t c = 0;
+  o.pair = c; c += kFeatures * 2;
+  o.src_emb = c; c += rows;
+  o.tgt_emb = c; c += rows;
+  o.pair_emb = c; c += o.cells;
+  o.bias = c; c += 1;
+  o.matrix = c; c += layers * o.cells * kCellWeights;
+  o.attn = c; c += heads * kHeadWeights + kSharedWeights;
+  o.tbias = c; c += rows * kTargets;
+  o.sbias = c; c += rows * kTargets;
+  o.scalars = c; c += kOutScalars * kTargets;
+  o.total = c;
+  return o;
+}
+
+bool shape_ok(const OrbitWarsCudaTrue2DShape& s) {
+  return s.layer_count > 0 && s.row_count >= kMinRows && s.row_count <= kMaxRows && s.head_count >= 1 &&
+         s.head_count <= kMaxHeads;
+}
+
+// Device-side view of the layout (passed by value).
+struct T2Dev {
+  int rows, cells, layers, heads, mid;
+  long long pair, src_emb, tgt_emb, pair_emb, bias, matrix, attn, tbias, sbias, scalars, total;
+};
+
+// Device copy of a model: the host layout with `pad` floats inserted before
+// the matrix-layer section so each cell's 12 weights start on a 16-byte
+// boundary (host offset 4239 for 64 rows is not), and the model stride
+// rounded up to 4 floats.
+size_t matrix_pad(const T2Layout& L) { return (4 - L.matrix % 4) % 4; }
+size_t dev_total(const T2Layout& L) { return (L.total + matrix_pad(L) + 3) / 4 * 4; }
+
+T2Dev dev_layout(const T2Layout& L) {
+  T2Dev d{};
+  const long long pad = static_cast<long long>(matrix_pad(L));
+  d.rows = static_cast<int>(L.rows);
+  d.cells = static_cast<int>(L.cells);
+  d.layers = static_cast<int>(L.layers);
+  d.heads = static_cast<int>(L.heads);
+  d.mid = static_cast<int>(L.layers / 2);  // attention_layer_index, true2d_model.rs:128-130
+  d.pair = L.pair; d.src_emb = L.src_emb; d.tgt_emb = L.tgt_emb; d.pair_emb = L.pair_emb; d.bias = L.bias;
+  d.matrix = L.matrix + pad; d.attn = L.attn + pad; d.tbias = L.tbias + pad; d.sbias = L.sbias + pad;
+  d.scalars = L.scalars + pad;
+  d.total = static_cast<long long>(dev_total(L));
+  return d;
+}
+
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+// One gated per-cell matrix layer, true2d_model.rs:419-461.
+__device__ __forceinline__ float matrix_cell(float v, const float* __restrict__ w12) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(w12));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(w12) + 1);
+  const float4 c = __ldg(reinterpret_cast<const float4*>(w12) + 2);
+  // a = (w0,w1,w2,w3) b = (w4,w5,w6,w7) c = (w8,w9,w10,w11)
+  const float ha = tanhf(fmaf(v, a.z, a.w));
+  const float hb = tanhf(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
+  const float g = sigmoid_f(fmaf(v, b.w, c.x));
+  const float u = fmaf(hb, c.y, fmaf(ha, c.z, c.w));
+  const float r = fmaf(v, 1.0f + a.x, a.y);
+  return tanhf(fmaf(g, u, r));
+}
+
+__device__ __forceinline__ const float* model_of(const float* __restrict__ all_w, const size_t* __restrict__ idx,
+                                                 int models, int r, long long total, int* err) {
+  size_t m = idx != nullptr ? idx[r] : 0;
+  if (m >= static_cast<size_t>(models)) {
+    ow::record_error(err, ow::kErrBadModelIndex);
+    m = 0;
+  }
+  return all_w + static_cast<long long>(m) * total;
+}
+
+// 1. expand + matrix layers [0, mid)
+__global__ void __launch_bounds__(256) t2_expand_pre(const float* __restrict__ x, const size_t* __restrict__ idx,
+                                                     const float* __restrict__ all_w, int models, T2Dev L,
+                                                     float* __restrict__ m, int* err) {
+  const int r = blockIdx.y;
+  const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+  if (cell >= L.cells) return;
+  const float* w = model_of(all_w, idx, models, r, L.total, err);
+  const int s = cell / L.rows, t = cell % L.rows;
+  const float* xs = x + (static_cast<long long>(r) * L.rows + s) * kFeatures;
+  const float* xt = x + (static_cast<long long>(r) * L.rows + t) * kFeatures;
+  const float* pw = w + L.pair;
+  float v = 0.0f;
+#pragma unroll
+  for (int f = 0; f < static_cast<int>(kFeatures); ++f) v = fmaf(xs[f], pw[f], v);
+#pragma unroll
+  for (int f = 0; f < static_cast<int>(kFeatures); ++f) v = fmaf(xt[f], pw[kFeatures + f], v);
+  v += w[L.src_emb + s] + w[L.tgt_emb + t] + w[L.pair_emb + cell] + w[L.bias];
+  v = tanhf(v);
+  const float* mw = w + L.matrix + static_cast<long long>(cell) * kCellWeights;
+  const long long per_layer = static_cast<long long>(L.cells) * kCellWeights;
+  for (int l = 0; l < L.mid; ++l) v = matrix_cell(v, mw + l * per_layer);
+  m[static_cast<long long>(r) * L.cells + cell] = v;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2. full scalar attention + attention FFN, CTA per request, in place on m.
+constexpr int kAttnThreads = 1024;
+constexpr int kQueriesPerThread = 4;  // cells <= 4096 for one pass; larger grids loop
+
+__global__ void __launch_bounds__(kAttnThreads) t2_attention(const size_t* __restrict__ idx,
+                                                             const float* __restrict__ all_w, int models, T2Dev L,
+                                                             float* __restrict__ m, int* err) {
+  extern __shared__ float2 s_kv[];  // [cells] (k, v)
+  __shared__ float s_red[2][32];
+  const int r = blockIdx.x;
+  const float* w = model_of(all_w, idx, models, r, L.total, err);
+  const float* aw = w + L.attn;
+  float* mr = m + static_cast<long long>(r) * L.cells;
+  const float kLog2e = 1.4426950408889634f;
+  for (int base = 0; base < L.cells; base += kAttnThreads * kQueriesPerThread) {
+    float mv[kQueriesPerThread], ctx[kQueriesPerThread];
+#pragma unroll
+    for (int i = 0; i < kQueriesPerThread; ++i) {
+      const int c = base + i * kAttnThreads + threadIdx.x;
+      mv[i] = c < L.cells ? mr[c] : 0.0f;
+      ctx[i] = 0.0f;
+    }
+    for (int h = 0; h < L.heads; ++h) {
+      const float* hw = aw + h * kHeadWeights;
+      const float wq = hw[0], bq = hw[1], wk = hw[2], bk = hw[3], wv = hw[4], bv = hw[5], wo = hw[6];
+      __syncthreads();  // previous head / chunk done with s_kv
+      float kmax = -INFINITY, kmin = INFINITY;
+      for (int c = threadIdx.x; c < L.cells; c += kAttnThreads) {
+        const float cv = mr[c];
+        const float k = fmaf(cv, wk, bk);
+        s_kv[c] = make_float2(k * kLog2e, fmaf(cv, wv, bv));
+        kmax = fmaxf(kmax, k);
+        kmin = fminf(kmin, k);
+      }
+      kmax = ow::warp_max(kmax);
+      kmin = -ow::warp_max(-kmin);
+      if ((threadIdx.x & 31) == 0) {
+        s_red[0][threadIdx.x >> 5] = kmax;
+        s_red[1][threadIdx.x >> 5] = kmin;
+      }
+      __syncthreads();
+      kmax = s_red[0][0];
+      kmin = s_red[1][0];
+      for (int i = 1; i < kAttnThreads / 32; ++i) {
+        kmax = fmaxf(kmax, s_red[0][i]);
+        kmin = fminf(kmin, s_red[1][i]);
+      }
+      float q[kQueriesPerThread], off[kQueriesPerThread], den[kQueriesPerThread], acc[kQueriesPerThread];
+#pragma unroll
+      for (int i = 0; i < kQueriesPerThread; ++i) {
+        q[i] = fmaf(mv[i], wq, bq);
+        // exact row max of the rank-1 scores q*k_j, in log2 units
+        off[i] = (q[i] >= 0.0f ? q[i] * kmax : q[i] * kmin) * kLog2e;
+        den[i] = 0.0f;
+        acc[i] = 0.0f;
+      }
+#pragma unroll 4
+      for (int j = 0; j < L.cells; ++j) {
+        const float2 kv = s_kv[j];
+#pragma unroll
+        for (int i = 0; i < kQueriesPerThread; ++i) {
+          const float e = ex2_approx(fmaf(q[i], kv.x, -off[i]));
+          den[i] += e;
+          acc[i] = fmaf(e, kv.y, acc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kQueriesPerThread; ++i) ctx[i] = fmaf(acc[i] / den[i], wo, ctx[i]);
+    }
+    const float* s = aw + L.heads * kHeadWeights;
+    __syncthreads();  // every thread has read the keys of this chunk before m is overwritten
+#pragma unroll
+    for (int i = 0; i < kQueriesPerThread; ++i) {
+      const int c = base + i * kAttnThreads + threadIdx.x;
+      if (c < L.cells) {
+        const float rr = fmaf(mv[i], s[0], ctx[i] + s[1]);
+        const float hid = tanhf(fmaf(rr, s[2], s[3]));
+        mr[c] = tanhf(fmaf(hid, s[4], rr + s[5]));
+      }
+    }
+  }
+}
+
+// 3. matrix layers [mid, layers) + collapse; CTA = 4 rows of one request.
+constexpr int kRowsPerCta = 4;
+
+__global__ void __launch_bounds__(512) t2_post_collapse(const size_t* __restrict__ idx, const float* __restrict__ all_w,
+                                                        int models, T2Dev L, const float* __restrict__ m,
+                                                        float* __restrict__ out, int* err) {
+  __shared__ float s_m[kRowsPerCta][kMaxRows];
+  __shared__ float s_send[kRowsPerCta][kTargets];
+  const int r = blockIdx.y;
+  const int row0 = blockIdx.x * kRowsPerCta;
+  const float* w = model_of(all_w, idx, models, r, L.total, err);
+  const long long per_layer = static_cast<long long>(L.cells) * kCellWeights;
+  for (int i = threadIdx.x; i < kRowsPerCta * L.rows; i += blockDim.x) {
+    const int lr = i / L.rows, t = i % L.rows;
+    const int row = row0 + lr;
+    if (row >= L.rows) continue;
+    const int cell = row * L.rows + t;
+    float v = m[static_cast<long long>(r) * L.cells + cell];
+    const float* mw = w + L.matrix + static_cast<long long>(cell) * kCellWeights;
+    for (int l = L.mid; l < L.layers; ++l) v = matrix_cell(v, mw + l * per_layer);
+    s_m[lr][t] = v;
+  }
+  __syncthreads();
+  // warp per (row, action): target softmax -> expected index; send softmax -> sigmoid
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int item = warp; item < kRowsPerCta * static_cast<int>(kTargets); item += nwarps) {
+    const int lr = item / kTargets, a = item % kTargets;
+    const int row = row0 + lr;
+    if (row >= L.rows) continue;
+    const float* sc = w + L.scalars + a * kOutScalars;
+    const float* tb = w + L.tbias + static_cast<long long>(a) * L.rows;
+    const float* sb = w + L.sbias + static_cast<long long>(a) * L.rows;
+    const float s0 = sc[0], s1 = sc[1];
+    float tmax = -INFINITY, smax = -INFINITY;
+    for (int t = lane; t < L.rows; t += 32) {
+      tmax = fmaxf(tmax, fmaf(s_m[lr][t], s0, tb[t]));
+      smax = fmaxf(smax, fmaf(s_m[lr][t], s1, sb[t]));
+    }
+    tmax = ow::warp_max(tmax);
+    smax = ow::warp_max(smax);
+    float tden = 0.0f, tnum = 0.0f, sden = 0.0f, snum = 0.0f;
+    const float inv_last = 1.0f / static_cast<float>(L.rows - 1);
+    for (int t = lane; t < L.rows; t += 32) {
+      const float v = s_m[lr][t];
+      const float et = expf(fmaf(v, s0, tb[t]) - tmax);
+      tden += et;
+      tnum = fmaf(et, static_cast<float>(t) * inv_last, tnum);
+      const float es = expf(fmaf(v, s1, sb[t]) - smax);
+      sden += es;
+      snum = fmaf(es, v, snum);
+    }
+    tden = ow::warp_sum(tden);
+    tnum = ow::warp_sum(tnum);
+    sden = ow::warp_sum(sden);
+    snum = ow::warp_sum(snum);
+    if (lane == 0) {
+      const float frac = fminf(fmaxf(tnum / tden, 0.0f), 1.0f);
+      const float logit = fmaf(snum / sden, sc[2], sc[4]);
+      s_send[lr][a] = sigmoid_f(logit * sc[3]);
+      out[(static_cast<long long>(r) * L.rows + row) * kOutPerRow + a * 2] = frac;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kRowsPerCta) {
+    const int lr = threadIdx.x, row = row0 + lr;
+    if (row < L.rows) {
+      float sum = 0.0f;
+      for (int a = 0; a < static_cast<int>(kTargets); ++a) sum += s_send[lr][a];
+      const float norm = sum > 1.0f ? 1.0f / sum : 1.0f;
+      for (int a = 0; a < static_cast<int>(kTargets); ++a)
+        out[(static_cast<long long>(r) * L.rows + row) * kOutPerRow + a * 2 + 1] = s_send[lr][a] * norm;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- legacy TrainableTransformer (model.rs:210-301)
+// CTA per game: hidden [rows][d] in shared memory; per layer, per head, scaled
+// max-subtracted softmax over rows; h = tanh(h + attn*scale); sigmoid heads.
+__global__ void trainable_kernel(const float* __restrict__ in, const float* __restrict__ w, float* __restrict__ out,
+                                 int rows, int d, int heads, int layers) {
+  extern __shared__ float sm[];
+  float* hid = sm;               // rows*d
+  float* nxt = sm + rows * d;    // rows*d
+  const int g = blockIdx.x;
+  const float* inp = w;
+  const float* pos = w + 2 * d;
+  const float* scales = pos + d;
+  const float* outp = scales + static_cast<long long>(layers) * d;
+  for (int i = threadIdx.x; i < rows * d; i += blockDim.x) {
+    const int r = i / d, k = i % d;
+    const float f0 = in[(static_cast<long long>(g) * rows + r) * 2];
+    const float f1 = in[(static_cast<long long>(g) * rows + r) * 2 + 1];
+    const float p = static_cast<float>(r) / static_cast<float>(rows);
+    hid[i] = tanhf(p * pos[k] + f0 * inp[k] + f1 * inp[d + k]);
+  }
+  __syncthreads();
+  const int hd = d / heads;
+  const float inv = 1.0f / sqrtf(static_cast<float>(hd));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int l = 0; l < layers; ++l) {
+    for (int item = warp; item < heads * rows; item += nw) {
+      const int h = item / rows, s = item % rows;
+      float mx = -INFINITY;
+      for (int t = 0; t < rows; ++t) {
+        float part = 0.0f;
+        for (int c = lane; c < hd; c += 32) part += hid[s * d + h * hd + c] * hid[t * d + h * hd + c];
+        mx = fmaxf(mx, ow::warp_sum(part) * inv);
+      }
+      float den = 0.0f;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // hd <= 256 -> 8 per lane
+      for (int t = 0; t < rows; ++t) {
+        float part = 0.0f;
+        for (int c = lane; c < hd; c += 32) part += hid[s * d + h * hd + c] * hid[t * d + h * hd + c];
+        const float e = expf(ow::warp_sum(part) * inv - mx);
+        den += e;
+        for (int c = lane, i = 0; c < hd; c += 32, ++i) acc[i] = fmaf(e, hid[t * d + h * hd + c], acc[i]);
+      }
+      for (int c = lane, i = 0; c < hd; c += 32, ++i) nxt[s * d + h * hd + c] = acc[i] / den;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * d; i += blockDim.x)
+      hid[i] = tanhf(hid[i] + nxt[i] * scales[static_cast<long long>(l) * d + (i % d)]);
+    __syncthreads();
+  }
+  const float sc = sqrtf(static_cast<float>(d));
+  for (int r = warp; r < rows; r += nw) {
+    float t0 = 0.0f, t1 = 0.0f;
+    for (int k = lane; k < d; k += 32) {
+      t0 += hid[r * d + k] * outp[k];
+      t1 += hid[r * d + k] * outp[d + k];
+    }
+    t0 = ow::warp_sum(t0);
+    t1 = ow::warp_sum(t1);
+    if (lane == 0) {
+      out[(static_cast<long long>(g) * rows + r) * 2] = sigmoid_f(t0 / sc);
+      out[(static_cast<long long>(g) * rows + r) * 2 + 1] = sigmoid_f(t1 / sc);
+    }
+  }
+}
+
+__global__ void copy_kernel(const float4* __restrict__ in, float4* __restrict__ out, size_t n4, const float* in_tail,
+                            float* out_tail, size_t tail) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4; i += gridDim.x * blockDim.x)
+    out[i] = in[i];
+  if (blockIdx.x == 0 && threadIdx.x < tail) out_tail[threadIdx.x] = in_tail[threadIdx.x];
+}
+
+// ---------------------------------------------------------------- process-global workspace
+struct Workspace {
+  std::mutex mu;
+  // population
+  float* weights = nullptr;
+  size_t weights_cap = 0;  // floats
+  size_t models = 0;
+  OrbitWarsCudaTrue2DShape shape{0, 0, 0};
+  bool resident = false;
+  size_t request_capacity = 0;
+  // per-call buffers
+  float* in = nullptr;
+  size_t in_cap = 0;
+  float* out = nullptr;
+  size_t out_cap = 0;
+  float* m = nullptr;
+  size_t m_cap = 0;
+  size_t* idx = nullptr;
+  size_t idx_cap = 0;
+  int* err = nullptr;
+  cudaStream_t stream = nullptr;
+};
+
+Workspace& ws() {
+  static Workspace* w = new Workspace();  // lives for the process, like the reference's
+  return *w;
+}
+
+template <typename T>
+cudaError_t ensure(T*& p, size_t& cap, size_t n) {
+  if (n <= cap && p != nullptr) return cudaSuccess;
+  if (p != nullptr) cudaFree(p);
+  p = nullptr;
+  cap = 0;
+  const cudaError_t e = cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T));
+  if (e == cudaSuccess) cap = n;
+  return e;
+}
+
+cudaError_t ensure_common(Workspace& W) {
+  if (W.stream == nullptr) {
+    const cudaError_t e = cudaStreamCreateWithFlags(&W.stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return e;
+  }
+  if (W.err == nullptr) {
+    const cudaError_t e = cudaMalloc(&W.err, sizeof(int));
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+bool same_shape(const OrbitWarsCudaTrue2DShape& a, const OrbitWarsCudaTrue2DShape& b) {
+  return a.layer_count == b.layer_count && a.row_count == b.row_count && a.head_count == b.head_count;
+}
+
+const char* device_error_text(int code) {
+  switch (code) {
+    case ow::kErrBadModelIndex: return "model index outside the population";
+    default: return "device error";
+  }
+}
+
+// Uploads `models` models into the resident population.
+OrbitWarsCudaStatus upload(Workspace& W, const float* all_w, size_t models, const OrbitWarsCudaTrue2DShape& shape) {
+  const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
+  const size_t dt = dev_total(L), pad = matrix_pad(L);
+  T2_TRY(ensure(W.weights, W.weights_cap, dt * models));
+  // prefix (input pair .. expand bias) and the rest (matrix .. output scalars), one strided copy each
+  T2_TRY(cudaMemcpy2DAsync(W.weights, dt * sizeof(float), all_w, L.total * sizeof(float), L.matrix * sizeof(float),
+                           models, cudaMemcpyHostToDevice, W.stream));
+  T2_TRY(cudaMemcpy2DAsync(W.weights + L.matrix + pad, dt * sizeof(float), all_w + L.matrix, L.total * sizeof(float),
+                           (L.total - L.matrix) * sizeof(float), models, cudaMemcpyHostToDevice, W.stream));
+  W.models = models;
+  W.shape = shape;
+  W.resident = true;
+  return ok();
+}
+
+// Runs the forward for `n` requests whose inputs are host buffers.
+OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const size_t* model_indices, float* output_rows,
+                                size_t n, const OrbitWarsCudaTrue2DShape& shape) {
+  const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
+  const T2Dev D = dev_layout(L);
+  const size_t in_n = n * L.rows * kFeatures, out_n = n * L.rows * kOutPerRow, m_n = n * L.cells;
+  T2_TRY(ensure(W.in, W.in_cap, in_n));
+  T2_TRY(ensure(W.out, W.out_cap, out_n));
+  T2_TRY(ensure(W.m, W.m_cap, m_n));
+  T2_TRY(ensure(W.idx, W.idx_cap, n));
+  T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
+  T2_TRY(cudaMemcpyAsync(W.in, input_rows, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
+  const size_t* didx = nullptr;
+  if (model_indices != nullptr) {
+    T2_TRY(cudaMemcpyAsync(W.idx, model_indices, n * sizeof(size_t), cudaMemcpyHostToDevice, W.stream));
+    didx = W.idx;
+  }
+  const int models = static_cast<int>(W.models);
+  const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n));
+  t2_expand_pre<<<g1, 256, 0, W.stream>>>(W.in, didx, W.weights, models, D, W.m, W.err);
+  T2_TRY(cudaGetLastError());
+  const size_t smem = L.cells * sizeof(float2);
+  T2_TRY(cudaFuncSetAttribute(t2_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  t2_attention<<<static_cast<unsigned>(n), kAttnThreads, smem, W.stream>>>(didx, W.weights, models, D, W.m, W.err);
+  T2_TRY(cudaGetLastError());
+  const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n));
+  const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
+  t2_post_collapse<<<g3, threads3, 0, W.stream>>>(didx, W.weights, models, D, W.m, W.out, W.err);
+  T2_TRY(cudaGetLastError());
+  int herr = 0;
+  T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+  T2_TRY(cudaMemcpyAsync(&herr, W.err, sizeof(int), cudaMemcpyDeviceToHost, W.stream));
+  T2_TRY(cudaStreamSynchronize(W.stream));
+  if (herr != 0) return rt(device_error_text(herr));
+  return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+OrbitWarsCudaStatus orbit_wars_cuda_status(void) {
+  int n = 0;
+  const cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return from_cuda(e);
+  if (n <= 0) return rt("no cuda devices");
+  return {kOk, "cuda device available"};
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_encode_identity_batch(const float* input_rows, float* output_rows,
+                                                          size_t game_count, size_t row_count, size_t feature_count) {
+  if (input_rows == nullptr || output_rows == nullptr || game_count == 0 || row_count == 0 || feature_count == 0)
+    return bad("invalid batch buffer");
+  const size_t n = game_count * row_count * feature_count;
+  const bool aligned = (reinterpret_cast<uintptr_t>(input_rows) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(output_rows) % 16 == 0);
+  const size_t n4 = aligned ? n / 4 : 0;
+  const size_t tail = n - n4 * 4;
+  if (tail > 1024) {
+    // unaligned large copy: plain device-to-device copy
+    T2_TRY(cudaMemcpy(output_rows, input_rows, n * sizeof(float), cudaMemcpyDeviceToDevice));
+    return from_cuda(cudaDeviceSynchronize());
+  }
+  const int blocks = static_cast<int>(std::min<size_t>((n4 + 255) / 256 + 1, 148 * 16));
+  copy_kernel<<<blocks, 256>>>(reinterpret_cast<const float4*>(input_rows), reinterpret_cast<float4*>(output_rows), n4,
+                               input_rows + n4 * 4, output_rows + n4 * 4, tail);
+  T2_TRY(cudaGetLastError());
+  return from_cuda(cudaDeviceSynchronize());
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_trainable_forward(const float* input_rows, const float* weights,
+                                                      float* output_rows, size_t game_count,
+                                                      OrbitWarsCudaTransformerShape shape) {
+  if (input_rows == nullptr || weights == nullptr || output_rows == nullptr || game_count == 0)
+    return bad("invalid trainable buffer");
+  // orbit_wars_cuda.cu:281-285 shape rule (d in [8, 256], heads | d)
+  if (shape.layer_count == 0 || shape.d_model < 8 || shape.d_model > 256 || shape.head_count == 0 ||
+      shape.row_count == 0 || shape.d_model % shape.head_count != 0 || shape.row_count > 256)
+    return bad("invalid transformer shape");
+  const size_t d = shape.d_model, rows = shape.row_count, L = shape.layer_count;
+  const size_t wcount = 2 * d + d + L * d + 2 * d;
+  const size_t in_n = game_count * rows * 2, out_n = game_count * rows * 2;
+  const size_t smem = 2 * rows * d * sizeof(float);
+  if (smem > 200 * 1024) return bad("trainable shape too large for one CTA");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  T2_TRY(ensure_common(W));
+  float *dw = nullptr, *din = nullptr, *dout = nullptr;
+  T2_TRY(cudaMalloc(&dw, wcount * sizeof(float)));
+  cudaError_t e = cudaMalloc(&din, in_n * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&dout, out_n * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dw, weights, wcount * sizeof(float), cudaMemcpyHostToDevice, W.stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(din, input_rows, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(trainable_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess) {
+    trainable_kernel<<<static_cast<unsigned>(game_count), 256, smem, W.stream>>>(
+        din, dw, dout, static_cast<int>(rows), static_cast<int>(d), static_cast<int>(shape.head_count),
+        static_cast<int>(L));
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(output_rows, dout, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(W.stream);
+  cudaFree(dw);
+  cudaFree(din);
+  cudaFree(dout);
+  return from_cuda(e);
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward(const float* input_rows, const float* weights, float* output_rows,
+                                                   size_t game_count, OrbitWarsCudaTrue2DShape shape) {
+  if (input_rows == nullptr || weights == nullptr || output_rows == nullptr || game_count == 0)
+    return bad("invalid true2d buffer");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  T2_TRY(ensure_common(W));
+  // single-model call: uploads that model (the resident population is replaced)
+  OrbitWarsCudaStatus s = upload(W, weights, 1, shape);
+  if (s.code != kOk) return s;
+  W.resident = false;  // a single-model upload is not a population
+  return run_forward(W, input_rows, nullptr, output_rows, game_count, shape);
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_many(const float* input_rows, const size_t* model_indices,
+                                                        const float* all_weights, float* output_rows,
+                                                        size_t request_count, size_t model_count,
+                                                        OrbitWarsCudaTrue2DShape shape) {
+  if (input_rows == nullptr || model_indices == nullptr || all_weights == nullptr || output_rows == nullptr ||
+      request_count == 0 || model_count == 0)
+    return bad("invalid true2d many buffer");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  for (size_t r = 0; r < request_count; ++r)
+    if (model_indices[r] >= model_count) return bad("model index out of range");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  T2_TRY(ensure_common(W));
+  OrbitWarsCudaStatus s = upload(W, all_weights, model_count, shape);
+  if (s.code != kOk) return s;
+  W.request_capacity = std::max(W.request_capacity, request_count);
+  return run_forward(W, input_rows, model_indices, output_rows, request_count, shape);
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_upload_population(const float* all_weights, size_t model_count,
+                                                             size_t request_capacity,
+                                                             OrbitWarsCudaTrue2DShape shape) {
+  if (all_weights == nullptr || model_count == 0 || request_capacity == 0) return bad("invalid true2d population");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  T2_TRY(ensure_common(W));
+  OrbitWarsCudaStatus s = upload(W, all_weights, model_count, shape);
+  if (s.code != kOk) return s;
+  // size the per-call buffers for the capacity up front (orbit_wars_cuda.cu:505-573)
+  const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
+  T2_TRY(ensure(W.in, W.in_cap, request_capacity * L.rows * kFeatures));
+  T2_TRY(ensure(W.out, W.out_cap, request_capacity * L.rows * kOutPerRow));
+  T2_TRY(ensure(W.m, W.m_cap, request_capacity * L.cells));
+  T2_TRY(ensure(W.idx, W.idx_cap, request_capacity));
+  W.request_capacity = request_capacity;
+  return from_cuda(cudaStreamSynchronize(W.stream));
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_many_resident(const float* input_rows,
+                                                                 const size_t* model_indices, float* output_rows,
+                                                                 size_t request_count,
+                                                                 OrbitWarsCudaTrue2DShape shape) {
+  if (input_rows == nullptr || model_indices == nullptr || output_rows == nullptr || request_count == 0)
+    return bad("invalid true2d resident buffer");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  if (!W.resident) return rt("true2d population is not loaded");  // orbit_wars_cuda.cu:2808-2813
+  if (!same_shape(W.shape, shape)) return bad("true2d shape differs from the resident population");
+  if (request_count > W.request_capacity) return rt("true2d request capacity exceeded");
+  for (size_t r = 0; r < request_count; ++r)
+    if (model_indices[r] >= W.models) return bad("model index out of range");
+  return run_forward(W, input_rows, model_indices, output_rows, request_count, shape);
+}
+
+typedef OrbitWarsCudaStatus (*TrainFn)(const float*, const float*, const int*, const float*, const size_t*, float*,
+                                       size_t, size_t, OrbitWarsCudaTrue2DShape, OrbitWarsCudaTrue2DTrainingConfig);
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
+    const float* input_rows, const float* output_rows, const int* rewards, const float* target_action_rewards,
+    const size_t* model_indices, float* all_weights, size_t sample_count, size_t model_count,
+    OrbitWarsCudaTrue2DShape shape, OrbitWarsCudaTrue2DTrainingConfig training_config) {
+  if (input_rows == nullptr || output_rows == nullptr || rewards == nullptr || target_action_rewards == nullptr ||
+      model_indices == nullptr || all_weights == nullptr || sample_count == 0 || model_count == 0)
+    return bad("invalid true2d training buffer");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  const char* path = std::getenv("ORBIT_WARS_CUDA_TRAIN_LIB_PATH");
+  if (path == nullptr || *path == '\0') return rt("training not provided");
+  static std::mutex mu;
+  static TrainFn fn = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (fn == nullptr) {
+    void* h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+    if (h == nullptr) return rt("training library could not be opened");
+    fn = reinterpret_cast<TrainFn>(dlsym(h, "orbit_wars_cuda_true2d_train_full_attention"));
+    if (fn == nullptr || fn == &orbit_wars_cuda_true2d_train_full_attention) {
+      fn = nullptr;
+      return rt("training library lacks the training symbol");
+    }
+  }
+  return fn(input_rows, output_rows, rewards, target_action_rewards, model_indices, all_weights, sample_count,
+            model_count, shape, training_config);
+}
+
+}  // extern "C"

@@ -1,0 +1,940 @@
+// Host side of the encoder-policy forward: handle lifetime, weight
+// conversion/upload, TMA descriptors, the per-precision launch sequence and
+// the extern "C" entry points declared in include/ow_policy.h.
+//
+// Error convention of the reference GPU ABI (native/cuda/orbit_wars_cuda.cu:
+// 12-14 status codes, :274-279 status_from_cuda): arguments are validated
+// before any launch (BAD_ARGUMENT), CUDA failures and device-side error flags
+// become RUNTIME_ERROR with a static message. There is no CPU fallback: a
+// missing device or a failed launch is an error.
+
+#include "ow_policy.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "ow_common.cuh"
+#include "ow_kernels.cuh"
+#include "ow_tc_gemm.cuh"
+
+namespace {
+
+using namespace ow;
+
+OwStatus st_ok() { return {OW_STATUS_OK, "ok"}; }
+OwStatus st_bad(const char* m) { return {OW_STATUS_BAD_ARGUMENT, m}; }
+OwStatus st_rt(const char* m) { return {OW_STATUS_RUNTIME_ERROR, m}; }
+OwStatus st_cuda(cudaError_t e) { return e == cudaSuccess ? st_ok() : st_rt(cudaGetErrorString(e)); }
+
+#define OW_TRY(expr)                         \
+  do {                                       \
+    const cudaError_t e_ = (expr);           \
+    if (e_ != cudaSuccess) return st_cuda(e_); \
+  } while (0)
+
+const char* device_error_message(int code) {
+  switch (code) {
+    case kErrWaitTimeout: return "device wait timed out (kernel aborted)";
+    case kErrBadCount: return "entity count outside [0, n_entities]";
+    case kErrBadModelIndex: return "model index outside the population";
+    default: return "device error";
+  }
+}
+
+// ---------------------------------------------------------------- weight layout (SPEC.md section 3)
+struct BlobLayout {
+  size_t we, be, lnf_g, lnf_b, wp, bp, wv, bv, total;
+  struct Layer {
+    size_t ln1g, ln1b, wqkv, bqkv, wo, bo, ln2g, ln2b, w1, b1, w2, b2;
+  };
+  std::vector<Layer> layer;
+};
+
+BlobLayout blob_layout(const OwPolicyConfig& c) {
+  BlobLayout o;
+  const size_t d = c.d_model, F = c.features, f = c.ffn, P = c.actions;
+  size_t at = 0;
+  auto take = [&at](size_t n) {
+    const size_t r = at;
+    at += n;
+    return r;
+  };
+  o.we = take(d * F);
+  o.be = take(d);
+  o.layer.resize(c.layers);
+  for (auto& L : o.layer) {
+    L.ln1g = take(d);
+    L.ln1b = take(d);
+    L.wqkv = take(3 * d * d);
+    L.bqkv = take(3 * d);
+    L.wo = take(d * d);
+    L.bo = take(d);
+    L.ln2g = take(d);
+    L.ln2b = take(d);
+    L.w1 = take(f * d);
+    L.b1 = take(f);
+    L.w2 = take(d * f);
+    L.b2 = take(d);
+  }
+  o.lnf_g = take(d);
+  o.lnf_b = take(d);
+  o.wp = take(P * d);
+  o.bp = take(P);
+  o.wv = take(d);
+  o.bv = take(1);
+  o.total = at;
+  return o;
+}
+
+const char* validate_config(const OwPolicyConfig& c) {
+  if (c.batch_capacity <= 0 || c.batch_capacity > (1 << 20)) return "batch_capacity out of range";
+  if (c.n_entities <= 0 || c.n_entities > 128) return "n_entities must be in [1, 128]";
+  if (c.features <= 0 || c.features > 32) return "features must be in [1, 32]";
+  if (c.d_model % 32 != 0 || c.d_model < 128 || c.d_model > 512) return "d_model must be a multiple of 32 in [128, 512]";
+  if (c.heads * 32 != c.d_model) return "heads must equal d_model / 32 (head_dim 32)";
+  if (c.ffn <= 0 || c.ffn % 128 != 0 || c.ffn > 4096) return "ffn must be a multiple of 128 in [128, 4096]";
+  if (c.layers <= 0 || c.layers > 64) return "layers must be in [1, 64]";
+  if (c.actions <= 0 || c.actions > 32) return "actions must be in [1, 32]";
+  if (c.precision < OW_PRECISION_F32 || c.precision > OW_PRECISION_FP8) return "unknown precision";
+  if (c.sample_actions != 0 && c.sample_actions != 1) return "sample_actions must be 0 or 1";
+  if ((c.logits_dtype != OW_DTYPE_F32 && c.logits_dtype != OW_DTYPE_BF16) ||
+      (c.value_dtype != OW_DTYPE_F32 && c.value_dtype != OW_DTYPE_BF16))
+    return "unknown output dtype";
+  if (c.io != OW_IO_HOST && c.io != OW_IO_DEVICE) return "unknown io mode";
+  if (c.precision != OW_PRECISION_F32) {
+    // tensor-core path: QKV tiles of 256 or 128 columns, LN-fused tiles of d columns
+    if ((3 * c.d_model) % 128 != 0) return "3*d_model must be a multiple of 128";
+    if (c.d_model != 128 && c.d_model != 256 && c.d_model != 384 && c.d_model != 512)
+      return "tensor-core path supports d_model 128, 256, 384, 512";
+    if (c.ffn % 256 != 0) return "tensor-core path needs ffn % 256 == 0";
+    if (c.precision == OW_PRECISION_FP8 && c.d_model != 256) return "fp8 path supports d_model 256";
+  }
+  return nullptr;
+}
+
+// ---------------------------------------------------------------- TMA descriptors
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// K-major 2-D map: rows of `inner` elements, box = 128 bytes x box_rows, 128 B swizzle.
+bool make_kmajor_map(CUtensorMap* map, const void* base, bool e4m3, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const uint32_t elt = e4m3 ? 1 : 2;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * elt};
+  cuuint32_t box[2] = {128 / elt, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, e4m3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------- host conversions
+uint16_t f32_to_bf16_bits(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u) return static_cast<uint16_t>((u >> 16) | ((u & 0xFFFFu) ? 0x40u : 0u));
+  const uint32_t rounding = 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>((u + rounding) >> 16);
+}
+
+// Saturating round-to-nearest-even f32 -> e4m3, the same conversion the
+// device kernels use (cuda_fp8.h, callable on the host).
+uint8_t f32_to_e4m3_bits(float f) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(f, __NV_SATFINITE, __NV_E4M3));
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- handle
+struct OwPolicy {
+  OwPolicyConfig cfg{};
+  BlobLayout lay;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int num_sms = 148;
+  size_t cap_rows = 0;
+
+  // weights (device arena)
+  uint8_t* warena = nullptr;
+  size_t warena_bytes = 0;
+  struct LayerW {
+    float *ln1g, *ln1b, *bqkv, *bo, *ln2g, *ln2b, *b1, *b2;
+    void *wqkv, *wo, *w1, *w2;      // f32 / bf16 / e4m3 [out, in]
+    float *sqkv, *so, *s1, *s2;     // e4m3 per-output-channel scales
+    CUtensorMap mqkv, mo, m1, m2;
+  };
+  std::vector<LayerW> lw;
+  float *we = nullptr, *be = nullptr, *lnfg = nullptr, *lnfb = nullptr, *wp = nullptr, *bp = nullptr,
+        *wv = nullptr, *bv = nullptr;
+
+  // workspace
+  uint8_t* ws = nullptr;
+  int *counts = nullptr, *offsets = nullptr, *err = nullptr;
+  float* feats = nullptr;
+  void *logits = nullptr, *value = nullptr;
+  int* actions = nullptr;
+  void *x = nullptr, *ln = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr;
+  uint8_t *ln8 = nullptr, *attn8 = nullptr, *h8 = nullptr;
+  float *ln_scale = nullptr, *attn_scale = nullptr, *h_scale = nullptr;
+  CUtensorMap m_ln, m_attn, m_h;
+  int qkv_block_n = 256;
+  int launches = 0;
+  // profiling (ow_policy_profile_begin/_end)
+  std::vector<cudaEvent_t> prof_events;
+  std::vector<const char*> prof_names;
+  size_t prof_used = 0;
+  bool prof_on = false;
+};
+
+namespace {
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev_);
+    if (prev_ != dev) cudaSetDevice(dev);
+    dev_ = dev;
+  }
+  ~DeviceGuard() {
+    if (prev_ != dev_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = 0, dev_ = 0;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+template <int BN, int EPI, bool FP8>
+cudaError_t set_gemm_attr() {
+  return cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              TcGemmShape<BN>::kSmemBytes);
+}
+
+template <int BN, int EPI, bool FP8>
+cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw, const TcGemmParams& prm) {
+  using S = TcGemmShape<BN>;
+  const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM) * (prm.n / BN);
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
+  tc_gemm_kernel<BN, EPI, FP8><<<grid, kGemmThreads, S::kSmemBytes, P.stream>>>(ma, mw, prm);
+  return cudaGetLastError();
+}
+
+// Dispatch on the d-wide LN-fused tile.
+cudaError_t launch_gemm_resid_ln(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw,
+                                 const TcGemmParams& prm, bool fp8) {
+  const int d = P.cfg.d_model;
+  if (fp8) return launch_gemm<256, kEpiResidLn, true>(P, ma, mw, prm);
+  switch (d) {
+    case 128: return launch_gemm<128, kEpiResidLn, false>(P, ma, mw, prm);
+    case 256: return launch_gemm<256, kEpiResidLn, false>(P, ma, mw, prm);
+    case 384: return launch_gemm<384, kEpiResidLn, false>(P, ma, mw, prm);
+    default: return launch_gemm<512, kEpiResidLn, false>(P, ma, mw, prm);
+  }
+}
+
+cudaError_t set_all_gemm_attrs() {
+  cudaError_t e = cudaSuccess;
+  auto upd = [&e](cudaError_t r) {
+    if (e == cudaSuccess) e = r;
+  };
+  upd(set_gemm_attr<128, kEpiBias, false>());
+  upd(set_gemm_attr<256, kEpiBias, false>());
+  upd(set_gemm_attr<256, kEpiBiasGelu, false>());
+  upd(set_gemm_attr<128, kEpiResidLn, false>());
+  upd(set_gemm_attr<256, kEpiResidLn, false>());
+  upd(set_gemm_attr<384, kEpiResidLn, false>());
+  upd(set_gemm_attr<512, kEpiResidLn, false>());
+  upd(set_gemm_attr<256, kEpiBias, true>());
+  upd(set_gemm_attr<256, kEpiBiasGelu, true>());
+  upd(set_gemm_attr<256, kEpiResidLn, true>());
+  return e;
+}
+
+template <int DPL>
+cudaError_t launch_embed(const OwPolicy& P, int batch) {
+  const auto& c = P.cfg;
+  const long long slots = static_cast<long long>(batch) * c.n_entities;
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((slots + 7) / 8, P.num_sms * 8LL)));
+  const size_t smem = static_cast<size_t>(c.features) * DPL * 32 * sizeof(float);
+  const float* g = P.lw[0].ln1g;
+  const float* b = P.lw[0].ln1b;
+  if (c.precision == OW_PRECISION_F32) {
+    auto k = embed_ln_kernel<DPL, float, 0>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
+                                     static_cast<float*>(P.x), P.ln, nullptr);
+  } else if (c.precision == OW_PRECISION_BF16) {
+    auto k = embed_ln_kernel<DPL, __nv_bfloat16, 1>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
+                                     static_cast<__nv_bfloat16*>(P.x), P.ln, nullptr);
+  } else {
+    auto k = embed_ln_kernel<DPL, __nv_bfloat16, 2>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
+                                     static_cast<__nv_bfloat16*>(P.x), P.ln8, P.ln_scale);
+  }
+  return cudaGetLastError();
+}
+
+template <int DPL, typename YT, bool LB, bool VB>
+void heads_launch(const OwPolicy& P, int batch, size_t smem, uint64_t seed, void* logits, void* value, int* actions) {
+  const auto& c = P.cfg;
+  cudaFuncSetAttribute(heads_kernel<DPL, YT, LB, VB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  heads_kernel<DPL, YT, LB, VB><<<batch, 128, smem, P.stream>>>(static_cast<const YT*>(P.ln), P.offsets,
+                                                                c.n_entities, c.actions, P.wp, P.bp, P.wv, P.bv,
+                                                                c.sample_actions, seed, logits, value, actions);
+}
+
+template <int DPL>
+cudaError_t launch_heads(const OwPolicy& P, int batch, uint64_t seed, void* logits, void* value, int* actions) {
+  const auto& c = P.cfg;
+  const size_t smem = static_cast<size_t>(c.actions + 4) * DPL * 32 * sizeof(float);
+  const bool lb = c.logits_dtype == OW_DTYPE_BF16, vb = c.value_dtype == OW_DTYPE_BF16;
+  if (c.precision == OW_PRECISION_F32) {
+    if (lb && vb) heads_launch<DPL, float, true, true>(P, batch, smem, seed, logits, value, actions);
+    else if (lb) heads_launch<DPL, float, true, false>(P, batch, smem, seed, logits, value, actions);
+    else if (vb) heads_launch<DPL, float, false, true>(P, batch, smem, seed, logits, value, actions);
+    else heads_launch<DPL, float, false, false>(P, batch, smem, seed, logits, value, actions);
+  } else {
+    if (lb && vb) heads_launch<DPL, __nv_bfloat16, true, true>(P, batch, smem, seed, logits, value, actions);
+    else if (lb) heads_launch<DPL, __nv_bfloat16, true, false>(P, batch, smem, seed, logits, value, actions);
+    else if (vb) heads_launch<DPL, __nv_bfloat16, false, true>(P, batch, smem, seed, logits, value, actions);
+    else heads_launch<DPL, __nv_bfloat16, false, false>(P, batch, smem, seed, logits, value, actions);
+  }
+  return cudaGetLastError();
+}
+
+template <int DPL>
+cudaError_t launch_ln_f32(const OwPolicy& P, const int* m_valid, const float* g, const float* b) {
+  const int grid = static_cast<int>(std::min<size_t>((P.cap_rows + 7) / 8, static_cast<size_t>(P.num_sms) * 8));
+  layernorm_f32_kernel<DPL><<<grid, 256, 0, P.stream>>>(static_cast<const float*>(P.x), m_valid, g, b,
+                                                        static_cast<float*>(P.ln));
+  return cudaGetLastError();
+}
+
+cudaError_t dispatch_embed(const OwPolicy& P, int batch) {
+  switch (P.cfg.d_model / 32) {
+    case 4: return launch_embed<4>(P, batch);
+    case 8: return launch_embed<8>(P, batch);
+    case 12: return launch_embed<12>(P, batch);
+    case 16: return launch_embed<16>(P, batch);
+    default: return cudaErrorInvalidValue;
+  }
+}
+cudaError_t dispatch_heads(const OwPolicy& P, int batch, uint64_t seed, void* logits, void* value, int* actions) {
+  switch (P.cfg.d_model / 32) {
+    case 4: return launch_heads<4>(P, batch, seed, logits, value, actions);
+    case 8: return launch_heads<8>(P, batch, seed, logits, value, actions);
+    case 12: return launch_heads<12>(P, batch, seed, logits, value, actions);
+    case 16: return launch_heads<16>(P, batch, seed, logits, value, actions);
+    default: return cudaErrorInvalidValue;
+  }
+}
+cudaError_t dispatch_ln_f32(const OwPolicy& P, const int* m_valid, const float* g, const float* b) {
+  switch (P.cfg.d_model / 32) {
+    case 4: return launch_ln_f32<4>(P, m_valid, g, b);
+    case 8: return launch_ln_f32<8>(P, m_valid, g, b);
+    case 12: return launch_ln_f32<12>(P, m_valid, g, b);
+    case 16: return launch_ln_f32<16>(P, m_valid, g, b);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_attention(const OwPolicy& P, int batch) {
+  const auto& c = P.cfg;
+  const dim3 grid(batch, c.heads);
+  const float scale = 1.0f / std::sqrt(32.0f);
+  if (c.precision == OW_PRECISION_F32) {
+    const float* q = static_cast<const float*>(P.qkv);
+    float* o = static_cast<float*>(P.attn);
+    if (c.n_entities <= 32) attention_f32_kernel<32><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, scale);
+    else if (c.n_entities <= 64) attention_f32_kernel<64><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, scale);
+    else attention_f32_kernel<128><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, scale);
+  } else {
+    const auto* q = static_cast<const __nv_bfloat16*>(P.qkv);
+    auto* o = static_cast<__nv_bfloat16*>(P.attn);
+    const float sl2 = scale * 1.4426950408889634f;
+    if (c.n_entities <= 32) attention_bf16_kernel<32><<<grid, 64, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
+    else if (c.n_entities <= 64) attention_bf16_kernel<64><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
+    else if (c.n_entities <= 96) attention_bf16_kernel<96><<<grid, 192, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
+    else attention_bf16_kernel<128><<<grid, 256, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(const OwPolicy& P, const void* in, int k, uint8_t* out, float* scale) {
+  const int grid = static_cast<int>(std::min<size_t>((P.cap_rows + 7) / 8, static_cast<size_t>(P.num_sms) * 8));
+  quantize_rows_e4m3_kernel<<<grid, 256, 0, P.stream>>>(static_cast<const __nv_bfloat16*>(in), P.offsets, k, out,
+                                                       scale);
+  return cudaGetLastError();
+}
+
+// m_valid lives at offsets[batch]: the kernels read it from there.
+cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void* value, int* actions) {
+  const auto& c = P.cfg;
+  const int* m_valid = P.offsets + batch;
+  int launches = 0;
+  cudaError_t e;
+#define OW_STEP(name, expr)                                         \
+  do {                                                              \
+    if (P.prof_on && P.prof_used + 1 < P.prof_events.size()) {      \
+      cudaEventRecord(P.prof_events[P.prof_used], P.stream);         \
+      P.prof_names[P.prof_used++] = (name);                          \
+    }                                                               \
+    e = (expr);                                                     \
+    if (e != cudaSuccess) return e;                                 \
+    ++launches;                                                     \
+  } while (0)
+  OW_STEP("scan_counts", (scan_counts_kernel<<<1, 1024, 0, P.stream>>>(P.counts, batch, c.n_entities, P.offsets, P.err),
+           cudaGetLastError()));
+  OW_STEP("embed_ln", dispatch_embed(P, batch));
+  const int d = c.d_model, f = c.ffn;
+  if (c.precision == OW_PRECISION_F32) {
+    const dim3 blk(256);
+    auto grid_for = [&](int n) { return dim3((n + 63) / 64, static_cast<unsigned>((P.cap_rows + 63) / 64)); };
+    float* x = static_cast<float*>(P.x);
+    float* ln = static_cast<float*>(P.ln);
+    float* qkv = static_cast<float*>(P.qkv);
+    float* attn = static_cast<float*>(P.attn);
+    float* h = static_cast<float*>(P.h);
+    for (int l = 0; l < c.layers; ++l) {
+      const auto& W = P.lw[l];
+      OW_STEP("gemm_f32_qkv", (gemm_f32_kernel<kF32Bias><<<grid_for(3 * d), blk, 0, P.stream>>>(
+                   ln, static_cast<const float*>(W.wqkv), W.bqkv, qkv, m_valid, 3 * d, d),
+               cudaGetLastError()));
+      OW_STEP("attention", launch_attention(P, batch));
+      OW_STEP("gemm_f32_out_resid", (gemm_f32_kernel<kF32BiasResid><<<grid_for(d), blk, 0, P.stream>>>(
+                   attn, static_cast<const float*>(W.wo), W.bo, x, m_valid, d, d),
+               cudaGetLastError()));
+      OW_STEP("layernorm_f32", dispatch_ln_f32(P, m_valid, W.ln2g, W.ln2b));
+      OW_STEP("gemm_f32_ffn_up", (gemm_f32_kernel<kF32BiasGelu><<<grid_for(f), blk, 0, P.stream>>>(
+                   ln, static_cast<const float*>(W.w1), W.b1, h, m_valid, f, d),
+               cudaGetLastError()));
+      OW_STEP("gemm_f32_ffn_down_resid", (gemm_f32_kernel<kF32BiasResid><<<grid_for(d), blk, 0, P.stream>>>(
+                   h, static_cast<const float*>(W.w2), W.b2, x, m_valid, d, f),
+               cudaGetLastError()));
+      const bool last = l + 1 == c.layers;
+      OW_STEP("layernorm_f32", dispatch_ln_f32(P, m_valid, last ? P.lnfg : P.lw[l + 1].ln1g, last ? P.lnfb : P.lw[l + 1].ln1b));
+    }
+  } else {
+    const bool fp8 = c.precision == OW_PRECISION_FP8;
+    for (int l = 0; l < c.layers; ++l) {
+      const auto& W = P.lw[l];
+      const bool last = l + 1 == c.layers;
+      TcGemmParams q{};
+      q.m_valid = m_valid;
+      q.err = P.err;
+      // QKV projection
+      q.n = 3 * d;
+      q.k_blocks = fp8 ? d / 128 : d / 64;
+      q.bias = W.bqkv;
+      q.out = static_cast<__nv_bfloat16*>(P.qkv);
+      q.ld_out = 3 * d;
+      q.a_scale = P.ln_scale;
+      q.b_scale = W.sqkv;
+      if (fp8) OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, true>(P, P.m_ln, W.mqkv, q)));
+      else if (P.qkv_block_n == 256) OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, false>(P, P.m_ln, W.mqkv, q)));
+      else OW_STEP("gemm_qkv", (launch_gemm<128, kEpiBias, false>(P, P.m_ln, W.mqkv, q)));
+      // attention
+      OW_STEP("attention", launch_attention(P, batch));
+      if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, P.attn, d, P.attn8, P.attn_scale));
+      // out-projection + residual + LN2
+      TcGemmParams o{};
+      o.m_valid = m_valid;
+      o.err = P.err;
+      o.n = d;
+      o.k_blocks = fp8 ? d / 128 : d / 64;
+      o.bias = W.bo;
+      o.resid = static_cast<__nv_bfloat16*>(P.x);
+      o.ln_g = W.ln2g;
+      o.ln_b = W.ln2b;
+      o.ln_fp8 = fp8 ? 1 : 0;
+      o.ln_out = fp8 ? static_cast<void*>(P.ln8) : P.ln;
+      o.ln_scale = P.ln_scale;
+      o.a_scale = P.attn_scale;
+      o.b_scale = W.so;
+      OW_STEP("gemm_out_resid_ln", launch_gemm_resid_ln(P, P.m_attn, W.mo, o, fp8));
+      // FFN up + GELU
+      TcGemmParams u{};
+      u.m_valid = m_valid;
+      u.err = P.err;
+      u.n = f;
+      u.k_blocks = fp8 ? d / 128 : d / 64;
+      u.bias = W.b1;
+      u.out = static_cast<__nv_bfloat16*>(P.h);
+      u.ld_out = f;
+      u.a_scale = P.ln_scale;
+      u.b_scale = W.s1;
+      if (fp8) OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, true>(P, P.m_ln, W.m1, u)));
+      else OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, false>(P, P.m_ln, W.m1, u)));
+      if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, P.h, f, P.h8, P.h_scale));
+      // FFN down + residual + next LN (LN1 of the next block, or the final LN)
+      TcGemmParams w{};
+      w.m_valid = m_valid;
+      w.err = P.err;
+      w.n = d;
+      w.k_blocks = fp8 ? f / 128 : f / 64;
+      w.bias = W.b2;
+      w.resid = static_cast<__nv_bfloat16*>(P.x);
+      w.ln_g = last ? P.lnfg : P.lw[l + 1].ln1g;
+      w.ln_b = last ? P.lnfb : P.lw[l + 1].ln1b;
+      w.ln_fp8 = (fp8 && !last) ? 1 : 0;
+      w.ln_out = w.ln_fp8 ? static_cast<void*>(P.ln8) : P.ln;
+      w.ln_scale = P.ln_scale;
+      w.a_scale = P.h_scale;
+      w.b_scale = W.s2;
+      OW_STEP("gemm_ffn_down_resid_ln", launch_gemm_resid_ln(P, P.m_h, W.m2, w, fp8));
+    }
+  }
+  OW_STEP("heads", dispatch_heads(P, batch, seed, logits, value, actions));
+  if (P.prof_on && P.prof_used < P.prof_events.size()) {
+    cudaEventRecord(P.prof_events[P.prof_used], P.stream);
+    P.prof_names[P.prof_used++] = nullptr;  // end of this forward
+  }
+#undef OW_STEP
+  P.launches = launches;
+  return cudaSuccess;
+}
+
+size_t elem_bytes_for(int precision) { return precision == OW_PRECISION_F32 ? 4 : (precision == OW_PRECISION_BF16 ? 2 : 1); }
+
+// Builds the device weight-arena image on the host and uploads it.
+OwStatus upload_weights(OwPolicy& P, const float* w) {
+  const auto& c = P.cfg;
+  const auto& L = P.lay;
+  const int prec = c.precision;
+  const size_t eb = elem_bytes_for(prec);
+  const size_t d = c.d_model, f = c.ffn;
+  // arena plan
+  std::vector<uint8_t> img;
+  auto reserve = [&img](size_t bytes) {
+    const size_t at = align_up(img.size(), 256);
+    img.resize(at + bytes);
+    return at;
+  };
+  auto put_f32 = [&](size_t src, size_t n) {
+    const size_t at = reserve(n * 4);
+    std::memcpy(img.data() + at, w + src, n * 4);
+    return at;
+  };
+  struct Mat {
+    size_t at, scale_at;
+  };
+  auto put_mat = [&](size_t src, size_t rows, size_t cols) {
+    Mat m{};
+    m.at = reserve(rows * cols * eb);
+    m.scale_at = 0;
+    if (prec == OW_PRECISION_F32) {
+      std::memcpy(img.data() + m.at, w + src, rows * cols * 4);
+    } else if (prec == OW_PRECISION_BF16) {
+      uint16_t* dst = reinterpret_cast<uint16_t*>(img.data() + m.at);
+      for (size_t i = 0; i < rows * cols; ++i) dst[i] = f32_to_bf16_bits(w[src + i]);
+    } else {
+      std::vector<float> scales(rows);
+      for (size_t r = 0; r < rows; ++r) {
+        float amax = 0.0f;
+        for (size_t k = 0; k < cols; ++k) amax = std::max(amax, std::fabs(w[src + r * cols + k]));
+        scales[r] = amax > 0.0f ? amax / 448.0f : 1.0f;
+      }
+      uint8_t* dst = img.data() + m.at;
+      for (size_t r = 0; r < rows; ++r)
+        for (size_t k = 0; k < cols; ++k) dst[r * cols + k] = f32_to_e4m3_bits(w[src + r * cols + k] / scales[r]);
+      m.scale_at = reserve(rows * 4);
+      std::memcpy(img.data() + m.scale_at, scales.data(), rows * 4);
+    }
+    return m;
+  };
+  const size_t we = put_f32(L.we, d * c.features), be = put_f32(L.be, d);
+  struct LayerAt {
+    size_t ln1g, ln1b, bqkv, bo, ln2g, ln2b, b1, b2;
+    Mat qkv, o, w1, w2;
+  };
+  std::vector<LayerAt> la(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const auto& s = L.layer[l];
+    la[l].ln1g = put_f32(s.ln1g, d);
+    la[l].ln1b = put_f32(s.ln1b, d);
+    la[l].qkv = put_mat(s.wqkv, 3 * d, d);
+    la[l].bqkv = put_f32(s.bqkv, 3 * d);
+    la[l].o = put_mat(s.wo, d, d);
+    la[l].bo = put_f32(s.bo, d);
+    la[l].ln2g = put_f32(s.ln2g, d);
+    la[l].ln2b = put_f32(s.ln2b, d);
+    la[l].w1 = put_mat(s.w1, f, d);
+    la[l].b1 = put_f32(s.b1, f);
+    la[l].w2 = put_mat(s.w2, d, f);
+    la[l].b2 = put_f32(s.b2, d);
+  }
+  const size_t lnfg = put_f32(L.lnf_g, d), lnfb = put_f32(L.lnf_b, d);
+  const size_t wp = put_f32(L.wp, c.actions * d), bp = put_f32(L.bp, c.actions);
+  const size_t wv = put_f32(L.wv, d), bv = put_f32(L.bv, 1);
+  img.resize(align_up(img.size(), 256));
+
+  if (P.warena == nullptr || P.warena_bytes != img.size()) {
+    if (P.warena != nullptr) cudaFree(P.warena);
+    P.warena = nullptr;
+    OW_TRY(cudaMalloc(&P.warena, img.size()));
+    P.warena_bytes = img.size();
+  }
+  OW_TRY(cudaMemcpyAsync(P.warena, img.data(), img.size(), cudaMemcpyHostToDevice, P.stream));
+  OW_TRY(cudaStreamSynchronize(P.stream));
+
+  uint8_t* base = P.warena;
+  auto F = [base](size_t at) { return reinterpret_cast<float*>(base + at); };
+  P.we = F(we);
+  P.be = F(be);
+  P.lnfg = F(lnfg);
+  P.lnfb = F(lnfb);
+  P.wp = F(wp);
+  P.bp = F(bp);
+  P.wv = F(wv);
+  P.bv = F(bv);
+  P.lw.resize(c.layers);
+  const bool tc = prec != OW_PRECISION_F32;
+  const bool e4 = prec == OW_PRECISION_FP8;
+  const uint32_t qkv_rows = static_cast<uint32_t>(P.qkv_block_n);
+  const uint32_t d_rows = d <= 256 ? static_cast<uint32_t>(d) : static_cast<uint32_t>(d / 2);
+  for (int l = 0; l < c.layers; ++l) {
+    auto& W = P.lw[l];
+    W.ln1g = F(la[l].ln1g);
+    W.ln1b = F(la[l].ln1b);
+    W.bqkv = F(la[l].bqkv);
+    W.bo = F(la[l].bo);
+    W.ln2g = F(la[l].ln2g);
+    W.ln2b = F(la[l].ln2b);
+    W.b1 = F(la[l].b1);
+    W.b2 = F(la[l].b2);
+    W.wqkv = base + la[l].qkv.at;
+    W.wo = base + la[l].o.at;
+    W.w1 = base + la[l].w1.at;
+    W.w2 = base + la[l].w2.at;
+    W.sqkv = e4 ? F(la[l].qkv.scale_at) : nullptr;
+    W.so = e4 ? F(la[l].o.scale_at) : nullptr;
+    W.s1 = e4 ? F(la[l].w1.scale_at) : nullptr;
+    W.s2 = e4 ? F(la[l].w2.scale_at) : nullptr;
+    if (tc) {
+      if (!make_kmajor_map(&W.mqkv, W.wqkv, e4, d, 3 * d, e4 ? 256u : qkv_rows) ||
+          !make_kmajor_map(&W.mo, W.wo, e4, d, d, d_rows) || !make_kmajor_map(&W.m1, W.w1, e4, d, f, 256u) ||
+          !make_kmajor_map(&W.m2, W.w2, e4, f, d, d_rows))
+        return st_rt("cuTensorMapEncodeTiled failed for a weight matrix");
+    }
+  }
+  return st_ok();
+}
+
+OwStatus alloc_workspace(OwPolicy& P) {
+  const auto& c = P.cfg;
+  const size_t B = c.batch_capacity, N = c.n_entities, rows = B * N;
+  P.cap_rows = rows;
+  const size_t act = c.precision == OW_PRECISION_F32 ? 4 : 2;
+  const size_t d = c.d_model, f = c.ffn;
+  size_t at = 0;
+  auto take = [&at](size_t bytes) {
+    const size_t r = align_up(at, 256);
+    at = r + bytes;
+    return r;
+  };
+  const size_t o_counts = take(B * 4), o_offsets = take((B + 1) * 4), o_err = take(16);
+  const size_t o_feats = take(rows * c.features * 4);
+  const size_t o_logits = take(rows * c.actions * 4), o_value = take(B * 4), o_actions = take(rows * 4);
+  const size_t o_x = take(rows * d * act), o_ln = take(rows * d * act), o_qkv = take(rows * 3 * d * act);
+  const size_t o_attn = take(rows * d * act), o_h = take(rows * f * act);
+  const bool e4 = c.precision == OW_PRECISION_FP8;
+  size_t o_ln8 = 0, o_attn8 = 0, o_h8 = 0, o_ls = 0, o_as = 0, o_hs = 0;
+  if (e4) {
+    o_ln8 = take(rows * d);
+    o_attn8 = take(rows * d);
+    o_h8 = take(rows * f);
+    o_ls = take(rows * 4);
+    o_as = take(rows * 4);
+    o_hs = take(rows * 4);
+  }
+  const size_t total = align_up(at, 256);
+  OW_TRY(cudaMalloc(&P.ws, total));
+  OW_TRY(cudaMemsetAsync(P.ws, 0, total, P.stream));
+  uint8_t* b = P.ws;
+  P.counts = reinterpret_cast<int*>(b + o_counts);
+  P.offsets = reinterpret_cast<int*>(b + o_offsets);
+  P.err = reinterpret_cast<int*>(b + o_err);
+  P.feats = reinterpret_cast<float*>(b + o_feats);
+  P.logits = b + o_logits;
+  P.value = b + o_value;
+  P.actions = reinterpret_cast<int*>(b + o_actions);
+  P.x = b + o_x;
+  P.ln = b + o_ln;
+  P.qkv = b + o_qkv;
+  P.attn = b + o_attn;
+  P.h = b + o_h;
+  if (e4) {
+    P.ln8 = b + o_ln8;
+    P.attn8 = b + o_attn8;
+    P.h8 = b + o_h8;
+    P.ln_scale = reinterpret_cast<float*>(b + o_ls);
+    P.attn_scale = reinterpret_cast<float*>(b + o_as);
+    P.h_scale = reinterpret_cast<float*>(b + o_hs);
+  }
+  if (c.precision != OW_PRECISION_F32) {
+    bool ok;
+    if (e4)
+      ok = make_kmajor_map(&P.m_ln, P.ln8, true, d, rows, 128) && make_kmajor_map(&P.m_attn, P.attn8, true, d, rows, 128) &&
+           make_kmajor_map(&P.m_h, P.h8, true, f, rows, 128);
+    else
+      ok = make_kmajor_map(&P.m_ln, P.ln, false, d, rows, 128) && make_kmajor_map(&P.m_attn, P.attn, false, d, rows, 128) &&
+           make_kmajor_map(&P.m_h, P.h, false, f, rows, 128);
+    if (!ok) return st_rt("cuTensorMapEncodeTiled failed for an activation buffer");
+  }
+  OW_TRY(cudaStreamSynchronize(P.stream));
+  return st_ok();
+}
+
+void release(OwPolicy* P) {
+  if (P == nullptr) return;
+  DeviceGuard g(P->device);
+  if (P->stream) cudaStreamSynchronize(P->stream);
+  for (auto ev : P->prof_events) cudaEventDestroy(ev);
+  if (P->ws) cudaFree(P->ws);
+  if (P->warena) cudaFree(P->warena);
+  if (P->own_stream && P->stream) cudaStreamDestroy(P->stream);
+  delete P;
+}
+
+}  // namespace
+
+extern "C" {
+
+OwStatus ow_policy_preset(int preset, OwPolicyConfig* config) {
+  if (config == nullptr) return st_bad("null config");
+  OwPolicyConfig c{};
+  c.features = 32;
+  c.actions = 16;
+  c.io = OW_IO_HOST;
+  c.logits_dtype = OW_DTYPE_BF16;
+  c.value_dtype = OW_DTYPE_F32;
+  switch (preset) {
+    case 1:
+      c.batch_capacity = 64; c.n_entities = 32; c.features = 16; c.d_model = 128; c.heads = 4; c.ffn = 512;
+      c.layers = 2; c.actions = 8; c.precision = OW_PRECISION_F32; c.logits_dtype = OW_DTYPE_F32;
+      break;
+    case 2:
+      c.batch_capacity = 1024; c.n_entities = 64; c.d_model = 256; c.heads = 8; c.ffn = 1024; c.layers = 4;
+      c.precision = OW_PRECISION_BF16;
+      break;
+    case 3:
+      c.batch_capacity = 4096; c.n_entities = 64; c.d_model = 256; c.heads = 8; c.ffn = 1024; c.layers = 4;
+      c.precision = OW_PRECISION_FP8; c.value_dtype = OW_DTYPE_BF16;
+      break;
+    case 4:
+      c.batch_capacity = 8192; c.n_entities = 96; c.d_model = 384; c.heads = 12; c.ffn = 1536; c.layers = 6;
+      c.precision = OW_PRECISION_BF16; c.sample_actions = 1;
+      break;
+    case 5:
+      c.batch_capacity = 65536; c.n_entities = 128; c.d_model = 512; c.heads = 16; c.ffn = 2048; c.layers = 8;
+      c.precision = OW_PRECISION_BF16;
+      break;
+    default:
+      return st_bad("preset must be 1..5");
+  }
+  *config = c;
+  return st_ok();
+}
+
+OwStatus ow_policy_weight_count(const OwPolicyConfig* config, size_t* count) {
+  if (config == nullptr || count == nullptr) return st_bad("null argument");
+  if (const char* m = validate_config(*config)) return st_bad(m);
+  *count = blob_layout(*config).total;
+  return st_ok();
+}
+
+OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, size_t weight_count, int device,
+                          void* stream, OwPolicy** out) {
+  if (config == nullptr || weights == nullptr || out == nullptr) return st_bad("null argument");
+  *out = nullptr;
+  if (const char* m = validate_config(*config)) return st_bad(m);
+  const BlobLayout lay = blob_layout(*config);
+  if (weight_count != lay.total) return st_bad("weight_count does not match the config");
+  for (size_t i = 0; i < weight_count; ++i)
+    if (!std::isfinite(weights[i])) return st_bad("non-finite weight");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) return st_rt("no cuda devices");
+  if (device < 0 || device >= ndev) return st_bad("device index out of range");
+  DeviceGuard g(device);
+  cudaDeviceProp prop{};
+  OW_TRY(cudaGetDeviceProperties(&prop, device));
+  if (config->precision != OW_PRECISION_F32 && prop.major != 10)
+    return st_rt("tensor-core path needs an sm_100 (B200) device");
+  auto* P = new OwPolicy();
+  P->cfg = *config;
+  P->lay = lay;
+  P->device = device;
+  P->num_sms = prop.multiProcessorCount;
+  P->qkv_block_n = (3 * config->d_model) % 256 == 0 ? 256 : 128;
+  if (stream != nullptr) {
+    P->stream = static_cast<cudaStream_t>(stream);
+  } else {
+    if (cudaStreamCreateWithFlags(&P->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      delete P;
+      return st_rt("stream creation failed");
+    }
+    P->own_stream = true;
+  }
+  OwStatus s = st_cuda(set_all_gemm_attrs());
+  if (s.code == OW_STATUS_OK) s = alloc_workspace(*P);
+  if (s.code == OW_STATUS_OK) s = upload_weights(*P, weights);
+  if (s.code != OW_STATUS_OK) {
+    release(P);
+    return s;
+  }
+  *out = P;
+  return st_ok();
+}
+
+OwStatus ow_policy_set_weights(OwPolicy* policy, const float* weights, size_t weight_count) {
+  if (policy == nullptr || weights == nullptr) return st_bad("null argument");
+  if (weight_count != policy->lay.total) return st_bad("weight_count does not match the config");
+  for (size_t i = 0; i < weight_count; ++i)
+    if (!std::isfinite(weights[i])) return st_bad("non-finite weight");
+  DeviceGuard g(policy->device);
+  OW_TRY(cudaStreamSynchronize(policy->stream));
+  return upload_weights(*policy, weights);
+}
+
+OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_t* counts, int32_t batch,
+                           void* logits, void* value, int32_t* actions, uint64_t seed) {
+  if (policy == nullptr) return st_bad("null policy");
+  auto& P = *policy;
+  const auto& c = P.cfg;
+  if (batch <= 0 || batch > c.batch_capacity) return st_bad("batch outside [1, batch_capacity]");
+  if (features == nullptr || counts == nullptr) return st_bad("null features or counts");
+  DeviceGuard g(P.device);
+  const size_t B = batch, N = c.n_entities;
+  const size_t lbytes = B * N * c.actions * (c.logits_dtype == OW_DTYPE_BF16 ? 2 : 4);
+  const size_t vbytes = B * (c.value_dtype == OW_DTYPE_BF16 ? 2 : 4);
+  if (c.io == OW_IO_HOST) {
+    for (size_t b = 0; b < B; ++b)
+      if (counts[b] < 0 || counts[b] > c.n_entities) return st_bad("entity count outside [0, n_entities]");
+    OW_TRY(cudaMemsetAsync(P.err, 0, sizeof(int), P.stream));
+    OW_TRY(cudaMemcpyAsync(P.feats, features, B * N * c.features * sizeof(float), cudaMemcpyHostToDevice, P.stream));
+    OW_TRY(cudaMemcpyAsync(P.counts, counts, B * sizeof(int), cudaMemcpyHostToDevice, P.stream));
+    OW_TRY(run_blocks(P, batch, seed, P.logits, P.value, P.actions));
+    if (logits) OW_TRY(cudaMemcpyAsync(logits, P.logits, lbytes, cudaMemcpyDeviceToHost, P.stream));
+    if (value) OW_TRY(cudaMemcpyAsync(value, P.value, vbytes, cudaMemcpyDeviceToHost, P.stream));
+    if (actions) OW_TRY(cudaMemcpyAsync(actions, P.actions, B * N * sizeof(int), cudaMemcpyDeviceToHost, P.stream));
+    int herr = 0;
+    OW_TRY(cudaMemcpyAsync(&herr, P.err, sizeof(int), cudaMemcpyDeviceToHost, P.stream));
+    OW_TRY(cudaStreamSynchronize(P.stream));
+    if (herr != 0) return st_rt(device_error_message(herr));
+    return st_ok();
+  }
+  // Device IO: features / counts / outputs are device pointers; the pipeline
+  // reads the features and counts in place and writes the outputs directly.
+  float* saved_feats = P.feats;
+  int* saved_counts = P.counts;
+  P.feats = const_cast<float*>(features);
+  P.counts = const_cast<int*>(counts);
+  const cudaError_t e = run_blocks(P, batch, seed, logits ? logits : P.logits, value ? value : P.value,
+                                   actions ? actions : P.actions);
+  P.feats = saved_feats;
+  P.counts = saved_counts;
+  return st_cuda(e);
+}
+
+OwStatus ow_policy_synchronize(OwPolicy* policy) {
+  if (policy == nullptr) return st_bad("null policy");
+  DeviceGuard g(policy->device);
+  int herr = 0;
+  OW_TRY(cudaMemcpyAsync(&herr, policy->err, sizeof(int), cudaMemcpyDeviceToHost, policy->stream));
+  OW_TRY(cudaStreamSynchronize(policy->stream));
+  if (herr != 0) {
+    cudaMemsetAsync(policy->err, 0, sizeof(int), policy->stream);
+    cudaStreamSynchronize(policy->stream);
+    return st_rt(device_error_message(herr));
+  }
+  return st_ok();
+}
+
+OwStatus ow_policy_device_weights(OwPolicy* policy, void** ptr, size_t* bytes) {
+  if (policy == nullptr || ptr == nullptr || bytes == nullptr) return st_bad("null argument");
+  *ptr = policy->warena;
+  *bytes = policy->warena_bytes;
+  return st_ok();
+}
+
+OwStatus ow_policy_profile_begin(OwPolicy* policy, int32_t max_forwards) {
+  if (policy == nullptr || max_forwards <= 0 || max_forwards > 100000) return st_bad("bad profile arguments");
+  DeviceGuard g(policy->device);
+  int32_t per = 0;
+  ow_policy_launches_per_forward(policy, &per);
+  const size_t need = static_cast<size_t>(max_forwards) * (per + 1) + 1;
+  while (policy->prof_events.size() < need) {
+    cudaEvent_t ev;
+    OW_TRY(cudaEventCreate(&ev));
+    policy->prof_events.push_back(ev);
+  }
+  policy->prof_names.assign(policy->prof_events.size(), nullptr);
+  policy->prof_used = 0;
+  policy->prof_on = true;
+  return st_ok();
+}
+
+OwStatus ow_policy_profile_end(OwPolicy* policy, OwKernelTiming* out, int32_t capacity, int32_t* count) {
+  if (policy == nullptr || count == nullptr) return st_bad("null argument");
+  DeviceGuard g(policy->device);
+  policy->prof_on = false;
+  OW_TRY(cudaStreamSynchronize(policy->stream));
+  int32_t n = 0;
+  for (size_t i = 0; i + 1 < policy->prof_used; ++i) {
+    const char* name = policy->prof_names[i];
+    if (name == nullptr) continue;
+    float ms = 0.0f;
+    OW_TRY(cudaEventElapsedTime(&ms, policy->prof_events[i], policy->prof_events[i + 1]));
+    int32_t k = 0;
+    while (k < n && std::strcmp(out[k].name, name) != 0) ++k;
+    if (k == n) {
+      if (out == nullptr || n >= capacity) continue;
+      out[n].name = name;
+      out[n].launches = 0;
+      out[n].total_ms = 0.0f;
+      ++n;
+    }
+    out[k].launches += 1;
+    out[k].total_ms += ms;
+  }
+  *count = n;
+  policy->prof_used = 0;
+  return st_ok();
+}
+
+OwStatus ow_policy_launches_per_forward(const OwPolicy* policy, int32_t* launches) {
+  if (policy == nullptr || launches == nullptr) return st_bad("null argument");
+  const auto& c = policy->cfg;
+  int per_layer = c.precision == OW_PRECISION_F32 ? 7 : (c.precision == OW_PRECISION_FP8 ? 7 : 5);
+  *launches = 3 + per_layer * c.layers;  // scan + embed + blocks + heads
+  return st_ok();
+}
+
+void ow_policy_destroy(OwPolicy* policy) { release(policy); }
+
+}  // extern "C"

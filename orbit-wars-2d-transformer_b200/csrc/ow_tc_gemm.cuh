@@ -1,0 +1,369 @@
+// Persistent tcgen05 GEMM for the encoder blocks: out[m, n] = A[m, :] . W[n, :] + epilogue.
+//
+//   A: activations, [rows, K] K-major (bf16 or e4m3), loaded by TMA with 128 B swizzle
+//   W: weights, [N, K] K-major ([out, in] as stored), same loader
+//   D: f32 accumulators in TMEM (128 lanes x BLOCK_N columns, double-buffered
+//      when two tiles fit in the 512 columns so the epilogue of tile i
+//      overlaps the MMAs of tile i+1)
+//
+// Roles (192 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues
+// tcgen05.mma (and warp 1 owns the TMEM allocation), warps 2..5 drain TMEM
+// (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of the tile).
+//
+// The number of valid rows is read from device memory (the packed token
+// count of the batch), so one launch shape serves every batch; tiles past the
+// valid rows are never scheduled.
+//
+// Epilogues:
+//   kEpiBias       out = bf16(acc*s + bias)                        (QKV projection)
+//   kEpiBiasGelu   out = bf16(gelu(acc*s + bias))                  (FFN up-projection)
+//   kEpiResidLn    x   = bf16(x + acc*s + bias) in place, and the
+//                  LayerNorm of that row (BLOCK_N == d, the whole row
+//                  is in this tile) -> ln_out as bf16, or e4m3 + per-row
+//                  scale for the fp8 path                          (out-proj, FFN down-projection)
+// where s = a_scale[m]*b_scale[n] for e4m3 operands and 1 otherwise.
+#pragma once
+
+#include "ow_common.cuh"
+
+namespace ow {
+
+enum EpiMode : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidLn = 2 };
+
+struct TcGemmParams {
+  const int* m_valid;  // device scalar: rows to compute
+  int n;               // output columns (multiple of BLOCK_N)
+  int k_blocks;        // K / (128 bytes of elements)
+  const float* bias;   // [n]
+  __nv_bfloat16* out;  // kEpiBias / kEpiBiasGelu: [rows, ld_out]
+  int ld_out;
+  __nv_bfloat16* resid;   // kEpiResidLn: x [rows, n], updated in place
+  const float* ln_g;      // [n]
+  const float* ln_b;      // [n]
+  void* ln_out;           // [rows, n] bf16, or e4m3 when ln_fp8
+  float* ln_scale;        // [rows] per-row dequant scale of ln_out (e4m3 only)
+  int ln_fp8;
+  const float* a_scale;   // [rows] (e4m3 operands only)
+  const float* b_scale;   // [n]    (e4m3 operands only)
+  int* err;
+};
+
+template <int BLOCK_N>
+struct TcGemmShape {
+  static constexpr int kBlockM = 128;
+  static constexpr int kRowBytes = 128;  // one swizzle atom row: 64 bf16 or 128 e4m3
+  static constexpr int kATileBytes = kBlockM * kRowBytes;
+  static constexpr int kBTileBytes = BLOCK_N * kRowBytes;
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kStages = (BLOCK_N <= 128) ? 6 : (BLOCK_N <= 256 ? 4 : (BLOCK_N <= 384 ? 3 : 2));
+  static constexpr int kInstN = BLOCK_N <= 256 ? BLOCK_N : BLOCK_N / 2;   // N of one tcgen05.mma
+  static constexpr int kInstCount = BLOCK_N / kInstN;
+  static constexpr int kBoxRows = BLOCK_N <= 256 ? BLOCK_N : BLOCK_N / 2;  // TMA box rows for W (<= 256)
+  static constexpr int kBoxCount = BLOCK_N / kBoxRows;
+  static constexpr int kAcc = (2 * BLOCK_N <= 512) ? 2 : 1;
+  static constexpr int kTmemColsNeeded = BLOCK_N * kAcc;
+  static constexpr int kTmemCols = kTmemColsNeeded <= 32 ? 32
+                                   : kTmemColsNeeded <= 64 ? 64
+                                   : kTmemColsNeeded <= 128 ? 128
+                                   : kTmemColsNeeded <= 256 ? 256 : 512;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
+  static_assert(kInstN % 16 == 0 && kInstN <= 256, "M=128 UMMA needs N % 16 == 0, N <= 256");
+  static_assert(kBoxRows <= 256, "TMA box rows <= 256");
+  static_assert(kTmemColsNeeded <= 512, "TMEM has 512 columns");
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
+
+constexpr int kGemmThreads = 192;
+
+template <int BLOCK_N, int EPI, bool FP8>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                   const TcGemmParams p) {
+  using S = TcGemmShape<BLOCK_N>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + S::kStages * S::kATileBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+  uint64_t* empty = full + S::kStages;
+  uint64_t* tfull = empty + S::kStages;
+  uint64_t* tempty = tfull + S::kAcc;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + S::kAcc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_valid = *p.m_valid;
+  const int m_tiles = (m_valid + S::kBlockM - 1) / S::kBlockM;
+  const int n_tiles = p.n / BLOCK_N;
+  const int num_tiles = m_tiles * n_tiles;
+  constexpr uint32_t kIdesc = FP8 ? idesc_e4m3(128, S::kInstN) : idesc_bf16(128, S::kInstN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < S::kAcc; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, S::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0 && num_tiles > 0) {
+      tma_prefetch_desc(&map_a);
+      tma_prefetch_desc(&map_w);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * S::kBlockM;
+        const int n0 = (tile % n_tiles) * BLOCK_N;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          const int kx = kb * (FP8 ? 128 : 64);
+          tma_load_2d(sa + stage * S::kATileBytes, &map_a, &full[stage], kx, m0);
+#pragma unroll
+          for (int c = 0; c < S::kBoxCount; ++c)
+            tma_load_2d(sb + stage * S::kBTileBytes + c * S::kBoxRows * S::kRowBytes, &map_w, &full[stage], kx,
+                        n0 + c * S::kBoxRows);
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && num_tiles > 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BLOCK_N);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sa + stage * S::kATileBytes);
+          const uint32_t b_base = smem_u32(sb + stage * S::kBTileBytes);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // 4 x 32 bytes of K per 128-byte row
+            const uint64_t adesc = sdesc_k_sw128(a_base + k * 32);
+#pragma unroll
+            for (int c = 0; c < S::kInstCount; ++c) {
+              const uint64_t bdesc = sdesc_k_sw128(b_base + c * S::kInstN * S::kRowBytes + k * 32);
+              const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+              if (FP8)
+                umma_f8(d_tmem + c * S::kInstN, adesc, bdesc, kIdesc, accumulate);
+              else
+                umma_f16(d_tmem + c * S::kInstN, adesc, bdesc, kIdesc, accumulate);
+            }
+          }
+          umma_commit(&empty[stage]);  // smem stage reusable once these MMAs retire
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        if (++acc == S::kAcc) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // Epilogue warps 2..5.
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int m = (tile / n_tiles) * S::kBlockM + row_in_tile;
+      const int n0 = (tile % n_tiles) * BLOCK_N;
+      const bool live = m < m_valid;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BLOCK_N);
+      const float a_s = (FP8 && live) ? p.a_scale[m] : 1.0f;
+
+      if (EPI == kEpiBias || EPI == kEpiBiasGelu) {
+#pragma unroll 1
+        for (int c = 0; c < BLOCK_N; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_ld_wait();
+          if (live) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const int n = n0 + c + i;
+              float v0 = __uint_as_float(r[i]);
+              float v1 = __uint_as_float(r[i + 1]);
+              if (FP8) {
+                v0 *= a_s * p.b_scale[n];
+                v1 *= a_s * p.b_scale[n + 1];
+              }
+              v0 += p.bias[n];
+              v1 += p.bias[n + 1];
+              if (EPI == kEpiBiasGelu) {
+                v0 = gelu_erf(v0);
+                v1 = gelu_erf(v1);
+              }
+              packed[i / 2] = pack_bf16x2(v0, v1);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(m) * p.ld_out + n0 + c);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          }
+        }
+      } else {
+        // Residual add + LayerNorm over the full row (BLOCK_N == n == d).
+        __nv_bfloat16* xrow = p.resid + static_cast<size_t>(live ? m : 0) * BLOCK_N;
+        float sum = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BLOCK_N; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_ld_wait();
+          uint4 xr[4];
+          const uint4* src = reinterpret_cast<const uint4*>(xrow + c);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) xr[q] = live ? src[q] : make_uint4(0, 0, 0, 0);
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(xr);
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int n = c + i;
+            float v0 = __uint_as_float(r[i]);
+            float v1 = __uint_as_float(r[i + 1]);
+            if (FP8) {
+              v0 *= a_s * p.b_scale[n];
+              v1 *= a_s * p.b_scale[n + 1];
+            }
+            v0 += p.bias[n] + bf16_lo(xw[i / 2]);
+            v1 += p.bias[n + 1] + bf16_hi(xw[i / 2]);
+            // The residual stream is stored bf16: normalise the stored value.
+            const uint32_t pk = pack_bf16x2(v0, v1);
+            v0 = bf16_lo(pk);
+            v1 = bf16_hi(pk);
+            sum += v0 + v1;
+            r[i] = __float_as_uint(v0);
+            r[i + 1] = __float_as_uint(v1);
+          }
+          tmem_st32(tbase + c, r);
+        }
+        tmem_st_wait();
+        const float mean = sum * (1.0f / BLOCK_N);
+        float sq = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BLOCK_N; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float dv = __uint_as_float(r[i]) - mean;
+            sq += dv * dv;
+          }
+        }
+        const float rstd = rsqrtf(sq * (1.0f / BLOCK_N) + 1e-5f);
+        float inv_scale = 1.0f;
+        if (p.ln_fp8) {
+          float amax = 0.0f;
+#pragma unroll 1
+          for (int c = 0; c < BLOCK_N; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float y = (__uint_as_float(r[i]) - mean) * rstd * p.ln_g[c + i] + p.ln_b[c + i];
+              amax = fmaxf(amax, fabsf(y));
+            }
+          }
+          const float scale = amax > 0.0f ? amax * (1.0f / 448.0f) : 1.0f;
+          inv_scale = 1.0f / scale;
+          if (live) p.ln_scale[m] = scale;
+        }
+#pragma unroll 1
+        for (int c = 0; c < BLOCK_N; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_ld_wait();
+          if (live) {
+            uint32_t xo[16];
+            float y[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float v0 = __uint_as_float(r[i]);
+              const float v1 = __uint_as_float(r[i + 1]);
+              xo[i / 2] = pack_bf16x2(v0, v1);
+              y[i] = (v0 - mean) * rstd * p.ln_g[c + i] + p.ln_b[c + i];
+              y[i + 1] = (v1 - mean) * rstd * p.ln_g[c + i + 1] + p.ln_b[c + i + 1];
+            }
+            uint4* xd = reinterpret_cast<uint4*>(xrow + c);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) xd[q] = make_uint4(xo[4 * q], xo[4 * q + 1], xo[4 * q + 2], xo[4 * q + 3]);
+            if (p.ln_fp8) {
+              uint32_t q8[8];
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
+                                        y[i + 3] * inv_scale);
+              uint4* ld = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ln_out) +
+                                                   static_cast<size_t>(m) * BLOCK_N + c);
+              ld[0] = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+              ld[1] = make_uint4(q8[4], q8[5], q8[6], q8[7]);
+            } else {
+              uint32_t yo[16];
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
+              uint4* ld = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ln_out) +
+                                                   static_cast<size_t>(m) * BLOCK_N + c);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) ld[q] = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == S::kAcc) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+}  // namespace ow

@@ -1,0 +1,129 @@
+"""Seeded synthetic inputs and weights (SPEC.md section 7).
+
+Random source: the reference's SplitMix-style mix
+(crates/orbit-wars-core/src/true2d_model.rs:653-663), keyed by
+(seed, tensor id, index) and scaled to U[0, 1]; Box-Muller for N(0, 1).
+Default seed 17 is the reference's DEFAULT_SEED (crates/orbit-wars-core/src/model.rs:10).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .presets import PolicyConfig
+
+MASK64 = (1 << 64) - 1
+ROW_FACTOR = 0x9E3779B97F4A7C15
+COL_FACTOR = 0xBF58476D1CE4E5B9
+MIX_FACTOR = 0x94D049BB133111EB
+TENSOR_FEATURES, TENSOR_COUNTS, TENSOR_ONEHOT, TENSOR_WEIGHTS = 1, 2, 3, 100
+DEFAULT_SEED = 17
+
+
+def mix64(seed: int, tensor: int, idx) -> np.ndarray:
+    idx = np.asarray(idx, dtype=np.uint64)
+    base = np.uint64((int(seed) ^ ((int(tensor) * ROW_FACTOR) & MASK64)) & MASK64)
+    with np.errstate(over="ignore"):
+        x = base ^ (idx * np.uint64(COL_FACTOR))
+        x ^= x >> np.uint64(30)
+        x = x * np.uint64(COL_FACTOR)
+        x ^= x >> np.uint64(27)
+        x = x * np.uint64(MIX_FACTOR)
+        x ^= x >> np.uint64(31)
+    return x
+
+
+def u01(seed: int, tensor: int, idx) -> np.ndarray:
+    return mix64(seed, tensor, idx).astype(np.float64) / float(MASK64)
+
+
+def normal(seed: int, tensor: int, idx) -> np.ndarray:
+    idx = np.asarray(idx, dtype=np.uint64)
+    u1 = np.maximum(u01(seed, tensor, idx * np.uint64(2)), 1e-300)
+    u2 = u01(seed, tensor, idx * np.uint64(2) + np.uint64(1))
+    return np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2)
+
+
+def counts_for(cfg: PolicyConfig, batch: int, seed: int = DEFAULT_SEED) -> np.ndarray:
+    u = u01(seed, TENSOR_COUNTS, np.arange(batch, dtype=np.uint64))
+    span = cfg.count_hi - cfg.count_lo + 1
+    c = cfg.count_lo + np.floor(u * span).astype(np.int64)
+    return np.minimum(c, cfg.count_hi).astype(np.int32)
+
+
+def make_inputs(cfg: PolicyConfig, batch: int | None = None, seed: int = DEFAULT_SEED,
+                counts: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """features f32 [B, N, F] (padded entities are 0) and counts int32 [B]."""
+    B = cfg.batch if batch is None else int(batch)
+    N, F = cfg.n_entities, cfg.features
+    cnt = counts_for(cfg, B, seed) if counts is None else np.asarray(counts, dtype=np.int32)
+    feats = np.zeros((B, N, F), dtype=np.float32)
+    valid = np.arange(N)[None, :] < cnt[:, None]          # [B, N]
+    b_idx, j_idx = np.nonzero(valid)
+    slot = (b_idx.astype(np.uint64) * np.uint64(N) + j_idx.astype(np.uint64))
+    chunk = 1 << 20
+    for s in range(0, slot.size, chunk):
+        sl = slot[s:s + chunk]
+        idx = sl[:, None] * np.uint64(F) + np.arange(F, dtype=np.uint64)[None, :]
+        vals = normal(seed, TENSOR_FEATURES, idx).astype(np.float32)
+        if cfg.onehot_features:
+            half = F // 2
+            vals[:, half:] = 0.0
+            blocks = (F - half) // 4
+            kidx = sl[:, None] * np.uint64(4) + np.arange(blocks, dtype=np.uint64)[None, :]
+            cls = np.minimum(np.floor(4.0 * u01(seed, TENSOR_ONEHOT, kidx)), 3).astype(np.int64)
+            rows = np.arange(sl.size)[:, None]
+            vals[rows, half + 4 * np.arange(blocks)[None, :] + cls] = 1.0
+        feats[b_idx[s:s + chunk], j_idx[s:s + chunk]] = vals
+    return feats, cnt
+
+
+def tensor_list(cfg: PolicyConfig) -> list[tuple[str, tuple[int, ...], str]]:
+    """(name, shape, kind) of every tensor of the weight blob, in order (SPEC.md section 3).
+
+    kind: 'mat' (Xavier), 'bias', 'ln_g', 'ln_b'.
+    """
+    d, F, f, P = cfg.d_model, cfg.features, cfg.ffn, cfg.actions
+    out = [("W_e", (d, F), "mat"), ("b_e", (d,), "bias")]
+    for l in range(cfg.layers):
+        out += [
+            (f"ln1_g.{l}", (d,), "ln_g"), (f"ln1_b.{l}", (d,), "ln_b"),
+            (f"W_qkv.{l}", (3 * d, d), "mat"), (f"b_qkv.{l}", (3 * d,), "bias"),
+            (f"W_o.{l}", (d, d), "mat"), (f"b_o.{l}", (d,), "bias"),
+            (f"ln2_g.{l}", (d,), "ln_g"), (f"ln2_b.{l}", (d,), "ln_b"),
+            (f"W_1.{l}", (f, d), "mat"), (f"b_1.{l}", (f,), "bias"),
+            (f"W_2.{l}", (d, f), "mat"), (f"b_2.{l}", (d,), "bias"),
+        ]
+    out += [("lnf_g", (d,), "ln_g"), ("lnf_b", (d,), "ln_b"),
+            ("W_p", (P, d), "mat"), ("b_p", (P,), "bias"), ("W_v", (1, d), "mat"), ("b_v", (1,), "bias")]
+    return out
+
+
+def weight_count(cfg: PolicyConfig) -> int:
+    return int(sum(np.prod(s) for _, s, _ in tensor_list(cfg)))
+
+
+def make_weights(cfg: PolicyConfig, seed: int = DEFAULT_SEED, affine_noise: bool = False) -> np.ndarray:
+    """Flat f32 weight blob: Xavier-uniform matrices; biases 0 and LN (1, 0) unless affine_noise."""
+    parts = []
+    for k, (_, shape, kind) in enumerate(tensor_list(cfg)):
+        n = int(np.prod(shape))
+        tid = TENSOR_WEIGHTS + k
+        if kind == "mat":
+            out_f, in_f = shape
+            a = np.sqrt(6.0 / (in_f + out_f))
+            parts.append(((2.0 * u01(seed, tid, np.arange(n, dtype=np.uint64)) - 1.0) * a).astype(np.float32))
+        elif not affine_noise:
+            parts.append(np.full(n, 1.0 if kind == "ln_g" else 0.0, dtype=np.float32))
+        else:
+            r = 0.1 * (2.0 * u01(seed, tid, np.arange(n, dtype=np.uint64)) - 1.0)
+            parts.append((r + (1.0 if kind == "ln_g" else 0.0)).astype(np.float32))
+    return np.concatenate(parts)
+
+
+def split_weights(cfg: PolicyConfig, blob: np.ndarray) -> dict[str, np.ndarray]:
+    out, at = {}, 0
+    for name, shape, _ in tensor_list(cfg):
+        n = int(np.prod(shape))
+        out[name] = blob[at:at + n].reshape(shape)
+        at += n
+    return out

@@ -1,0 +1,162 @@
+"""GPU parity of the encoder-policy forward against the CPU oracle (float64 truth).
+
+Tolerances (SPEC.md section 8): fp32 rel <= 1e-4, bf16 <= 1e-2, fp8 <= 3e-2 on
+logits and value; greedy argmax agreement >= 99.9% (ties within the
+precision's noise excluded); masks bit-exact.
+"""
+import numpy as np
+import pytest
+
+import orbit_wars_b200 as ow
+from tests.util import TOL, argmax_agreement, near_tie_mask, rel_err, valid_mask
+
+pytestmark = pytest.mark.gpu
+
+# (preset, states compared) -- sizes the float64 oracle finishes in seconds
+CASES = [(1, 64), (2, 48), (3, 48), (4, 12), (5, 4)]
+TIE_MARGIN = {"f32": 1e-5, "bf16": 5e-2, "fp8": 1.5e-1}
+
+
+def edge_counts(cfg, batch, seed):
+    _, counts = ow.make_inputs(cfg, batch=batch, seed=seed)
+    counts[0] = 0
+    counts[1] = 1
+    counts[2] = cfg.n_entities
+    if batch > 3:
+        counts[3] = 15 if cfg.n_entities > 16 else cfg.n_entities  # ragged vs the 16-row attention blocks
+    return counts
+
+
+def check_parity(cfg, gpu, ref, counts):
+    g_lg, g_v, g_a = gpu
+    r_lg, r_v, r_a = ref
+    m = valid_mask(counts, cfg.n_entities)
+    # masks and indices bit-exact
+    assert np.all(g_lg[~m] == 0.0)
+    assert np.all(g_a[~m] == -1)
+    assert np.all((g_a[m] >= 0) & (g_a[m] < cfg.actions))
+    tol = TOL[cfg.precision]
+    e_l = rel_err(g_lg[m], r_lg[m])
+    e_v = rel_err(g_v, r_v)
+    assert e_l <= tol, f"logits rel err {e_l:.3e} > {tol}"
+    assert e_v <= tol, f"value rel err {e_v:.3e} > {tol}"
+    return e_l, e_v
+
+
+@pytest.mark.parametrize("pid,batch", CASES)
+def test_policy_matches_oracle(oracle, pid, batch):
+    cfg = ow.preset(pid).with_(batch=batch)
+    w = ow.make_weights(cfg, seed=11, affine_noise=True)
+    counts = edge_counts(cfg, batch, seed=21)
+    feats, counts = ow.make_inputs(cfg, batch=batch, seed=21, counts=counts)
+    with ow.EncoderPolicy(cfg, w) as pol:
+        gpu = pol.forward(feats, counts, seed=5)
+    ref = oracle.policy_forward(cfg, w, feats, counts, f64=True, sample=False)
+    e_l, e_v = check_parity(cfg, gpu, ref, counts)
+    if not cfg.sample_actions:
+        m = valid_mask(counts, cfg.n_entities) & ~near_tie_mask(ref[0], counts, cfg.n_entities,
+                                                                 TIE_MARGIN[cfg.precision])
+        agree = float((gpu[2][m] == ref[2][m]).mean()) if m.any() else 1.0
+        assert agree >= 0.999, f"argmax agreement {agree:.4f}"
+        assert argmax_agreement(gpu[2], ref[2], counts, cfg.n_entities) >= 0.99
+    print(f"{cfg.name}: logits rel {e_l:.2e} value rel {e_v:.2e}")
+
+
+def test_gumbel_actions_replicate_spec(oracle):
+    """C4 sampling: actions == argmax(gpu logits + G) with G from the spec's Philox stream."""
+    cfg = ow.preset(4).with_(batch=8)
+    w = ow.make_weights(cfg, seed=2)
+    feats, counts = ow.make_inputs(cfg, batch=8, seed=3)
+    seed = 0xABCDEF0123
+    with ow.EncoderPolicy(cfg, w) as pol:
+        lg, _, a = pol.forward(feats, counts, seed=seed)
+    m = valid_mask(counts, cfg.n_entities)
+    agree = total = 0
+    for b in range(cfg.batch):
+        for j in range(int(counts[b])):
+            g = np.array([oracle.gumbel(seed, b, j, p) for p in range(cfg.actions)])
+            s = lg[b, j].astype(np.float64) + g
+            top2 = np.sort(s)[-2:]
+            if top2[1] - top2[0] < 1e-4:
+                continue
+            total += 1
+            agree += int(np.argmax(s) == a[b, j])
+    assert total > 0 and agree == total
+    assert np.all(a[~m] == -1)
+
+
+def test_device_io_matches_host_io():
+    torch = pytest.importorskip("torch")
+    cfg = ow.preset(2).with_(batch=64)
+    w = ow.make_weights(cfg, seed=4)
+    feats, counts = ow.make_inputs(cfg, batch=64, seed=6)
+    with ow.EncoderPolicy(cfg, w) as pol:
+        h_lg, h_v, h_a = pol.forward(feats, counts)
+    stream = torch.cuda.current_stream()
+    with ow.EncoderPolicy(cfg, w, io="device", stream=stream.cuda_stream) as pol:
+        f = torch.from_numpy(feats).cuda()
+        c = torch.from_numpy(counts).cuda()
+        lg = torch.empty((64, cfg.n_entities, cfg.actions), dtype=torch.bfloat16, device="cuda")
+        v = torch.empty((64,), dtype=torch.float32, device="cuda")
+        a = torch.empty((64, cfg.n_entities), dtype=torch.int32, device="cuda")
+        pol.forward_device(f.data_ptr(), c.data_ptr(), 64, lg.data_ptr(), v.data_ptr(), a.data_ptr())
+        pol.synchronize()
+        assert np.array_equal(lg.float().cpu().numpy(), h_lg)
+        assert np.array_equal(v.cpu().numpy(), h_v)
+        assert np.array_equal(a.cpu().numpy(), h_a)
+
+
+def test_full_batch_properties():
+    """Config-2 full batch: deterministic, permutation-equivariant, padding-invariant (bit-exact)."""
+    cfg = ow.preset(2)
+    w = ow.make_weights(cfg, seed=17)
+    feats, counts = ow.make_inputs(cfg, seed=17)
+    with ow.EncoderPolicy(cfg, w) as pol:
+        r1 = pol.forward(feats, counts)
+        r2 = pol.forward(feats, counts)
+        for x, y in zip(r1, r2):
+            assert np.array_equal(x, y)
+        perm = np.random.default_rng(0).permutation(cfg.batch)
+        r3 = pol.forward(feats[perm], counts[perm])
+        for x, y in zip(r1, r3):
+            assert np.array_equal(x[perm], y)
+        dirty = feats.copy()
+        dirty[~valid_mask(counts, cfg.n_entities)] = 77.0
+        r4 = pol.forward(dirty, counts)
+        for x, y in zip(r1, r4):
+            assert np.array_equal(x, y)
+        assert np.all(np.isfinite(r1[0])) and np.all(np.isfinite(r1[1]))
+
+
+def test_bad_count_is_rejected():
+    cfg = ow.preset(1)
+    w = ow.make_weights(cfg)
+    feats, counts = ow.make_inputs(cfg, batch=4)
+    counts[2] = cfg.n_entities + 3
+    with ow.EncoderPolicy(cfg, w) as pol:
+        with pytest.raises(ow.OwError) as e:
+            pol.forward(feats, counts)
+        assert e.value.code == 1
+        # the handle stays usable after a rejected call
+        counts[2] = 1
+        pol.forward(feats, counts)
+
+
+def test_device_side_bad_count_reports_runtime_error():
+    torch = pytest.importorskip("torch")
+    cfg = ow.preset(2).with_(batch=8)
+    w = ow.make_weights(cfg)
+    feats, counts = ow.make_inputs(cfg, batch=8)
+    counts[3] = -4
+    stream = torch.cuda.current_stream()
+    with ow.EncoderPolicy(cfg, w, io="device", stream=stream.cuda_stream) as pol:
+        f = torch.from_numpy(feats).cuda()
+        c = torch.from_numpy(counts).cuda()
+        lg = torch.empty((8, cfg.n_entities, cfg.actions), dtype=torch.bfloat16, device="cuda")
+        v = torch.empty((8,), dtype=torch.float32, device="cuda")
+        a = torch.empty((8, cfg.n_entities), dtype=torch.int32, device="cuda")
+        pol.forward_device(f.data_ptr(), c.data_ptr(), 8, lg.data_ptr(), v.data_ptr(), a.data_ptr())
+        with pytest.raises(ow.OwError) as e:
+            pol.synchronize()
+        assert e.value.code == 2
+        pol.synchronize()  # error word cleared; handle usable

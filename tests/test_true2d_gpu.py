@@ -1,0 +1,128 @@
+"""GPU parity of the True2D drop-in (include/orbit_wars_cuda.h) against the
+CPU oracle (pinned to the reference's cpu_reference) and, when present, the
+reference's own CUDA library built from source into oracle/_ref.
+
+Gate: max abs diff <= 5e-4, the reference's own (config.rs:111,
+orbit_wars_cuda_true2d_smoke.cpp:24); outputs in [0, 1]; per-row send sum <= 1 + 1e-6.
+"""
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import orbit_wars_b200 as ow
+from orbit_wars_b200 import _lib
+from tests.golden.make_true2d_golden import fixture_inputs
+
+pytestmark = pytest.mark.gpu
+GATE = 5e-4
+SHAPE = ow.True2DShape(61, 64, 1)
+REF_LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "liborbit_wars_cuda_ref.so"
+
+
+def invariants(out):
+    out = out.reshape(-1, 64, 12, 2)
+    assert np.all(np.isfinite(out))
+    assert np.all((out >= 0) & (out <= 1))
+    assert np.all(out[..., 1].sum(-1) <= 1 + 1e-6)
+
+
+def test_single_model_matches_golden():
+    g = np.load(Path(__file__).parent / "golden" / "true2d_smoke_fixture.npz")
+    x, w1, w2 = fixture_inputs()
+    t2 = ow.CudaTrue2D()
+    for w, key in ((w1, "out_model_a"), (w2, "out_model_b")):
+        out = t2.forward_packed(x, w, 2, SHAPE).reshape(-1)
+        invariants(out)
+        assert np.abs(out - g[key]).max() <= GATE
+        assert np.abs(out - g[key]).max() <= 2e-5  # fp32 single-pass softmax: far inside the gate
+
+
+def test_many_and_resident_paths(oracle):
+    rng = np.random.default_rng(1)
+    n_models, n_req = 3, 9
+    per = SHAPE.parameter_count()
+    pop = np.concatenate([oracle.true2d_seeded(19 + i, per) * (1 + 20 * i) for i in range(n_models)])
+    x = rng.uniform(-1, 1, size=(n_req, 64, 7)).astype(np.float32)
+    idx = rng.integers(0, n_models, size=n_req).astype(np.uintp)
+    ref = oracle.true2d_forward(x, pop, model_indices=idx)
+    t2 = ow.CudaTrue2D()
+    many = t2.forward_population_packed(x, idx, pop, SHAPE).reshape(-1)
+    invariants(many)
+    assert np.abs(many - ref).max() <= GATE
+    t2.upload_population(pop, request_capacity=16, shape=SHAPE)
+    res = t2.forward_population_resident_packed(x, idx, n_models, SHAPE).reshape(-1)
+    assert np.abs(res - ref).max() <= GATE
+    assert np.array_equal(res, many)
+
+
+def test_heads_and_rows_variants(oracle):
+    rng = np.random.default_rng(2)
+    for layers, rows, heads in ((4, 64, 3), (3, 16, 1), (5, 2, 2)):
+        shape = ow.True2DShape(layers, rows, heads)
+        w = (rng.standard_normal(shape.parameter_count()) * 0.3).astype(np.float32)
+        x = rng.uniform(-1, 1, size=(3, rows, 7)).astype(np.float32)
+        ref = oracle.true2d_forward(x, w, layers=layers, rows=rows, heads=heads)
+        out = ow.CudaTrue2D().forward_packed(x, w, 3, shape).reshape(-1)
+        assert np.abs(out - ref).max() <= GATE, (layers, rows, heads)
+
+
+def test_resident_errors():
+    lib = _lib.load_library()
+    x = np.zeros(64 * 7, np.float32)
+    out = np.zeros(64 * 24, np.float32)
+    idx = np.zeros(1, np.uintp)
+    t2 = ow.CudaTrue2D()
+    per = SHAPE.parameter_count()
+    t2.upload_population(np.zeros(per, np.float32), request_capacity=1, shape=SHAPE)
+    idx2 = np.zeros(2, np.uintp)
+    x2 = np.zeros(2 * 64 * 7, np.float32)
+    out2 = np.zeros(2 * 64 * 24, np.float32)
+    st = lib.orbit_wars_cuda_true2d_forward_many_resident(x2.ctypes.data, idx2.ctypes.data, out2.ctypes.data, 2,
+                                                          SHAPE.c())
+    assert st.code == 2 and b"capacity" in st.message
+    idx[0] = 5
+    st = lib.orbit_wars_cuda_true2d_forward_many_resident(x.ctypes.data, idx.ctypes.data, out.ctypes.data, 1,
+                                                          SHAPE.c())
+    assert st.code == 1
+    st = lib.orbit_wars_cuda_true2d_train_full_attention(x.ctypes.data, out.ctypes.data, x.ctypes.data, x.ctypes.data,
+                                                         idx.ctypes.data, x.ctypes.data, 1, 1, SHAPE.c(),
+                                                         _lib.TrainingConfigC())
+    assert st.code == 2
+
+
+def test_trainable_legacy_matches_oracle(oracle):
+    lib = _lib.load_library()
+    d, heads, layers, rows, games = 32, 4, 3, 64, 3
+    n = 2 * d + d + layers * d + 2 * d
+    w = (np.sin(np.arange(1, n + 1) * 0.3) * 0.25).astype(np.float32)
+    x = np.sin(np.arange(1, games * rows * 2 + 1) * 0.7).astype(np.float32)
+    out = np.zeros(games * rows * 2, np.float32)
+    _lib.check("trainable", lib.orbit_wars_cuda_trainable_forward(
+        x.ctypes.data, w.ctypes.data, out.ctypes.data, games, _lib.TransformerShapeC(layers, d, heads, rows)))
+    ref = oracle.trainable_forward(x, w, games, layers, d, heads, rows)
+    assert np.abs(out - ref).max() <= 1e-5
+
+
+def test_identity_copy():
+    torch = pytest.importorskip("torch")
+    lib = _lib.load_library()
+    a = torch.randn(3, 64, 7, device="cuda")
+    b = torch.zeros_like(a)
+    _lib.check("identity", lib.orbit_wars_cuda_encode_identity_batch(a.data_ptr(), b.data_ptr(), 3, 64, 7))
+    assert torch.equal(a, b)
+
+
+@pytest.mark.skipif(not REF_LIB.exists(), reason="reference CUDA library not built (make -C oracle ref)")
+def test_matches_reference_gpu_build():
+    """Same inputs through the reference's own kernels (built from its source for sm_100a)."""
+    ref = C.CDLL(str(REF_LIB), mode=2)
+    ref.orbit_wars_cuda_true2d_forward.restype = _lib.Status
+    ref.orbit_wars_cuda_true2d_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, _lib.True2DShapeC]
+    x, w1, _ = fixture_inputs()
+    out_ref = np.zeros(2 * 64 * 24, np.float32)
+    _lib.check("reference true2d", ref.orbit_wars_cuda_true2d_forward(x.ctypes.data, w1.ctypes.data,
+                                                                      out_ref.ctypes.data, 2, SHAPE.c()))
+    ours = ow.CudaTrue2D().forward_packed(x, w1, 2, SHAPE).reshape(-1)
+    assert np.abs(ours - out_ref).max() <= GATE
