@@ -108,6 +108,17 @@ OwStatus ow_policy_launches_per_forward(const OwPolicy* policy, int32_t* launche
 
 void ow_policy_destroy(OwPolicy* policy);
 
+/* Test hook, not part of the forward: one tensor-core GEMM launch on device
+ * buffers, out[m, n] = a[m, :] . w[n, :] + epilogue, exactly as the forward
+ * issues it. precision OW_PRECISION_BF16 or _FP8 (then a_scale[m], b_scale[n]
+ * dequantise); epilogue 0 bias -> bf16 out, 1 bias + GELU -> bf16 out,
+ * 2 residual (f32 resid, in place) + LayerNorm -> ln_out (ln_mode 0 bf16,
+ * 1 e4m3 + ln_scale, 2 f32). Synchronous on `stream`. */
+OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, const void* a, const void* w,
+                          const float* bias, void* out, float* resid, const float* ln_g, const float* ln_b,
+                          void* ln_out, int ln_mode, float* ln_scale, const float* a_scale, const float* b_scale,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -193,7 +193,7 @@ struct OwPolicy {
   float* feats = nullptr;
   void *logits = nullptr, *value = nullptr;
   int* actions = nullptr;
-  void *x = nullptr, *ln = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr;
+  void *x = nullptr, *ln = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr;
   uint8_t *ln8 = nullptr, *attn8 = nullptr, *h8 = nullptr;
   float *ln_scale = nullptr, *attn_scale = nullptr, *h_scale = nullptr;
   CUtensorMap m_ln, m_attn, m_h;
@@ -280,20 +280,20 @@ cudaError_t launch_embed(const OwPolicy& P, int batch) {
   const float* g = P.lw[0].ln1g;
   const float* b = P.lw[0].ln1b;
   if (c.precision == OW_PRECISION_F32) {
-    auto k = embed_ln_kernel<DPL, float, 0>;
+    auto k = embed_ln_kernel<DPL, 0>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
                                      static_cast<float*>(P.x), P.ln, nullptr);
   } else if (c.precision == OW_PRECISION_BF16) {
-    auto k = embed_ln_kernel<DPL, __nv_bfloat16, 1>;
+    auto k = embed_ln_kernel<DPL, 1>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
-                                     static_cast<__nv_bfloat16*>(P.x), P.ln, nullptr);
+                                     static_cast<float*>(P.x), P.ln, nullptr);
   } else {
-    auto k = embed_ln_kernel<DPL, __nv_bfloat16, 2>;
+    auto k = embed_ln_kernel<DPL, 2>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
-                                     static_cast<__nv_bfloat16*>(P.x), P.ln8, P.ln_scale);
+                                     static_cast<float*>(P.x), P.ln8, P.ln_scale);
   }
   return cudaGetLastError();
 }
@@ -303,7 +303,7 @@ void heads_launch(const OwPolicy& P, int batch, size_t smem, uint64_t seed, void
   const auto& c = P.cfg;
   cudaFuncSetAttribute(heads_kernel<DPL, YT, LB, VB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  heads_kernel<DPL, YT, LB, VB><<<batch, 128, smem, P.stream>>>(static_cast<const YT*>(P.ln), P.offsets,
+  heads_kernel<DPL, YT, LB, VB><<<batch, 128, smem, P.stream>>>(static_cast<const YT*>(P.y), P.offsets,
                                                                 c.n_entities, c.actions, P.wp, P.bp, P.wv, P.bv,
                                                                 c.sample_actions, seed, logits, value, actions);
 }
@@ -313,17 +313,11 @@ cudaError_t launch_heads(const OwPolicy& P, int batch, uint64_t seed, void* logi
   const auto& c = P.cfg;
   const size_t smem = static_cast<size_t>(c.actions + 4) * DPL * 32 * sizeof(float);
   const bool lb = c.logits_dtype == OW_DTYPE_BF16, vb = c.value_dtype == OW_DTYPE_BF16;
-  if (c.precision == OW_PRECISION_F32) {
-    if (lb && vb) heads_launch<DPL, float, true, true>(P, batch, smem, seed, logits, value, actions);
-    else if (lb) heads_launch<DPL, float, true, false>(P, batch, smem, seed, logits, value, actions);
-    else if (vb) heads_launch<DPL, float, false, true>(P, batch, smem, seed, logits, value, actions);
-    else heads_launch<DPL, float, false, false>(P, batch, smem, seed, logits, value, actions);
-  } else {
-    if (lb && vb) heads_launch<DPL, __nv_bfloat16, true, true>(P, batch, smem, seed, logits, value, actions);
-    else if (lb) heads_launch<DPL, __nv_bfloat16, true, false>(P, batch, smem, seed, logits, value, actions);
-    else if (vb) heads_launch<DPL, __nv_bfloat16, false, true>(P, batch, smem, seed, logits, value, actions);
-    else heads_launch<DPL, __nv_bfloat16, false, false>(P, batch, smem, seed, logits, value, actions);
-  }
+  // the final LayerNorm output is f32 on every path
+  if (lb && vb) heads_launch<DPL, float, true, true>(P, batch, smem, seed, logits, value, actions);
+  else if (lb) heads_launch<DPL, float, true, false>(P, batch, smem, seed, logits, value, actions);
+  else if (vb) heads_launch<DPL, float, false, true>(P, batch, smem, seed, logits, value, actions);
+  else heads_launch<DPL, float, false, false>(P, batch, smem, seed, logits, value, actions);
   return cudaGetLastError();
 }
 
@@ -468,10 +462,10 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       o.n = d;
       o.k_blocks = fp8 ? d / 128 : d / 64;
       o.bias = W.bo;
-      o.resid = static_cast<__nv_bfloat16*>(P.x);
+      o.resid = static_cast<float*>(P.x);
       o.ln_g = W.ln2g;
       o.ln_b = W.ln2b;
-      o.ln_fp8 = fp8 ? 1 : 0;
+      o.ln_mode = fp8 ? kLnE4m3 : kLnBf16;
       o.ln_out = fp8 ? static_cast<void*>(P.ln8) : P.ln;
       o.ln_scale = P.ln_scale;
       o.a_scale = P.attn_scale;
@@ -498,11 +492,11 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       w.n = d;
       w.k_blocks = fp8 ? f / 128 : f / 64;
       w.bias = W.b2;
-      w.resid = static_cast<__nv_bfloat16*>(P.x);
+      w.resid = static_cast<float*>(P.x);
       w.ln_g = last ? P.lnfg : P.lw[l + 1].ln1g;
       w.ln_b = last ? P.lnfb : P.lw[l + 1].ln1b;
-      w.ln_fp8 = (fp8 && !last) ? 1 : 0;
-      w.ln_out = w.ln_fp8 ? static_cast<void*>(P.ln8) : P.ln;
+      w.ln_mode = last ? kLnF32 : (fp8 ? kLnE4m3 : kLnBf16);
+      w.ln_out = last ? P.y : (fp8 ? static_cast<void*>(P.ln8) : P.ln);
       w.ln_scale = P.ln_scale;
       w.a_scale = P.h_scale;
       w.b_scale = W.s2;
@@ -660,7 +654,8 @@ OwStatus alloc_workspace(OwPolicy& P) {
   const size_t o_counts = take(B * 4), o_offsets = take((B + 1) * 4), o_err = take(16);
   const size_t o_feats = take(rows * c.features * 4);
   const size_t o_logits = take(rows * c.actions * 4), o_value = take(B * 4), o_actions = take(rows * 4);
-  const size_t o_x = take(rows * d * act), o_ln = take(rows * d * act), o_qkv = take(rows * 3 * d * act);
+  const size_t o_x = take(rows * d * 4), o_ln = take(rows * d * act), o_qkv = take(rows * 3 * d * act);
+  const size_t o_y = c.precision == OW_PRECISION_F32 ? o_ln : take(rows * d * 4);
   const size_t o_attn = take(rows * d * act), o_h = take(rows * f * act);
   const bool e4 = c.precision == OW_PRECISION_FP8;
   size_t o_ln8 = 0, o_attn8 = 0, o_h8 = 0, o_ls = 0, o_as = 0, o_hs = 0;
@@ -685,6 +680,7 @@ OwStatus alloc_workspace(OwPolicy& P) {
   P.actions = reinterpret_cast<int*>(b + o_actions);
   P.x = b + o_x;
   P.ln = b + o_ln;
+  P.y = b + o_y;
   P.qkv = b + o_qkv;
   P.attn = b + o_attn;
   P.h = b + o_h;
@@ -924,6 +920,85 @@ OwStatus ow_policy_profile_end(OwPolicy* policy, OwKernelTiming* out, int32_t ca
   }
   *count = n;
   policy->prof_used = 0;
+  return st_ok();
+}
+
+OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, const void* a, const void* w,
+                          const float* bias, void* out, float* resid, const float* ln_g, const float* ln_b,
+                          void* ln_out, int ln_mode, float* ln_scale, const float* a_scale, const float* b_scale,
+                          void* stream) {
+  const bool fp8 = precision == OW_PRECISION_FP8;
+  if (precision != OW_PRECISION_BF16 && !fp8) return st_bad("selftest precision must be bf16 or fp8");
+  if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || w == nullptr || bias == nullptr) return st_bad("bad selftest args");
+  if (k % (fp8 ? 128 : 64) != 0) return st_bad("k must be a multiple of 128 bytes");
+  int bn = 0;
+  if (epilogue == kEpiResidLn) {
+    if (resid == nullptr || ln_g == nullptr || ln_b == nullptr || ln_out == nullptr) return st_bad("bad ln args");
+    if (!(n == 128 || n == 256 || n == 384 || n == 512) || (fp8 && n != 256)) return st_bad("unsupported ln width");
+    bn = n;
+  } else if (epilogue == kEpiBias || epilogue == kEpiBiasGelu) {
+    if (out == nullptr) return st_bad("null out");
+    bn = n % 256 == 0 ? 256 : (n % 128 == 0 ? 128 : 0);
+    if (bn == 0 || (fp8 && bn != 256) || (epilogue == kEpiBiasGelu && bn != 256)) return st_bad("unsupported n");
+  } else {
+    return st_bad("unknown epilogue");
+  }
+  if (fp8 && (a_scale == nullptr || b_scale == nullptr)) return st_bad("fp8 needs scales");
+  int dev = 0;
+  OW_TRY(cudaGetDevice(&dev));
+  OwPolicy P;
+  P.device = dev;
+  P.stream = static_cast<cudaStream_t>(stream);
+  P.cap_rows = static_cast<size_t>(m);
+  cudaDeviceProp prop{};
+  OW_TRY(cudaGetDeviceProperties(&prop, dev));
+  P.num_sms = prop.multiProcessorCount;
+  OW_TRY(set_all_gemm_attrs());
+  const uint32_t box_rows = bn <= 256 ? static_cast<uint32_t>(bn) : static_cast<uint32_t>(bn / 2);
+  CUtensorMap ma, mw;
+  if (!make_kmajor_map(&ma, a, fp8, k, m, 128) || !make_kmajor_map(&mw, w, fp8, k, n, box_rows))
+    return st_rt("cuTensorMapEncodeTiled failed");
+  int* d_m = nullptr;
+  int* d_err = nullptr;
+  OW_TRY(cudaMalloc(&d_m, 2 * sizeof(int)));
+  d_err = d_m + 1;
+  const int host_m[2] = {m, 0};
+  cudaError_t e = cudaMemcpyAsync(d_m, host_m, sizeof(host_m), cudaMemcpyHostToDevice, P.stream);
+  TcGemmParams q{};
+  q.m_valid = d_m;
+  q.err = d_err;
+  q.n = n;
+  q.k_blocks = fp8 ? k / 128 : k / 64;
+  q.bias = bias;
+  q.out = static_cast<__nv_bfloat16*>(out);
+  q.ld_out = n;
+  q.resid = resid;
+  q.ln_g = ln_g;
+  q.ln_b = ln_b;
+  q.ln_out = ln_out;
+  q.ln_mode = ln_mode;
+  q.ln_scale = ln_scale;
+  q.a_scale = a_scale;
+  q.b_scale = b_scale;
+  if (e == cudaSuccess) {
+    if (epilogue == kEpiResidLn) {
+      P.cfg.d_model = n;
+      e = launch_gemm_resid_ln(P, ma, mw, q, fp8);
+    } else if (epilogue == kEpiBias) {
+      if (fp8) e = launch_gemm<256, kEpiBias, true>(P, ma, mw, q);
+      else if (bn == 256) e = launch_gemm<256, kEpiBias, false>(P, ma, mw, q);
+      else e = launch_gemm<128, kEpiBias, false>(P, ma, mw, q);
+    } else {
+      if (fp8) e = launch_gemm<256, kEpiBiasGelu, true>(P, ma, mw, q);
+      else e = launch_gemm<256, kEpiBiasGelu, false>(P, ma, mw, q);
+    }
+  }
+  int herr = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost, P.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(P.stream);
+  cudaFree(d_m);
+  if (e != cudaSuccess) return st_cuda(e);
+  if (herr != 0) return st_rt(device_error_message(herr));
   return st_ok();
 }
 

@@ -17,10 +17,11 @@
 // Epilogues:
 //   kEpiBias       out = bf16(acc*s + bias)                        (QKV projection)
 //   kEpiBiasGelu   out = bf16(gelu(acc*s + bias))                  (FFN up-projection)
-//   kEpiResidLn    x   = bf16(x + acc*s + bias) in place, and the
-//                  LayerNorm of that row (BLOCK_N == d, the whole row
-//                  is in this tile) -> ln_out as bf16, or e4m3 + per-row
-//                  scale for the fp8 path                          (out-proj, FFN down-projection)
+//   kEpiResidLn    x   = x + acc*s + bias in place (fp32 residual stream),
+//                  and the LayerNorm of that row (BLOCK_N == d, the whole
+//                  row is in this tile) -> ln_out as bf16 (next GEMM's A),
+//                  e4m3 + per-row scale (fp8 path), or f32 (the final LN
+//                  feeding the heads)                              (out-proj, FFN down-projection)
 // where s = a_scale[m]*b_scale[n] for e4m3 operands and 1 otherwise.
 #pragma once
 
@@ -29,6 +30,7 @@
 namespace ow {
 
 enum EpiMode : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidLn = 2 };
+enum LnMode : int { kLnBf16 = 0, kLnE4m3 = 1, kLnF32 = 2 };
 
 struct TcGemmParams {
   const int* m_valid;  // device scalar: rows to compute
@@ -37,12 +39,12 @@ struct TcGemmParams {
   const float* bias;   // [n]
   __nv_bfloat16* out;  // kEpiBias / kEpiBiasGelu: [rows, ld_out]
   int ld_out;
-  __nv_bfloat16* resid;   // kEpiResidLn: x [rows, n], updated in place
+  float* resid;           // kEpiResidLn: x [rows, n] f32, updated in place
   const float* ln_g;      // [n]
   const float* ln_b;      // [n]
-  void* ln_out;           // [rows, n] bf16, or e4m3 when ln_fp8
+  void* ln_out;           // [rows, n]: bf16, e4m3 or f32 per ln_mode
   float* ln_scale;        // [rows] per-row dequant scale of ln_out (e4m3 only)
-  int ln_fp8;
+  int ln_mode;            // kLnBf16, kLnE4m3, kLnF32
   const float* a_scale;   // [rows] (e4m3 operands only)
   const float* b_scale;   // [n]    (e4m3 operands only)
   int* err;
@@ -241,36 +243,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else {
         // Residual add + LayerNorm over the full row (BLOCK_N == n == d).
-        __nv_bfloat16* xrow = p.resid + static_cast<size_t>(live ? m : 0) * BLOCK_N;
+        float* xrow = p.resid + static_cast<size_t>(live ? m : 0) * BLOCK_N;
         float sum = 0.0f;
 #pragma unroll 1
         for (int c = 0; c < BLOCK_N; c += 32) {
           uint32_t r[32];
           tmem_ld32(tbase + c, r);
           tmem_ld_wait();
-          uint4 xr[4];
-          const uint4* src = reinterpret_cast<const uint4*>(xrow + c);
+          float4 xr[8];
+          const float4* src = reinterpret_cast<const float4*>(xrow + c);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) xr[q] = live ? src[q] : make_uint4(0, 0, 0, 0);
-          const uint32_t* xw = reinterpret_cast<const uint32_t*>(xr);
+          for (int q = 0; q < 8; ++q) xr[q] = live ? src[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float* xv = reinterpret_cast<const float*>(xr);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int n = c + i;
-            float v0 = __uint_as_float(r[i]);
-            float v1 = __uint_as_float(r[i + 1]);
-            if (FP8) {
-              v0 *= a_s * p.b_scale[n];
-              v1 *= a_s * p.b_scale[n + 1];
-            }
-            v0 += p.bias[n] + bf16_lo(xw[i / 2]);
-            v1 += p.bias[n + 1] + bf16_hi(xw[i / 2]);
-            // The residual stream is stored bf16: normalise the stored value.
-            const uint32_t pk = pack_bf16x2(v0, v1);
-            v0 = bf16_lo(pk);
-            v1 = bf16_hi(pk);
-            sum += v0 + v1;
-            r[i] = __float_as_uint(v0);
-            r[i + 1] = __float_as_uint(v1);
+          for (int i = 0; i < 32; ++i) {
+            float v = __uint_as_float(r[i]);
+            if (FP8) v *= a_s * p.b_scale[c + i];
+            v += p.bias[c + i] + xv[i];
+            sum += v;
+            r[i] = __float_as_uint(v);
           }
           tmem_st32(tbase + c, r);
         }
@@ -290,7 +281,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         const float rstd = rsqrtf(sq * (1.0f / BLOCK_N) + 1e-5f);
         float inv_scale = 1.0f;
-        if (p.ln_fp8) {
+        if (p.ln_mode == kLnE4m3) {
           float amax = 0.0f;
 #pragma unroll 1
           for (int c = 0; c < BLOCK_N; c += 32) {
@@ -313,20 +304,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld32(tbase + c, r);
           tmem_ld_wait();
           if (live) {
-            uint32_t xo[16];
             float y[32];
+            float4* xd = reinterpret_cast<float4*>(xrow + c);
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float v0 = __uint_as_float(r[i]);
-              const float v1 = __uint_as_float(r[i + 1]);
-              xo[i / 2] = pack_bf16x2(v0, v1);
-              y[i] = (v0 - mean) * rstd * p.ln_g[c + i] + p.ln_b[c + i];
-              y[i + 1] = (v1 - mean) * rstd * p.ln_g[c + i + 1] + p.ln_b[c + i + 1];
-            }
-            uint4* xd = reinterpret_cast<uint4*>(xrow + c);
+            for (int q = 0; q < 8; ++q)
+              xd[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                  __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) xd[q] = make_uint4(xo[4 * q], xo[4 * q + 1], xo[4 * q + 2], xo[4 * q + 3]);
-            if (p.ln_fp8) {
+            for (int i = 0; i < 32; ++i) y[i] = (__uint_as_float(r[i]) - mean) * rstd * p.ln_g[c + i] + p.ln_b[c + i];
+            if (p.ln_mode == kLnE4m3) {
               uint32_t q8[8];
 #pragma unroll
               for (int i = 0; i < 32; i += 4)
@@ -336,6 +322,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                                    static_cast<size_t>(m) * BLOCK_N + c);
               ld[0] = make_uint4(q8[0], q8[1], q8[2], q8[3]);
               ld[1] = make_uint4(q8[4], q8[5], q8[6], q8[7]);
+            } else if (p.ln_mode == kLnF32) {
+              float4* ld = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.ln_out) + static_cast<size_t>(m) * BLOCK_N + c);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) ld[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
             } else {
               uint32_t yo[16];
 #pragma unroll

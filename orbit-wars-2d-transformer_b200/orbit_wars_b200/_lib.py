@@ -70,6 +70,8 @@ SIGNATURES = {
     "ow_policy_profile_begin": (Status, [P, C.c_int32]),
     "ow_policy_profile_end": (Status, [P, C.POINTER(KernelTimingC), C.c_int32, C.POINTER(C.c_int32)]),
     "ow_policy_destroy": (None, [P]),
+    "ow_selftest_gemm": (Status, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, C.c_int, P, P,
+                                  P, P]),
     # include/orbit_wars_cuda.h
     "orbit_wars_cuda_status": (Status, []),
     "orbit_wars_cuda_encode_identity_batch": (Status, [P, P, SZ, SZ, SZ]),

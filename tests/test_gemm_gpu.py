@@ -1,0 +1,110 @@
+"""Single tcgen05 GEMM launches (ow_selftest_gemm) against a plain PyTorch fp32
+reference of the same op, for every epilogue the forward uses."""
+import numpy as np
+import pytest
+
+from orbit_wars_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+BF16, FP8 = 1, 2
+EPI_BIAS, EPI_GELU, EPI_LN = 0, 1, 2
+LN_BF16, LN_E4M3, LN_F32 = 0, 1, 2
+
+
+def call(precision, epi, m, n, k, a, w, bias, out=None, resid=None, g=None, b=None, ln_out=None, ln_mode=0,
+         ln_scale=None, a_scale=None, b_scale=None):
+    lib = _lib.load_library()
+    p = _lib.ptr
+    st = lib.ow_selftest_gemm(precision, epi, m, n, k, p(a), p(w), p(bias), p(out), p(resid), p(g), p(b), p(ln_out),
+                              ln_mode, p(ln_scale), p(a_scale), p(b_scale), torch.cuda.current_stream().cuda_stream)
+    _lib.check("ow_selftest_gemm", st)
+
+
+def close(x, ref, rel):
+    err = (x.float() - ref).abs().max().item() / max(ref.abs().max().item(), 1e-6)
+    assert err <= rel, f"rel err {err:.3e} > {rel}"
+    return err
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 768, 256), (1000, 384, 256), (77, 256, 1024)])
+def test_bf16_bias(m, n, k):
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).bfloat16()
+    bias = torch.randn(n, device="cuda", generator=g)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    call(BF16, EPI_BIAS, m, n, k, a, w, bias, out=out)
+    ref = a.float() @ w.float().T + bias
+    close(out, ref, 8e-3)
+
+
+def test_bf16_gelu():
+    m, n, k = 513, 1024, 256
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") / 16).bfloat16()
+    bias = torch.randn(n, device="cuda")
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    call(BF16, EPI_GELU, m, n, k, a, w, bias, out=out)
+    ref = torch.nn.functional.gelu(a.float() @ w.float().T + bias)
+    close(out, ref, 8e-3)
+
+
+@pytest.mark.parametrize("n", [128, 256, 384, 512])
+@pytest.mark.parametrize("ln_mode", [LN_BF16, LN_F32])
+def test_bf16_resid_ln(n, ln_mode):
+    m, k = 333, 1024 if n != 384 else 256
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") / k ** 0.5).bfloat16()
+    bias = torch.randn(n, device="cuda") * 0.1
+    resid = torch.randn(m, n, device="cuda")
+    resid0 = resid.clone()
+    gam = 1 + 0.1 * torch.randn(n, device="cuda")
+    bet = 0.1 * torch.randn(n, device="cuda")
+    ln_out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16 if ln_mode == LN_BF16 else torch.float32)
+    call(BF16, EPI_LN, m, n, k, a, w, bias, resid=resid, g=gam, b=bet, ln_out=ln_out, ln_mode=ln_mode)
+    x_ref = resid0 + a.float() @ w.float().T + bias
+    close(resid, x_ref, 1e-4)
+    y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
+    close(ln_out, y_ref, 8e-3 if ln_mode == LN_BF16 else 1e-4)
+
+
+def quant_rows(x):
+    s = (x.abs().amax(dim=1).clamp_min(1e-30) / 448.0)
+    q = (x / s[:, None]).to(torch.float8_e4m3fn)
+    return q, s
+
+
+@pytest.mark.parametrize("epi,n", [(EPI_BIAS, 768), (EPI_GELU, 1024)])
+def test_fp8_bias_gelu(epi, n):
+    m, k = 260, 256
+    a, sa = quant_rows(torch.randn(m, k, device="cuda"))
+    w, sw = quant_rows(torch.randn(n, k, device="cuda") / 16)
+    bias = torch.randn(n, device="cuda")
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    call(FP8, epi, m, n, k, a, w, bias, out=out, a_scale=sa, b_scale=sw)
+    ref = (a.float() * sa[:, None]) @ (w.float() * sw[:, None]).T + bias
+    if epi == EPI_GELU:
+        ref = torch.nn.functional.gelu(ref)
+    close(out, ref, 8e-3)
+
+
+def test_fp8_resid_ln():
+    m, n, k = 200, 256, 1024
+    a, sa = quant_rows(torch.randn(m, k, device="cuda"))
+    w, sw = quant_rows(torch.randn(n, k, device="cuda") / 32)
+    bias = torch.randn(n, device="cuda") * 0.1
+    resid = torch.randn(m, n, device="cuda")
+    resid0 = resid.clone()
+    gam = torch.ones(n, device="cuda")
+    bet = torch.zeros(n, device="cuda")
+    ln_out = torch.empty(m, n, device="cuda", dtype=torch.uint8)
+    ln_scale = torch.empty(m, device="cuda")
+    call(FP8, EPI_LN, m, n, k, a, w, bias, resid=resid, g=gam, b=bet, ln_out=ln_out, ln_mode=LN_E4M3,
+         ln_scale=ln_scale, a_scale=sa, b_scale=sw)
+    x_ref = resid0 + (a.float() * sa[:, None]) @ (w.float() * sw[:, None]).T + bias
+    close(resid, x_ref, 1e-4)
+    y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
+    y = ln_out.view(torch.float8_e4m3fn).float() * ln_scale[:, None]
+    close(y, y_ref, 7e-2)
