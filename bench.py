@@ -64,7 +64,7 @@ def workload_name(cfg) -> str:
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -72,6 +72,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.window = None  # (t0, t1) wall-clock bounds of the loaded region
 
     def __enter__(self):
         try:
@@ -80,12 +81,14 @@ class ClockSampler:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(1.0)  # let nvidia-smi start sampling before the load begins
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *a):
         if self.proc is not None:
+            time.sleep(0.3)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -95,18 +98,23 @@ class ClockSampler:
     def summary(self) -> dict:
         if self.path is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        from datetime import datetime
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in Path(self.path).read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clk = float(parts[2])
+                smax = float(parts[3])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            if self.window is not None and not (self.window[0] - 0.25 <= ts <= self.window[1] + 0.25):
+                continue
+            sm.append(clk)
+            for n, v in zip(names, parts[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         os.unlink(self.path)
@@ -230,7 +238,9 @@ def run_ours(args, cfg) -> None:
     m_valid = int(counts.sum())
     sq_counts = int((counts.astype(np.int64) ** 2).sum())
 
-    stream = torch.cuda.current_stream(dev)
+    # one non-default stream carries the library's kernels, torch's copies/flushes and the timing events
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     pol = ow.EncoderPolicy(cfg, weights, device=local, stream=stream.cuda_stream, io="device")
     f_d = torch.from_numpy(feats).to(dev)
     c_d = torch.from_numpy(counts).to(dev)
@@ -254,14 +264,17 @@ def run_ours(args, cfg) -> None:
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    pol.profile_begin(args.steps)
+    prof_steps = min(args.steps, 100)
+    pol.profile_begin(prof_steps)  # per-kernel events on the first timed steps
     with ClockSampler(local) as clk:
+        clk.window = (time.time(), None)
         for i in range(args.steps):
             flush.zero_()  # L2 flush outside the step's events
             starts[i].record(stream)
             step(args.warmup + i)
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
+        clk.window = (clk.window[0], time.time())
     prof = pol.profile_end()
     pol.synchronize()
     if world > 1:
@@ -279,6 +292,7 @@ def run_ours(args, cfg) -> None:
 
     # e2e through the host-buffer API (pinned host buffers)
     e2e = None
+    e2e_steps = min(args.steps, 200)
     if not args.no_e2e:
         hp = ow.EncoderPolicy(cfg, weights, device=local, stream=stream.cuda_stream, io="host")
         f_h = torch.from_numpy(feats).pin_memory()
@@ -296,7 +310,7 @@ def run_ours(args, cfg) -> None:
         if world > 1:
             dist.barrier()
         wall = []
-        for i in range(args.steps):
+        for i in range(e2e_steps):
             flush.zero_()
             torch.cuda.synchronize(dev)
             t0 = time.perf_counter()
@@ -307,14 +321,15 @@ def run_ours(args, cfg) -> None:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         h2d = feats.nbytes + counts.nbytes
         d2h = lg_h.numel() * lg_h.element_size() + vv_h.numel() * vv_h.element_size() + aa_h.numel() * 4
-        e2e = {"value": world * B * args.steps / float(te.item()), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h), "timing": "wall clock per synchronous host-buffer call, max over ranks"}
+        e2e = {"value": world * B * e2e_steps / float(te.item()), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
+               "timing": "wall clock per synchronous host-buffer call (pinned buffers), max over ranks"}
         hp.close()
 
     # roofline of the dominant kernel
     peaks, peak_src = load_peaks()
     kernels = {}
-    for name, (n_launch, total_ms) in prof.items():
+    for name, (n_launch, total_ms) in prof.items():  # from the first `prof_steps` timed steps
         bound, work = kernel_work(cfg, name, m_valid, sq_counts, B)
         avg_s = total_ms / 1000.0 / max(n_launch, 1)
         ach = work / avg_s if avg_s > 0 else 0.0
@@ -338,7 +353,8 @@ def run_ours(args, cfg) -> None:
                 "frac": round(k["achieved"] / peak, 4), "traffic": None,
                 "peak_source": peak_src + (" (fp8 peak = 2x measured bf16)" if cfg.precision == "fp8" else ""),
                 "work_per_launch": "2*M_valid*N*K FLOPs, M_valid = valid tokens of the batch"
-                if k["bound"] == "tensor" else "bytes read + written"}
+                if k["bound"] == "tensor" else "bytes read + written",
+                "timed_steps_profiled": prof_steps}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -371,8 +387,8 @@ def run_ours(args, cfg) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=17)

@@ -78,8 +78,8 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(const float* __restrict__
   constexpr int D = DPL * 32;
   extern __shared__ float s_w[];  // [F][D] transposed embedding weights
   for (int i = threadIdx.x; i < n_feat * D; i += blockDim.x) {
-    const int f = i / D, c = i % D;
-    s_w[i] = w_e[c * n_feat + f];
+    const int c = i / n_feat, f = i % n_feat;  // coalesced read of W_e[c, f]
+    s_w[f * D + c] = w_e[i];
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -458,112 +458,135 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1
   return c;
 }
 
-template <typename T>
-__device__ __forceinline__ float load_as_f32(const T* p) {
-  if constexpr (sizeof(T) == 2)
-    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(p));
-  else
-    return *reinterpret_cast<const float*>(p);
-}
-
-// One CTA (4 warps) per state. y: final-LN output rows [rows, d] (f32 or bf16).
-// logits[b, j, :] = W_p.y + b_p for valid j, 0 for padded; actions = argmax
-// (+ Gumbel noise when sample), -1 for padded; value[b] = W_v.mean_j(y_j) + b_v.
-template <int DPL, typename YT, bool LOGITS_BF16, bool VALUE_BF16>
-__global__ void __launch_bounds__(128) heads_kernel(const YT* __restrict__ y, const int* __restrict__ offsets,
-                                                    int n_entities, int n_actions, const float* __restrict__ w_p,
-                                                    const float* __restrict__ b_p, const float* __restrict__ w_v,
-                                                    const float* __restrict__ b_v, int sample, uint64_t seed,
-                                                    void* __restrict__ logits, void* __restrict__ value,
-                                                    int* __restrict__ actions) {
+// Heads. Persistent CTAs (4 warps) walk the states; W_p is staged in shared
+// memory once per CTA. Lane l owns the float4 column groups l, l+32, ... so
+// y loads are coalesced and W_p reads are conflict-free LDS.128. Each lane
+// forms partial dots for all PP (= P rounded up to 8/16/32) actions, then a
+// butterfly reduce-scatter leaves logit p in lanes p*32/PP .. +32/PP-1.
+//   logits[b, j, :] = W_p.y_j + b_p (valid j), 0 (padded); actions = argmax
+//   (+ Gumbel noise when sampling), -1 (padded); value[b] = W_v.mean_j(y_j) + b_v.
+template <int DPL, int PP, bool LOGITS_BF16, bool VALUE_BF16>
+__global__ void __launch_bounds__(128) heads_kernel(const float* __restrict__ y, const int* __restrict__ offsets,
+                                                    int batch, int n_entities, int n_actions,
+                                                    const float* __restrict__ w_p, const float* __restrict__ b_p,
+                                                    const float* __restrict__ w_v, const float* __restrict__ b_v,
+                                                    int sample, uint64_t seed, void* __restrict__ logits,
+                                                    void* __restrict__ value, int* __restrict__ actions) {
   constexpr int D = DPL * 32;
+  constexpr int G = DPL / 4;  // float4 groups per lane
+  constexpr int LOG_PP = PP == 8 ? 3 : (PP == 16 ? 4 : 5);
   extern __shared__ float smem[];
-  float* s_wp = smem;               // [P][D]
-  float* s_pool = smem + n_actions * D;  // [4][D]
-  for (int i = threadIdx.x; i < n_actions * D; i += blockDim.x) s_wp[i] = w_p[i];
+  float* s_wp = smem;              // [PP][D], rows >= n_actions zero
+  float* s_pool = smem + PP * D;   // [4][D]
+  for (int i = threadIdx.x; i < PP * D; i += blockDim.x) s_wp[i] = (i / D) < n_actions ? w_p[i] : 0.0f;
   __syncthreads();
-  const int b = blockIdx.x;
-  const int row0 = offsets[b];
-  const int cnt = offsets[b + 1] - row0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float pool[DPL];
+  const int my_p = lane >> (5 - LOG_PP);
+  const bool writer = (lane & ((32 / PP) - 1)) == 0 && my_p < n_actions;
+  const float my_bias = my_p < n_actions ? b_p[my_p] : 0.0f;
+  for (int b = blockIdx.x; b < batch; b += gridDim.x) {
+    const int row0 = offsets[b];
+    const int cnt = offsets[b + 1] - row0;
+    float4 pool[G];
 #pragma unroll
-  for (int i = 0; i < DPL; ++i) pool[i] = 0.0f;
-  const float my_bias = lane < n_actions ? b_p[lane] : 0.0f;
-  for (int j = warp; j < n_entities; j += 4) {
-    const size_t slot = static_cast<size_t>(b) * n_entities + j;
-    if (j >= cnt) {
-      if (lane < n_actions) {
+    for (int g = 0; g < G; ++g) pool[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = warp; j < n_entities; j += 4) {
+      const size_t slot = static_cast<size_t>(b) * n_entities + j;
+      if (j >= cnt) {
+        if (writer) {
+          if (LOGITS_BF16)
+            reinterpret_cast<__nv_bfloat16*>(logits)[slot * n_actions + my_p] = __float2bfloat16_rn(0.0f);
+          else
+            reinterpret_cast<float*>(logits)[slot * n_actions + my_p] = 0.0f;
+        }
+        if (lane == 0) actions[slot] = -1;
+        continue;
+      }
+      float4 yv[G];
+      const float4* yr = reinterpret_cast<const float4*>(y + static_cast<size_t>(row0 + j) * D);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        yv[g] = yr[lane + 32 * g];
+        pool[g].x += yv[g].x;
+        pool[g].y += yv[g].y;
+        pool[g].z += yv[g].z;
+        pool[g].w += yv[g].w;
+      }
+      float v[PP];
+#pragma unroll
+      for (int p = 0; p < PP; ++p) {
+        float a = 0.0f;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 w = *reinterpret_cast<const float4*>(s_wp + p * D + 4 * (lane + 32 * g));
+          a = fmaf(yv[g].x, w.x, fmaf(yv[g].y, w.y, fmaf(yv[g].z, w.z, fmaf(yv[g].w, w.w, a))));
+        }
+        v[p] = a;
+      }
+      // reduce-scatter: each level halves the values a lane keeps
+#pragma unroll
+      for (int lvl = 0; lvl < LOG_PP; ++lvl) {
+        const int o = 16 >> lvl;
+        const int half = PP >> (lvl + 1);
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int k = 0; k < half; ++k) {
+          const float send = upper ? v[k] : v[k + half];
+          const float keep = upper ? v[k + half] : v[k];
+          v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+#pragma unroll
+      for (int o = (16 >> LOG_PP); o > 0; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+      float lg = v[0] + my_bias;
+      if (LOGITS_BF16) lg = __bfloat162float(__float2bfloat16_rn(lg));
+      if (writer) {
         if (LOGITS_BF16)
-          reinterpret_cast<__nv_bfloat16*>(logits)[slot * n_actions + lane] = __float2bfloat16_rn(0.0f);
+          reinterpret_cast<__nv_bfloat16*>(logits)[slot * n_actions + my_p] = __float2bfloat16_rn(lg);
         else
-          reinterpret_cast<float*>(logits)[slot * n_actions + lane] = 0.0f;
+          reinterpret_cast<float*>(logits)[slot * n_actions + my_p] = lg;
       }
-      if (lane == 0) actions[slot] = -1;
-      continue;
-    }
-    float yv[DPL];
+      float score = my_p < n_actions ? lg : -INFINITY;
+      if (sample && my_p < n_actions) {
+        const uint4 r = philox4x32_10(make_uint4(static_cast<uint32_t>(my_p) >> 2, static_cast<uint32_t>(j),
+                                                 static_cast<uint32_t>(b), 0u),
+                                      static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
+        const int w4 = my_p & 3;
+        const uint32_t word = w4 == 0 ? r.x : (w4 == 1 ? r.y : (w4 == 2 ? r.z : r.w));
+        const float u = (static_cast<float>(word) + 0.5f) * 2.3283064365386963e-10f;
+        score += -logf(-logf(u));
+      }
+      int idx = my_p;
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      yv[i] = load_as_f32(y + static_cast<size_t>(row0 + j) * D + i * 32 + lane);
-      pool[i] += yv[i];
+      for (int o = 16; o > 0; o >>= 1) {
+        const float os = __shfl_xor_sync(0xffffffffu, score, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (os > score || (os == score && oi < idx)) {
+          score = os;
+          idx = oi;
+        }
+      }
+      if (lane == 0) actions[slot] = idx;
     }
-    float mine = 0.0f;  // lane p keeps logit p
-    for (int p = 0; p < n_actions; ++p) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) *reinterpret_cast<float4*>(s_pool + warp * D + 4 * (lane + 32 * g)) = pool[g];
+    __syncthreads();
+    if (warp == 0) {
       float part = 0.0f;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) part = fmaf(yv[i], s_wp[p * D + i * 32 + lane], part);
+      for (int c = lane; c < D; c += 32) {
+        const float m = s_pool[c] + s_pool[D + c] + s_pool[2 * D + c] + s_pool[3 * D + c];
+        part = fmaf(m, w_v[c], part);
+      }
       part = warp_sum(part);
-      if (lane == p) mine = part;
-    }
-    float lg = mine + my_bias;
-    if (LOGITS_BF16) lg = __bfloat162float(__float2bfloat16_rn(lg));
-    if (lane < n_actions) {
-      if (LOGITS_BF16)
-        reinterpret_cast<__nv_bfloat16*>(logits)[slot * n_actions + lane] = __float2bfloat16_rn(lg);
-      else
-        reinterpret_cast<float*>(logits)[slot * n_actions + lane] = lg;
-    }
-    float score = lane < n_actions ? lg : -INFINITY;
-    if (sample && lane < n_actions) {
-      const uint4 r = philox4x32_10(make_uint4(static_cast<uint32_t>(lane) >> 2, static_cast<uint32_t>(j),
-                                               static_cast<uint32_t>(b), 0u),
-                                    static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
-      const uint32_t word = (lane & 3) == 0 ? r.x : ((lane & 3) == 1 ? r.y : ((lane & 3) == 2 ? r.z : r.w));
-      const float u = (static_cast<float>(word) + 0.5f) * 2.3283064365386963e-10f;
-      score += -logf(-logf(u));
-    }
-    int idx = lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float os = __shfl_xor_sync(0xffffffffu, score, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-      if (os > score || (os == score && oi < idx)) {
-        score = os;
-        idx = oi;
+      if (lane == 0) {
+        const float v = b_v[0] + (cnt > 0 ? part / static_cast<float>(cnt) : 0.0f);
+        if (VALUE_BF16)
+          reinterpret_cast<__nv_bfloat16*>(value)[b] = __float2bfloat16_rn(v);
+        else
+          reinterpret_cast<float*>(value)[b] = v;
       }
     }
-    if (lane == 0) actions[slot] = idx;
-  }
-#pragma unroll
-  for (int i = 0; i < DPL; ++i) s_pool[warp * D + i * 32 + lane] = pool[i];
-  __syncthreads();
-  if (warp == 0) {
-    float part = 0.0f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      const int c = i * 32 + lane;
-      const float m = s_pool[c] + s_pool[D + c] + s_pool[2 * D + c] + s_pool[3 * D + c];
-      part = fmaf(m, w_v[c], part);
-    }
-    part = warp_sum(part);
-    if (lane == 0) {
-      const float v = b_v[0] + (cnt > 0 ? part / static_cast<float>(cnt) : 0.0f);
-      if (VALUE_BF16)
-        reinterpret_cast<__nv_bfloat16*>(value)[b] = __float2bfloat16_rn(v);
-      else
-        reinterpret_cast<float*>(value)[b] = v;
-    }
+    __syncthreads();  // s_pool reused by the next state
   }
 }
 

@@ -236,7 +236,8 @@ cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensor
   using S = TcGemmShape<BN>;
   const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM) * (prm.n / BN);
   const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
-  tc_gemm_kernel<BN, EPI, FP8><<<grid, kGemmThreads, S::kSmemBytes, P.stream>>>(ma, mw, prm);
+  if (prm.n * ((FP8 ? 2 : 1) + (EPI == kEpiResidLn ? 2 : 0)) > kParamFloats) return cudaErrorInvalidValue;
+  tc_gemm_kernel<BN, EPI, FP8><<<grid, EpiWarps<EPI>::kThreads, S::kSmemBytes, P.stream>>>(ma, mw, prm);
   return cudaGetLastError();
 }
 
@@ -275,7 +276,7 @@ template <int DPL>
 cudaError_t launch_embed(const OwPolicy& P, int batch) {
   const auto& c = P.cfg;
   const long long slots = static_cast<long long>(batch) * c.n_entities;
-  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((slots + 7) / 8, P.num_sms * 8LL)));
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((slots + 7) / 8, P.num_sms * 2LL)));
   const size_t smem = static_cast<size_t>(c.features) * DPL * 32 * sizeof(float);
   const float* g = P.lw[0].ln1g;
   const float* b = P.lw[0].ln1b;
@@ -298,26 +299,34 @@ cudaError_t launch_embed(const OwPolicy& P, int batch) {
   return cudaGetLastError();
 }
 
-template <int DPL, typename YT, bool LB, bool VB>
-void heads_launch(const OwPolicy& P, int batch, size_t smem, uint64_t seed, void* logits, void* value, int* actions) {
+template <int DPL, int PP, bool LB, bool VB>
+void heads_launch(const OwPolicy& P, int batch, uint64_t seed, void* logits, void* value, int* actions) {
   const auto& c = P.cfg;
-  cudaFuncSetAttribute(heads_kernel<DPL, YT, LB, VB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const size_t smem = static_cast<size_t>(PP + 4) * DPL * 32 * sizeof(float);
+  cudaFuncSetAttribute(heads_kernel<DPL, PP, LB, VB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  heads_kernel<DPL, YT, LB, VB><<<batch, 128, smem, P.stream>>>(static_cast<const YT*>(P.y), P.offsets,
-                                                                c.n_entities, c.actions, P.wp, P.bp, P.wv, P.bv,
-                                                                c.sample_actions, seed, logits, value, actions);
+  const int grid = std::max(1, std::min(batch, P.num_sms * 8));
+  heads_kernel<DPL, PP, LB, VB><<<grid, 128, smem, P.stream>>>(static_cast<const float*>(P.y), P.offsets, batch,
+                                                               c.n_entities, c.actions, P.wp, P.bp, P.wv, P.bv,
+                                                               c.sample_actions, seed, logits, value, actions);
+}
+
+template <int DPL, int PP>
+void heads_dtype(const OwPolicy& P, int batch, uint64_t seed, void* logits, void* value, int* actions) {
+  const bool lb = P.cfg.logits_dtype == OW_DTYPE_BF16, vb = P.cfg.value_dtype == OW_DTYPE_BF16;
+  if (lb && vb) heads_launch<DPL, PP, true, true>(P, batch, seed, logits, value, actions);
+  else if (lb) heads_launch<DPL, PP, true, false>(P, batch, seed, logits, value, actions);
+  else if (vb) heads_launch<DPL, PP, false, true>(P, batch, seed, logits, value, actions);
+  else heads_launch<DPL, PP, false, false>(P, batch, seed, logits, value, actions);
 }
 
 template <int DPL>
 cudaError_t launch_heads(const OwPolicy& P, int batch, uint64_t seed, void* logits, void* value, int* actions) {
-  const auto& c = P.cfg;
-  const size_t smem = static_cast<size_t>(c.actions + 4) * DPL * 32 * sizeof(float);
-  const bool lb = c.logits_dtype == OW_DTYPE_BF16, vb = c.value_dtype == OW_DTYPE_BF16;
   // the final LayerNorm output is f32 on every path
-  if (lb && vb) heads_launch<DPL, float, true, true>(P, batch, smem, seed, logits, value, actions);
-  else if (lb) heads_launch<DPL, float, true, false>(P, batch, smem, seed, logits, value, actions);
-  else if (vb) heads_launch<DPL, float, false, true>(P, batch, smem, seed, logits, value, actions);
-  else heads_launch<DPL, float, false, false>(P, batch, smem, seed, logits, value, actions);
+  const int a = P.cfg.actions;
+  if (a <= 8) heads_dtype<DPL, 8>(P, batch, seed, logits, value, actions);
+  else if (a <= 16) heads_dtype<DPL, 16>(P, batch, seed, logits, value, actions);
+  else heads_dtype<DPL, 32>(P, batch, seed, logits, value, actions);
   return cudaGetLastError();
 }
 
@@ -379,9 +388,10 @@ cudaError_t launch_attention(const OwPolicy& P, int batch) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize(const OwPolicy& P, const void* in, int k, uint8_t* out, float* scale) {
+cudaError_t launch_quantize(const OwPolicy& P, const int* m_valid, const void* in, int k, uint8_t* out,
+                            float* scale) {
   const int grid = static_cast<int>(std::min<size_t>((P.cap_rows + 7) / 8, static_cast<size_t>(P.num_sms) * 8));
-  quantize_rows_e4m3_kernel<<<grid, 256, 0, P.stream>>>(static_cast<const __nv_bfloat16*>(in), P.offsets, k, out,
+  quantize_rows_e4m3_kernel<<<grid, 256, 0, P.stream>>>(static_cast<const __nv_bfloat16*>(in), m_valid, k, out,
                                                        scale);
   return cudaGetLastError();
 }
@@ -454,7 +464,7 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       else OW_STEP("gemm_qkv", (launch_gemm<128, kEpiBias, false>(P, P.m_ln, W.mqkv, q)));
       // attention
       OW_STEP("attention", launch_attention(P, batch));
-      if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, P.attn, d, P.attn8, P.attn_scale));
+      if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, m_valid, P.attn, d, P.attn8, P.attn_scale));
       // out-projection + residual + LN2
       TcGemmParams o{};
       o.m_valid = m_valid;
@@ -484,7 +494,7 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       u.b_scale = W.s1;
       if (fp8) OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, true>(P, P.m_ln, W.m1, u)));
       else OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, false>(P, P.m_ln, W.m1, u)));
-      if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, P.h, f, P.h8, P.h_scale));
+      if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, m_valid, P.h, f, P.h8, P.h_scale));
       // FFN down + residual + next LN (LN1 of the next block, or the final LN)
       TcGemmParams w{};
       w.m_valid = m_valid;

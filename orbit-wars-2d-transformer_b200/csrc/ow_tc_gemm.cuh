@@ -6,9 +6,13 @@
 //      when two tiles fit in the 512 columns so the epilogue of tile i
 //      overlaps the MMAs of tile i+1)
 //
-// Roles (192 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues
-// tcgen05.mma (and warp 1 owns the TMEM allocation), warps 2..5 drain TMEM
-// (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of the tile).
+// Roles: warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma (and
+// warp 1 owns the TMEM allocation), the epilogue warps drain TMEM. A warp may
+// only read TMEM lanes 32*(warp%4)..+31, i.e. 32 rows of the tile; the
+// bias/GELU epilogues run 8 warps (two per lane quadrant, each taking half of
+// the columns), the LayerNorm epilogue 4 (one thread owns one whole row).
+// Bias, LayerNorm gamma/beta and fp8 channel scales are staged in shared
+// memory once per CTA and read as broadcast float4.
 //
 // The number of valid rows is read from device memory (the packed token
 // count of the batch), so one launch shape serves every batch; tiles past the
@@ -50,6 +54,8 @@ struct TcGemmParams {
   int* err;
 };
 
+constexpr int kParamFloats = 4096;  // staged epilogue vectors (bias + scales, or bias/g/b/scales)
+
 template <int BLOCK_N>
 struct TcGemmShape {
   static constexpr int kBlockM = 128;
@@ -69,20 +75,26 @@ struct TcGemmShape {
                                    : kTmemColsNeeded <= 128 ? 128
                                    : kTmemColsNeeded <= 256 ? 256 : 512;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
+  static constexpr int kParamBytes = kParamFloats * 4;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + kParamBytes + 1024;  // + align slack
   static_assert(kInstN % 16 == 0 && kInstN <= 256, "M=128 UMMA needs N % 16 == 0, N <= 256");
   static_assert(kBoxRows <= 256, "TMA box rows <= 256");
   static_assert(kTmemColsNeeded <= 512, "TMEM has 512 columns");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
-constexpr int kGemmThreads = 192;
+template <int EPI>
+struct EpiWarps {
+  static constexpr int kCount = EPI == kEpiResidLn ? 4 : 8;
+  static constexpr int kThreads = 64 + 32 * kCount;
+};
 
 template <int BLOCK_N, int EPI, bool FP8>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                    const TcGemmParams p) {
   using S = TcGemmShape<BLOCK_N>;
+  constexpr int kEpiWarps = EpiWarps<EPI>::kCount;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
@@ -93,6 +105,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + S::kAcc;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + S::kAcc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* s_par = reinterpret_cast<float*>(smem + S::kStages * S::kStageBytes + S::kBarrierBytes);
+  // staged vectors: s_bias[n], then (fp8) s_bscale[n], then (LN) s_g[n], s_b[n]
+  float* s_bias = s_par;
+  float* s_bscale = s_par + p.n;
+  float* s_g = s_par + (FP8 ? 2 : 1) * p.n;
+  float* s_b = s_g + p.n;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -109,12 +127,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < S::kAcc; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_holder, S::kTmemCols);
+  for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
+    s_bias[i] = p.bias[i];
+    if (FP8) s_bscale[i] = p.b_scale[i];
+    if (EPI == kEpiResidLn) {
+      s_g[i] = p.ln_g[i];
+      s_b[i] = p.ln_b[i];
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -196,9 +222,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5.
+    // Epilogue warps 2 .. 2+kEpiWarps-1.
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
+    constexpr int kCols = EPI == kEpiResidLn ? BLOCK_N : BLOCK_N * 4 / kEpiWarps;  // columns this warp drains
+    const int col0 = EPI == kEpiResidLn ? 0 : ((warp - 2) / 4) * kCols;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -211,75 +239,90 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const float a_s = (FP8 && live) ? p.a_scale[m] : 1.0f;
 
       if (EPI == kEpiBias || EPI == kEpiBiasGelu) {
+        static_assert(kCols % 64 == 0, "64-column epilogue chunks");
 #pragma unroll 1
-        for (int c = 0; c < BLOCK_N; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c, r);
+        for (int c = col0; c < col0 + kCols; c += 64) {
+          uint32_t r[64];
+          tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
           tmem_ld_wait();
           if (live) {
-            uint32_t packed[16];
+            uint32_t packed[32];
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const int n = n0 + c + i;
-              float v0 = __uint_as_float(r[i]);
-              float v1 = __uint_as_float(r[i + 1]);
+            for (int i = 0; i < 64; i += 4) {
+              const float4 bv = *reinterpret_cast<const float4*>(s_bias + n0 + c + i);
+              float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
+              float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
               if (FP8) {
-                v0 *= a_s * p.b_scale[n];
-                v1 *= a_s * p.b_scale[n + 1];
+                const float4 sv = *reinterpret_cast<const float4*>(s_bscale + n0 + c + i);
+                v0 *= a_s * sv.x;
+                v1 *= a_s * sv.y;
+                v2 *= a_s * sv.z;
+                v3 *= a_s * sv.w;
               }
-              v0 += p.bias[n];
-              v1 += p.bias[n + 1];
+              v0 += bv.x;
+              v1 += bv.y;
+              v2 += bv.z;
+              v3 += bv.w;
               if (EPI == kEpiBiasGelu) {
                 v0 = gelu_erf(v0);
                 v1 = gelu_erf(v1);
+                v2 = gelu_erf(v2);
+                v3 = gelu_erf(v3);
               }
               packed[i / 2] = pack_bf16x2(v0, v1);
+              packed[i / 2 + 1] = pack_bf16x2(v2, v3);
             }
             uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(m) * p.ld_out + n0 + c);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
+            for (int q = 0; q < 8; ++q)
               dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
           }
         }
       } else {
-        // Residual add + LayerNorm over the full row (BLOCK_N == n == d).
+        // Residual add + LayerNorm over the full row (BLOCK_N == n == d): two
+        // passes over TMEM. Pass 1 forms v = x + acc*s + bias, writes it back to
+        // TMEM and accumulates shifted statistics (shift = the row's first v,
+        // which keeps E[(v-k)^2] - E[v-k]^2 well conditioned); pass 2 writes x
+        // and the normalised row.
         float* xrow = p.resid + static_cast<size_t>(live ? m : 0) * BLOCK_N;
-        float sum = 0.0f;
+        float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
 #pragma unroll 1
         for (int c = 0; c < BLOCK_N; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c, r);
-          tmem_ld_wait();
           float4 xr[8];
           const float4* src = reinterpret_cast<const float4*>(xrow + c);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) xr[q] = live ? src[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int q = 0; q < 8; ++q) xr[q] = src[q];
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_ld_wait();
           const float* xv = reinterpret_cast<const float*>(xr);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float v = __uint_as_float(r[i]);
-            if (FP8) v *= a_s * p.b_scale[c + i];
-            v += p.bias[c + i] + xv[i];
-            sum += v;
-            r[i] = __float_as_uint(v);
+          for (int i = 0; i < 32; i += 4) {
+            const float4 bv = *reinterpret_cast<const float4*>(s_bias + c + i);
+            float4 sv = make_float4(1.f, 1.f, 1.f, 1.f);
+            if (FP8) sv = *reinterpret_cast<const float4*>(s_bscale + c + i);
+            const float b4[4] = {bv.x, bv.y, bv.z, bv.w};
+            const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float v = __uint_as_float(r[i + j]);
+              if (FP8) v *= a_s * s4[j];
+              v += b4[j] + xv[i + j];
+              if (c == 0 && i + j == 0) shift = v;
+              const float dv = v - shift;
+              s1 += dv;
+              s2 = fmaf(dv, dv, s2);
+              r[i + j] = __float_as_uint(v);
+            }
           }
           tmem_st32(tbase + c, r);
         }
         tmem_st_wait();
-        const float mean = sum * (1.0f / BLOCK_N);
-        float sq = 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < BLOCK_N; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float dv = __uint_as_float(r[i]) - mean;
-            sq += dv * dv;
-          }
-        }
-        const float rstd = rsqrtf(sq * (1.0f / BLOCK_N) + 1e-5f);
+        const float md = s1 * (1.0f / BLOCK_N);
+        const float var = fmaxf(s2 * (1.0f / BLOCK_N) - md * md, 0.0f);
+        const float mean = shift + md;
+        const float rstd = rsqrtf(var + 1e-5f);
         float inv_scale = 1.0f;
         if (p.ln_mode == kLnE4m3) {
           float amax = 0.0f;
@@ -290,7 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float y = (__uint_as_float(r[i]) - mean) * rstd * p.ln_g[c + i] + p.ln_b[c + i];
+              const float y = (__uint_as_float(r[i]) - mean) * rstd * s_g[c + i] + s_b[c + i];
               amax = fmaxf(amax, fabsf(y));
             }
           }
@@ -311,7 +354,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               xd[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                   __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
 #pragma unroll
-            for (int i = 0; i < 32; ++i) y[i] = (__uint_as_float(r[i]) - mean) * rstd * p.ln_g[c + i] + p.ln_b[c + i];
+            for (int i = 0; i < 32; i += 4) {
+              const float4 gv = *reinterpret_cast<const float4*>(s_g + c + i);
+              const float4 bv = *reinterpret_cast<const float4*>(s_b + c + i);
+              y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
+              y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
+              y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
+              y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
+            }
             if (p.ln_mode == kLnE4m3) {
               uint32_t q8[8];
 #pragma unroll
