@@ -76,10 +76,11 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(const float* __restrict__
                                                        float* __restrict__ x, void* __restrict__ ln_out,
                                                        float* __restrict__ ln_scale) {
   constexpr int D = DPL * 32;
-  extern __shared__ float s_w[];  // [F][D] transposed embedding weights
+  constexpr int PITCH = D + 1;    // odd pitch: the transposing fill is bank-conflict free
+  extern __shared__ float s_w[];  // [F][PITCH] transposed embedding weights
   for (int i = threadIdx.x; i < n_feat * D; i += blockDim.x) {
     const int c = i / n_feat, f = i % n_feat;  // coalesced read of W_e[c, f]
-    s_w[f * D + c] = w_e[i];
+    s_w[f * PITCH + c] = w_e[i];
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(const float* __restrict__
     for (int f = 0; f < n_feat; ++f) {
       const float xf = __shfl_sync(0xffffffffu, fv, f);
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] = fmaf(xf, s_w[f * D + i * 32 + lane], acc[i]);
+      for (int i = 0; i < DPL; ++i) acc[i] = fmaf(xf, s_w[f * PITCH + i * 32 + lane], acc[i]);
     }
     float s = 0.0f;
 #pragma unroll

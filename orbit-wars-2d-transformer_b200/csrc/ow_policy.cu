@@ -228,12 +228,12 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 template <int BN, int EPI, bool FP8>
 cudaError_t set_gemm_attr() {
   return cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              TcGemmShape<BN>::kSmemBytes);
+                              TcGemmShape<BN, EPI>::kSmemBytes);
 }
 
 template <int BN, int EPI, bool FP8>
 cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw, const TcGemmParams& prm) {
-  using S = TcGemmShape<BN>;
+  using S = TcGemmShape<BN, EPI>;
   const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM) * (prm.n / BN);
   const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
   if (prm.n * ((FP8 ? 2 : 1) + (EPI == kEpiResidLn ? 2 : 0)) > kParamFloats) return cudaErrorInvalidValue;
@@ -276,8 +276,8 @@ template <int DPL>
 cudaError_t launch_embed(const OwPolicy& P, int batch) {
   const auto& c = P.cfg;
   const long long slots = static_cast<long long>(batch) * c.n_entities;
-  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((slots + 7) / 8, P.num_sms * 2LL)));
-  const size_t smem = static_cast<size_t>(c.features) * DPL * 32 * sizeof(float);
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((slots + 7) / 8, P.num_sms * 6LL)));
+  const size_t smem = static_cast<size_t>(c.features) * (DPL * 32 + 1) * sizeof(float);
   const float* g = P.lw[0].ln1g;
   const float* b = P.lw[0].ln1b;
   if (c.precision == OW_PRECISION_F32) {

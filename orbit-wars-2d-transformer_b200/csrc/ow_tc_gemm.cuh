@@ -55,15 +55,21 @@ struct TcGemmParams {
 };
 
 constexpr int kParamFloats = 4096;  // staged epilogue vectors (bias + scales, or bias/g/b/scales)
+constexpr int kSmemLimit = 232448;   // dynamic shared memory per CTA on sm_100
 
-template <int BLOCK_N>
+template <int EPI>
+struct EpiWarps {
+  static constexpr int kCount = EPI == kEpiResidLn ? 4 : 8;
+  static constexpr int kThreads = 64 + 32 * kCount;
+};
+
+template <int BLOCK_N, int EPI>
 struct TcGemmShape {
   static constexpr int kBlockM = 128;
   static constexpr int kRowBytes = 128;  // one swizzle atom row: 64 bf16 or 128 e4m3
   static constexpr int kATileBytes = kBlockM * kRowBytes;
   static constexpr int kBTileBytes = BLOCK_N * kRowBytes;
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
-  static constexpr int kStages = (BLOCK_N <= 128) ? 6 : (BLOCK_N <= 256 ? 4 : (BLOCK_N <= 384 ? 3 : 2));
   static constexpr int kInstN = BLOCK_N <= 256 ? BLOCK_N : BLOCK_N / 2;   // N of one tcgen05.mma
   static constexpr int kInstCount = BLOCK_N / kInstN;
   static constexpr int kBoxRows = BLOCK_N <= 256 ? BLOCK_N : BLOCK_N / 2;  // TMA box rows for W (<= 256)
@@ -76,24 +82,46 @@ struct TcGemmShape {
                                    : kTmemColsNeeded <= 256 ? 256 : 512;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kParamBytes = kParamFloats * 4;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + kParamBytes + 1024;  // + align slack
+  static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * 4096;  // per-warp 32 x 128 B transpose tile
+  static constexpr int kFixedBytes = kBarrierBytes + kParamBytes + kXposeBytes + 1024;  // + align slack
+  static constexpr int kStagesFit = (kSmemLimit - kFixedBytes) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kFixedBytes;
+  static_assert(kStages >= 2, "at least double-buffered operand stages");
   static_assert(kInstN % 16 == 0 && kInstN <= 256, "M=128 UMMA needs N % 16 == 0, N <= 256");
   static_assert(kBoxRows <= 256, "TMA box rows <= 256");
   static_assert(kTmemColsNeeded <= 512, "TMEM has 512 columns");
-  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory per CTA");
 };
 
-template <int EPI>
-struct EpiWarps {
-  static constexpr int kCount = EPI == kEpiResidLn ? 4 : 8;
-  static constexpr int kThreads = 64 + 32 * kCount;
-};
+// Warp-cooperative transpose through a 32 x 128 B shared tile. 16-byte chunk
+// j of row r lives at chunk slot j ^ (r & 7), so both the row-per-thread side
+// (thread r touches row r) and the row-per-8-lanes side (8 lanes cover one
+// 128 B row) are bank-conflict free.
+__device__ __forceinline__ uint4* xpose_slot(uint8_t* tile, int row, int chunk) {
+  return reinterpret_cast<uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+// rows [0, rows) of the tile -> global rows of `row_bytes` bytes (chunks_per_row 16 B chunks each)
+__device__ __forceinline__ void xpose_store(uint8_t* tile, uint8_t* gbase, size_t gstride, int rows, int chunks_per_row,
+                                            int lane) {
+  const int rows_per_iter = 32 / chunks_per_row;
+  const int j = lane % chunks_per_row;
+  for (int r = lane / chunks_per_row; r < rows; r += rows_per_iter)
+    *reinterpret_cast<uint4*>(gbase + r * gstride + j * 16) = *xpose_slot(tile, r, j);
+}
+__device__ __forceinline__ void xpose_load(uint8_t* tile, const uint8_t* gbase, size_t gstride, int rows,
+                                           int chunks_per_row, int lane) {
+  const int rows_per_iter = 32 / chunks_per_row;
+  const int j = lane % chunks_per_row;
+  for (int r = lane / chunks_per_row; r < rows; r += rows_per_iter)
+    *xpose_slot(tile, r, j) = *reinterpret_cast<const uint4*>(gbase + r * gstride + j * 16);
+}
 
 template <int BLOCK_N, int EPI, bool FP8>
 __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                    const TcGemmParams p) {
-  using S = TcGemmShape<BLOCK_N>;
+  using S = TcGemmShape<BLOCK_N, EPI>;
   constexpr int kEpiWarps = EpiWarps<EPI>::kCount;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -106,6 +134,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + S::kAcc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* s_par = reinterpret_cast<float*>(smem + S::kStages * S::kStageBytes + S::kBarrierBytes);
+  uint8_t* s_xpose = smem + S::kStages * S::kStageBytes + S::kBarrierBytes + S::kParamBytes;
   // staged vectors: s_bias[n], then (fp8) s_bscale[n], then (LN) s_g[n], s_b[n]
   float* s_bias = s_par;
   float* s_bscale = s_par + p.n;
@@ -222,9 +251,11 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2 .. 2+kEpiWarps-1.
+    // Epilogue warps 2 .. 2+kEpiWarps-1. Thread `lane` of a warp owns tile row
+    // quad*32 + lane on the TMEM side; global traffic goes through the warp's
+    // transpose tile so each warp instruction moves whole 128 B rows.
     const int quad = warp & 3;
-    const int row_in_tile = quad * 32 + lane;
+    uint8_t* xt = s_xpose + (warp - 2) * 4096;
     constexpr int kCols = EPI == kEpiResidLn ? BLOCK_N : BLOCK_N * 4 / kEpiWarps;  // columns this warp drains
     const int col0 = EPI == kEpiResidLn ? 0 : ((warp - 2) / 4) * kCols;
     int acc = 0;
@@ -232,7 +263,9 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
-      const int m = (tile / n_tiles) * S::kBlockM + row_in_tile;
+      const int row_base = (tile / n_tiles) * S::kBlockM + quad * 32;  // first row of this warp's 32
+      const int m = row_base + lane;
+      const int rows = min(32, m_valid - row_base);                    // valid rows of the 32 (may be <= 0)
       const int n0 = (tile % n_tiles) * BLOCK_N;
       const bool live = m < m_valid;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BLOCK_N);
@@ -246,38 +279,40 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           tmem_ld32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
           tmem_ld_wait();
-          if (live) {
-            uint32_t packed[32];
+          uint32_t packed[32];
 #pragma unroll
-            for (int i = 0; i < 64; i += 4) {
-              const float4 bv = *reinterpret_cast<const float4*>(s_bias + n0 + c + i);
-              float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
-              float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
-              if (FP8) {
-                const float4 sv = *reinterpret_cast<const float4*>(s_bscale + n0 + c + i);
-                v0 *= a_s * sv.x;
-                v1 *= a_s * sv.y;
-                v2 *= a_s * sv.z;
-                v3 *= a_s * sv.w;
-              }
-              v0 += bv.x;
-              v1 += bv.y;
-              v2 += bv.z;
-              v3 += bv.w;
-              if (EPI == kEpiBiasGelu) {
-                v0 = gelu_erf(v0);
-                v1 = gelu_erf(v1);
-                v2 = gelu_erf(v2);
-                v3 = gelu_erf(v3);
-              }
-              packed[i / 2] = pack_bf16x2(v0, v1);
-              packed[i / 2 + 1] = pack_bf16x2(v2, v3);
+          for (int i = 0; i < 64; i += 4) {
+            const float4 bv = *reinterpret_cast<const float4*>(s_bias + n0 + c + i);
+            float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
+            float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
+            if (FP8) {
+              const float4 sv = *reinterpret_cast<const float4*>(s_bscale + n0 + c + i);
+              v0 *= a_s * sv.x;
+              v1 *= a_s * sv.y;
+              v2 *= a_s * sv.z;
+              v3 *= a_s * sv.w;
             }
-            uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(m) * p.ld_out + n0 + c);
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            v0 += bv.x;
+            v1 += bv.y;
+            v2 += bv.z;
+            v3 += bv.w;
+            if (EPI == kEpiBiasGelu) {
+              v0 = gelu_erf(v0);
+              v1 = gelu_erf(v1);
+              v2 = gelu_erf(v2);
+              v3 = gelu_erf(v3);
+            }
+            packed[i / 2] = pack_bf16x2(v0, v1);
+            packed[i / 2 + 1] = pack_bf16x2(v2, v3);
           }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *xpose_slot(xt, lane, q) = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          __syncwarp();
+          if (rows > 0)
+            xpose_store(xt, reinterpret_cast<uint8_t*>(p.out + static_cast<size_t>(row_base) * p.ld_out + n0 + c),
+                        static_cast<size_t>(p.ld_out) * 2, rows, 8, lane);
+          __syncwarp();
         }
       } else {
         // Residual add + LayerNorm over the full row (BLOCK_N == n == d): two
@@ -285,18 +320,26 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
         // TMEM and accumulates shifted statistics (shift = the row's first v,
         // which keeps E[(v-k)^2] - E[v-k]^2 well conditioned); pass 2 writes x
         // and the normalised row.
-        float* xrow = p.resid + static_cast<size_t>(live ? m : 0) * BLOCK_N;
+        uint8_t* xg = reinterpret_cast<uint8_t*>(p.resid + static_cast<size_t>(row_base > 0 ? row_base : 0) * BLOCK_N);
+        const size_t xstride = static_cast<size_t>(BLOCK_N) * 4;
         float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
 #pragma unroll 1
         for (int c = 0; c < BLOCK_N; c += 32) {
-          float4 xr[8];
-          const float4* src = reinterpret_cast<const float4*>(xrow + c);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) xr[q] = src[q];
+          if (rows > 0) xpose_load(xt, xg + c * 4, xstride, rows, 8, lane);  // 32 rows x 32 f32 of x
           uint32_t r[32];
           tmem_ld32(tbase + c, r);
           tmem_ld_wait();
-          const float* xv = reinterpret_cast<const float*>(xr);
+          __syncwarp();
+          float xv[32];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 t4 = live ? *reinterpret_cast<const float4*>(xpose_slot(xt, lane, q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xv[4 * q] = t4.x;
+            xv[4 * q + 1] = t4.y;
+            xv[4 * q + 2] = t4.z;
+            xv[4 * q + 3] = t4.w;
+          }
+          __syncwarp();
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             const float4 bv = *reinterpret_cast<const float4*>(s_bias + c + i);
@@ -341,51 +384,57 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           inv_scale = 1.0f / scale;
           if (live) p.ln_scale[m] = scale;
         }
+        const int ln_elt = p.ln_mode == kLnF32 ? 4 : (p.ln_mode == kLnE4m3 ? 1 : 2);
+        uint8_t* lg = reinterpret_cast<uint8_t*>(p.ln_out) + static_cast<size_t>(row_base > 0 ? row_base : 0) * BLOCK_N * ln_elt;
+        const size_t lstride = static_cast<size_t>(BLOCK_N) * ln_elt;
 #pragma unroll 1
         for (int c = 0; c < BLOCK_N; c += 32) {
           uint32_t r[32];
           tmem_ld32(tbase + c, r);
           tmem_ld_wait();
-          if (live) {
-            float y[32];
-            float4* xd = reinterpret_cast<float4*>(xrow + c);
+          // x (f32): 32 columns = one 128 B row segment per thread
+#pragma unroll
+          for (int q = 0; q < 8; ++q) *xpose_slot(xt, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          __syncwarp();
+          if (rows > 0) xpose_store(xt, xg + c * 4, xstride, rows, 8, lane);
+          __syncwarp();
+          float y[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 gv = *reinterpret_cast<const float4*>(s_g + c + i);
+            const float4 bv = *reinterpret_cast<const float4*>(s_b + c + i);
+            y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
+            y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
+            y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
+            y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
+          }
+          int chunks;
+          if (p.ln_mode == kLnE4m3) {
+            uint32_t q8[8];
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
+                                      y[i + 3] * inv_scale);
+            *xpose_slot(xt, lane, 0) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+            *xpose_slot(xt, lane, 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
+            chunks = 2;
+          } else if (p.ln_mode == kLnF32) {
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              xd[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                  __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+              *xpose_slot(xt, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
+                                                    __float_as_uint(y[4 * q + 2]), __float_as_uint(y[4 * q + 3]));
+            chunks = 8;
+          } else {
+            uint32_t yo[16];
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              const float4 gv = *reinterpret_cast<const float4*>(s_g + c + i);
-              const float4 bv = *reinterpret_cast<const float4*>(s_b + c + i);
-              y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
-              y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
-              y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
-              y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
-            }
-            if (p.ln_mode == kLnE4m3) {
-              uint32_t q8[8];
+            for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
 #pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
-                                        y[i + 3] * inv_scale);
-              uint4* ld = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ln_out) +
-                                                   static_cast<size_t>(m) * BLOCK_N + c);
-              ld[0] = make_uint4(q8[0], q8[1], q8[2], q8[3]);
-              ld[1] = make_uint4(q8[4], q8[5], q8[6], q8[7]);
-            } else if (p.ln_mode == kLnF32) {
-              float4* ld = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.ln_out) + static_cast<size_t>(m) * BLOCK_N + c);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) ld[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-            } else {
-              uint32_t yo[16];
-#pragma unroll
-              for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
-              uint4* ld = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ln_out) +
-                                                   static_cast<size_t>(m) * BLOCK_N + c);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) ld[q] = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
-            }
+            for (int q = 0; q < 4; ++q) *xpose_slot(xt, lane, q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
+            chunks = 4;
           }
+          __syncwarp();
+          if (rows > 0) xpose_store(xt, lg + c * ln_elt, lstride, rows, chunks, lane);
+          __syncwarp();
         }
       }
       tc_fence_before();
