@@ -131,20 +131,28 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// K-major 2-D map: rows of `inner` elements, box = 128 bytes x box_rows, 128 B swizzle.
-bool make_kmajor_map(CUtensorMap* map, const void* base, bool e4m3, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+// Row-major 2-D map over [rows, inner] elements of `elt` bytes with a box of
+// (128 bytes of a row) x box_rows and the 128 B swizzle: the layout both the
+// UMMA operand descriptors and the epilogue staging tiles use.
+enum MapType { kMapBf16, kMapU8, kMapF32 };
+bool make_map_128b(CUtensorMap* map, const void* base, MapType t, uint64_t inner, uint64_t rows, uint32_t box_rows) {
   auto enc = tensor_map_encoder();
-  if (enc == nullptr) return false;
-  const uint32_t elt = e4m3 ? 1 : 2;
+  if (enc == nullptr || base == nullptr) return false;
+  const uint32_t elt = t == kMapF32 ? 4 : (t == kMapBf16 ? 2 : 1);
+  const CUtensorMapDataType dt = t == kMapF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : (t == kMapBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8);
   cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {inner * elt};
   cuuint32_t box[2] = {128 / elt, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, e4m3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+// K-major GEMM operand map (bf16 or e4m3), box = 128 bytes x box_rows.
+bool make_kmajor_map(CUtensorMap* map, const void* base, bool e4m3, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  return make_map_128b(map, base, e4m3 ? kMapU8 : kMapBf16, inner, rows, box_rows);
 }
 
 // ---------------------------------------------------------------- host conversions
@@ -196,7 +204,9 @@ struct OwPolicy {
   void *x = nullptr, *ln = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr;
   uint8_t *ln8 = nullptr, *attn8 = nullptr, *h8 = nullptr;
   float *ln_scale = nullptr, *attn_scale = nullptr, *h_scale = nullptr;
-  CUtensorMap m_ln, m_attn, m_h;
+  CUtensorMap m_ln, m_attn, m_h;       // GEMM A operands
+  CUtensorMap e_qkv, e_h, e_x;         // epilogue outputs: qkv / h (bf16, 32-row boxes), x (f32)
+  CUtensorMap e_ln, e_y;               // LayerNorm outputs: ln (bf16 or e4m3), y (f32, final LN)
   int qkv_block_n = 256;
   int launches = 0;
   // profiling (ow_policy_profile_begin/_end)
@@ -232,25 +242,26 @@ cudaError_t set_gemm_attr() {
 }
 
 template <int BN, int EPI, bool FP8>
-cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw, const TcGemmParams& prm) {
+cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo,
+                        const CUtensorMap& ml, const TcGemmParams& prm) {
   using S = TcGemmShape<BN, EPI>;
   const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM) * (prm.n / BN);
   const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
-  if (prm.n * ((FP8 ? 2 : 1) + (EPI == kEpiResidLn ? 2 : 0)) > kParamFloats) return cudaErrorInvalidValue;
-  tc_gemm_kernel<BN, EPI, FP8><<<grid, EpiWarps<EPI>::kThreads, S::kSmemBytes, P.stream>>>(ma, mw, prm);
+  if (prm.n * ((FP8 ? 2 : 1) + (EPI == kEpiResidLn ? 2 : 0)) > S::kParamFloats) return cudaErrorInvalidValue;
+  tc_gemm_kernel<BN, EPI, FP8><<<grid, EpiWarps<EPI>::kThreads, S::kSmemBytes, P.stream>>>(ma, mw, mo, ml, prm);
   return cudaGetLastError();
 }
 
 // Dispatch on the d-wide LN-fused tile.
 cudaError_t launch_gemm_resid_ln(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw,
-                                 const TcGemmParams& prm, bool fp8) {
+                                 const CUtensorMap& mx, const CUtensorMap& ml, const TcGemmParams& prm, bool fp8) {
   const int d = P.cfg.d_model;
-  if (fp8) return launch_gemm<256, kEpiResidLn, true>(P, ma, mw, prm);
+  if (fp8) return launch_gemm<256, kEpiResidLn, true>(P, ma, mw, mx, ml, prm);
   switch (d) {
-    case 128: return launch_gemm<128, kEpiResidLn, false>(P, ma, mw, prm);
-    case 256: return launch_gemm<256, kEpiResidLn, false>(P, ma, mw, prm);
-    case 384: return launch_gemm<384, kEpiResidLn, false>(P, ma, mw, prm);
-    default: return launch_gemm<512, kEpiResidLn, false>(P, ma, mw, prm);
+    case 128: return launch_gemm<128, kEpiResidLn, false>(P, ma, mw, mx, ml, prm);
+    case 256: return launch_gemm<256, kEpiResidLn, false>(P, ma, mw, mx, ml, prm);
+    case 384: return launch_gemm<384, kEpiResidLn, false>(P, ma, mw, mx, ml, prm);
+    default: return launch_gemm<512, kEpiResidLn, false>(P, ma, mw, mx, ml, prm);
   }
 }
 
@@ -459,9 +470,10 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       q.ld_out = 3 * d;
       q.a_scale = P.ln_scale;
       q.b_scale = W.sqkv;
-      if (fp8) OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, true>(P, P.m_ln, W.mqkv, q)));
-      else if (P.qkv_block_n == 256) OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, false>(P, P.m_ln, W.mqkv, q)));
-      else OW_STEP("gemm_qkv", (launch_gemm<128, kEpiBias, false>(P, P.m_ln, W.mqkv, q)));
+      if (fp8) OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, true>(P, P.m_ln, W.mqkv, P.e_qkv, P.e_qkv, q)));
+      else if (P.qkv_block_n == 256)
+        OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, false>(P, P.m_ln, W.mqkv, P.e_qkv, P.e_qkv, q)));
+      else OW_STEP("gemm_qkv", (launch_gemm<128, kEpiBias, false>(P, P.m_ln, W.mqkv, P.e_qkv, P.e_qkv, q)));
       // attention
       OW_STEP("attention", launch_attention(P, batch));
       if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, m_valid, P.attn, d, P.attn8, P.attn_scale));
@@ -480,7 +492,7 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       o.ln_scale = P.ln_scale;
       o.a_scale = P.attn_scale;
       o.b_scale = W.so;
-      OW_STEP("gemm_out_resid_ln", launch_gemm_resid_ln(P, P.m_attn, W.mo, o, fp8));
+      OW_STEP("gemm_out_resid_ln", launch_gemm_resid_ln(P, P.m_attn, W.mo, P.e_x, P.e_ln, o, fp8));
       // FFN up + GELU
       TcGemmParams u{};
       u.m_valid = m_valid;
@@ -492,8 +504,8 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       u.ld_out = f;
       u.a_scale = P.ln_scale;
       u.b_scale = W.s1;
-      if (fp8) OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, true>(P, P.m_ln, W.m1, u)));
-      else OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, false>(P, P.m_ln, W.m1, u)));
+      if (fp8) OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, true>(P, P.m_ln, W.m1, P.e_h, P.e_h, u)));
+      else OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, false>(P, P.m_ln, W.m1, P.e_h, P.e_h, u)));
       if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, m_valid, P.h, f, P.h8, P.h_scale));
       // FFN down + residual + next LN (LN1 of the next block, or the final LN)
       TcGemmParams w{};
@@ -510,7 +522,8 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       w.ln_scale = P.ln_scale;
       w.a_scale = P.h_scale;
       w.b_scale = W.s2;
-      OW_STEP("gemm_ffn_down_resid_ln", launch_gemm_resid_ln(P, P.m_h, W.m2, w, fp8));
+      OW_STEP("gemm_ffn_down_resid_ln",
+              launch_gemm_resid_ln(P, P.m_h, W.m2, P.e_x, last ? P.e_y : P.e_ln, w, fp8));
     }
   }
   OW_STEP("heads", dispatch_heads(P, batch, seed, logits, value, actions));
@@ -710,6 +723,10 @@ OwStatus alloc_workspace(OwPolicy& P) {
     else
       ok = make_kmajor_map(&P.m_ln, P.ln, false, d, rows, 128) && make_kmajor_map(&P.m_attn, P.attn, false, d, rows, 128) &&
            make_kmajor_map(&P.m_h, P.h, false, f, rows, 128);
+    ok = ok && make_map_128b(&P.e_qkv, P.qkv, kMapBf16, 3 * d, rows, 32) &&
+         make_map_128b(&P.e_h, P.h, kMapBf16, f, rows, 32) && make_map_128b(&P.e_x, P.x, kMapF32, d, rows, 32) &&
+         make_map_128b(&P.e_y, P.y, kMapF32, d, rows, 32) &&
+         (e4 ? make_map_128b(&P.e_ln, P.ln8, kMapU8, d, rows, 32) : make_map_128b(&P.e_ln, P.ln, kMapBf16, d, rows, 32));
     if (!ok) return st_rt("cuTensorMapEncodeTiled failed for an activation buffer");
   }
   OW_TRY(cudaStreamSynchronize(P.stream));
@@ -965,9 +982,18 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   P.num_sms = prop.multiProcessorCount;
   OW_TRY(set_all_gemm_attrs());
   const uint32_t box_rows = bn <= 256 ? static_cast<uint32_t>(bn) : static_cast<uint32_t>(bn / 2);
-  CUtensorMap ma, mw;
+  CUtensorMap ma, mw, mo, ml;
   if (!make_kmajor_map(&ma, a, fp8, k, m, 128) || !make_kmajor_map(&mw, w, fp8, k, n, box_rows))
     return st_rt("cuTensorMapEncodeTiled failed");
+  bool mok;
+  if (epilogue == kEpiResidLn) {
+    const MapType lt = ln_mode == kLnF32 ? kMapF32 : (ln_mode == kLnE4m3 ? kMapU8 : kMapBf16);
+    mok = make_map_128b(&mo, resid, kMapF32, n, m, 32) && make_map_128b(&ml, ln_out, lt, n, m, 32);
+  } else {
+    mok = make_map_128b(&mo, out, kMapBf16, n, m, 32);
+    ml = mo;
+  }
+  if (!mok) return st_rt("cuTensorMapEncodeTiled failed for an epilogue buffer");
   int* d_m = nullptr;
   int* d_err = nullptr;
   OW_TRY(cudaMalloc(&d_m, 2 * sizeof(int)));
@@ -993,14 +1019,14 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   if (e == cudaSuccess) {
     if (epilogue == kEpiResidLn) {
       P.cfg.d_model = n;
-      e = launch_gemm_resid_ln(P, ma, mw, q, fp8);
+      e = launch_gemm_resid_ln(P, ma, mw, mo, ml, q, fp8);
     } else if (epilogue == kEpiBias) {
-      if (fp8) e = launch_gemm<256, kEpiBias, true>(P, ma, mw, q);
-      else if (bn == 256) e = launch_gemm<256, kEpiBias, false>(P, ma, mw, q);
-      else e = launch_gemm<128, kEpiBias, false>(P, ma, mw, q);
+      if (fp8) e = launch_gemm<256, kEpiBias, true>(P, ma, mw, mo, ml, q);
+      else if (bn == 256) e = launch_gemm<256, kEpiBias, false>(P, ma, mw, mo, ml, q);
+      else e = launch_gemm<128, kEpiBias, false>(P, ma, mw, mo, ml, q);
     } else {
-      if (fp8) e = launch_gemm<256, kEpiBiasGelu, true>(P, ma, mw, q);
-      else e = launch_gemm<256, kEpiBiasGelu, false>(P, ma, mw, q);
+      if (fp8) e = launch_gemm<256, kEpiBiasGelu, true>(P, ma, mw, mo, ml, q);
+      else e = launch_gemm<256, kEpiBiasGelu, false>(P, ma, mw, mo, ml, q);
     }
   }
   int herr = 0;

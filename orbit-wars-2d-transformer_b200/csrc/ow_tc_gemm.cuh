@@ -14,6 +14,12 @@
 // Bias, LayerNorm gamma/beta and fp8 channel scales are staged in shared
 // memory once per CTA and read as broadcast float4.
 //
+// Epilogue I/O is TMA-only: each epilogue warp owns 32 x 128 B staging tiles
+// in the 128 B-swizzled layout (16 B chunk j of row r at slot j ^ (r & 7)),
+// which the row-per-thread TMEM side writes without bank conflicts; outputs
+// leave as asynchronous tiled TMA stores (bulk groups), and the LayerNorm
+// epilogue's residual rows arrive as double-buffered TMA loads.
+//
 // The number of valid rows is read from device memory (the packed token
 // count of the batch), so one launch shape serves every batch; tiles past the
 // valid rows are never scheduled.
@@ -21,6 +27,9 @@
 // Epilogues:
 //   kEpiBias       out = bf16(acc*s + bias)                        (QKV projection)
 //   kEpiBiasGelu   out = bf16(gelu(acc*s + bias))                  (FFN up-projection)
+// map_o is the output map (bf16, box 64 x 32) for the bias epilogues and the
+// f32 residual map (box 32 x 32) for the LayerNorm epilogue; map_l is the
+// LayerNorm output map (box 128 B x 32 rows of its dtype).
 //   kEpiResidLn    x   = x + acc*s + bias in place (fp32 residual stream),
 //                  and the LayerNorm of that row (BLOCK_N == d, the whole
 //                  row is in this tile) -> ln_out as bf16 (next GEMM's A),
@@ -54,8 +63,7 @@ struct TcGemmParams {
   int* err;
 };
 
-constexpr int kParamFloats = 4096;  // staged epilogue vectors (bias + scales, or bias/g/b/scales)
-constexpr int kSmemLimit = 232448;   // dynamic shared memory per CTA on sm_100
+constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 
 template <int EPI>
 struct EpiWarps {
@@ -80,9 +88,14 @@ struct TcGemmShape {
                                    : kTmemColsNeeded <= 64 ? 64
                                    : kTmemColsNeeded <= 128 ? 128
                                    : kTmemColsNeeded <= 256 ? 256 : 512;
-  static constexpr int kBarrierBytes = 256;
+  static constexpr int kBarrierBytes = 512;
+  static constexpr int kParamFloats = EPI == kEpiResidLn ? 2048 : 4096;  // staged bias/scale/g/b vectors
   static constexpr int kParamBytes = kParamFloats * 4;
-  static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * 4096;  // per-warp 32 x 128 B transpose tile
+  // staging tiles per epilogue warp: bias/GELU -> 2 output tiles; LayerNorm ->
+  // 2 residual tiles (loads, then x stores) + 2 (or 1 at d=512) LN-output tiles
+  static constexpr int kLnTiles = BLOCK_N <= 384 ? 2 : 1;
+  static constexpr int kTilesPerWarp = EPI == kEpiResidLn ? 2 + kLnTiles : 2;
+  static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * kTilesPerWarp * 4096;
   static constexpr int kFixedBytes = kBarrierBytes + kParamBytes + kXposeBytes + 1024;  // + align slack
   static constexpr int kStagesFit = (kSmemLimit - kFixedBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
@@ -92,34 +105,18 @@ struct TcGemmShape {
   static_assert(kBoxRows <= 256, "TMA box rows <= 256");
   static_assert(kTmemColsNeeded <= 512, "TMEM has 512 columns");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory per CTA");
+  static_assert(kStageBytes % 1024 == 0 && kXposeBytes % 1024 == 0, "swizzled tiles stay 1024 B aligned");
 };
 
-// Warp-cooperative transpose through a 32 x 128 B shared tile. 16-byte chunk
-// j of row r lives at chunk slot j ^ (r & 7), so both the row-per-thread side
-// (thread r touches row r) and the row-per-8-lanes side (8 lanes cover one
-// 128 B row) are bank-conflict free.
+// 16 B chunk j of row r of a 32 x 128 B staging tile (128 B swizzle).
 __device__ __forceinline__ uint4* xpose_slot(uint8_t* tile, int row, int chunk) {
   return reinterpret_cast<uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-// rows [0, rows) of the tile -> global rows of `row_bytes` bytes (chunks_per_row 16 B chunks each)
-__device__ __forceinline__ void xpose_store(uint8_t* tile, uint8_t* gbase, size_t gstride, int rows, int chunks_per_row,
-                                            int lane) {
-  const int rows_per_iter = 32 / chunks_per_row;
-  const int j = lane % chunks_per_row;
-  for (int r = lane / chunks_per_row; r < rows; r += rows_per_iter)
-    *reinterpret_cast<uint4*>(gbase + r * gstride + j * 16) = *xpose_slot(tile, r, j);
-}
-__device__ __forceinline__ void xpose_load(uint8_t* tile, const uint8_t* gbase, size_t gstride, int rows,
-                                           int chunks_per_row, int lane) {
-  const int rows_per_iter = 32 / chunks_per_row;
-  const int j = lane % chunks_per_row;
-  for (int r = lane / chunks_per_row; r < rows; r += rows_per_iter)
-    *xpose_slot(tile, r, j) = *reinterpret_cast<const uint4*>(gbase + r * gstride + j * 16);
 }
 
 template <int BLOCK_N, int EPI, bool FP8>
 __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                   const __grid_constant__ CUtensorMap map_o, const __grid_constant__ CUtensorMap map_l,
                    const TcGemmParams p) {
   using S = TcGemmShape<BLOCK_N, EPI>;
   constexpr int kEpiWarps = EpiWarps<EPI>::kCount;
@@ -127,14 +124,17 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + S::kStages * S::kATileBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+  // layout: [operand stages][staging tiles (1024 B aligned: the swizzle phase
+  // is taken from address bits)][barriers][epilogue vectors]
+  uint8_t* s_xpose = smem + S::kStages * S::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_xpose + S::kXposeBytes);
   uint64_t* empty = full + S::kStages;
   uint64_t* tfull = empty + S::kStages;
   uint64_t* tempty = tfull + S::kAcc;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + S::kAcc);
+  uint64_t* xbar = tempty + S::kAcc;  // LayerNorm residual loads: 2 per epilogue warp
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xbar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* s_par = reinterpret_cast<float*>(smem + S::kStages * S::kStageBytes + S::kBarrierBytes);
-  uint8_t* s_xpose = smem + S::kStages * S::kStageBytes + S::kBarrierBytes + S::kParamBytes;
+  float* s_par = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + S::kBarrierBytes);
   // staged vectors: s_bias[n], then (fp8) s_bscale[n], then (LN) s_g[n], s_b[n]
   float* s_bias = s_par;
   float* s_bscale = s_par + p.n;
@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], kEpiWarps);
     }
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&xbar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -179,6 +180,8 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     if (lane == 0 && num_tiles > 0) {
       tma_prefetch_desc(&map_a);
       tma_prefetch_desc(&map_w);
+      tma_prefetch_desc(&map_o);
+      if (EPI == kEpiResidLn) tma_prefetch_desc(&map_l);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -251,21 +254,25 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2 .. 2+kEpiWarps-1. Thread `lane` of a warp owns tile row
-    // quad*32 + lane on the TMEM side; global traffic goes through the warp's
-    // transpose tile so each warp instruction moves whole 128 B rows.
+    // Epilogue warps 2 .. 2+kEpiWarps-1. Thread `lane` owns tile row
+    // quad*32 + lane on the TMEM side; global traffic is TMA through the
+    // warp's staging tiles.
+    const int ew = warp - 2;
     const int quad = warp & 3;
-    uint8_t* xt = s_xpose + (warp - 2) * 4096;
+    uint8_t* tiles = s_xpose + ew * S::kTilesPerWarp * 4096;
     constexpr int kCols = EPI == kEpiResidLn ? BLOCK_N : BLOCK_N * 4 / kEpiWarps;  // columns this warp drains
-    const int col0 = EPI == kEpiResidLn ? 0 : ((warp - 2) / 4) * kCols;
+    const int col0 = EPI == kEpiResidLn ? 0 : (ew / 4) * kCols;
+    uint64_t* my_xbar = xbar + 2 * ew;
+    uint32_t xphase[2] = {0u, 0u};
     int acc = 0;
     uint32_t acc_phase = 0;
+    int out_k = 0;  // output tiles used so far (alternates the double buffer)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
       const int row_base = (tile / n_tiles) * S::kBlockM + quad * 32;  // first row of this warp's 32
       const int m = row_base + lane;
-      const int rows = min(32, m_valid - row_base);                    // valid rows of the 32 (may be <= 0)
+      const bool any = row_base < m_valid;
       const int n0 = (tile % n_tiles) * BLOCK_N;
       const bool live = m < m_valid;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BLOCK_N);
@@ -274,10 +281,11 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       if (EPI == kEpiBias || EPI == kEpiBiasGelu) {
         static_assert(kCols % 64 == 0, "64-column epilogue chunks");
 #pragma unroll 1
-        for (int c = col0; c < col0 + kCols; c += 64) {
+        for (int c = col0; c < col0 + kCols && any; c += 64) {
           uint32_t r[64];
           tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           tmem_ld32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          if (lane == 0) bulk_wait_read<1>();  // the store that last used this tile has read it
           tmem_ld_wait();
           uint32_t packed[32];
 #pragma unroll
@@ -305,46 +313,66 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
             packed[i / 2] = pack_bf16x2(v0, v1);
             packed[i / 2 + 1] = pack_bf16x2(v2, v3);
           }
+          uint8_t* ot = tiles + (out_k & 1) * 4096;
+          __syncwarp();
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            *xpose_slot(xt, lane, q) = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            *xpose_slot(ot, lane, q) = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          fence_proxy_async_smem();
           __syncwarp();
-          if (rows > 0)
-            xpose_store(xt, reinterpret_cast<uint8_t*>(p.out + static_cast<size_t>(row_base) * p.ld_out + n0 + c),
-                        static_cast<size_t>(p.ld_out) * 2, rows, 8, lane);
-          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_o, ot, n0 + c, row_base);
+            bulk_commit();
+          }
+          ++out_k;
         }
-      } else {
+      } else if (any) {
         // Residual add + LayerNorm over the full row (BLOCK_N == n == d): two
         // passes over TMEM. Pass 1 forms v = x + acc*s + bias, writes it back to
         // TMEM and accumulates shifted statistics (shift = the row's first v,
         // which keeps E[(v-k)^2] - E[v-k]^2 well conditioned); pass 2 writes x
         // and the normalised row.
-        uint8_t* xg = reinterpret_cast<uint8_t*>(p.resid + static_cast<size_t>(row_base > 0 ? row_base : 0) * BLOCK_N);
-        const size_t xstride = static_cast<size_t>(BLOCK_N) * 4;
+        constexpr int kChunks = BLOCK_N / 32;
+        uint8_t* xt[2] = {tiles, tiles + 4096};
+        uint8_t* lt[2] = {tiles + 8192, tiles + 8192 + (S::kLnTiles - 1) * 4096};
+        if (lane == 0) {
+          bulk_wait_read<0>();  // both residual tiles are free (earlier x stores have read them)
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            mbar_arrive_expect_tx(&my_xbar[b], 4096);
+            tma_load_2d(xt[b], &map_o, &my_xbar[b], b * 32, row_base);
+          }
+        }
+        __syncwarp();
         float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
+        bool ok = true;
 #pragma unroll 1
-        for (int c = 0; c < BLOCK_N; c += 32) {
-          if (rows > 0) xpose_load(xt, xg + c * 4, xstride, rows, 8, lane);  // 32 rows x 32 f32 of x
+        for (int c = 0; c < kChunks; ++c) {
           uint32_t r[32];
-          tmem_ld32(tbase + c, r);
+          tmem_ld32(tbase + c * 32, r);
+          const int b = c & 1;
+          if (!mbar_wait(&my_xbar[b], xphase[b], abort_flag, p.err)) ok = false;
+          xphase[b] ^= 1u;
           tmem_ld_wait();
-          __syncwarp();
           float xv[32];
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const float4 t4 = live ? *reinterpret_cast<const float4*>(xpose_slot(xt, lane, q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 t4 = *reinterpret_cast<const float4*>(xpose_slot(xt[b], lane, q));
             xv[4 * q] = t4.x;
             xv[4 * q + 1] = t4.y;
             xv[4 * q + 2] = t4.z;
             xv[4 * q + 3] = t4.w;
           }
           __syncwarp();
+          if (lane == 0 && c + 2 < kChunks && ok) {
+            mbar_arrive_expect_tx(&my_xbar[b], 4096);
+            tma_load_2d(xt[b], &map_o, &my_xbar[b], (c + 2) * 32, row_base);
+          }
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
-            const float4 bv = *reinterpret_cast<const float4*>(s_bias + c + i);
+            const float4 bv = *reinterpret_cast<const float4*>(s_bias + c * 32 + i);
             float4 sv = make_float4(1.f, 1.f, 1.f, 1.f);
-            if (FP8) sv = *reinterpret_cast<const float4*>(s_bscale + c + i);
+            if (FP8) sv = *reinterpret_cast<const float4*>(s_bscale + c * 32 + i);
             const float b4[4] = {bv.x, bv.y, bv.z, bv.w};
             const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
@@ -359,7 +387,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
               r[i + j] = __float_as_uint(v);
             }
           }
-          tmem_st32(tbase + c, r);
+          tmem_st32(tbase + c * 32, r);
         }
         tmem_st_wait();
         const float md = s1 * (1.0f / BLOCK_N);
@@ -384,57 +412,73 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           inv_scale = 1.0f / scale;
           if (live) p.ln_scale[m] = scale;
         }
+        // LN output: 32 columns are 32*elt bytes of a 128 B box row
         const int ln_elt = p.ln_mode == kLnF32 ? 4 : (p.ln_mode == kLnE4m3 ? 1 : 2);
-        uint8_t* lg = reinterpret_cast<uint8_t*>(p.ln_out) + static_cast<size_t>(row_base > 0 ? row_base : 0) * BLOCK_N * ln_elt;
-        const size_t lstride = static_cast<size_t>(BLOCK_N) * ln_elt;
+        const int per_box = 4 / ln_elt;  // 32-column pieces per 128 B box row
+        int lbox = 0;
 #pragma unroll 1
-        for (int c = 0; c < BLOCK_N; c += 32) {
+        for (int c = 0; c < kChunks; ++c) {
           uint32_t r[32];
-          tmem_ld32(tbase + c, r);
+          tmem_ld32(tbase + c * 32, r);
+          if (lane == 0) bulk_wait_read<1>();
           tmem_ld_wait();
-          // x (f32): 32 columns = one 128 B row segment per thread
+          __syncwarp();
+          // x (f32): one 128 B row piece per thread
+          uint8_t* xo = xt[c & 1];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) *xpose_slot(xt, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          for (int q = 0; q < 8; ++q) *xpose_slot(xo, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          fence_proxy_async_smem();
           __syncwarp();
-          if (rows > 0) xpose_store(xt, xg + c * 4, xstride, rows, 8, lane);
-          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_o, xo, c * 32, row_base);
+            bulk_commit();
+          }
           float y[32];
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
-            const float4 gv = *reinterpret_cast<const float4*>(s_g + c + i);
-            const float4 bv = *reinterpret_cast<const float4*>(s_b + c + i);
+            const float4 gv = *reinterpret_cast<const float4*>(s_g + c * 32 + i);
+            const float4 bv = *reinterpret_cast<const float4*>(s_b + c * 32 + i);
             y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
             y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
             y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
             y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
           }
-          int chunks;
+          const int piece = c % per_box;
+          uint8_t* lo = lt[lbox & (S::kLnTiles - 1)];
+          if (piece == 0 && S::kLnTiles == 1) {
+            if (lane == 0) bulk_wait_read<0>();  // single LN tile: its previous store must have read it
+            __syncwarp();
+          }
           if (p.ln_mode == kLnE4m3) {
             uint32_t q8[8];
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
               q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
                                       y[i + 3] * inv_scale);
-            *xpose_slot(xt, lane, 0) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
-            *xpose_slot(xt, lane, 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
-            chunks = 2;
+            *xpose_slot(lo, lane, 2 * piece) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+            *xpose_slot(lo, lane, 2 * piece + 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
           } else if (p.ln_mode == kLnF32) {
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              *xpose_slot(xt, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
+              *xpose_slot(lo, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
                                                     __float_as_uint(y[4 * q + 2]), __float_as_uint(y[4 * q + 3]));
-            chunks = 8;
           } else {
             uint32_t yo[16];
 #pragma unroll
             for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) *xpose_slot(xt, lane, q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
-            chunks = 4;
+            for (int q = 0; q < 4; ++q)
+              *xpose_slot(lo, lane, 4 * piece + q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
           }
-          __syncwarp();
-          if (rows > 0) xpose_store(xt, lg + c * ln_elt, lstride, rows, chunks, lane);
-          __syncwarp();
+          if (piece == per_box - 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&map_l, lo, (c + 1 - per_box) * 32, row_base);
+              bulk_commit();
+            }
+            ++lbox;
+          }
         }
       }
       tc_fence_before();
@@ -445,6 +489,8 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_all();  // every TMA store of this warp has completed
+    __syncwarp();
   }
 
   __syncthreads();
