@@ -194,6 +194,7 @@ struct OwPolicy {
   std::vector<LayerW> lw;
   float *we = nullptr, *be = nullptr, *lnfg = nullptr, *lnfb = nullptr, *wp = nullptr, *bp = nullptr,
         *wv = nullptr, *bv = nullptr;
+  __nv_bfloat16* we16 = nullptr;  // W_e as bf16 [d][32] (features zero-padded) for the tensor-core embedding
 
   // workspace
   uint8_t* ws = nullptr;
@@ -201,6 +202,8 @@ struct OwPolicy {
   float* feats = nullptr;
   void *logits = nullptr, *value = nullptr;
   int* actions = nullptr;
+  int* row_slot = nullptr;  // packed row -> b*N + j
+  float* sval = nullptr;    // packed row -> y.W_v (value head, before the per-state mean)
   void *x = nullptr, *ln = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr;
   uint8_t *ln8 = nullptr, *attn8 = nullptr, *h8 = nullptr;
   float *ln_scale = nullptr, *attn_scale = nullptr, *h_scale = nullptr;
@@ -296,16 +299,22 @@ cudaError_t launch_embed(const OwPolicy& P, int batch) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
                                      static_cast<float*>(P.x), P.ln, nullptr);
-  } else if (c.precision == OW_PRECISION_BF16) {
-    auto k = embed_ln_kernel<DPL, 1>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
-                                     static_cast<float*>(P.x), P.ln, nullptr);
   } else {
-    auto k = embed_ln_kernel<DPL, 2>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<grid, 256, smem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we, P.be, g, b,
-                                     static_cast<float*>(P.x), P.ln8, P.ln_scale);
+    constexpr int D = DPL * 32;
+    const size_t esmem = static_cast<size_t>(D) * 40 * 2 + 4 * 16 * 40 * 2 + 3 * D * sizeof(float);
+    const int eg = static_cast<int>(std::max<size_t>(1, std::min<size_t>((P.cap_rows + 63) / 64,
+                                                                          static_cast<size_t>(P.num_sms) * 4)));
+    if (c.precision == OW_PRECISION_BF16) {
+      auto k = embed_mma_kernel<D, 1>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
+      k<<<eg, 128, esmem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we16, P.be, g, b,
+                                      static_cast<float*>(P.x), P.ln, nullptr, P.row_slot);
+    } else {
+      auto k = embed_mma_kernel<D, 2>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
+      k<<<eg, 128, esmem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we16, P.be, g, b,
+                                      static_cast<float*>(P.x), P.ln8, P.ln_scale, P.row_slot);
+    }
   }
   return cudaGetLastError();
 }
@@ -331,9 +340,49 @@ void heads_dtype(const OwPolicy& P, int batch, uint64_t seed, void* logits, void
   else heads_launch<DPL, PP, false, false>(P, batch, seed, logits, value, actions);
 }
 
+template <int D, int NTILE, bool LB>
+void heads_mma_launch(const OwPolicy& P, int batch, uint64_t seed, void* logits, int* actions) {
+  const auto& c = P.cfg;
+  const size_t smem = static_cast<size_t>(NTILE) * 8 * (D + 16) * sizeof(float);
+  cudaFuncSetAttribute(heads_mma_kernel<D, NTILE, LB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((P.cap_rows + 63) / 64,
+                                                                         static_cast<size_t>(P.num_sms) * 4)));
+  heads_mma_kernel<D, NTILE, LB><<<grid, 128, smem, P.stream>>>(static_cast<const float*>(P.y), P.offsets, batch,
+                                                                c.n_entities, c.actions, P.row_slot, P.wp, P.bp,
+                                                                P.wv, c.sample_actions, seed, logits, actions, P.sval);
+}
+
+template <int D>
+cudaError_t launch_heads_tc(const OwPolicy& P, int batch, uint64_t seed, void* logits, int* actions) {
+  const int a = P.cfg.actions;
+  const bool lb = P.cfg.logits_dtype == OW_DTYPE_BF16;
+  // 8-column tiles covering the P logits plus the value column
+  if (a < 8) lb ? heads_mma_launch<D, 1, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 1, false>(P, batch, seed, logits, actions);
+  else if (a < 16) lb ? heads_mma_launch<D, 2, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 2, false>(P, batch, seed, logits, actions);
+  else if (a < 24) lb ? heads_mma_launch<D, 3, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 3, false>(P, batch, seed, logits, actions);
+  else if (a < 32) lb ? heads_mma_launch<D, 4, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 4, false>(P, batch, seed, logits, actions);
+  else lb ? heads_mma_launch<D, 5, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 5, false>(P, batch, seed, logits, actions);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(const OwPolicy& P, int batch, void* logits, void* value, int* actions) {
+  const auto& c = P.cfg;
+  const int threads = (c.n_entities + 31) / 32 * 32;
+  const bool lb = c.logits_dtype == OW_DTYPE_BF16, vb = c.value_dtype == OW_DTYPE_BF16;
+#define OW_FIN(LB, VB) \
+  state_finalize_kernel<LB, VB><<<batch, threads, 0, P.stream>>>(P.offsets, c.n_entities, c.actions, P.sval, P.bv, logits, value, actions)
+  if (lb && vb) OW_FIN(true, true);
+  else if (lb) OW_FIN(true, false);
+  else if (vb) OW_FIN(false, true);
+  else OW_FIN(false, false);
+#undef OW_FIN
+  return cudaGetLastError();
+}
+
 template <int DPL>
 cudaError_t launch_heads(const OwPolicy& P, int batch, uint64_t seed, void* logits, void* value, int* actions) {
-  // the final LayerNorm output is f32 on every path
+  // SIMT heads of the f32 path (f32 dot products for the 1e-4 tolerance)
   const int a = P.cfg.actions;
   if (a <= 8) heads_dtype<DPL, 8>(P, batch, seed, logits, value, actions);
   else if (a <= 16) heads_dtype<DPL, 16>(P, batch, seed, logits, value, actions);
@@ -355,6 +404,15 @@ cudaError_t dispatch_embed(const OwPolicy& P, int batch) {
     case 8: return launch_embed<8>(P, batch);
     case 12: return launch_embed<12>(P, batch);
     case 16: return launch_embed<16>(P, batch);
+    default: return cudaErrorInvalidValue;
+  }
+}
+cudaError_t dispatch_heads_tc(const OwPolicy& P, int batch, uint64_t seed, void* logits, int* actions) {
+  switch (P.cfg.d_model) {
+    case 128: return launch_heads_tc<128>(P, batch, seed, logits, actions);
+    case 256: return launch_heads_tc<256>(P, batch, seed, logits, actions);
+    case 384: return launch_heads_tc<384>(P, batch, seed, logits, actions);
+    case 512: return launch_heads_tc<512>(P, batch, seed, logits, actions);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -391,10 +449,31 @@ cudaError_t launch_attention(const OwPolicy& P, int batch) {
     const auto* q = static_cast<const __nv_bfloat16*>(P.qkv);
     auto* o = static_cast<__nv_bfloat16*>(P.attn);
     const float sl2 = scale * 1.4426950408889634f;
-    if (c.n_entities <= 32) attention_bf16_kernel<32><<<grid, 64, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
-    else if (c.n_entities <= 64) attention_bf16_kernel<64><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
-    else if (c.n_entities <= 96) attention_bf16_kernel<96><<<grid, 192, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
-    else attention_bf16_kernel<128><<<grid, 256, 0, P.stream>>>(q, o, P.offsets, c.d_model, sl2);
+    const int nmax = c.n_entities <= 32 ? 32 : (c.n_entities <= 64 ? 64 : (c.n_entities <= 96 ? 96 : 128));
+    // largest head group (8, 4, 2, 1) dividing the head count whose staged Q/K/V fit ~110 KB
+    int hg = 8;
+    while (hg > 1 && (c.heads % hg != 0 || 3 * nmax * (hg * 32 + 8) * 2 > 112 * 1024)) hg /= 2;
+    const dim3 g2(batch, c.heads / hg);
+    const size_t smem = static_cast<size_t>(3) * nmax * (hg * 32 + 8) * 2;
+#define OW_ATTN(NM, HGV)                                                                                   \
+  do {                                                                                                     \
+    cudaFuncSetAttribute(attention_bf16_kernel<NM, HGV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                         static_cast<int>(smem));                                                          \
+    attention_bf16_kernel<NM, HGV><<<g2, 256, smem, P.stream>>>(q, o, P.offsets, c.d_model, sl2);          \
+  } while (0)
+#define OW_ATTN_HG(NM)              \
+  do {                              \
+    if (hg == 8) OW_ATTN(NM, 8);    \
+    else if (hg == 4) OW_ATTN(NM, 4); \
+    else if (hg == 2) OW_ATTN(NM, 2); \
+    else OW_ATTN(NM, 1);            \
+  } while (0)
+    if (nmax == 32) OW_ATTN_HG(32);
+    else if (nmax == 64) OW_ATTN_HG(64);
+    else if (nmax == 96) OW_ATTN_HG(96);
+    else OW_ATTN_HG(128);
+#undef OW_ATTN_HG
+#undef OW_ATTN
   }
   return cudaGetLastError();
 }
@@ -526,7 +605,12 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
               launch_gemm_resid_ln(P, P.m_h, W.m2, P.e_x, last ? P.e_y : P.e_ln, w, fp8));
     }
   }
-  OW_STEP("heads", dispatch_heads(P, batch, seed, logits, value, actions));
+  if (c.precision == OW_PRECISION_F32) {
+    OW_STEP("heads", dispatch_heads(P, batch, seed, logits, value, actions));
+  } else {
+    OW_STEP("heads", dispatch_heads_tc(P, batch, seed, logits, actions));
+    OW_STEP("state_finalize", launch_finalize(P, batch, logits, value, actions));
+  }
   if (P.prof_on && P.prof_used < P.prof_events.size()) {
     cudaEventRecord(P.prof_events[P.prof_used], P.stream);
     P.prof_names[P.prof_used++] = nullptr;  // end of this forward
@@ -585,6 +669,13 @@ OwStatus upload_weights(OwPolicy& P, const float* w) {
     return m;
   };
   const size_t we = put_f32(L.we, d * c.features), be = put_f32(L.be, d);
+  const size_t we16 = reserve(d * 32 * 2);
+  {
+    uint16_t* dst = reinterpret_cast<uint16_t*>(img.data() + we16);
+    for (size_t r = 0; r < d; ++r)
+      for (size_t f = 0; f < 32; ++f)
+        dst[r * 32 + f] = f < static_cast<size_t>(c.features) ? f32_to_bf16_bits(w[L.we + r * c.features + f]) : 0;
+  }
   struct LayerAt {
     size_t ln1g, ln1b, bqkv, bo, ln2g, ln2b, b1, b2;
     Mat qkv, o, w1, w2;
@@ -623,6 +714,7 @@ OwStatus upload_weights(OwPolicy& P, const float* w) {
   auto F = [base](size_t at) { return reinterpret_cast<float*>(base + at); };
   P.we = F(we);
   P.be = F(be);
+  P.we16 = reinterpret_cast<__nv_bfloat16*>(base + we16);
   P.lnfg = F(lnfg);
   P.lnfb = F(lnfb);
   P.wp = F(wp);
@@ -677,6 +769,7 @@ OwStatus alloc_workspace(OwPolicy& P) {
   const size_t o_counts = take(B * 4), o_offsets = take((B + 1) * 4), o_err = take(16);
   const size_t o_feats = take(rows * c.features * 4);
   const size_t o_logits = take(rows * c.actions * 4), o_value = take(B * 4), o_actions = take(rows * 4);
+  const size_t o_slot = take(rows * 4), o_sval = take(rows * 4);
   const size_t o_x = take(rows * d * 4), o_ln = take(rows * d * act), o_qkv = take(rows * 3 * d * act);
   const size_t o_y = c.precision == OW_PRECISION_F32 ? o_ln : take(rows * d * 4);
   const size_t o_attn = take(rows * d * act), o_h = take(rows * f * act);
@@ -701,6 +794,8 @@ OwStatus alloc_workspace(OwPolicy& P) {
   P.logits = b + o_logits;
   P.value = b + o_value;
   P.actions = reinterpret_cast<int*>(b + o_actions);
+  P.row_slot = reinterpret_cast<int*>(b + o_slot);
+  P.sval = reinterpret_cast<float*>(b + o_sval);
   P.x = b + o_x;
   P.ln = b + o_ln;
   P.y = b + o_y;
@@ -1042,7 +1137,7 @@ OwStatus ow_policy_launches_per_forward(const OwPolicy* policy, int32_t* launche
   if (policy == nullptr || launches == nullptr) return st_bad("null argument");
   const auto& c = policy->cfg;
   int per_layer = c.precision == OW_PRECISION_F32 ? 7 : (c.precision == OW_PRECISION_FP8 ? 7 : 5);
-  *launches = 3 + per_layer * c.layers;  // scan + embed + blocks + heads
+  *launches = 3 + per_layer * c.layers + (c.precision == OW_PRECISION_F32 ? 0 : 1);  // scan, embed, blocks, heads(+finalize)
   return st_ok();
 }
 
