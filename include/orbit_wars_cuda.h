@@ -129,6 +129,29 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
     OrbitWarsCudaTrue2DShape shape,
     OrbitWarsCudaTrue2DTrainingConfig training_config);
 
+/* Allocation-free forward -- no counterpart in the reference ABI.
+ * For callers that cannot allocate device memory: an engine whose device
+ * memory is all reserved by its own pool or budget (a cudaMalloc would fail or
+ * fragment it), or a self-play loop that must not pay the implicit device-wide
+ * synchronisation of cudaMalloc/cudaFree between turns. Same math as
+ * orbit_wars_cuda_true2d_forward for one model, but input_rows
+ * (games x rows x 7), weights (the reference layout) and output_rows
+ * (games x rows x 24) are DEVICE pointers, the call is enqueued on `stream`
+ * (NULL: the legacy default stream) and returns without waiting.
+ * Scratch is a fixed 1 MiB device array inside the library, held by every GPU
+ * that loads it until exit: game_count * row_count^2 must be <= 262,080
+ * (63 requests at 64 rows), else BAD_ARGUMENT. The first call on a device
+ * resolves the array's device address; make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller. */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(
+    const float* input_rows,
+    const float* weights,
+    float* output_rows,
+    size_t game_count,
+    OrbitWarsCudaTrue2DShape shape,
+    void* stream);
+
 #ifdef __cplusplus
 }
 #endif

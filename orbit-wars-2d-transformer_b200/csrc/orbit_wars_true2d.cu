@@ -118,11 +118,21 @@ T2Dev dev_layout(const T2Layout& L) {
 
 __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-// One gated per-cell matrix layer, true2d_model.rs:419-461.
+// One gated per-cell matrix layer, true2d_model.rs:419-461. VEC: the 12
+// weights are 16-byte aligned (padded device layout) and read as three float4;
+// otherwise (the reference's own layout) as scalars.
+template <bool VEC>
 __device__ __forceinline__ float matrix_cell(float v, const float* __restrict__ w12) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(w12));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(w12) + 1);
-  const float4 c = __ldg(reinterpret_cast<const float4*>(w12) + 2);
+  float4 a, b, c;
+  if (VEC) {
+    a = __ldg(reinterpret_cast<const float4*>(w12));
+    b = __ldg(reinterpret_cast<const float4*>(w12) + 1);
+    c = __ldg(reinterpret_cast<const float4*>(w12) + 2);
+  } else {
+    a = make_float4(__ldg(w12), __ldg(w12 + 1), __ldg(w12 + 2), __ldg(w12 + 3));
+    b = make_float4(__ldg(w12 + 4), __ldg(w12 + 5), __ldg(w12 + 6), __ldg(w12 + 7));
+    c = make_float4(__ldg(w12 + 8), __ldg(w12 + 9), __ldg(w12 + 10), __ldg(w12 + 11));
+  }
   // a = (w0,w1,w2,w3) b = (w4,w5,w6,w7) c = (w8,w9,w10,w11)
   const float ha = tanhf(fmaf(v, a.z, a.w));
   const float hb = tanhf(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
@@ -143,6 +153,7 @@ __device__ __forceinline__ const float* model_of(const float* __restrict__ all_w
 }
 
 // 1. expand + matrix layers [0, mid)
+template <bool VEC>
 __global__ void __launch_bounds__(256) t2_expand_pre(const float* __restrict__ x, const size_t* __restrict__ idx,
                                                      const float* __restrict__ all_w, int models, T2Dev L,
                                                      float* __restrict__ m, int* err) {
@@ -163,7 +174,7 @@ __global__ void __launch_bounds__(256) t2_expand_pre(const float* __restrict__ x
   v = tanhf(v);
   const float* mw = w + L.matrix + static_cast<long long>(cell) * kCellWeights;
   const long long per_layer = static_cast<long long>(L.cells) * kCellWeights;
-  for (int l = 0; l < L.mid; ++l) v = matrix_cell(v, mw + l * per_layer);
+  for (int l = 0; l < L.mid; ++l) v = matrix_cell<VEC>(v, mw + l * per_layer);
   m[static_cast<long long>(r) * L.cells + cell] = v;
 }
 
@@ -259,6 +270,7 @@ __global__ void __launch_bounds__(kAttnThreads) t2_attention(const size_t* __res
 // 3. matrix layers [mid, layers) + collapse; CTA = 4 rows of one request.
 constexpr int kRowsPerCta = 4;
 
+template <bool VEC>
 __global__ void __launch_bounds__(512) t2_post_collapse(const size_t* __restrict__ idx, const float* __restrict__ all_w,
                                                         int models, T2Dev L, const float* __restrict__ m,
                                                         float* __restrict__ out, int* err) {
@@ -275,7 +287,7 @@ __global__ void __launch_bounds__(512) t2_post_collapse(const size_t* __restrict
     const int cell = row * L.rows + t;
     float v = m[static_cast<long long>(r) * L.cells + cell];
     const float* mw = w + L.matrix + static_cast<long long>(cell) * kCellWeights;
-    for (int l = L.mid; l < L.layers; ++l) v = matrix_cell(v, mw + l * per_layer);
+    for (int l = L.mid; l < L.layers; ++l) v = matrix_cell<VEC>(v, mw + l * per_layer);
     s_m[lr][t] = v;
   }
   __syncthreads();
@@ -403,6 +415,48 @@ __global__ void copy_kernel(const float4* __restrict__ in, float4* __restrict__ 
   if (blockIdx.x == 0 && threadIdx.x < tail) out_tail[threadIdx.x] = in_tail[threadIdx.x];
 }
 
+// ---------------------------------------------------------------- allocation-free forward
+// Scratch of orbit_wars_cuda_true2d_forward_noalloc: a fixed device array
+// every GPU that loads this library holds until exit (1 MiB). The first 256
+// bytes hold the error word; the rest holds the per-request cell matrices
+// (game_count * rows^2 floats at most kNoAllocCells).
+constexpr size_t kNoAllocFloats = size_t(1) << 18;
+constexpr size_t kNoAllocHeaderFloats = 64;
+constexpr size_t kNoAllocCells = kNoAllocFloats - kNoAllocHeaderFloats;  // 262,080 cells
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
+
+// Device address of g_noalloc_scratch for `dev` (must be the current device).
+// Resolved once per device with cudaGetSymbolAddress: in host code the
+// array's name is only a host-side stand-in, never a device address.
+cudaError_t noalloc_scratch_address(int dev, float** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *out = static_cast<float*>(addr[dev]);
+  return cudaSuccess;
+}
+
+// The reference's weight layout on the device, unpadded (scalar weight loads).
+T2Dev ref_layout_dev(const T2Layout& L) {
+  T2Dev d{};
+  d.rows = static_cast<int>(L.rows);
+  d.cells = static_cast<int>(L.cells);
+  d.layers = static_cast<int>(L.layers);
+  d.heads = static_cast<int>(L.heads);
+  d.mid = static_cast<int>(L.layers / 2);
+  d.pair = L.pair; d.src_emb = L.src_emb; d.tgt_emb = L.tgt_emb; d.pair_emb = L.pair_emb; d.bias = L.bias;
+  d.matrix = L.matrix; d.attn = L.attn; d.tbias = L.tbias; d.sbias = L.sbias; d.scalars = L.scalars;
+  d.total = static_cast<long long>(L.total);
+  return d;
+}
+
 // ---------------------------------------------------------------- process-global workspace
 struct Workspace {
   std::mutex mu;
@@ -500,7 +554,7 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   }
   const int models = static_cast<int>(W.models);
   const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n));
-  t2_expand_pre<<<g1, 256, 0, W.stream>>>(W.in, didx, W.weights, models, D, W.m, W.err);
+  t2_expand_pre<true><<<g1, 256, 0, W.stream>>>(W.in, didx, W.weights, models, D, W.m, W.err);
   T2_TRY(cudaGetLastError());
   const size_t smem = L.cells * sizeof(float2);
   T2_TRY(cudaFuncSetAttribute(t2_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -508,7 +562,7 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   T2_TRY(cudaGetLastError());
   const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
-  t2_post_collapse<<<g3, threads3, 0, W.stream>>>(didx, W.weights, models, D, W.m, W.out, W.err);
+  t2_post_collapse<true><<<g3, threads3, 0, W.stream>>>(didx, W.weights, models, D, W.m, W.out, W.err);
   T2_TRY(cudaGetLastError());
   int herr = 0;
   T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
@@ -690,4 +744,41 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
             model_count, shape, training_config);
 }
 
+// Allocation-free variant of orbit_wars_cuda_true2d_forward (no counterpart in
+// the reference): device buffers in, device buffers out, scratch from the
+// fixed device array above. Enqueued on `stream`; no cudaMalloc/cudaFree.
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(const float* input_rows, const float* weights,
+                                                           float* output_rows, size_t game_count,
+                                                           OrbitWarsCudaTrue2DShape shape, void* stream) {
+  if (input_rows == nullptr || weights == nullptr || output_rows == nullptr || game_count == 0)
+    return bad("invalid true2d buffer");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
+  if (game_count > kNoAllocCells / L.cells)
+    return bad("game_count x row_count^2 exceeds the allocation-free scratch (262080 cells)");
+  int dev = 0;
+  T2_TRY(cudaGetDevice(&dev));
+  float* scratch = nullptr;
+  T2_TRY(noalloc_scratch_address(dev, &scratch));
+  int* err = reinterpret_cast<int*>(scratch);
+  float* m = scratch + kNoAllocHeaderFloats;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the array keeps the previous call's contents: clear the error word
+  T2_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+  const T2Dev D = ref_layout_dev(L);
+  const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(game_count));
+  t2_expand_pre<false><<<g1, 256, 0, s>>>(input_rows, nullptr, weights, 1, D, m, err);
+  T2_TRY(cudaGetLastError());
+  const size_t smem = L.cells * sizeof(float2);
+  if (smem > 48 * 1024)
+    T2_TRY(cudaFuncSetAttribute(t2_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  t2_attention<<<static_cast<unsigned>(game_count), kAttnThreads, smem, s>>>(nullptr, weights, 1, D, m, err);
+  T2_TRY(cudaGetLastError());
+  const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(game_count));
+  const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
+  t2_post_collapse<false><<<g3, threads3, 0, s>>>(nullptr, weights, 1, D, m, output_rows, err);
+  return from_cuda(cudaGetLastError());
+}
+
 }  // extern "C"
+

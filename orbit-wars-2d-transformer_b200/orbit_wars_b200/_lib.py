@@ -80,6 +80,7 @@ SIGNATURES = {
     "orbit_wars_cuda_true2d_forward_many": (Status, [P, P, P, P, SZ, SZ, True2DShapeC]),
     "orbit_wars_cuda_true2d_upload_population": (Status, [P, SZ, SZ, True2DShapeC]),
     "orbit_wars_cuda_true2d_forward_many_resident": (Status, [P, P, P, SZ, True2DShapeC]),
+    "orbit_wars_cuda_true2d_forward_noalloc": (Status, [P, P, P, SZ, True2DShapeC, P]),
     "orbit_wars_cuda_true2d_train_full_attention": (
         Status, [P, P, P, P, P, P, SZ, SZ, True2DShapeC, TrainingConfigC]),
 }
