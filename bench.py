@@ -48,6 +48,17 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 L2_FLUSH_BYTES = 256 << 20
 
 
+def ncu_traffic(config: int, kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu capture of this
+    config (profiles/ncu_traffic_c<config>.json), or None."""
+    p = REPO / "profiles" / f"ncu_traffic_c{config}.json"
+    if not p.exists():
+        return None, None
+    d = json.loads(p.read_text())
+    k = d.get("kernels", {}).get(kernel)
+    return (k["dram_bytes_per_launch"] if k else None), d.get("workload")
+
+
 def load_peaks() -> tuple[dict, str]:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -349,8 +360,10 @@ def run_ours(args, cfg) -> None:
                 peak *= 2.0
         else:
             peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        traffic, traffic_src = ncu_traffic(args.config, dom_name)
         roof = {"kernel": dom_name, "bound": k["bound"], "achieved": k["achieved"], "peak": peak, "unit": k["unit"],
-                "frac": round(k["achieved"] / peak, 4), "traffic": None,
+                "frac": round(k["achieved"] / peak, 4), "traffic": traffic,
+                "traffic_source": traffic_src,
                 "peak_source": peak_src + (" (fp8 peak = 2x measured bf16)" if cfg.precision == "fp8" else ""),
                 "work_per_launch": "2*M_valid*N*K FLOPs, M_valid = valid tokens of the batch"
                 if k["bound"] == "tensor" else "bytes read + written",
