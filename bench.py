@@ -234,17 +234,12 @@ def run_ours(args, cfg) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
-    # weights: rank 0 builds them, one NCCL broadcast to every rank
-    n_w = ow.weight_count(cfg)
-    wt = torch.empty(n_w, dtype=torch.float32, device=dev)
-    if rank == 0:
-        wt.copy_(torch.from_numpy(ow.make_weights(cfg, seed=args.seed)))
-    if world > 1:
-        dist.broadcast(wt, src=0)
-    weights = wt.cpu().numpy()
+    from orbit_wars_b200.shard import broadcast_weights, shard_inputs
 
-    # this rank's shard of states
-    feats, counts = ow.make_inputs(cfg, seed=args.seed + rank)
+    # weights: rank 0 builds them, one NCCL broadcast to every rank
+    weights = broadcast_weights(cfg, args.seed, rank, device=dev)
+    # this rank's shard of the global batch (world * B states)
+    feats, counts = shard_inputs(cfg, args.seed, rank)
     B = cfg.batch
     m_valid = int(counts.sum())
     sq_counts = int((counts.astype(np.int64) ** 2).sum())

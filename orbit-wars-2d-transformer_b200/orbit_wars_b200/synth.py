@@ -43,23 +43,24 @@ def normal(seed: int, tensor: int, idx) -> np.ndarray:
     return np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2)
 
 
-def counts_for(cfg: PolicyConfig, batch: int, seed: int = DEFAULT_SEED) -> np.ndarray:
-    u = u01(seed, TENSOR_COUNTS, np.arange(batch, dtype=np.uint64))
+def counts_for(cfg: PolicyConfig, batch: int, seed: int = DEFAULT_SEED, state_offset: int = 0) -> np.ndarray:
+    u = u01(seed, TENSOR_COUNTS, np.arange(state_offset, state_offset + batch, dtype=np.uint64))
     span = cfg.count_hi - cfg.count_lo + 1
     c = cfg.count_lo + np.floor(u * span).astype(np.int64)
     return np.minimum(c, cfg.count_hi).astype(np.int32)
 
 
 def make_inputs(cfg: PolicyConfig, batch: int | None = None, seed: int = DEFAULT_SEED,
-                counts: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
-    """features f32 [B, N, F] (padded entities are 0) and counts int32 [B]."""
+                counts: np.ndarray | None = None, state_offset: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """features f32 [B, N, F] (padded entities are 0) and counts int32 [B] of
+    global states state_offset .. state_offset+B-1 (a rank's shard of a larger batch)."""
     B = cfg.batch if batch is None else int(batch)
     N, F = cfg.n_entities, cfg.features
-    cnt = counts_for(cfg, B, seed) if counts is None else np.asarray(counts, dtype=np.int32)
+    cnt = counts_for(cfg, B, seed, state_offset) if counts is None else np.asarray(counts, dtype=np.int32)
     feats = np.zeros((B, N, F), dtype=np.float32)
     valid = np.arange(N)[None, :] < cnt[:, None]          # [B, N]
     b_idx, j_idx = np.nonzero(valid)
-    slot = (b_idx.astype(np.uint64) * np.uint64(N) + j_idx.astype(np.uint64))
+    slot = ((b_idx.astype(np.uint64) + np.uint64(state_offset)) * np.uint64(N) + j_idx.astype(np.uint64))
     chunk = 1 << 20
     for s in range(0, slot.size, chunk):
         sl = slot[s:s + chunk]
