@@ -232,6 +232,7 @@ def run_ours(args, cfg) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout (one JSON line)
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     from orbit_wars_b200.shard import broadcast_weights, shard_inputs

@@ -132,23 +132,35 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // Row-major 2-D map over [rows, inner] elements of `elt` bytes with a box of
-// (128 bytes of a row) x box_rows and the 128 B swizzle: the layout both the
-// UMMA operand descriptors and the epilogue staging tiles use.
+// box_bytes (128, 64 or 32 bytes of a row) x box_rows, in the swizzle of that
+// width: the layout the UMMA operand descriptors (128 B) and the epilogue
+// staging tiles (128/64/32 B) use.
 enum MapType { kMapBf16, kMapU8, kMapF32 };
-bool make_map_128b(CUtensorMap* map, const void* base, MapType t, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+bool make_map_box(CUtensorMap* map, const void* base, MapType t, uint64_t inner, uint64_t rows, uint32_t box_bytes,
+                  uint32_t box_rows) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr || base == nullptr) return false;
   const uint32_t elt = t == kMapF32 ? 4 : (t == kMapBf16 ? 2 : 1);
   const CUtensorMapDataType dt = t == kMapF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : (t == kMapBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8);
+  const CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : (box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
   cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {inner * elt};
-  cuuint32_t box[2] = {128 / elt, box_rows};
+  cuuint32_t box[2] = {box_bytes / elt, box_rows};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+bool make_map_128b(CUtensorMap* map, const void* base, MapType t, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  return make_map_box(map, base, t, inner, rows, 128, box_rows);
+}
+// LayerNorm-output map of the epilogue: 32 columns x 32 rows in the element
+// type's swizzle (f32 128 B, bf16 64 B, e4m3 32 B).
+bool make_ln_map(CUtensorMap* map, const void* base, MapType t, uint64_t inner, uint64_t rows) {
+  const uint32_t elt = t == kMapF32 ? 4 : (t == kMapBf16 ? 2 : 1);
+  return make_map_box(map, base, t, inner, rows, 32 * elt, 32);
 }
 // K-major GEMM operand map (bf16 or e4m3), box = 128 bytes x box_rows.
 bool make_kmajor_map(CUtensorMap* map, const void* base, bool e4m3, uint64_t inner, uint64_t rows, uint32_t box_rows) {
@@ -820,8 +832,8 @@ OwStatus alloc_workspace(OwPolicy& P) {
            make_kmajor_map(&P.m_h, P.h, false, f, rows, 128);
     ok = ok && make_map_128b(&P.e_qkv, P.qkv, kMapBf16, 3 * d, rows, 32) &&
          make_map_128b(&P.e_h, P.h, kMapBf16, f, rows, 32) && make_map_128b(&P.e_x, P.x, kMapF32, d, rows, 32) &&
-         make_map_128b(&P.e_y, P.y, kMapF32, d, rows, 32) &&
-         (e4 ? make_map_128b(&P.e_ln, P.ln8, kMapU8, d, rows, 32) : make_map_128b(&P.e_ln, P.ln, kMapBf16, d, rows, 32));
+         make_ln_map(&P.e_y, P.y, kMapF32, d, rows) &&
+         (e4 ? make_ln_map(&P.e_ln, P.ln8, kMapU8, d, rows) : make_ln_map(&P.e_ln, P.ln, kMapBf16, d, rows));
     if (!ok) return st_rt("cuTensorMapEncodeTiled failed for an activation buffer");
   }
   OW_TRY(cudaStreamSynchronize(P.stream));
@@ -1083,7 +1095,7 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   bool mok;
   if (epilogue == kEpiResidLn) {
     const MapType lt = ln_mode == kLnF32 ? kMapF32 : (ln_mode == kLnE4m3 ? kMapU8 : kMapBf16);
-    mok = make_map_128b(&mo, resid, kMapF32, n, m, 32) && make_map_128b(&ml, ln_out, lt, n, m, 32);
+    mok = make_map_128b(&mo, resid, kMapF32, n, m, 32) && make_ln_map(&ml, ln_out, lt, n, m);
   } else {
     mok = make_map_128b(&mo, out, kMapBf16, n, m, 32);
     ml = mo;

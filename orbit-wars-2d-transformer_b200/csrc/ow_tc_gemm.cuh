@@ -67,7 +67,7 @@ constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 
 template <int EPI>
 struct EpiWarps {
-  static constexpr int kCount = EPI == kEpiResidLn ? 4 : 8;
+  static constexpr int kCount = 8;
   static constexpr int kThreads = 64 + 32 * kCount;
 };
 
@@ -91,12 +91,14 @@ struct TcGemmShape {
   static constexpr int kBarrierBytes = 512;
   static constexpr int kParamFloats = EPI == kEpiResidLn ? 2048 : 4096;  // staged bias/scale/g/b vectors
   static constexpr int kParamBytes = kParamFloats * 4;
-  // staging tiles per epilogue warp: bias/GELU -> 2 output tiles; LayerNorm ->
-  // 2 residual tiles (loads, then x stores) + 2 (or 1 at d=512) LN-output tiles
-  static constexpr int kLnTiles = BLOCK_N <= 384 ? 2 : 1;
-  static constexpr int kTilesPerWarp = EPI == kEpiResidLn ? 2 + kLnTiles : 2;
+  // staging tiles (4 KB) per epilogue warp, used by the TMA loads of the
+  // residual and the TMA stores of the outputs: 2, or 1 at d = 512 (budget)
+  static constexpr int kTilesPerWarp = (EPI == kEpiResidLn && BLOCK_N > 384) ? 1 : 2;
   static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * kTilesPerWarp * 4096;
-  static constexpr int kFixedBytes = kBarrierBytes + kParamBytes + kXposeBytes + 1024;  // + align slack
+  // LayerNorm: per-row partial statistics exchanged between the two warps of a
+  // lane quadrant: [2 parities][8 warps][32 lanes] x (mean, M2, amax, pad)
+  static constexpr int kStatsBytes = EPI == kEpiResidLn ? 2 * 8 * 32 * 16 : 0;
+  static constexpr int kFixedBytes = kBarrierBytes + kParamBytes + kXposeBytes + kStatsBytes + 1024;  // + align slack
   static constexpr int kStagesFit = (kSmemLimit - kFixedBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
   static constexpr int kSmemBytes = kStages * kStageBytes + kFixedBytes;
@@ -111,6 +113,14 @@ struct TcGemmShape {
 // 16 B chunk j of row r of a 32 x 128 B staging tile (128 B swizzle).
 __device__ __forceinline__ uint4* xpose_slot(uint8_t* tile, int row, int chunk) {
   return reinterpret_cast<uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+// Same for 32 x 64 B boxes (64 B swizzle: chunk j of row r at j ^ ((r >> 1) & 3)).
+__device__ __forceinline__ uint4* xpose_slot64(uint8_t* tile, int row, int chunk) {
+  return reinterpret_cast<uint4*>(tile + row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
+}
+// Same for 32 x 32 B boxes (32 B swizzle: chunk j of row r at j ^ ((r >> 2) & 1)).
+__device__ __forceinline__ uint4* xpose_slot32(uint8_t* tile, int row, int chunk) {
+  return reinterpret_cast<uint4*>(tile + row * 32 + ((chunk ^ ((row >> 2) & 1)) << 4));
 }
 
 template <int BLOCK_N, int EPI, bool FP8>
@@ -131,10 +141,11 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
   uint64_t* empty = full + S::kStages;
   uint64_t* tfull = empty + S::kStages;
   uint64_t* tempty = tfull + S::kAcc;
-  uint64_t* xbar = tempty + S::kAcc;  // LayerNorm residual loads: 2 per epilogue warp
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xbar + 2 * kEpiWarps);
+  uint64_t* xbar = tempty + S::kAcc;  // residual loads: one barrier per staging tile of each epilogue warp
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xbar + S::kTilesPerWarp * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* s_par = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + S::kBarrierBytes);
+  float4* s_stats = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(s_par) + S::kParamBytes);
   // staged vectors: s_bias[n], then (fp8) s_bscale[n], then (LN) s_g[n], s_b[n]
   float* s_bias = s_par;
   float* s_bscale = s_par + p.n;
@@ -158,7 +169,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], kEpiWarps);
     }
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&xbar[i], 1);
+    for (int i = 0; i < S::kTilesPerWarp * kEpiWarps; ++i) mbar_init(&xbar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -262,12 +273,26 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     uint8_t* tiles = s_xpose + ew * S::kTilesPerWarp * 4096;
     constexpr int kCols = EPI == kEpiResidLn ? BLOCK_N : BLOCK_N * 4 / kEpiWarps;  // columns this warp drains
     const int col0 = EPI == kEpiResidLn ? 0 : (ew / 4) * kCols;
-    uint64_t* my_xbar = xbar + 2 * ew;
+    uint64_t* my_xbar = xbar + S::kTilesPerWarp * ew;
     uint32_t xphase[2] = {0u, 0u};
+    int stat_par = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     int out_k = 0;  // output tiles used so far (alternates the double buffer)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (EPI == kEpiResidLn) {
+        // issue this tile's first residual chunks now: they land while the MMAs run
+        const int rb = (tile / n_tiles) * S::kBlockM + quad * 32;
+        if (lane == 0 && rb < m_valid) {
+          bulk_wait_read<0>();  // staging tiles free: earlier stores have read them
+#pragma unroll
+          for (int b = 0; b < S::kTilesPerWarp; ++b) {
+            mbar_arrive_expect_tx(&my_xbar[b], 4096);
+            tma_load_2d(tiles + b * 4096, &map_o, &my_xbar[b], (ew >> 2) * (BLOCK_N / 2) + b * 32, rb);
+          }
+        }
+        __syncwarp();
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
       const int row_base = (tile / n_tiles) * S::kBlockM + quad * 32;  // first row of this warp's 32
@@ -327,52 +352,48 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           ++out_k;
         }
       } else if (any) {
-        // Residual add + LayerNorm over the full row (BLOCK_N == n == d): two
-        // passes over TMEM. Pass 1 forms v = x + acc*s + bias, writes it back to
-        // TMEM and accumulates shifted statistics (shift = the row's first v,
-        // which keeps E[(v-k)^2] - E[v-k]^2 well conditioned); pass 2 writes x
-        // and the normalised row.
-        constexpr int kChunks = BLOCK_N / 32;
-        uint8_t* xt[2] = {tiles, tiles + 4096};
-        uint8_t* lt[2] = {tiles + 8192, tiles + 8192 + (S::kLnTiles - 1) * 4096};
-        if (lane == 0) {
-          bulk_wait_read<0>();  // both residual tiles are free (earlier x stores have read them)
-#pragma unroll
-          for (int b = 0; b < 2; ++b) {
-            mbar_arrive_expect_tx(&my_xbar[b], 4096);
-            tma_load_2d(xt[b], &map_o, &my_xbar[b], b * 32, row_base);
-          }
-        }
-        __syncwarp();
+        // Residual add + LayerNorm over the full row (BLOCK_N == n == d). The
+        // two warps of a lane quadrant split the row (half = ew / 4). Pass 1:
+        // v = x + acc*s + bias (residual chunks arrive by TMA, issued before
+        // this tile's accumulator was ready), written back to TMEM, shifted
+        // statistics per half; the halves' (mean, M2) are merged exactly
+        // (Chan et al.) through shared memory. Pass 2: x and the LN output
+        // leave by TMA stores, alternating between the warp's staging tiles.
+        constexpr int HW = BLOCK_N / 2;
+        constexpr int kChunks = HW / 32;
+        constexpr int NT = S::kTilesPerWarp;
+        const int half = ew >> 2;
+        const int cbase = half * HW;
         float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
         bool ok = true;
 #pragma unroll 1
         for (int c = 0; c < kChunks; ++c) {
           uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          const int b = c & 1;
+          tmem_ld32(tbase + cbase + c * 32, r);
+          const int b = c % NT;
           if (!mbar_wait(&my_xbar[b], xphase[b], abort_flag, p.err)) ok = false;
           xphase[b] ^= 1u;
           tmem_ld_wait();
           float xv[32];
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const float4 t4 = *reinterpret_cast<const float4*>(xpose_slot(xt[b], lane, q));
+            const float4 t4 = *reinterpret_cast<const float4*>(xpose_slot(tiles + b * 4096, lane, q));
             xv[4 * q] = t4.x;
             xv[4 * q + 1] = t4.y;
             xv[4 * q + 2] = t4.z;
             xv[4 * q + 3] = t4.w;
           }
           __syncwarp();
-          if (lane == 0 && c + 2 < kChunks && ok) {
+          if (lane == 0 && c + NT < kChunks && ok) {
             mbar_arrive_expect_tx(&my_xbar[b], 4096);
-            tma_load_2d(xt[b], &map_o, &my_xbar[b], (c + 2) * 32, row_base);
+            tma_load_2d(tiles + b * 4096, &map_o, &my_xbar[b], cbase + (c + NT) * 32, row_base);
           }
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
-            const float4 bv = *reinterpret_cast<const float4*>(s_bias + c * 32 + i);
+            const int col = cbase + c * 32 + i;
+            const float4 bv = *reinterpret_cast<const float4*>(s_bias + col);
             float4 sv = make_float4(1.f, 1.f, 1.f, 1.f);
-            if (FP8) sv = *reinterpret_cast<const float4*>(s_bscale + c * 32 + i);
+            if (FP8) sv = *reinterpret_cast<const float4*>(s_bscale + col);
             const float b4[4] = {bv.x, bv.y, bv.z, bv.w};
             const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
@@ -387,80 +408,95 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
               r[i + j] = __float_as_uint(v);
             }
           }
-          tmem_st32(tbase + c * 32, r);
+          tmem_st32(tbase + cbase + c * 32, r);
         }
         tmem_st_wait();
-        const float md = s1 * (1.0f / BLOCK_N);
-        const float var = fmaxf(s2 * (1.0f / BLOCK_N) - md * md, 0.0f);
-        const float mean = shift + md;
+        // merge the two halves' statistics (same operation order in both warps)
+        const float mh = shift + s1 * (1.0f / HW);
+        const float m2h = fmaxf(s2 - s1 * s1 * (1.0f / HW), 0.0f);
+        float4* st = s_stats + (stat_par * 8) * 32;
+        st[ew * 32 + lane] = make_float4(mh, m2h, 0.0f, 0.0f);
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
+        const float4 lo = st[(ew & 3) * 32 + lane];  // the pair: epilogue warps ew & 3 (half 0) and +4 (half 1)
+        const float4 hi = st[((ew & 3) + 4) * 32 + lane];
+        const float delta = hi.x - lo.x;
+        const float mean = 0.5f * (lo.x + hi.x);
+        const float var = (lo.y + hi.y + delta * delta * (0.25f * BLOCK_N)) * (1.0f / BLOCK_N);
         const float rstd = rsqrtf(var + 1e-5f);
         float inv_scale = 1.0f;
         if (p.ln_mode == kLnE4m3) {
           float amax = 0.0f;
 #pragma unroll 1
-          for (int c = 0; c < BLOCK_N; c += 32) {
+          for (int c = 0; c < kChunks; ++c) {
             uint32_t r[32];
-            tmem_ld32(tbase + c, r);
+            tmem_ld32(tbase + cbase + c * 32, r);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float y = (__uint_as_float(r[i]) - mean) * rstd * s_g[c + i] + s_b[c + i];
+              const int col = cbase + c * 32 + i;
+              const float y = (__uint_as_float(r[i]) - mean) * rstd * s_g[col] + s_b[col];
               amax = fmaxf(amax, fabsf(y));
             }
           }
+          st[ew * 32 + lane].z = amax;
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
+          amax = fmaxf(st[(ew & 3) * 32 + lane].z, st[((ew & 3) + 4) * 32 + lane].z);
           const float scale = amax > 0.0f ? amax * (1.0f / 448.0f) : 1.0f;
           inv_scale = 1.0f / scale;
-          if (live) p.ln_scale[m] = scale;
+          if (live && half == 0) p.ln_scale[m] = scale;
         }
-        // LN output: 32 columns are 32*elt bytes of a 128 B box row
+        stat_par ^= 1;
         const int ln_elt = p.ln_mode == kLnF32 ? 4 : (p.ln_mode == kLnE4m3 ? 1 : 2);
-        const int per_box = 4 / ln_elt;  // 32-column pieces per 128 B box row
-        int lbox = 0;
 #pragma unroll 1
         for (int c = 0; c < kChunks; ++c) {
+          const int col0 = cbase + c * 32;
           uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          if (lane == 0) bulk_wait_read<1>();
+          tmem_ld32(tbase + col0, r);
+          // x (f32, 128 B box rows): the tile's previous store must have read it
+          uint8_t* xt = tiles + 0;
+          uint8_t* lt = tiles + (NT - 1) * 4096;
+          if (lane == 0) {
+            if (NT == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+          }
           tmem_ld_wait();
           __syncwarp();
-          // x (f32): one 128 B row piece per thread
-          uint8_t* xo = xt[c & 1];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) *xpose_slot(xo, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          for (int q = 0; q < 8; ++q) *xpose_slot(xt, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&map_o, xo, c * 32, row_base);
+            tma_store_2d(&map_o, xt, col0, row_base);
             bulk_commit();
           }
           float y[32];
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
-            const float4 gv = *reinterpret_cast<const float4*>(s_g + c * 32 + i);
-            const float4 bv = *reinterpret_cast<const float4*>(s_b + c * 32 + i);
+            const float4 gv = *reinterpret_cast<const float4*>(s_g + col0 + i);
+            const float4 bv = *reinterpret_cast<const float4*>(s_b + col0 + i);
             y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
             y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
             y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
             y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
           }
-          const int piece = c % per_box;
-          uint8_t* lo = lt[lbox & (S::kLnTiles - 1)];
-          if (piece == 0 && S::kLnTiles == 1) {
-            if (lane == 0) bulk_wait_read<0>();  // single LN tile: its previous store must have read it
-            __syncwarp();
+          // LN output: 32 columns = one 32 x (32*elt) B box in the matching swizzle
+          if (lane == 0) {
+            if (NT == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
           }
+          __syncwarp();
           if (p.ln_mode == kLnE4m3) {
             uint32_t q8[8];
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
               q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
                                       y[i + 3] * inv_scale);
-            *xpose_slot(lo, lane, 2 * piece) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
-            *xpose_slot(lo, lane, 2 * piece + 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
+            *xpose_slot32(lt, lane, 0) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+            *xpose_slot32(lt, lane, 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
           } else if (p.ln_mode == kLnF32) {
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              *xpose_slot(lo, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
+              *xpose_slot(lt, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
                                                     __float_as_uint(y[4 * q + 2]), __float_as_uint(y[4 * q + 3]));
           } else {
             uint32_t yo[16];
@@ -468,18 +504,16 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
             for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              *xpose_slot(lo, lane, 4 * piece + q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
+              *xpose_slot64(lt, lane, q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
           }
-          if (piece == per_box - 1) {
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&map_l, lo, (c + 1 - per_box) * 32, row_base);
-              bulk_commit();
-            }
-            ++lbox;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_l, lt, col0, row_base);
+            bulk_commit();
           }
         }
+        (void)ln_elt;
       }
       tc_fence_before();
       __syncwarp();

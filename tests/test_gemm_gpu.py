@@ -22,9 +22,15 @@ def call(precision, epi, m, n, k, a, w, bias, out=None, resid=None, g=None, b=No
     _lib.check("ow_selftest_gemm", st)
 
 
-def close(x, ref, rel):
-    err = (x.float() - ref).abs().max().item() / max(ref.abs().max().item(), 1e-6)
-    assert err <= rel, f"rel err {err:.3e} > {rel}"
+def close(x, ref, rel, what=""):
+    diff = (x.float() - ref).abs()
+    err = diff.max().item() / max(ref.abs().max().item(), 1e-6)
+    if not err <= rel:
+        bad = torch.nonzero(~(diff <= rel * max(ref.abs().max().item(), 1e-6)))
+        rows = torch.unique(bad[:, 0]).tolist() if bad.ndim == 2 else []
+        cols = torch.unique(bad[:, 1]).tolist() if bad.ndim == 2 else []
+        raise AssertionError(f"{what}: rel err {err:.3e} > {rel}; {bad.shape[0]} bad, rows {rows[:8]}.. ({len(rows)}), "
+                             f"cols {cols[:8]}.. ({len(cols)})")
     return err
 
 
@@ -65,9 +71,9 @@ def test_bf16_resid_ln(n, ln_mode):
     ln_out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16 if ln_mode == LN_BF16 else torch.float32)
     call(BF16, EPI_LN, m, n, k, a, w, bias, resid=resid, g=gam, b=bet, ln_out=ln_out, ln_mode=ln_mode)
     x_ref = resid0 + a.float() @ w.float().T + bias
-    close(resid, x_ref, 1e-4)
+    close(resid, x_ref, 1e-4, "x")
     y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
-    close(ln_out, y_ref, 8e-3 if ln_mode == LN_BF16 else 1e-4)
+    close(ln_out, y_ref, 8e-3 if ln_mode == LN_BF16 else 1e-4, "ln")
 
 
 def quant_rows(x):
