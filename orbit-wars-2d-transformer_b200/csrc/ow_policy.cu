@@ -156,8 +156,8 @@ bool make_map_box(CUtensorMap* map, const void* base, MapType t, uint64_t inner,
 bool make_map_128b(CUtensorMap* map, const void* base, MapType t, uint64_t inner, uint64_t rows, uint32_t box_rows) {
   return make_map_box(map, base, t, inner, rows, 128, box_rows);
 }
-// LayerNorm-output map of the epilogue: 32 columns x 32 rows in the element
-// type's swizzle (f32 128 B, bf16 64 B, e4m3 32 B).
+// Epilogue output map: 32 columns x 32 rows in the element type's swizzle
+// (f32 128 B, bf16 64 B, e4m3 32 B).
 bool make_ln_map(CUtensorMap* map, const void* base, MapType t, uint64_t inner, uint64_t rows) {
   const uint32_t elt = t == kMapF32 ? 4 : (t == kMapBf16 ? 2 : 1);
   return make_map_box(map, base, t, inner, rows, 32 * elt, 32);
@@ -830,8 +830,8 @@ OwStatus alloc_workspace(OwPolicy& P) {
     else
       ok = make_kmajor_map(&P.m_ln, P.ln, false, d, rows, 128) && make_kmajor_map(&P.m_attn, P.attn, false, d, rows, 128) &&
            make_kmajor_map(&P.m_h, P.h, false, f, rows, 128);
-    ok = ok && make_map_128b(&P.e_qkv, P.qkv, kMapBf16, 3 * d, rows, 32) &&
-         make_map_128b(&P.e_h, P.h, kMapBf16, f, rows, 32) && make_map_128b(&P.e_x, P.x, kMapF32, d, rows, 32) &&
+    ok = ok && make_ln_map(&P.e_qkv, P.qkv, kMapBf16, 3 * d, rows) && make_ln_map(&P.e_h, P.h, kMapBf16, f, rows) &&
+         make_map_128b(&P.e_x, P.x, kMapF32, d, rows, 32) &&
          make_ln_map(&P.e_y, P.y, kMapF32, d, rows) &&
          (e4 ? make_ln_map(&P.e_ln, P.ln8, kMapU8, d, rows) : make_ln_map(&P.e_ln, P.ln, kMapBf16, d, rows));
     if (!ok) return st_rt("cuTensorMapEncodeTiled failed for an activation buffer");
@@ -1097,7 +1097,7 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
     const MapType lt = ln_mode == kLnF32 ? kMapF32 : (ln_mode == kLnE4m3 ? kMapU8 : kMapBf16);
     mok = make_map_128b(&mo, resid, kMapF32, n, m, 32) && make_ln_map(&ml, ln_out, lt, n, m);
   } else {
-    mok = make_map_128b(&mo, out, kMapBf16, n, m, 32);
+    mok = make_ln_map(&mo, out, kMapBf16, n, m);
     ml = mo;
   }
   if (!mok) return st_rt("cuTensorMapEncodeTiled failed for an epilogue buffer");

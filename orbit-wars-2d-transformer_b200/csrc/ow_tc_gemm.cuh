@@ -67,7 +67,7 @@ constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 
 template <int EPI>
 struct EpiWarps {
-  static constexpr int kCount = 8;
+  static constexpr int kCount = EPI == kEpiResidLn ? 8 : 16;
   static constexpr int kThreads = 64 + 32 * kCount;
 };
 
@@ -94,7 +94,9 @@ struct TcGemmShape {
   // staging tiles (4 KB) per epilogue warp, used by the TMA loads of the
   // residual and the TMA stores of the outputs: 2, or 1 at d = 512 (budget)
   static constexpr int kTilesPerWarp = (EPI == kEpiResidLn && BLOCK_N > 384) ? 1 : 2;
-  static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * kTilesPerWarp * 4096;
+  // bias/GELU epilogues stage 32 rows x 32 bf16 columns (64 B rows); LayerNorm 32 x 128 B
+  static constexpr int kTileBytes = EPI == kEpiResidLn ? 4096 : 2048;
+  static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * kTilesPerWarp * kTileBytes;
   // LayerNorm: per-row partial statistics exchanged between the two warps of a
   // lane quadrant: [2 parities][8 warps][32 lanes] x (mean, M2, amax, pad)
   static constexpr int kStatsBytes = EPI == kEpiResidLn ? 2 * 8 * 32 * 16 : 0;
@@ -270,9 +272,9 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     // warp's staging tiles.
     const int ew = warp - 2;
     const int quad = warp & 3;
-    uint8_t* tiles = s_xpose + ew * S::kTilesPerWarp * 4096;
+    uint8_t* tiles = s_xpose + ew * S::kTilesPerWarp * S::kTileBytes;
     constexpr int kCols = EPI == kEpiResidLn ? BLOCK_N : BLOCK_N * 4 / kEpiWarps;  // columns this warp drains
-    const int col0 = EPI == kEpiResidLn ? 0 : (ew / 4) * kCols;
+    const int col0 = EPI == kEpiResidLn ? 0 : (ew / 4) * kCols;  // warps ew, ew+4, ... share a lane quadrant
     uint64_t* my_xbar = xbar + S::kTilesPerWarp * ew;
     uint32_t xphase[2] = {0u, 0u};
     int stat_par = 0;
@@ -304,17 +306,16 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       const float a_s = (FP8 && live) ? p.a_scale[m] : 1.0f;
 
       if (EPI == kEpiBias || EPI == kEpiBiasGelu) {
-        static_assert(kCols % 64 == 0, "64-column epilogue chunks");
+        static_assert(kCols % 32 == 0, "32-column epilogue chunks");
 #pragma unroll 1
-        for (int c = col0; c < col0 + kCols && any; c += 64) {
-          uint32_t r[64];
-          tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-          tmem_ld32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        for (int c = col0; c < col0 + kCols && any; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
           if (lane == 0) bulk_wait_read<1>();  // the store that last used this tile has read it
           tmem_ld_wait();
-          uint32_t packed[32];
+          uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 64; i += 4) {
+          for (int i = 0; i < 32; i += 4) {
             const float4 bv = *reinterpret_cast<const float4*>(s_bias + n0 + c + i);
             float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
             float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
@@ -338,11 +339,11 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
             packed[i / 2] = pack_bf16x2(v0, v1);
             packed[i / 2 + 1] = pack_bf16x2(v2, v3);
           }
-          uint8_t* ot = tiles + (out_k & 1) * 4096;
+          uint8_t* ot = tiles + (out_k & 1) * S::kTileBytes;
           __syncwarp();
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *xpose_slot(ot, lane, q) = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          for (int q = 0; q < 4; ++q)
+            *xpose_slot64(ot, lane, q) = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {

@@ -114,3 +114,18 @@ def test_fp8_resid_ln():
     y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
     y = ln_out.view(torch.float8_e4m3fn).float() * ln_scale[:, None]
     close(y, y_ref, 7e-2)
+
+
+@pytest.mark.parametrize("epi,n", [(EPI_BIAS, 768), (EPI_GELU, 1024)])
+def test_bf16_repeatable(epi, n):
+    """Two launches on the same inputs give bit-identical outputs."""
+    m, k = 40000, 256
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") / 16).bfloat16()
+    bias = torch.randn(n, device="cuda")
+    o1 = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    o2 = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    call(BF16, epi, m, n, k, a, w, bias, out=o1)
+    call(BF16, epi, m, n, k, a, w, bias, out=o2)
+    bad = torch.nonzero(o1.view(torch.int16) != o2.view(torch.int16))
+    assert bad.shape[0] == 0, f"{bad.shape[0]} differing elements, first {bad[:4].tolist()}"

@@ -118,20 +118,25 @@ def test_full_batch_properties():
     cfg = ow.preset(2)
     w = ow.make_weights(cfg, seed=17)
     feats, counts = ow.make_inputs(cfg, seed=17)
+    names = ("logits", "value", "actions")
+
+    def same(x, y, what):
+        for n, a, b in zip(names, x, y):
+            if not np.array_equal(a, b):
+                diff = np.argwhere(a != b)
+                raise AssertionError(f"{what}: {n} differs at {len(diff)} places, first {diff[:3].tolist()}")
+
     with ow.EncoderPolicy(cfg, w) as pol:
         r1 = pol.forward(feats, counts)
         r2 = pol.forward(feats, counts)
-        for x, y in zip(r1, r2):
-            assert np.array_equal(x, y)
+        same(r1, r2, "repeat")
         perm = np.random.default_rng(0).permutation(cfg.batch)
         r3 = pol.forward(feats[perm], counts[perm])
-        for x, y in zip(r1, r3):
-            assert np.array_equal(x[perm], y)
+        same(tuple(x[perm] for x in r1), r3, "permutation")
         dirty = feats.copy()
         dirty[~valid_mask(counts, cfg.n_entities)] = 77.0
         r4 = pol.forward(dirty, counts)
-        for x, y in zip(r1, r4):
-            assert np.array_equal(x, y)
+        same(r1, r4, "padding")
         assert np.all(np.isfinite(r1[0])) and np.all(np.isfinite(r1[1]))
 
 
