@@ -46,6 +46,7 @@ METRIC = "policy-forward states/sec (config {c})"
 UNIT = "states/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
+REFERENCE_RUN_S = 120.0  # CPU time budget of one --impl reference run
 
 
 def ncu_traffic(config: int, kernel: str):
@@ -189,12 +190,14 @@ def run_reference(args, cfg) -> None:
     weights = ow.make_weights(cfg, seed=args.seed)
     feats, counts = ow.make_inputs(cfg, seed=args.seed)
     threads = bind.max_threads()
-    # sample size so one step takes ~3 s of CPU work
+    # sample size: the whole warm-up + timed run takes about REFERENCE_RUN_S of CPU work
     n = 4
+    bind.policy_forward(cfg, weights, feats[:n], counts[:n], f64=False, threads=threads)  # warm
     t0 = time.perf_counter()
     bind.policy_forward(cfg, weights, feats[:n], counts[:n], f64=False, threads=threads)
     per_state = (time.perf_counter() - t0) / n
-    n = int(max(1, min(cfg.batch, 3.0 / max(per_state, 1e-6))))
+    step_s = min(3.0, REFERENCE_RUN_S / (args.steps + args.warmup))
+    n = int(max(1, min(cfg.batch, step_s / max(per_state, 1e-6))))
     for i in range(args.warmup):
         bind.policy_forward(cfg, weights, feats[:n], counts[:n], f64=False, threads=threads)
     times = []
@@ -393,6 +396,242 @@ def run_ours(args, cfg) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------- True2D drop-in workload
+# The reference engine's self-play forward (crates/orbit-wars-core/src/true2d_model.rs:197-283)
+# through the reference ABI: a resident population of seeded models
+# (True2DTransformer::seeded) and one batch of engine-shaped requests per step,
+# forward_many_resident as the engine calls it (cuda_true2d.rs:275-358).
+T2_METRIC = "True2D drop-in forward requests/sec (61 layers, 64 rows, 1 head; resident population)"
+T2_UNIT = "requests/s"
+
+
+def true2d_workload(args):
+    from orbit_wars_b200 import synth
+    from orbit_wars_b200.true2d import True2DShape
+    shape = True2DShape()  # config.rs defaults: 61 matrix layers, 64 rows, 1 attention head
+    per = shape.parameter_count()
+    pop = synth.true2d_population(args.seed, args.models, per)
+    x, idx = synth.true2d_requests(args.seed, args.requests, shape.rows, args.models)
+    return shape, per, pop, x, idx
+
+
+def true2d_workload_name(args, shape) -> str:
+    return (f"True2D self-play batch: {args.requests} requests x {shape.rows} rows x 7 features, "
+            f"population of {args.models} seeded models ({shape.parameter_count():,} f32 weights each, "
+            f"{args.models * shape.parameter_count() * 4 / 1e6:.0f} MB resident), "
+            f"{shape.layers} matrix layers, {shape.heads} attention head")
+
+
+def true2d_ex2_per_request(shape) -> float:
+    """Exponentials per request in the attention kernel: cells^2 per head (one pass)."""
+    cells = shape.rows * shape.rows
+    return float(cells) * cells * shape.heads
+
+
+def true2d_cpu_reference(args, shape, pop, per, x, target_s: float) -> dict | None:
+    """The reference's own CPU forward (native/cuda/orbit_wars_cuda_true2d_smoke.cpp:127-260,
+    cpu_reference: 2 requests of one model per call, single-threaded), compiled from the
+    reference source into oracle/_ref, run concurrently on every host thread."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import bind
+    if not bind.ref_available():
+        return None
+    lib = bind.load_ref_cpu()
+    games = int(lib.ref_true2d_smoke_games())
+    if int(lib.ref_true2d_smoke_weight_count()) != per or shape.heads != 1:
+        return None
+    threads = os.cpu_count() or 1
+    rows_per_call = games * shape.rows * 7
+    calls_avail = max(1, x.size // rows_per_call)
+
+    def one(i):
+        c = i % calls_avail
+        xin = np.ascontiguousarray(x[c * rows_per_call:(c + 1) * rows_per_call])
+        w = pop[(i % args.models) * per:(i % args.models + 1) * per]
+        out = np.zeros(games * shape.rows * 24, np.float32)
+        lib.ref_true2d_cpu_reference(xin.ctypes.data, w.ctypes.data, out.ctypes.data)
+        return out
+
+    t0 = time.perf_counter()
+    one(0)
+    per_call = time.perf_counter() - t0
+    # about target_s of wall time when every thread runs calls back to back
+    calls = max(threads, min(100000, int(target_s / max(per_call, 1e-6)) * threads))
+    with ThreadPoolExecutor(threads) as ex:
+        t0 = time.perf_counter()
+        list(ex.map(one, range(calls)))
+        dt = time.perf_counter() - t0
+    return {"value": calls * games / dt, "unit": T2_UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{calls * games} requests ({calls} calls of the reference's cpu_reference, {games} requests "
+                      f"each, models cycling over the population) on {threads} threads, {dt:.1f} s"}
+
+
+def run_true2d_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    shape, per, pop, x, idx = true2d_workload(args)
+    budget = min(30.0, REFERENCE_RUN_S / (args.steps + args.warmup))
+    for _ in range(args.warmup):
+        true2d_cpu_reference(args, shape, pop, per, x, target_s=budget)
+    vals = []
+    for _ in range(args.steps):
+        r = true2d_cpu_reference(args, shape, pop, per, x, target_s=budget)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference's cpu_reference was not built from source (make -C oracle ref)"}))
+            return
+        vals.append(r)
+    value = float(np.mean([v["value"] for v in vals]))
+    cpu = dict(vals[-1])
+    cpu["value"] = value
+    line = {
+        "impl": "reference", "metric": T2_METRIC, "value": value, "unit": T2_UNIT,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * args.requests / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded True2DTransformer::seeded models)",
+        "config": {"workload": true2d_workload_name(args, shape)},
+        "cpu_baseline": cpu, "e2e": {"value": value, "unit": T2_UNIT, "h2d_bytes_per_step": 0,
+                                     "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def reference_gpu_true2d(args, shape, pop, x, idx, steps: int) -> dict | None:
+    """The reference's own CUDA library (native/cuda/orbit_wars_cuda.cu, built from source for
+    sm_100a into oracle/_ref) on the same workload and the same ABI call."""
+    import ctypes as C
+    from orbit_wars_b200 import _lib
+    path = REPO / "oracle" / "_ref" / "liborbit_wars_cuda_ref.so"
+    if not path.exists():
+        return None
+    ref = C.CDLL(str(path), mode=2)
+    ref.orbit_wars_cuda_true2d_upload_population.restype = _lib.Status
+    ref.orbit_wars_cuda_true2d_upload_population.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t,
+                                                             _lib.True2DShapeC]
+    ref.orbit_wars_cuda_true2d_forward_many_resident.restype = _lib.Status
+    ref.orbit_wars_cuda_true2d_forward_many_resident.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                                                 _lib.True2DShapeC]
+    _lib.check("reference upload", ref.orbit_wars_cuda_true2d_upload_population(
+        pop.ctypes.data, args.models, args.requests, shape.c()))
+    out = np.zeros(args.requests * shape.rows * 24, np.float32)
+
+    def call():
+        _lib.check("reference forward", ref.orbit_wars_cuda_true2d_forward_many_resident(
+            x.ctypes.data, idx.ctypes.data, out.ctypes.data, args.requests, shape.c()))
+
+    for _ in range(3):
+        call()
+    wall = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        call()
+        wall.append(time.perf_counter() - t0)
+    return {"value": args.requests * steps / float(np.sum(wall)), "unit": T2_UNIT, "steps": steps,
+            "timing": "wall clock per synchronous forward_many_resident call (host buffers), same workload",
+            "library": "oracle/_ref/liborbit_wars_cuda_ref.so (reference source, nvcc sm_100a)", "output": out}
+
+
+def run_true2d(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from orbit_wars_b200.true2d import CudaTrue2D
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)  # the reference ABI uses the calling thread's current device
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    shape, per, pop, x, idx = true2d_workload(args)  # replicas: every rank runs the same workload
+    lib = CudaTrue2D()
+    lib.upload_population(pop, args.requests, shape)
+
+    def step():
+        return lib.forward_population_resident_packed(x, idx, args.models, shape)
+
+    for _ in range(args.warmup):
+        out = step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    lib.profile_begin(args.steps)
+    wall = []
+    with ClockSampler(local) as clk:
+        clk.window = (time.time(), None)
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            out = step()
+            wall.append(time.perf_counter() - t0)
+        clk.window = (clk.window[0], time.time())
+    prof = lib.profile_end()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    dev_s = sum(v[1] for v in prof.values()) / 1000.0
+    t = torch.tensor([dev_s, float(np.sum(wall))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_dev, t_wall = float(t[0].item()), float(t[1].item())
+    value = world * args.requests * args.steps / t_dev
+    e2e = {"value": world * args.requests * args.steps / t_wall, "unit": T2_UNIT,
+           "h2d_bytes_per_step": int(x.nbytes + idx.nbytes),
+           "d2h_bytes_per_step": int(args.requests * shape.rows * 24 * 4 + 4),
+           "timing": "wall clock per synchronous forward_many_resident call (host buffers), max over ranks"}
+    kernels = {}
+    for name, (n, ms) in prof.items():
+        kernels[name] = {"launches": n, "total_ms": round(ms, 4), "avg_us": round(ms * 1000.0 / max(n, 1), 2)}
+    total = sum(k["total_ms"] for k in kernels.values()) or 1.0
+    for k in kernels.values():
+        k["share"] = round(k["total_ms"] / total, 4)
+    clocks = clk.summary()
+    props = torch.cuda.get_device_properties(dev)
+    roof = None
+    if "t2_attention" in kernels:
+        a = kernels["t2_attention"]
+        ach = true2d_ex2_per_request(shape) * args.requests / (a["avg_us"] * 1e-6) / 1e9
+        mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
+        peak = 16.0 * props.multi_processor_count * mhz * 1e6 / 1e9
+        roof = {"kernel": "t2_attention", "bound": "mufu", "achieved": round(ach, 1), "peak": round(peak, 1),
+                "unit": "G ex2/s", "frac": round(ach / peak, 4), "traffic": None,
+                "peak_source": f"computed: 16 ex2/clk/SM x {props.multi_processor_count} SMs x {mhz:.0f} MHz "
+                               "(median sampled SM clock); not a measured peak",
+                "work_per_launch": f"rows^4 x heads = {true2d_ex2_per_request(shape):.0f} exponentials per request"}
+    ref_gpu = None
+    if rank == 0 and world == 1:
+        ref_gpu = reference_gpu_true2d(args, shape, pop, x, idx, steps=min(args.steps, 50))
+        if ref_gpu is not None:
+            ro = ref_gpu.pop("output")
+            ref_gpu["max_abs_diff_vs_ours"] = float(np.abs(ro - out.reshape(-1)).max())
+            ref_gpu["ours_e2e_over_reference"] = round(e2e["value"] / ref_gpu["value"], 3)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = true2d_cpu_reference(args, shape, pop, per, x, target_s=12.0)
+    if rank == 0:
+        line = {
+            "metric": T2_METRIC, "value": value, "unit": T2_UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * t_dev / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded True2DTransformer::seeded models, N(0,1)/2 request rows)",
+            "config": {"workload": true2d_workload_name(args, shape), "requests_per_gpu": args.requests,
+                       "models": args.models,
+                       "l2": f"population of {args.models * per * 4 / 1e6:.0f} MB > 126 MB L2, read every step",
+                       "parallelism": f"replicas x{world} (the reference ABI is single-device)",
+                       "value_timing": "sum of the three kernels' CUDA events per call (inputs already on the device)"},
+            "e2e": e2e, "gpu_launches": 3 * args.steps, "roofline": roof, "cpu_baseline": cpu,
+            "reference_gpu": ref_gpu, "clocks": clocks, "kernels": kernels,
+            "outputs_finite": bool(np.isfinite(out).all()),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -404,9 +643,15 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=None, help="override the config's per-GPU batch")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="policy", choices=["policy", "true2d"],
+                    help="policy: the encoder-policy forward (default); true2d: the reference ABI drop-in")
+    ap.add_argument("--requests", type=int, default=1024, help="true2d: requests per step")
+    ap.add_argument("--models", type=int, default=64, help="true2d: resident population size")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.workload == "true2d":
+        return run_true2d_reference(args) if args.impl == "reference" else run_true2d(args)
     import orbit_wars_b200 as ow
     cfg = ow.preset(args.config)
     if args.batch:

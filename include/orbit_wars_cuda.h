@@ -14,6 +14,7 @@
 #pragma once
 
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -151,6 +152,25 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(
     size_t game_count,
     OrbitWarsCudaTrue2DShape shape,
     void* stream);
+
+/* Device timing of the True2D forwards -- no counterpart in the reference ABI;
+ * for benchmarks. profile_begin arms CUDA events around each kernel of the next
+ * `max_calls` calls of ..._true2d_forward / _forward_many / _forward_many_resident
+ * (events only, no extra synchronisation). profile_end waits for the library's
+ * stream and returns, per kernel name, the launches and the summed
+ * event-to-event milliseconds; names are static strings. */
+typedef struct OrbitWarsCudaKernelTiming {
+  const char* name;
+  int32_t launches;
+  float total_ms;
+} OrbitWarsCudaKernelTiming;
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_profile_begin(int32_t max_calls);
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_profile_end(
+    OrbitWarsCudaKernelTiming* out,
+    int32_t capacity,
+    int32_t* count);
 
 #ifdef __cplusplus
 }

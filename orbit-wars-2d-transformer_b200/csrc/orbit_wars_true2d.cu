@@ -478,6 +478,13 @@ struct Workspace {
   size_t idx_cap = 0;
   int* err = nullptr;
   cudaStream_t stream = nullptr;
+  // device timing (orbit_wars_cuda_true2d_profile_begin/_end): an event before
+  // each kernel of run_forward and one after the last, names[i] = the kernel
+  // launched after events[i] (nullptr for the closing event)
+  std::vector<cudaEvent_t> prof_events;
+  std::vector<const char*> prof_names;
+  size_t prof_used = 0;
+  bool prof_on = false;
 };
 
 Workspace& ws() {
@@ -553,17 +560,28 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
     didx = W.idx;
   }
   const int models = static_cast<int>(W.models);
-  const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n));
-  t2_expand_pre<true><<<g1, 256, 0, W.stream>>>(W.in, didx, W.weights, models, D, W.m, W.err);
-  T2_TRY(cudaGetLastError());
+  const bool prof = W.prof_on && W.prof_used + 4 <= W.prof_events.size();
+  auto mark = [&](const char* name) {
+    if (prof) {
+      cudaEventRecord(W.prof_events[W.prof_used], W.stream);
+      W.prof_names[W.prof_used++] = name;
+    }
+  };
   const size_t smem = L.cells * sizeof(float2);
   T2_TRY(cudaFuncSetAttribute(t2_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n));
+  mark("t2_expand_pre");
+  t2_expand_pre<true><<<g1, 256, 0, W.stream>>>(W.in, didx, W.weights, models, D, W.m, W.err);
+  T2_TRY(cudaGetLastError());
+  mark("t2_attention");
   t2_attention<<<static_cast<unsigned>(n), kAttnThreads, smem, W.stream>>>(didx, W.weights, models, D, W.m, W.err);
   T2_TRY(cudaGetLastError());
   const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
+  mark("t2_post_collapse");
   t2_post_collapse<true><<<g3, threads3, 0, W.stream>>>(didx, W.weights, models, D, W.m, W.out, W.err);
   T2_TRY(cudaGetLastError());
+  mark(nullptr);
   int herr = 0;
   T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
   T2_TRY(cudaMemcpyAsync(&herr, W.err, sizeof(int), cudaMemcpyDeviceToHost, W.stream));
@@ -778,6 +796,52 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(const float* input_ro
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   t2_post_collapse<false><<<g3, threads3, 0, s>>>(nullptr, weights, 1, D, m, output_rows, err);
   return from_cuda(cudaGetLastError());
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_profile_begin(int32_t max_calls) {
+  if (max_calls <= 0 || max_calls > 100000) return bad("max_calls must be in [1, 100000]");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  const size_t need = static_cast<size_t>(max_calls) * 4;
+  while (W.prof_events.size() < need) {
+    cudaEvent_t ev;
+    T2_TRY(cudaEventCreate(&ev));
+    W.prof_events.push_back(ev);
+  }
+  W.prof_names.assign(W.prof_events.size(), nullptr);
+  W.prof_used = 0;
+  W.prof_on = true;
+  return ok();
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_profile_end(OrbitWarsCudaKernelTiming* out, int32_t capacity,
+                                                       int32_t* count) {
+  if (count == nullptr || (out == nullptr && capacity > 0)) return bad("null argument");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  W.prof_on = false;
+  if (W.stream != nullptr) T2_TRY(cudaStreamSynchronize(W.stream));
+  int32_t n = 0;
+  for (size_t i = 0; i + 1 < W.prof_used; ++i) {
+    const char* name = W.prof_names[i];
+    if (name == nullptr) continue;  // closing event of a call: the next event opens another call
+    float ms = 0.0f;
+    T2_TRY(cudaEventElapsedTime(&ms, W.prof_events[i], W.prof_events[i + 1]));
+    int32_t k = 0;
+    while (k < n && std::strcmp(out[k].name, name) != 0) ++k;
+    if (k == n) {
+      if (n >= capacity) continue;
+      out[n].name = name;
+      out[n].launches = 0;
+      out[n].total_ms = 0.0f;
+      ++n;
+    }
+    out[k].launches += 1;
+    out[k].total_ms += ms;
+  }
+  *count = n;
+  W.prof_used = 0;
+  return ok();
 }
 
 }  // extern "C"

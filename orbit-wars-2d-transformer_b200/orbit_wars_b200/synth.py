@@ -16,6 +16,7 @@ ROW_FACTOR = 0x9E3779B97F4A7C15
 COL_FACTOR = 0xBF58476D1CE4E5B9
 MIX_FACTOR = 0x94D049BB133111EB
 TENSOR_FEATURES, TENSOR_COUNTS, TENSOR_ONEHOT, TENSOR_WEIGHTS = 1, 2, 3, 100
+TENSOR_TRUE2D_ROWS, TENSOR_TRUE2D_MODELS = 4, 5
 DEFAULT_SEED = 17
 
 
@@ -128,3 +129,29 @@ def split_weights(cfg: PolicyConfig, blob: np.ndarray) -> dict[str, np.ndarray]:
         out[name] = blob[at:at + n].reshape(shape)
         at += n
     return out
+
+
+# ---------------------------------------------------------------- True2D drop-in workloads
+
+def true2d_seeded(seed: int, count: int) -> np.ndarray:
+    """True2DTransformer::seeded (true2d_model.rs:159-169): weight[i] =
+    deterministic_weight(seed, 0, i) * 0.02, deterministic_weight(:653-663) =
+    mix / u64::MAX * 2 - 1 rounded to f32 as the reference does."""
+    x = u01(seed, 0, np.arange(count, dtype=np.uint64)).astype(np.float32)
+    return (x * np.float32(2.0) - np.float32(1.0)) * np.float32(0.02)
+
+
+def true2d_population(seed: int, models: int, count: int) -> np.ndarray:
+    """`models` seeded True2D models back to back (model k uses seed + k)."""
+    return np.concatenate([true2d_seeded(seed + k, count) for k in range(models)]) if models else \
+        np.zeros(0, np.float32)
+
+
+def true2d_requests(seed: int, requests: int, rows: int, models: int) -> tuple[np.ndarray, np.ndarray]:
+    """Engine-shaped request rows (requests x rows x 7, N(0,1)/2) and seeded
+    model indices uniform over the population."""
+    n = requests * rows * 7
+    x = (normal(seed, TENSOR_TRUE2D_ROWS, np.arange(n, dtype=np.uint64)) * 0.5).astype(np.float32)
+    idx = (u01(seed, TENSOR_TRUE2D_MODELS, np.arange(requests, dtype=np.uint64)) * models).astype(np.uintp)
+    return x, np.minimum(idx, models - 1).astype(np.uintp)
+

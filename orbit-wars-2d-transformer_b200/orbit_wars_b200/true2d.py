@@ -114,3 +114,15 @@ class CudaTrue2D:
         _lib.check("cuda_true2d_forward_many_resident", self.lib.orbit_wars_cuda_true2d_forward_many_resident(
             x.ctypes.data, idx.ctypes.data, out.ctypes.data, n, shape.c()))
         return unpack_outputs(out, n, shape)
+
+    def profile_begin(self, max_calls: int) -> None:
+        """Arms device timing of each kernel of the next `max_calls` forward calls."""
+        _lib.check("cuda_true2d_profile_begin", self.lib.orbit_wars_cuda_true2d_profile_begin(int(max_calls)))
+
+    def profile_end(self) -> dict:
+        """{kernel: (launches, total_ms)} over the calls since profile_begin."""
+        cap = 8
+        arr = (_lib.KernelTimingC * cap)()
+        n = C.c_int32(0)
+        _lib.check("cuda_true2d_profile_end", self.lib.orbit_wars_cuda_true2d_profile_end(arr, cap, C.byref(n)))
+        return {arr[i].name.decode(): (int(arr[i].launches), float(arr[i].total_ms)) for i in range(n.value)}

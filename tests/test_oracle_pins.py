@@ -73,3 +73,10 @@ def test_trainable_oracle_shape_and_range(oracle):
     x = np.sin(np.arange(1, 2 * rows * 2 + 1) * 0.7).astype(np.float32)
     out = oracle.trainable_forward(x, w, 2, layers, d, heads, rows)
     assert out.shape == (2 * rows * 2,) and np.all((out > 0) & (out < 1))
+
+
+def test_true2d_seeded_generator_matches_oracle(oracle):
+    """The package's numpy True2DTransformer::seeded (bench workload) is bit-exact with the oracle's C one."""
+    from orbit_wars_b200 import synth
+    for seed in (0, 17, 123456789):
+        assert np.array_equal(synth.true2d_seeded(seed, 50_000), oracle.true2d_seeded(seed, 50_000))

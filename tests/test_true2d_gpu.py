@@ -126,3 +126,19 @@ def test_matches_reference_gpu_build():
                                                                       out_ref.ctypes.data, 2, SHAPE.c()))
     ours = ow.CudaTrue2D().forward_packed(x, w1, 2, SHAPE).reshape(-1)
     assert np.abs(ours - out_ref).max() <= GATE
+
+
+def test_profile_counts_each_kernel():
+    """Device timing hooks: three kernels per call, every call counted."""
+    lib = ow.CudaTrue2D()
+    x = (np.sin(np.arange(3 * 64 * 7) * 0.3) * 0.5).astype(np.float32)
+    from orbit_wars_b200 import synth
+    w = synth.true2d_population(5, 2, SHAPE.parameter_count())
+    lib.upload_population(w, 3, SHAPE)
+    lib.profile_begin(4)
+    for _ in range(4):
+        lib.forward_population_resident_packed(x, np.array([0, 1, 1], np.uintp), 2, SHAPE)
+    prof = lib.profile_end()
+    assert set(prof) == {"t2_expand_pre", "t2_attention", "t2_post_collapse"}
+    assert all(n == 4 and ms > 0 for n, ms in prof.values())
+    assert lib.profile_end() == {}
