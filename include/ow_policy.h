@@ -119,6 +119,16 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
                           void* ln_out, int ln_mode, float* ln_scale, const float* a_scale, const float* b_scale,
                           void* stream);
 
+/* Test hook, not part of the forward: one launch of the fused feed-forward
+ * kernel on device buffers, as the bf16 forward issues it at d = 256:
+ * x[m, d] += GELU(ln . w1^T + b1) . w2^T + b2 (f32, in place), then
+ * ln_out = LayerNorm(x) * ln_g + ln_b (ln_mode 0 bf16, 2 f32). ln, w1 [f, d]
+ * and w2 [d, f] are bf16; f a multiple of 128, at most 1280. Synchronous on
+ * `stream`. */
+OwStatus ow_selftest_ffn(int m, int d, int f, const void* ln, const void* w1, const float* b1, const void* w2,
+                         const float* b2, float* x, const float* ln_g, const float* ln_b, void* ln_out, int ln_mode,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

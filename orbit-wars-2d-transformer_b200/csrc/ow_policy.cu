@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -21,6 +22,7 @@
 #include "ow_common.cuh"
 #include "ow_kernels.cuh"
 #include "ow_tc_gemm.cuh"
+#include "ow_tc_ffn.cuh"
 
 namespace {
 
@@ -202,6 +204,7 @@ struct OwPolicy {
     void *wqkv, *wo, *w1, *w2;      // f32 / bf16 / e4m3 [out, in]
     float *sqkv, *so, *s1, *s2;     // e4m3 per-output-channel scales
     CUtensorMap mqkv, mo, m1, m2;
+    CUtensorMap m1f, m2f;           // fused FFN: W1 / W2 in 128-row boxes
   };
   std::vector<LayerW> lw;
   float *we = nullptr, *be = nullptr, *lnfg = nullptr, *lnfb = nullptr, *wp = nullptr, *bp = nullptr,
@@ -223,6 +226,7 @@ struct OwPolicy {
   CUtensorMap e_qkv, e_h, e_x;         // epilogue outputs: qkv / h (bf16, 32-row boxes), x (f32)
   CUtensorMap e_ln, e_y;               // LayerNorm outputs: ln (bf16 or e4m3), y (f32, final LN)
   int qkv_block_n = 256;
+  bool fuse_ffn = false;  // ORBIT_WARS_FFN_FUSED=1 at create selects the fused FFN kernel (d = 256, bf16)
   int launches = 0;
   // profiling (ow_policy_profile_begin/_end)
   std::vector<cudaEvent_t> prof_events;
@@ -280,6 +284,23 @@ cudaError_t launch_gemm_resid_ln(const OwPolicy& P, const CUtensorMap& ma, const
   }
 }
 
+// The fused FFN kernel serves the bf16 path at d = 256 (its TMEM plan), f a
+// multiple of 128 with b1, b2, gamma and beta staged in shared memory.
+bool ffn_fused(const OwPolicy& P) {
+  const auto& c = P.cfg;
+  return P.fuse_ffn && c.precision == OW_PRECISION_BF16 && c.d_model == 256 && c.ffn % 128 == 0 &&
+         c.ffn + 3 * c.d_model <= TcFfnShape<256>::kParamFloats;
+}
+
+cudaError_t launch_ffn(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& m1, const CUtensorMap& m2,
+                       const CUtensorMap& mx, const CUtensorMap& ml, const TcGemmParams& prm) {
+  using S = TcFfnShape<256>;
+  const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM);
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
+  tc_ffn_kernel<256><<<grid, S::kThreads, S::kSmemBytes, P.stream>>>(ma, m1, m2, mx, ml, prm);
+  return cudaGetLastError();
+}
+
 cudaError_t set_all_gemm_attrs() {
   cudaError_t e = cudaSuccess;
   auto upd = [&e](cudaError_t r) {
@@ -295,6 +316,8 @@ cudaError_t set_all_gemm_attrs() {
   upd(set_gemm_attr<256, kEpiBias, true>());
   upd(set_gemm_attr<256, kEpiBiasGelu, true>());
   upd(set_gemm_attr<256, kEpiResidLn, true>());
+  upd(cudaFuncSetAttribute(tc_ffn_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TcFfnShape<256>::kSmemBytes));
   return e;
 }
 
@@ -584,6 +607,22 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       o.a_scale = P.attn_scale;
       o.b_scale = W.so;
       OW_STEP("gemm_out_resid_ln", launch_gemm_resid_ln(P, P.m_attn, W.mo, P.e_x, P.e_ln, o, fp8));
+      if (ffn_fused(P)) {
+        // FFN up + GELU + down + residual + next LN in one kernel
+        TcGemmParams w{};
+        w.m_valid = m_valid;
+        w.err = P.err;
+        w.n = f;
+        w.bias = W.b1;
+        w.bias2 = W.b2;
+        w.resid = static_cast<float*>(P.x);
+        w.ln_g = last ? P.lnfg : P.lw[l + 1].ln1g;
+        w.ln_b = last ? P.lnfb : P.lw[l + 1].ln1b;
+        w.ln_mode = last ? kLnF32 : kLnBf16;
+        w.ln_out = last ? P.y : P.ln;
+        OW_STEP("ffn_fused", launch_ffn(P, P.m_ln, W.m1f, W.m2f, P.e_x, last ? P.e_y : P.e_ln, w));
+        continue;
+      }
       // FFN up + GELU
       TcGemmParams u{};
       u.m_valid = m_valid;
@@ -761,6 +800,9 @@ OwStatus upload_weights(OwPolicy& P, const float* w) {
           !make_kmajor_map(&W.mo, W.wo, e4, d, d, d_rows) || !make_kmajor_map(&W.m1, W.w1, e4, d, f, 256u) ||
           !make_kmajor_map(&W.m2, W.w2, e4, f, d, d_rows))
         return st_rt("cuTensorMapEncodeTiled failed for a weight matrix");
+      if (ffn_fused(P) && (!make_kmajor_map(&W.m1f, W.w1, false, d, f, 128u) ||
+                           !make_kmajor_map(&W.m2f, W.w2, false, f, d, 128u)))
+        return st_rt("cuTensorMapEncodeTiled failed for an FFN weight matrix");
     }
   }
   return st_ok();
@@ -921,6 +963,10 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
   P->device = device;
   P->num_sms = prop.multiProcessorCount;
   P->qkv_block_n = (3 * config->d_model) % 256 == 0 ? 256 : 128;
+  {
+    const char* e = std::getenv("ORBIT_WARS_FFN_FUSED");
+    P->fuse_ffn = e != nullptr && e[0] == '1';
+  }
   if (stream != nullptr) {
     P->stream = static_cast<cudaStream_t>(stream);
   } else {
@@ -1145,10 +1191,60 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   return st_ok();
 }
 
+OwStatus ow_selftest_ffn(int m, int d, int f, const void* ln, const void* w1, const float* b1, const void* w2,
+                         const float* b2, float* x, const float* ln_g, const float* ln_b, void* ln_out, int ln_mode,
+                         void* stream) {
+  if (m <= 0 || d != 256 || f <= 0 || f % 128 != 0 || f + 3 * d > TcFfnShape<256>::kParamFloats)
+    return st_bad("fused FFN selftest needs d = 256 and f a multiple of 128 (f <= 1280)");
+  if (ln == nullptr || w1 == nullptr || b1 == nullptr || w2 == nullptr || b2 == nullptr || x == nullptr ||
+      ln_g == nullptr || ln_b == nullptr || ln_out == nullptr || (ln_mode != kLnBf16 && ln_mode != kLnF32))
+    return st_bad("bad fused FFN selftest args");
+  int dev = 0;
+  OW_TRY(cudaGetDevice(&dev));
+  OwPolicy P;
+  P.device = dev;
+  P.stream = static_cast<cudaStream_t>(stream);
+  P.cap_rows = static_cast<size_t>(m);
+  cudaDeviceProp prop{};
+  OW_TRY(cudaGetDeviceProperties(&prop, dev));
+  P.num_sms = prop.multiProcessorCount;
+  OW_TRY(set_all_gemm_attrs());
+  CUtensorMap ma, m1, m2, mx, ml;
+  if (!make_kmajor_map(&ma, ln, false, d, m, 128) || !make_kmajor_map(&m1, w1, false, d, f, 128) ||
+      !make_kmajor_map(&m2, w2, false, f, d, 128) || !make_map_128b(&mx, x, kMapF32, d, m, 32) ||
+      !make_ln_map(&ml, ln_out, ln_mode == kLnF32 ? kMapF32 : kMapBf16, d, m))
+    return st_rt("cuTensorMapEncodeTiled failed");
+  int* d_m = nullptr;
+  OW_TRY(cudaMalloc(&d_m, 2 * sizeof(int)));
+  int* d_err = d_m + 1;
+  const int host_m[2] = {m, 0};
+  cudaError_t e = cudaMemcpyAsync(d_m, host_m, sizeof(host_m), cudaMemcpyHostToDevice, P.stream);
+  TcGemmParams q{};
+  q.m_valid = d_m;
+  q.err = d_err;
+  q.n = f;
+  q.bias = b1;
+  q.bias2 = b2;
+  q.resid = x;
+  q.ln_g = ln_g;
+  q.ln_b = ln_b;
+  q.ln_out = ln_out;
+  q.ln_mode = ln_mode;
+  if (e == cudaSuccess) e = launch_ffn(P, ma, m1, m2, mx, ml, q);
+  int herr = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost, P.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(P.stream);
+  cudaFree(d_m);
+  if (e != cudaSuccess) return st_cuda(e);
+  if (herr != 0) return st_rt(device_error_message(herr));
+  return st_ok();
+}
+
 OwStatus ow_policy_launches_per_forward(const OwPolicy* policy, int32_t* launches) {
   if (policy == nullptr || launches == nullptr) return st_bad("null argument");
   const auto& c = policy->cfg;
   int per_layer = c.precision == OW_PRECISION_F32 ? 7 : (c.precision == OW_PRECISION_FP8 ? 7 : 5);
+  if (ffn_fused(*policy)) per_layer = 4;  // qkv, attention, out-proj, fused FFN
   *launches = 3 + per_layer * c.layers + (c.precision == OW_PRECISION_F32 ? 0 : 1);  // scan, embed, blocks, heads(+finalize)
   return st_ok();
 }

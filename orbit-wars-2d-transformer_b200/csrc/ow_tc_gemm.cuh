@@ -50,6 +50,7 @@ struct TcGemmParams {
   int n;               // output columns (multiple of BLOCK_N)
   int k_blocks;        // K / (128 bytes of elements)
   const float* bias;   // [n]
+  const float* bias2;  // fused FFN: b2 [d]
   __nv_bfloat16* out;  // kEpiBias / kEpiBiasGelu: [rows, ld_out]
   int ld_out;
   float* resid;           // kEpiResidLn: x [rows, n] f32, updated in place
@@ -125,6 +126,192 @@ __device__ __forceinline__ uint4* xpose_slot32(uint8_t* tile, int row, int chunk
   return reinterpret_cast<uint4*>(tile + row * 32 + ((chunk ^ ((row >> 2) & 1)) << 4));
 }
 
+// Rendezvous of the two epilogue warps that share a lane quadrant: all 64
+// threads arrive on the pair's mbarrier (count 64) and wait for the phase,
+// bounded like every other wait (an expired wait raises the abort flag and the
+// kernel runs out without further waiting).
+__device__ __forceinline__ void pair_sync(uint64_t* bar, uint32_t& phase, volatile int* abort, int* err) {
+  mbar_arrive(bar);
+  mbar_wait(bar, phase, abort, err);
+  phase ^= 1u;
+}
+
+// Residual add + LayerNorm over a full row (BLOCK_N == n == d) for one
+// epilogue warp: TMEM lanes of quadrant `quad`, columns [half*BLOCK_N/2, +BLOCK_N/2)
+// with half = ew / 4; the other half of each row is the epilogue warp ew ^ 4.
+// The caller has issued the residual loads of this warp's first NT chunks
+// (tile b <- columns cbase + b*32) on my_xbar[b]; bit b of xbits is that
+// barrier's phase parity. Pass 1: v = x + acc*s + bias,
+// written back to TMEM, shifted statistics per half; the halves' (mean, M2)
+// are merged exactly (Chan et al.) through `st` and the pair's mbarrier
+// (64 arrivals, bounded wait). Pass 2: x and the LN output leave by TMA
+// stores from the warp's staging tiles.
+template <int BLOCK_N, bool FP8, int NT>
+__device__ __forceinline__ void resid_ln_epilogue(uint32_t tbase, uint8_t* tiles, uint64_t* my_xbar, uint32_t& xbits,
+                                                  float4* st, const float* s_bias, const float* s_bscale,
+                                                  const float* s_g, const float* s_b, const CUtensorMap* map_o,
+                                                  const CUtensorMap* map_l, const TcGemmParams& p,
+                                                  volatile int* abort_flag, uint64_t* pair_bar, uint32_t& pair_phase,
+                                                  int ew, int quad, int lane, int row_base, int m, bool live,
+                                                  float a_s) {
+  constexpr int HW = BLOCK_N / 2;
+  constexpr int kChunks = HW / 32;
+  const int half = ew >> 2;
+  const int cbase = half * HW;
+  float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
+  bool ok = true;
+#pragma unroll 1
+  for (int c = 0; c < kChunks; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tbase + cbase + c * 32, r);
+    const int b = c % NT;
+    if (!mbar_wait(&my_xbar[b], (xbits >> b) & 1u, abort_flag, p.err)) ok = false;
+    xbits ^= 1u << b;
+    tmem_ld_wait();
+    float xv[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 t4 = *reinterpret_cast<const float4*>(xpose_slot(tiles + b * 4096, lane, q));
+      xv[4 * q] = t4.x;
+      xv[4 * q + 1] = t4.y;
+      xv[4 * q + 2] = t4.z;
+      xv[4 * q + 3] = t4.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const int col = cbase + c * 32 + i;
+      const float4 bv = *reinterpret_cast<const float4*>(s_bias + col);
+      float4 sv = make_float4(1.f, 1.f, 1.f, 1.f);
+      if (FP8) sv = *reinterpret_cast<const float4*>(s_bscale + col);
+      const float b4[4] = {bv.x, bv.y, bv.z, bv.w};
+      const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v = __uint_as_float(r[i + j]);
+        if (FP8) v *= a_s * s4[j];
+        v += b4[j] + xv[i + j];
+        if (c == 0 && i + j == 0) shift = v;
+        const float dv = v - shift;
+        s1 += dv;
+        s2 = fmaf(dv, dv, s2);
+        r[i + j] = __float_as_uint(v);
+      }
+    }
+    tmem_st32(tbase + cbase + c * 32, r);
+    // Refill staging tile b with chunk c + NT only now: the TMEM store consumes
+    // every value read from the tile, so those shared-memory reads have
+    // completed before the TMA write is issued (a write-after-read across
+    // proxies; issued right after the reads, the TMA data could land first
+    // while the tensor cores keep shared memory busy).
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && c + NT < kChunks && ok) {
+      mbar_arrive_expect_tx(&my_xbar[b], 4096);
+      tma_load_2d(tiles + b * 4096, map_o, &my_xbar[b], cbase + (c + NT) * 32, row_base);
+    }
+  }
+  tmem_st_wait();
+  // merge the two halves' statistics (same operation order in both warps)
+  const float mh = shift + s1 * (1.0f / HW);
+  const float m2h = fmaxf(s2 - s1 * s1 * (1.0f / HW), 0.0f);
+  st[ew * 32 + lane] = make_float4(mh, m2h, 0.0f, 0.0f);
+  pair_sync(pair_bar, pair_phase, abort_flag, p.err);
+  const float4 lo = st[(ew & 3) * 32 + lane];  // the pair: epilogue warps ew & 3 (half 0) and +4 (half 1)
+  const float4 hi = st[((ew & 3) + 4) * 32 + lane];
+  const float delta = hi.x - lo.x;
+  const float mean = 0.5f * (lo.x + hi.x);
+  const float var = (lo.y + hi.y + delta * delta * (0.25f * BLOCK_N)) * (1.0f / BLOCK_N);
+  const float rstd = rsqrtf(var + 1e-5f);
+  float inv_scale = 1.0f;
+  if (p.ln_mode == kLnE4m3) {
+    float amax = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < kChunks; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tbase + cbase + c * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int col = cbase + c * 32 + i;
+        const float y = (__uint_as_float(r[i]) - mean) * rstd * s_g[col] + s_b[col];
+        amax = fmaxf(amax, fabsf(y));
+      }
+    }
+    st[ew * 32 + lane].z = amax;
+    pair_sync(pair_bar, pair_phase, abort_flag, p.err);
+    amax = fmaxf(st[(ew & 3) * 32 + lane].z, st[((ew & 3) + 4) * 32 + lane].z);
+    const float scale = amax > 0.0f ? amax * (1.0f / 448.0f) : 1.0f;
+    inv_scale = 1.0f / scale;
+    if (live && half == 0) p.ln_scale[m] = scale;
+  }
+#pragma unroll 1
+  for (int c = 0; c < kChunks; ++c) {
+    const int col0 = cbase + c * 32;
+    uint32_t r[32];
+    tmem_ld32(tbase + col0, r);
+    // x (f32, 128 B box rows): the tile's previous store must have read it
+    uint8_t* xt = tiles + 0;
+    uint8_t* lt = tiles + (NT - 1) * 4096;
+    if (lane == 0) {
+      if (NT == 2) bulk_wait_read<1>();
+      else bulk_wait_read<0>();
+    }
+    tmem_ld_wait();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 8; ++q) *xpose_slot(xt, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map_o, xt, col0, row_base);
+      bulk_commit();
+    }
+    float y[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 gv = *reinterpret_cast<const float4*>(s_g + col0 + i);
+      const float4 bv = *reinterpret_cast<const float4*>(s_b + col0 + i);
+      y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
+      y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
+      y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
+      y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
+    }
+    // LN output: 32 columns = one 32 x (32*elt) B box in the matching swizzle
+    if (lane == 0) {
+      if (NT == 2) bulk_wait_read<1>();
+      else bulk_wait_read<0>();
+    }
+    __syncwarp();
+    if (p.ln_mode == kLnE4m3) {
+      uint32_t q8[8];
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
+                                y[i + 3] * inv_scale);
+      *xpose_slot32(lt, lane, 0) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+      *xpose_slot32(lt, lane, 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
+    } else if (p.ln_mode == kLnF32) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *xpose_slot(lt, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
+                                              __float_as_uint(y[4 * q + 2]), __float_as_uint(y[4 * q + 3]));
+    } else {
+      uint32_t yo[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *xpose_slot64(lt, lane, q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map_l, lt, col0, row_base);
+      bulk_commit();
+    }
+  }
+}
+
 template <int BLOCK_N, int EPI, bool FP8>
 __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
@@ -144,7 +331,8 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
   uint64_t* tfull = empty + S::kStages;
   uint64_t* tempty = tfull + S::kAcc;
   uint64_t* xbar = tempty + S::kAcc;  // residual loads: one barrier per staging tile of each epilogue warp
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xbar + S::kTilesPerWarp * kEpiWarps);
+  uint64_t* pair_bar = xbar + S::kTilesPerWarp * kEpiWarps;  // LayerNorm: one per lane quadrant (64 arrivals)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pair_bar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* s_par = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + S::kBarrierBytes);
   float4* s_stats = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(s_par) + S::kParamBytes);
@@ -172,6 +360,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       mbar_init(&tempty[a], kEpiWarps);
     }
     for (int i = 0; i < S::kTilesPerWarp * kEpiWarps; ++i) mbar_init(&xbar[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -276,7 +465,8 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     constexpr int kCols = EPI == kEpiResidLn ? BLOCK_N : BLOCK_N * 4 / kEpiWarps;  // columns this warp drains
     const int col0 = EPI == kEpiResidLn ? 0 : (ew / 4) * kCols;  // warps ew, ew+4, ... share a lane quadrant
     uint64_t* my_xbar = xbar + S::kTilesPerWarp * ew;
-    uint32_t xphase[2] = {0u, 0u};
+    uint32_t xbits = 0u;  // residual-load barrier parities, bit b = staging tile b
+    uint32_t pair_phase = 0u;
     int stat_par = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -353,168 +543,11 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           ++out_k;
         }
       } else if (any) {
-        // Residual add + LayerNorm over the full row (BLOCK_N == n == d). The
-        // two warps of a lane quadrant split the row (half = ew / 4). Pass 1:
-        // v = x + acc*s + bias (residual chunks arrive by TMA, issued before
-        // this tile's accumulator was ready), written back to TMEM, shifted
-        // statistics per half; the halves' (mean, M2) are merged exactly
-        // (Chan et al.) through shared memory. Pass 2: x and the LN output
-        // leave by TMA stores, alternating between the warp's staging tiles.
-        constexpr int HW = BLOCK_N / 2;
-        constexpr int kChunks = HW / 32;
-        constexpr int NT = S::kTilesPerWarp;
-        const int half = ew >> 2;
-        const int cbase = half * HW;
-        float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
-        bool ok = true;
-#pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + cbase + c * 32, r);
-          const int b = c % NT;
-          if (!mbar_wait(&my_xbar[b], xphase[b], abort_flag, p.err)) ok = false;
-          xphase[b] ^= 1u;
-          tmem_ld_wait();
-          float xv[32];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 t4 = *reinterpret_cast<const float4*>(xpose_slot(tiles + b * 4096, lane, q));
-            xv[4 * q] = t4.x;
-            xv[4 * q + 1] = t4.y;
-            xv[4 * q + 2] = t4.z;
-            xv[4 * q + 3] = t4.w;
-          }
-          __syncwarp();
-          if (lane == 0 && c + NT < kChunks && ok) {
-            mbar_arrive_expect_tx(&my_xbar[b], 4096);
-            tma_load_2d(tiles + b * 4096, &map_o, &my_xbar[b], cbase + (c + NT) * 32, row_base);
-          }
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const int col = cbase + c * 32 + i;
-            const float4 bv = *reinterpret_cast<const float4*>(s_bias + col);
-            float4 sv = make_float4(1.f, 1.f, 1.f, 1.f);
-            if (FP8) sv = *reinterpret_cast<const float4*>(s_bscale + col);
-            const float b4[4] = {bv.x, bv.y, bv.z, bv.w};
-            const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float v = __uint_as_float(r[i + j]);
-              if (FP8) v *= a_s * s4[j];
-              v += b4[j] + xv[i + j];
-              if (c == 0 && i + j == 0) shift = v;
-              const float dv = v - shift;
-              s1 += dv;
-              s2 = fmaf(dv, dv, s2);
-              r[i + j] = __float_as_uint(v);
-            }
-          }
-          tmem_st32(tbase + cbase + c * 32, r);
-        }
-        tmem_st_wait();
-        // merge the two halves' statistics (same operation order in both warps)
-        const float mh = shift + s1 * (1.0f / HW);
-        const float m2h = fmaxf(s2 - s1 * s1 * (1.0f / HW), 0.0f);
-        float4* st = s_stats + (stat_par * 8) * 32;
-        st[ew * 32 + lane] = make_float4(mh, m2h, 0.0f, 0.0f);
-        asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
-        const float4 lo = st[(ew & 3) * 32 + lane];  // the pair: epilogue warps ew & 3 (half 0) and +4 (half 1)
-        const float4 hi = st[((ew & 3) + 4) * 32 + lane];
-        const float delta = hi.x - lo.x;
-        const float mean = 0.5f * (lo.x + hi.x);
-        const float var = (lo.y + hi.y + delta * delta * (0.25f * BLOCK_N)) * (1.0f / BLOCK_N);
-        const float rstd = rsqrtf(var + 1e-5f);
-        float inv_scale = 1.0f;
-        if (p.ln_mode == kLnE4m3) {
-          float amax = 0.0f;
-#pragma unroll 1
-          for (int c = 0; c < kChunks; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tbase + cbase + c * 32, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int col = cbase + c * 32 + i;
-              const float y = (__uint_as_float(r[i]) - mean) * rstd * s_g[col] + s_b[col];
-              amax = fmaxf(amax, fabsf(y));
-            }
-          }
-          st[ew * 32 + lane].z = amax;
-          asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
-          amax = fmaxf(st[(ew & 3) * 32 + lane].z, st[((ew & 3) + 4) * 32 + lane].z);
-          const float scale = amax > 0.0f ? amax * (1.0f / 448.0f) : 1.0f;
-          inv_scale = 1.0f / scale;
-          if (live && half == 0) p.ln_scale[m] = scale;
-        }
+        resid_ln_epilogue<BLOCK_N, FP8, S::kTilesPerWarp>(tbase, tiles, my_xbar, xbits, s_stats + (stat_par * 8) * 32,
+                                                          s_bias, s_bscale, s_g, s_b, &map_o, &map_l, p, abort_flag,
+                                                          &pair_bar[quad], pair_phase, ew, quad, lane, row_base, m,
+                                                          live, a_s);
         stat_par ^= 1;
-        const int ln_elt = p.ln_mode == kLnF32 ? 4 : (p.ln_mode == kLnE4m3 ? 1 : 2);
-#pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
-          const int col0 = cbase + c * 32;
-          uint32_t r[32];
-          tmem_ld32(tbase + col0, r);
-          // x (f32, 128 B box rows): the tile's previous store must have read it
-          uint8_t* xt = tiles + 0;
-          uint8_t* lt = tiles + (NT - 1) * 4096;
-          if (lane == 0) {
-            if (NT == 2) bulk_wait_read<1>();
-            else bulk_wait_read<0>();
-          }
-          tmem_ld_wait();
-          __syncwarp();
-#pragma unroll
-          for (int q = 0; q < 8; ++q) *xpose_slot(xt, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&map_o, xt, col0, row_base);
-            bulk_commit();
-          }
-          float y[32];
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float4 gv = *reinterpret_cast<const float4*>(s_g + col0 + i);
-            const float4 bv = *reinterpret_cast<const float4*>(s_b + col0 + i);
-            y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
-            y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
-            y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
-            y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
-          }
-          // LN output: 32 columns = one 32 x (32*elt) B box in the matching swizzle
-          if (lane == 0) {
-            if (NT == 2) bulk_wait_read<1>();
-            else bulk_wait_read<0>();
-          }
-          __syncwarp();
-          if (p.ln_mode == kLnE4m3) {
-            uint32_t q8[8];
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
-                                      y[i + 3] * inv_scale);
-            *xpose_slot32(lt, lane, 0) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
-            *xpose_slot32(lt, lane, 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
-          } else if (p.ln_mode == kLnF32) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              *xpose_slot(lt, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
-                                                    __float_as_uint(y[4 * q + 2]), __float_as_uint(y[4 * q + 3]));
-          } else {
-            uint32_t yo[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              *xpose_slot64(lt, lane, q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&map_l, lt, col0, row_base);
-            bulk_commit();
-          }
-        }
-        (void)ln_elt;
       }
       tc_fence_before();
       __syncwarp();

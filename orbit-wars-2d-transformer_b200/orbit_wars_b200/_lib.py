@@ -72,6 +72,7 @@ SIGNATURES = {
     "ow_policy_destroy": (None, [P]),
     "ow_selftest_gemm": (Status, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, C.c_int, P, P,
                                   P, P]),
+    "ow_selftest_ffn": (Status, [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, P, C.c_int, P]),
     # include/orbit_wars_cuda.h
     "orbit_wars_cuda_status": (Status, []),
     "orbit_wars_cuda_encode_identity_batch": (Status, [P, P, SZ, SZ, SZ]),

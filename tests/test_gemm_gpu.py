@@ -129,3 +129,61 @@ def test_bf16_repeatable(epi, n):
     call(BF16, epi, m, n, k, a, w, bias, out=o2)
     bad = torch.nonzero(o1.view(torch.int16) != o2.view(torch.int16))
     assert bad.shape[0] == 0, f"{bad.shape[0]} differing elements, first {bad[:4].tolist()}"
+
+
+def test_bf16_resid_ln_repeatable_many_tiles():
+    """The LayerNorm epilogue at 315 row tiles (several per CTA) repeats bit for bit:
+    its staging tiles are refilled only after every value read from them is consumed."""
+    m, n, k = 40271, 256, 1024
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") / 32).bfloat16()
+    bias = torch.randn(n, device="cuda") * 0.1
+    resid0 = torch.randn(m, n, device="cuda")
+    gam = 1 + 0.1 * torch.randn(n, device="cuda")
+    bet = 0.1 * torch.randn(n, device="cuda")
+    outs = []
+    for _ in range(2):
+        resid = resid0.clone()
+        ln_out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        call(BF16, EPI_LN, m, n, k, a, w, bias, resid=resid, g=gam, b=bet, ln_out=ln_out, ln_mode=LN_BF16)
+        outs.append((resid, ln_out))
+    x_ref = resid0 + a.float() @ w.float().T + bias
+    close(outs[0][0], x_ref, 1e-4, "x")
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def ffn_call(m, f, ln, w1, b1, w2, b2, x, g, b, ln_out, ln_mode):
+    lib = _lib.load_library()
+    p = _lib.ptr
+    st = lib.ow_selftest_ffn(m, 256, f, p(ln), p(w1), p(b1), p(w2), p(b2), p(x), p(g), p(b), p(ln_out), ln_mode,
+                             torch.cuda.current_stream().cuda_stream)
+    _lib.check("ow_selftest_ffn", st)
+
+
+@pytest.mark.parametrize("m,f,ln_mode", [(77, 1024, LN_BF16), (5000, 512, LN_F32), (40271, 1024, LN_BF16)])
+def test_fused_ffn(m, f, ln_mode):
+    """Fused up-projection + GELU + down-projection + residual + LayerNorm (d = 256)
+    against the same op in PyTorch fp32 with the hidden layer rounded to bf16 as
+    the kernel keeps it; 40,271 rows = 315 tiles, several per CTA; repeats bit for bit."""
+    d = 256
+    g = torch.Generator(device="cuda").manual_seed(m + f)
+    ln = torch.randn(m, d, device="cuda", generator=g).bfloat16()
+    w1 = (torch.randn(f, d, device="cuda", generator=g) * 0.06).bfloat16()
+    w2 = (torch.randn(d, f, device="cuda", generator=g) * 0.03).bfloat16()
+    b1 = torch.randn(f, device="cuda", generator=g) * 0.1
+    b2 = torch.randn(d, device="cuda", generator=g) * 0.1
+    x0 = torch.randn(m, d, device="cuda", generator=g)
+    gam = 1 + 0.1 * torch.randn(d, device="cuda", generator=g)
+    bet = 0.1 * torch.randn(d, device="cuda", generator=g)
+    outs = []
+    for _ in range(2):
+        x = x0.clone()
+        lo = torch.empty(m, d, device="cuda", dtype=torch.bfloat16 if ln_mode == LN_BF16 else torch.float32)
+        ffn_call(m, f, ln, w1, b1, w2, b2, x, gam, bet, lo, ln_mode)
+        outs.append((x, lo))
+    h = torch.nn.functional.gelu(ln.float() @ w1.float().T + b1).bfloat16().float()
+    x_ref = x0 + h @ w2.float().T + b2
+    close(outs[0][0], x_ref, 2e-3, "x")
+    y_ref = torch.nn.functional.layer_norm(x_ref, (d,), gam, bet, eps=1e-5)
+    close(outs[0][1], y_ref, 8e-3 if ln_mode == LN_BF16 else 2e-3, "ln")
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])

@@ -172,3 +172,27 @@ def test_device_side_bad_count_reports_runtime_error():
             pol.synchronize()
         assert e.value.code == 2
         pol.synchronize()  # error word cleared; handle usable
+
+
+def test_fused_ffn_matches_two_kernel_path(monkeypatch):
+    """Config-2 full batch (315 row tiles, several per CTA): the fused FFN kernel
+    (ORBIT_WARS_FFN_FUSED=1) against the default up-projection + down-projection
+    kernels. Each CTA starts the hidden-chunk walk at its own chunk, so the
+    down-projection sums the same terms in another order: outputs agree to f32
+    rounding, far inside the bf16 tolerance, and each path repeats bit for bit."""
+    cfg = ow.preset(2)
+    w = ow.make_weights(cfg, seed=17)
+    feats, counts = ow.make_inputs(cfg, seed=17)
+    with ow.EncoderPolicy(cfg, w) as pol:
+        two = pol.forward(feats, counts)
+        assert pol.launches_per_forward() == 3 + 5 * cfg.layers + 1
+    monkeypatch.setenv("ORBIT_WARS_FFN_FUSED", "1")
+    with ow.EncoderPolicy(cfg, w) as pol:
+        fused = pol.forward(feats, counts)
+        again = pol.forward(feats, counts)
+        assert pol.launches_per_forward() == 3 + 4 * cfg.layers + 1
+    for a, b in zip(fused, again):
+        assert np.array_equal(a, b)
+    m = valid_mask(counts, cfg.n_entities)
+    assert rel_err(fused[0][m], two[0][m]) <= 1e-2 and rel_err(fused[1], two[1]) <= 1e-2
+    assert float((fused[2][m] == two[2][m]).mean()) >= 0.99
