@@ -84,6 +84,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// griddepcontrol.wait blocks until the kernel launched before this one on the
+// stream has completed and its memory writes are visible; a kernel launched
+// with programmatic stream serialization may start while its predecessor is
+// still running, so everything it reads from that kernel (and, transitively,
+// from earlier ones) comes after this wait. launch_dependents allows the next
+// such kernel to start launching its CTAs. Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

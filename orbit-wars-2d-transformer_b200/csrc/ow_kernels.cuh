@@ -62,6 +62,7 @@ __global__ void __launch_bounds__(1024) scan_counts_kernel(const int* counts, in
       offsets[b + 1] = run;
     }
   }
+  pdl_trigger();  // the next kernel on the stream may start launching
 }
 
 // ------------------------------------------------------------------ embedding (+ first LayerNorm)
@@ -411,6 +412,7 @@ __global__ void __launch_bounds__(256) attention_bf16_kernel(const __nv_bfloat16
   __nv_bfloat16* sq = s_qkv;
   __nv_bfloat16* sk = s_qkv + NMAX * PITCH;
   __nv_bfloat16* sv = s_qkv + 2 * NMAX * PITCH;
+  pdl_wait();  // q, k, v come from the projection launched before
   const int b = blockIdx.x, hg = blockIdx.y;
   const int row0 = offsets[b];
   const int cnt = offsets[b + 1] - row0;
@@ -453,6 +455,7 @@ __global__ void __launch_bounds__(256) attention_bf16_kernel(const __nv_bfloat16
       default: if (NMAX >= 128) attention_task<(NMAX >= 128 ? 8 : 1), PITCH>(sq, sk, sv, hc, q0, cnt, lane, scale_log2, out_row0, d, oc); break;
     }
   }
+  pdl_trigger();  // the next kernel on the stream may start launching
 }
 
 // ------------------------------------------------------------------ embedding on tensor cores
@@ -509,6 +512,7 @@ __global__ void __launch_bounds__(128) embed_mma_kernel(const float* __restrict_
       if (i < kVec) reinterpret_cast<float4*>(s_vec)[i] = u[k];
     }
   }
+  pdl_wait();  // weights above are constant; offsets and features come from earlier work
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, t = lane & 3;
@@ -647,6 +651,7 @@ __global__ void __launch_bounds__(128) embed_mma_kernel(const float* __restrict_
       }
     }
   }
+  pdl_trigger();  // the next kernel on the stream may start launching
 }
 
 // ------------------------------------------------------------------ e4m3 quantiser (fp8 path)
@@ -654,6 +659,7 @@ __global__ void __launch_bounds__(128) embed_mma_kernel(const float* __restrict_
 __global__ void __launch_bounds__(256) quantize_rows_e4m3_kernel(const __nv_bfloat16* __restrict__ in,
                                                                  const int* __restrict__ m_valid, int k,
                                                                  uint8_t* __restrict__ out, float* __restrict__ scale) {
+  pdl_wait();  // the rows come from the kernel launched before
   const int lane = threadIdx.x & 31;
   const int rows = *m_valid;
   for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += gridDim.x * (blockDim.x >> 5)) {
@@ -678,6 +684,7 @@ __global__ void __launch_bounds__(256) quantize_rows_e4m3_kernel(const __nv_bflo
       *reinterpret_cast<uint2*>(out + static_cast<size_t>(row) * k + c) = o;
     }
   }
+  pdl_trigger();  // the next kernel on the stream may start launching
 }
 
 // ------------------------------------------------------------------ heads
@@ -888,6 +895,7 @@ __global__ void __launch_bounds__(128) heads_mma_kernel(const float* __restrict_
     else if (n == n_actions) v = w_v[k];
     s_wh[n * WPITCH + k] = v;
   }
+  pdl_wait();  // the head weights above are constant; y comes from the last block
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -973,6 +981,7 @@ __global__ void __launch_bounds__(128) heads_mma_kernel(const float* __restrict_
       if (t == 0 && live) actions[slot] = besti;
     }
   }
+  pdl_trigger();  // the next kernel on the stream may start launching
 }
 
 // Per state: value = b_v + mean over its rows of sval; padded entity slots
@@ -982,6 +991,7 @@ __global__ void state_finalize_kernel(const int* __restrict__ offsets, int n_ent
                                       const float* __restrict__ sval, const float* __restrict__ b_v,
                                       void* __restrict__ logits, void* __restrict__ value,
                                       int* __restrict__ actions) {
+  pdl_wait();  // sval comes from the heads kernel
   __shared__ float s_red[4];
   const int b = blockIdx.x, j = threadIdx.x;
   const int row0 = offsets[b];

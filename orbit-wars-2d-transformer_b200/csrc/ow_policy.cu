@@ -226,6 +226,7 @@ struct OwPolicy {
   CUtensorMap e_qkv, e_h, e_x;         // epilogue outputs: qkv / h (bf16, 32-row boxes), x (f32)
   CUtensorMap e_ln, e_y;               // LayerNorm outputs: ln (bf16 or e4m3), y (f32, final LN)
   int qkv_block_n = 256;
+  bool pdl = false;       // tensor-core path: programmatic dependent launches (ORBIT_WARS_PDL=0 turns them off)
   bool fuse_ffn = false;  // ORBIT_WARS_FFN_FUSED=1 at create selects the fused FFN kernel (d = 256, bf16)
   int launches = 0;
   // profiling (ow_policy_profile_begin/_end)
@@ -254,6 +255,25 @@ class DeviceGuard {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Launches `kernel` on P's stream. With P.pdl the launch is a programmatic
+// dependent launch: the kernel may start (and run its weight-only prologue)
+// while the previous kernel finishes; its pdl_wait() orders every read of
+// earlier results. Only kernels that call pdl_wait() are launched this way.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(const OwPolicy& P, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = P.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = P.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <int BN, int EPI, bool FP8>
 cudaError_t set_gemm_attr() {
   return cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -267,8 +287,7 @@ cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensor
   const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM) * (prm.n / BN);
   const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
   if (prm.n * ((FP8 ? 2 : 1) + (EPI == kEpiResidLn ? 2 : 0)) > S::kParamFloats) return cudaErrorInvalidValue;
-  tc_gemm_kernel<BN, EPI, FP8><<<grid, EpiWarps<EPI>::kThreads, S::kSmemBytes, P.stream>>>(ma, mw, mo, ml, prm);
-  return cudaGetLastError();
+  return launch_k(P, tc_gemm_kernel<BN, EPI, FP8>, grid, EpiWarps<EPI>::kThreads, S::kSmemBytes, ma, mw, mo, ml, prm);
 }
 
 // Dispatch on the d-wide LN-fused tile.
@@ -297,8 +316,7 @@ cudaError_t launch_ffn(const OwPolicy& P, const CUtensorMap& ma, const CUtensorM
   using S = TcFfnShape<256>;
   const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM);
   const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
-  tc_ffn_kernel<256><<<grid, S::kThreads, S::kSmemBytes, P.stream>>>(ma, m1, m2, mx, ml, prm);
-  return cudaGetLastError();
+  return launch_k(P, tc_ffn_kernel<256>, grid, S::kThreads, S::kSmemBytes, ma, m1, m2, mx, ml, prm);
 }
 
 cudaError_t set_all_gemm_attrs() {
@@ -342,13 +360,17 @@ cudaError_t launch_embed(const OwPolicy& P, int batch) {
     if (c.precision == OW_PRECISION_BF16) {
       auto k = embed_mma_kernel<D, 1>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
-      k<<<eg, 128, esmem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we16, P.be, g, b,
-                                      static_cast<float*>(P.x), P.ln, nullptr, P.row_slot);
+      return launch_k(P, k, eg, 128, esmem, static_cast<const float*>(P.feats), static_cast<const int*>(P.offsets),
+                      batch, c.n_entities, c.features, static_cast<const __nv_bfloat16*>(P.we16),
+                      static_cast<const float*>(P.be), g, b, static_cast<float*>(P.x), static_cast<void*>(P.ln),
+                      static_cast<float*>(nullptr), P.row_slot);
     } else {
       auto k = embed_mma_kernel<D, 2>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
-      k<<<eg, 128, esmem, P.stream>>>(P.feats, P.offsets, batch, c.n_entities, c.features, P.we16, P.be, g, b,
-                                      static_cast<float*>(P.x), P.ln8, P.ln_scale, P.row_slot);
+      return launch_k(P, k, eg, 128, esmem, static_cast<const float*>(P.feats), static_cast<const int*>(P.offsets),
+                      batch, c.n_entities, c.features, static_cast<const __nv_bfloat16*>(P.we16),
+                      static_cast<const float*>(P.be), g, b, static_cast<float*>(P.x), static_cast<void*>(P.ln8),
+                      P.ln_scale, P.row_slot);
     }
   }
   return cudaGetLastError();
@@ -376,16 +398,17 @@ void heads_dtype(const OwPolicy& P, int batch, uint64_t seed, void* logits, void
 }
 
 template <int D, int NTILE, bool LB>
-void heads_mma_launch(const OwPolicy& P, int batch, uint64_t seed, void* logits, int* actions) {
+cudaError_t heads_mma_launch(const OwPolicy& P, int batch, uint64_t seed, void* logits, int* actions) {
   const auto& c = P.cfg;
   const size_t smem = static_cast<size_t>(NTILE) * 8 * (D + 16) * sizeof(float);
   cudaFuncSetAttribute(heads_mma_kernel<D, NTILE, LB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
   const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((P.cap_rows + 63) / 64,
                                                                          static_cast<size_t>(P.num_sms) * 4)));
-  heads_mma_kernel<D, NTILE, LB><<<grid, 128, smem, P.stream>>>(static_cast<const float*>(P.y), P.offsets, batch,
-                                                                c.n_entities, c.actions, P.row_slot, P.wp, P.bp,
-                                                                P.wv, c.sample_actions, seed, logits, actions, P.sval);
+  return launch_k(P, heads_mma_kernel<D, NTILE, LB>, grid, 128, smem, static_cast<const float*>(P.y),
+           static_cast<const int*>(P.offsets), batch, c.n_entities, c.actions, static_cast<const int*>(P.row_slot),
+           static_cast<const float*>(P.wp), static_cast<const float*>(P.bp), static_cast<const float*>(P.wv),
+           c.sample_actions, seed, logits, actions, P.sval);
 }
 
 template <int D>
@@ -393,26 +416,26 @@ cudaError_t launch_heads_tc(const OwPolicy& P, int batch, uint64_t seed, void* l
   const int a = P.cfg.actions;
   const bool lb = P.cfg.logits_dtype == OW_DTYPE_BF16;
   // 8-column tiles covering the P logits plus the value column
-  if (a < 8) lb ? heads_mma_launch<D, 1, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 1, false>(P, batch, seed, logits, actions);
-  else if (a < 16) lb ? heads_mma_launch<D, 2, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 2, false>(P, batch, seed, logits, actions);
-  else if (a < 24) lb ? heads_mma_launch<D, 3, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 3, false>(P, batch, seed, logits, actions);
-  else if (a < 32) lb ? heads_mma_launch<D, 4, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 4, false>(P, batch, seed, logits, actions);
-  else lb ? heads_mma_launch<D, 5, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 5, false>(P, batch, seed, logits, actions);
-  return cudaGetLastError();
+  if (a < 8) return lb ? heads_mma_launch<D, 1, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 1, false>(P, batch, seed, logits, actions);
+  if (a < 16) return lb ? heads_mma_launch<D, 2, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 2, false>(P, batch, seed, logits, actions);
+  if (a < 24) return lb ? heads_mma_launch<D, 3, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 3, false>(P, batch, seed, logits, actions);
+  if (a < 32) return lb ? heads_mma_launch<D, 4, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 4, false>(P, batch, seed, logits, actions);
+  return lb ? heads_mma_launch<D, 5, true>(P, batch, seed, logits, actions) : heads_mma_launch<D, 5, false>(P, batch, seed, logits, actions);
 }
 
 cudaError_t launch_finalize(const OwPolicy& P, int batch, void* logits, void* value, int* actions) {
   const auto& c = P.cfg;
   const int threads = (c.n_entities + 31) / 32 * 32;
   const bool lb = c.logits_dtype == OW_DTYPE_BF16, vb = c.value_dtype == OW_DTYPE_BF16;
-#define OW_FIN(LB, VB) \
-  state_finalize_kernel<LB, VB><<<batch, threads, 0, P.stream>>>(P.offsets, c.n_entities, c.actions, P.sval, P.bv, logits, value, actions)
+#define OW_FIN(LB, VB)                                                                                      \
+  return launch_k(P, state_finalize_kernel<LB, VB>, batch, threads, 0, static_cast<const int*>(P.offsets),  \
+                  c.n_entities, c.actions, static_cast<const float*>(P.sval), static_cast<const float*>(P.bv), \
+                  logits, value, actions)
   if (lb && vb) OW_FIN(true, true);
-  else if (lb) OW_FIN(true, false);
-  else if (vb) OW_FIN(false, true);
-  else OW_FIN(false, false);
+  if (lb) OW_FIN(true, false);
+  if (vb) OW_FIN(false, true);
+  OW_FIN(false, false);
 #undef OW_FIN
-  return cudaGetLastError();
 }
 
 template <int DPL>
@@ -490,11 +513,13 @@ cudaError_t launch_attention(const OwPolicy& P, int batch) {
     while (hg > 1 && (c.heads % hg != 0 || 3 * nmax * (hg * 32 + 8) * 2 > 112 * 1024)) hg /= 2;
     const dim3 g2(batch, c.heads / hg);
     const size_t smem = static_cast<size_t>(3) * nmax * (hg * 32 + 8) * 2;
+    cudaError_t e = cudaSuccess;
 #define OW_ATTN(NM, HGV)                                                                                   \
   do {                                                                                                     \
     cudaFuncSetAttribute(attention_bf16_kernel<NM, HGV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                          static_cast<int>(smem));                                                          \
-    attention_bf16_kernel<NM, HGV><<<g2, 256, smem, P.stream>>>(q, o, P.offsets, c.d_model, sl2);          \
+    e = launch_k(P, attention_bf16_kernel<NM, HGV>, g2, 256, smem, q, o,                                 \
+                 static_cast<const int*>(P.offsets), c.d_model, sl2);                                     \
   } while (0)
 #define OW_ATTN_HG(NM)              \
   do {                              \
@@ -509,6 +534,7 @@ cudaError_t launch_attention(const OwPolicy& P, int batch) {
     else OW_ATTN_HG(128);
 #undef OW_ATTN_HG
 #undef OW_ATTN
+    if (e != cudaSuccess) return e;
   }
   return cudaGetLastError();
 }
@@ -516,9 +542,8 @@ cudaError_t launch_attention(const OwPolicy& P, int batch) {
 cudaError_t launch_quantize(const OwPolicy& P, const int* m_valid, const void* in, int k, uint8_t* out,
                             float* scale) {
   const int grid = static_cast<int>(std::min<size_t>((P.cap_rows + 7) / 8, static_cast<size_t>(P.num_sms) * 8));
-  quantize_rows_e4m3_kernel<<<grid, 256, 0, P.stream>>>(static_cast<const __nv_bfloat16*>(in), m_valid, k, out,
-                                                       scale);
-  return cudaGetLastError();
+  return launch_k(P, quantize_rows_e4m3_kernel, grid, 256, 0, static_cast<const __nv_bfloat16*>(in), m_valid, k,
+                  out, scale);
 }
 
 // m_valid lives at offsets[batch]: the kernels read it from there.
@@ -966,6 +991,8 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
   {
     const char* e = std::getenv("ORBIT_WARS_FFN_FUSED");
     P->fuse_ffn = e != nullptr && e[0] == '1';
+    const char* q = std::getenv("ORBIT_WARS_PDL");
+    P->pdl = config->precision != OW_PRECISION_F32 && !(q != nullptr && q[0] == '0');
   }
   if (stream != nullptr) {
     P->stream = static_cast<cudaStream_t>(stream);

@@ -100,8 +100,6 @@ __global__ void __launch_bounds__(TcFfnShape<D>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_valid = *p.m_valid;
-  const int m_tiles = (m_valid + S::kBlockM - 1) / S::kBlockM;
   const int n_chunks = p.n / S::kChunk;
   // Each CTA walks the hidden chunks from its own starting chunk, so the CTAs
   // do not all stream the same weight boxes from the same L2 lines at once.
@@ -130,17 +128,22 @@ __global__ void __launch_bounds__(TcFfnShape<D>::kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_holder, S::kTmemCols);
   for (int i = threadIdx.x; i < p.n; i += blockDim.x) s_b1[i] = p.bias[i];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     s_b2[i] = p.bias2[i];
     s_g[i] = p.ln_g[i];
     s_be[i] = p.ln_b[i];
   }
+  // weights only above; rows, residual and token count come from earlier kernels
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 1) tmem_alloc(tmem_holder, S::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const int m_valid = *p.m_valid;
+  const int m_tiles = (m_valid + S::kBlockM - 1) / S::kBlockM;
 
   if (warp == 0) {
     if (lane == 0 && m_tiles > blockIdx.x) {

@@ -344,10 +344,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_valid = *p.m_valid;
-  const int m_tiles = (m_valid + S::kBlockM - 1) / S::kBlockM;
   const int n_tiles = p.n / BLOCK_N;
-  const int num_tiles = m_tiles * n_tiles;
   constexpr uint32_t kIdesc = FP8 ? idesc_e4m3(128, S::kInstN) : idesc_bf16(128, S::kInstN);
 
   if (threadIdx.x == 0) {
@@ -364,7 +361,6 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_holder, S::kTmemCols);
   for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
     s_bias[i] = p.bias[i];
     if (FP8) s_bscale[i] = p.b_scale[i];
@@ -373,10 +369,18 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       s_b[i] = p.ln_b[i];
     }
   }
+  // Everything above reads only weights; the operands, the residual and the
+  // token count come from earlier kernels (programmatic dependent launch).
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 1) tmem_alloc(tmem_holder, S::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const int m_valid = *p.m_valid;
+  const int m_tiles = (m_valid + S::kBlockM - 1) / S::kBlockM;
+  const int num_tiles = m_tiles * n_tiles;
 
   if (warp == 0) {
     if (lane == 0 && num_tiles > 0) {
