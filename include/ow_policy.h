@@ -82,6 +82,20 @@ OwStatus ow_policy_set_weights(OwPolicy* policy, const float* weights, size_t we
 OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_t* counts, int32_t batch,
                            void* logits, void* value, int32_t* actions, uint64_t seed);
 
+/* Pipelined host IO (host-IO handles). ow_policy_submit validates the counts,
+ * enqueues the upload of `features` / `counts`, the forward and the download
+ * of the outputs, and returns at once with a ticket; ow_policy_wait(ticket)
+ * blocks until that submission's outputs are in the host buffers and returns
+ * its status (a device-side error of that forward included). Two submissions
+ * may be in flight: the uploads and downloads of one overlap the forward of
+ * the other when the host buffers are pinned. The host buffers must stay
+ * valid until the wait; a third submit before the older one is waited for
+ * returns BAD_ARGUMENT. Not thread-safe per handle. ow_policy_forward on a
+ * host-IO handle is submit + wait. */
+OwStatus ow_policy_submit(OwPolicy* policy, const float* features, const int32_t* counts, int32_t batch,
+                          void* logits, void* value, int32_t* actions, uint64_t seed, int64_t* ticket);
+OwStatus ow_policy_wait(OwPolicy* policy, int64_t ticket);
+
 /* Waits for the handle's stream and reports any device-side error
  * (a bad count, a bounded wait that expired). */
 OwStatus ow_policy_synchronize(OwPolicy* policy);

@@ -229,6 +229,25 @@ struct OwPolicy {
   bool pdl = false;       // tensor-core path: programmatic dependent launches (ORBIT_WARS_PDL=0 turns them off)
   bool fuse_ffn = false;  // ORBIT_WARS_FFN_FUSED=1 at create selects the fused FFN kernel (d = 256, bf16)
   int launches = 0;
+  // host-IO submissions (ow_policy_submit / ow_policy_wait): two slots, each
+  // with its own device inputs, outputs and error word. Uploads run on
+  // copy_in, the forward on `stream`, downloads on copy_out; events chain
+  // them, so one slot's transfers overlap the other slot's forward.
+  struct IoSlot {
+    float* feats = nullptr;
+    int* counts = nullptr;
+    void* logits = nullptr;
+    void* value = nullptr;
+    int* actions = nullptr;
+    int* err = nullptr;
+    int* host_err = nullptr;  // pinned: the slot's device error word after the download
+    cudaEvent_t in_done = nullptr, comp_done = nullptr, out_done = nullptr;
+    int64_t ticket = -1;  // submission occupying the slot; -1 when free
+  };
+  static constexpr int kIoSlots = 2;
+  IoSlot io[kIoSlots];
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  int64_t next_ticket = 0;
   // profiling (ow_policy_profile_begin/_end)
   std::vector<cudaEvent_t> prof_events;
   std::vector<const char*> prof_names;
@@ -848,6 +867,12 @@ OwStatus alloc_workspace(OwPolicy& P) {
   const size_t o_counts = take(B * 4), o_offsets = take((B + 1) * 4), o_err = take(16);
   const size_t o_feats = take(rows * c.features * 4);
   const size_t o_logits = take(rows * c.actions * 4), o_value = take(B * 4), o_actions = take(rows * 4);
+  // the second host-IO slot's inputs, outputs and error word (the first slot uses the ones above)
+  const bool host_io = c.io == OW_IO_HOST;
+  const size_t o2_counts = host_io ? take(B * 4) : 0, o2_err = host_io ? take(16) : 0;
+  const size_t o2_feats = host_io ? take(rows * c.features * 4) : 0;
+  const size_t o2_logits = host_io ? take(rows * c.actions * 4) : 0, o2_value = host_io ? take(B * 4) : 0;
+  const size_t o2_actions = host_io ? take(rows * 4) : 0;
   const size_t o_slot = take(rows * 4), o_sval = take(rows * 4);
   const size_t o_x = take(rows * d * 4), o_ln = take(rows * d * act), o_qkv = take(rows * 3 * d * act);
   const size_t o_y = c.precision == OW_PRECISION_F32 ? o_ln : take(rows * d * 4);
@@ -873,6 +898,29 @@ OwStatus alloc_workspace(OwPolicy& P) {
   P.logits = b + o_logits;
   P.value = b + o_value;
   P.actions = reinterpret_cast<int*>(b + o_actions);
+  if (host_io) {
+    P.io[0].feats = P.feats;
+    P.io[0].counts = P.counts;
+    P.io[0].logits = P.logits;
+    P.io[0].value = P.value;
+    P.io[0].actions = P.actions;
+    P.io[0].err = P.err;
+    P.io[1].feats = reinterpret_cast<float*>(b + o2_feats);
+    P.io[1].counts = reinterpret_cast<int*>(b + o2_counts);
+    P.io[1].logits = b + o2_logits;
+    P.io[1].value = b + o2_value;
+    P.io[1].actions = reinterpret_cast<int*>(b + o2_actions);
+    P.io[1].err = reinterpret_cast<int*>(b + o2_err);
+    OW_TRY(cudaStreamCreateWithFlags(&P.copy_in, cudaStreamNonBlocking));
+    OW_TRY(cudaStreamCreateWithFlags(&P.copy_out, cudaStreamNonBlocking));
+    for (auto& sl : P.io) {
+      OW_TRY(cudaMallocHost(&sl.host_err, sizeof(int)));
+      *sl.host_err = 0;
+      OW_TRY(cudaEventCreateWithFlags(&sl.in_done, cudaEventDisableTiming));
+      OW_TRY(cudaEventCreateWithFlags(&sl.comp_done, cudaEventDisableTiming));
+      OW_TRY(cudaEventCreateWithFlags(&sl.out_done, cudaEventDisableTiming));
+    }
+  }
   P.row_slot = reinterpret_cast<int*>(b + o_slot);
   P.sval = reinterpret_cast<float*>(b + o_sval);
   P.x = b + o_x;
@@ -911,6 +959,16 @@ void release(OwPolicy* P) {
   if (P == nullptr) return;
   DeviceGuard g(P->device);
   if (P->stream) cudaStreamSynchronize(P->stream);
+  if (P->copy_in) cudaStreamSynchronize(P->copy_in);
+  if (P->copy_out) cudaStreamSynchronize(P->copy_out);
+  for (auto& sl : P->io) {
+    if (sl.in_done) cudaEventDestroy(sl.in_done);
+    if (sl.comp_done) cudaEventDestroy(sl.comp_done);
+    if (sl.out_done) cudaEventDestroy(sl.out_done);
+    if (sl.host_err) cudaFreeHost(sl.host_err);
+  }
+  if (P->copy_in) cudaStreamDestroy(P->copy_in);
+  if (P->copy_out) cudaStreamDestroy(P->copy_out);
   for (auto ev : P->prof_events) cudaEventDestroy(ev);
   if (P->ws) cudaFree(P->ws);
   if (P->warena) cudaFree(P->warena);
@@ -1024,6 +1082,68 @@ OwStatus ow_policy_set_weights(OwPolicy* policy, const float* weights, size_t we
   return upload_weights(*policy, weights);
 }
 
+OwStatus ow_policy_submit(OwPolicy* policy, const float* features, const int32_t* counts, int32_t batch,
+                          void* logits, void* value, int32_t* actions, uint64_t seed, int64_t* ticket) {
+  if (policy == nullptr || ticket == nullptr) return st_bad("null argument");
+  auto& P = *policy;
+  const auto& c = P.cfg;
+  if (c.io != OW_IO_HOST) return st_bad("submit / wait need a host-IO handle");
+  if (batch <= 0 || batch > c.batch_capacity) return st_bad("batch outside [1, batch_capacity]");
+  if (features == nullptr || counts == nullptr) return st_bad("null features or counts");
+  for (int32_t b = 0; b < batch; ++b)
+    if (counts[b] < 0 || counts[b] > c.n_entities) return st_bad("entity count outside [0, n_entities]");
+  auto& sl = P.io[P.next_ticket % OwPolicy::kIoSlots];
+  if (sl.ticket >= 0) return st_bad("two submissions in flight: wait for the older one first");
+  DeviceGuard g(P.device);
+  const size_t B = batch, N = c.n_entities;
+  const size_t lbytes = B * N * c.actions * (c.logits_dtype == OW_DTYPE_BF16 ? 2 : 4);
+  const size_t vbytes = B * (c.value_dtype == OW_DTYPE_BF16 ? 2 : 4);
+  // upload (the slot's previous forward has completed: its submission was waited for)
+  OW_TRY(cudaMemsetAsync(sl.err, 0, sizeof(int), P.copy_in));
+  OW_TRY(cudaMemcpyAsync(sl.feats, features, B * N * c.features * sizeof(float), cudaMemcpyHostToDevice, P.copy_in));
+  OW_TRY(cudaMemcpyAsync(sl.counts, counts, B * sizeof(int), cudaMemcpyHostToDevice, P.copy_in));
+  OW_TRY(cudaEventRecord(sl.in_done, P.copy_in));
+  // forward on the handle's stream, reading and writing the slot's buffers
+  OW_TRY(cudaStreamWaitEvent(P.stream, sl.in_done, 0));
+  float* saved_feats = P.feats;
+  int* saved_counts = P.counts;
+  int* saved_err = P.err;
+  P.feats = sl.feats;
+  P.counts = sl.counts;
+  P.err = sl.err;
+  const cudaError_t e = run_blocks(P, batch, seed, sl.logits, sl.value, sl.actions);
+  P.feats = saved_feats;
+  P.counts = saved_counts;
+  P.err = saved_err;
+  OW_TRY(e);
+  OW_TRY(cudaEventRecord(sl.comp_done, P.stream));
+  // download
+  OW_TRY(cudaStreamWaitEvent(P.copy_out, sl.comp_done, 0));
+  if (logits) OW_TRY(cudaMemcpyAsync(logits, sl.logits, lbytes, cudaMemcpyDeviceToHost, P.copy_out));
+  if (value) OW_TRY(cudaMemcpyAsync(value, sl.value, vbytes, cudaMemcpyDeviceToHost, P.copy_out));
+  if (actions) OW_TRY(cudaMemcpyAsync(actions, sl.actions, B * N * sizeof(int), cudaMemcpyDeviceToHost, P.copy_out));
+  OW_TRY(cudaMemcpyAsync(sl.host_err, sl.err, sizeof(int), cudaMemcpyDeviceToHost, P.copy_out));
+  OW_TRY(cudaEventRecord(sl.out_done, P.copy_out));
+  sl.ticket = P.next_ticket;
+  *ticket = P.next_ticket++;
+  return st_ok();
+}
+
+OwStatus ow_policy_wait(OwPolicy* policy, int64_t ticket) {
+  if (policy == nullptr) return st_bad("null policy");
+  auto& P = *policy;
+  if (P.cfg.io != OW_IO_HOST) return st_bad("submit / wait need a host-IO handle");
+  if (ticket < 0) return st_bad("unknown ticket");
+  auto& sl = P.io[ticket % OwPolicy::kIoSlots];
+  if (sl.ticket != ticket) return st_bad("unknown ticket");
+  DeviceGuard g(P.device);
+  const cudaError_t e = cudaEventSynchronize(sl.out_done);
+  sl.ticket = -1;
+  OW_TRY(e);
+  if (*sl.host_err != 0) return st_rt(device_error_message(*sl.host_err));
+  return st_ok();
+}
+
 OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_t* counts, int32_t batch,
                            void* logits, void* value, int32_t* actions, uint64_t seed) {
   if (policy == nullptr) return st_bad("null policy");
@@ -1032,24 +1152,11 @@ OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_
   if (batch <= 0 || batch > c.batch_capacity) return st_bad("batch outside [1, batch_capacity]");
   if (features == nullptr || counts == nullptr) return st_bad("null features or counts");
   DeviceGuard g(P.device);
-  const size_t B = batch, N = c.n_entities;
-  const size_t lbytes = B * N * c.actions * (c.logits_dtype == OW_DTYPE_BF16 ? 2 : 4);
-  const size_t vbytes = B * (c.value_dtype == OW_DTYPE_BF16 ? 2 : 4);
   if (c.io == OW_IO_HOST) {
-    for (size_t b = 0; b < B; ++b)
-      if (counts[b] < 0 || counts[b] > c.n_entities) return st_bad("entity count outside [0, n_entities]");
-    OW_TRY(cudaMemsetAsync(P.err, 0, sizeof(int), P.stream));
-    OW_TRY(cudaMemcpyAsync(P.feats, features, B * N * c.features * sizeof(float), cudaMemcpyHostToDevice, P.stream));
-    OW_TRY(cudaMemcpyAsync(P.counts, counts, B * sizeof(int), cudaMemcpyHostToDevice, P.stream));
-    OW_TRY(run_blocks(P, batch, seed, P.logits, P.value, P.actions));
-    if (logits) OW_TRY(cudaMemcpyAsync(logits, P.logits, lbytes, cudaMemcpyDeviceToHost, P.stream));
-    if (value) OW_TRY(cudaMemcpyAsync(value, P.value, vbytes, cudaMemcpyDeviceToHost, P.stream));
-    if (actions) OW_TRY(cudaMemcpyAsync(actions, P.actions, B * N * sizeof(int), cudaMemcpyDeviceToHost, P.stream));
-    int herr = 0;
-    OW_TRY(cudaMemcpyAsync(&herr, P.err, sizeof(int), cudaMemcpyDeviceToHost, P.stream));
-    OW_TRY(cudaStreamSynchronize(P.stream));
-    if (herr != 0) return st_rt(device_error_message(herr));
-    return st_ok();
+    int64_t t = 0;
+    const OwStatus s = ow_policy_submit(policy, features, counts, batch, logits, value, actions, seed, &t);
+    if (s.code != OW_STATUS_OK) return s;
+    return ow_policy_wait(policy, t);
   }
   // Device IO: features / counts / outputs are device pointers; the pipeline
   // reads the features and counts in place and writes the outputs directly.

@@ -64,6 +64,8 @@ SIGNATURES = {
     "ow_policy_create": (Status, [C.POINTER(PolicyConfigC), FP, SZ, C.c_int, P, C.POINTER(P)]),
     "ow_policy_set_weights": (Status, [P, FP, SZ]),
     "ow_policy_forward": (Status, [P, P, P, C.c_int32, P, P, P, C.c_uint64]),
+    "ow_policy_submit": (Status, [P, P, P, C.c_int32, P, P, P, C.c_uint64, C.POINTER(C.c_int64)]),
+    "ow_policy_wait": (Status, [P, C.c_int64]),
     "ow_policy_synchronize": (Status, [P]),
     "ow_policy_device_weights": (Status, [P, C.POINTER(P), C.POINTER(SZ)]),
     "ow_policy_launches_per_forward": (Status, [P, C.POINTER(C.c_int32)]),

@@ -81,6 +81,20 @@ class EncoderPolicy:
 
     forward_device = forward_raw
 
+    def submit_raw(self, features_ptr, counts_ptr, batch: int, logits_ptr, value_ptr, actions_ptr,
+                   seed: int = 0) -> int:
+        """Host-IO pipelined forward: enqueue upload, forward and download; returns a ticket.
+        The host buffers (pinned for overlap) must stay valid until wait(ticket)."""
+        t = C.c_int64()
+        _lib.check("ow_policy_submit", self.lib.ow_policy_submit(
+            self.handle, features_ptr, counts_ptr, int(batch), logits_ptr, value_ptr, actions_ptr, C.c_uint64(seed),
+            C.byref(t)))
+        return t.value
+
+    def wait(self, ticket: int) -> None:
+        """Blocks until the submission's outputs are in its host buffers; raises on its errors."""
+        _lib.check("ow_policy_wait", self.lib.ow_policy_wait(self.handle, C.c_int64(ticket)))
+
     def synchronize(self) -> None:
         _lib.check("ow_policy_synchronize", self.lib.ow_policy_synchronize(self.handle))
 

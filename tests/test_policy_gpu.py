@@ -196,3 +196,39 @@ def test_fused_ffn_matches_two_kernel_path(monkeypatch):
     m = valid_mask(counts, cfg.n_entities)
     assert rel_err(fused[0][m], two[0][m]) <= 1e-2 and rel_err(fused[1], two[1]) <= 1e-2
     assert float((fused[2][m] == two[2][m]).mean()) >= 0.99
+
+
+def test_submit_wait_pipeline():
+    """Pipelined host IO: two submissions in flight give the synchronous forward's
+    outputs bit for bit; a third submit before a wait and unknown tickets are rejected."""
+    cfg = ow.preset(2).with_(batch=96)
+    w = ow.make_weights(cfg, seed=3)
+    fa, ca = ow.make_inputs(cfg, seed=4)
+    fb, cb = ow.make_inputs(cfg, seed=5)
+    with ow.EncoderPolicy(cfg, w) as pol:
+        ref_a = pol.forward(fa, ca, seed=1)
+        ref_b = pol.forward(fb, cb, seed=2)
+        bufs = []
+        for f, c in ((fa, ca), (fb, cb)):
+            lg = np.empty((cfg.batch, cfg.n_entities, cfg.actions), np.uint16)
+            v = np.empty((cfg.batch,), np.float32)
+            a = np.empty((cfg.batch, cfg.n_entities), np.int32)
+            bufs.append((np.ascontiguousarray(f), np.ascontiguousarray(c, dtype=np.int32), lg, v, a))
+        tickets = [pol.submit_raw(f.ctypes.data, c.ctypes.data, cfg.batch, lg.ctypes.data, v.ctypes.data,
+                                  a.ctypes.data, seed=s) for (f, c, lg, v, a), s in zip(bufs, (1, 2))]
+        f, c, lg, v, a = bufs[0]
+        with pytest.raises(ow.OwError) as e:
+            pol.submit_raw(f.ctypes.data, c.ctypes.data, cfg.batch, lg.ctypes.data, v.ctypes.data, a.ctypes.data)
+        assert e.value.code == 1
+        with pytest.raises(ow.OwError):
+            pol.wait(tickets[1] + 5)
+        for t in tickets:
+            pol.wait(t)
+        with pytest.raises(ow.OwError):
+            pol.wait(tickets[0])  # already waited for
+        for (f, c, lg, v, a), ref in zip(bufs, (ref_a, ref_b)):
+            assert np.array_equal((lg.astype(np.uint32) << 16).view(np.float32), ref[0])
+            assert np.array_equal(v, ref[1]) and np.array_equal(a, ref[2])
+        # the handle keeps working synchronously afterwards
+        again = pol.forward(fa, ca, seed=1)
+        assert np.array_equal(again[0], ref_a[0])
