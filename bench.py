@@ -134,33 +134,54 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
-def kernel_work(cfg, name: str, m_valid: int, sq_counts: int, batch: int) -> tuple[str, float]:
-    """(bound, algorithmic work per launch): FLOPs for tensor-bound kernels, bytes for HBM-bound ones."""
-    d, f, F, P, N = cfg.d_model, cfg.ffn, cfg.features, cfg.actions, cfg.n_entities
-    act = 4 if cfg.precision == "f32" else 2
-    a8 = 1 if cfg.precision == "fp8" else act
+def kernel_work(cfg, name: str, m_valid: int, sq_counts: int, batch: int) -> tuple[float, float]:
+    """(algorithmic FLOPs, algorithmic HBM bytes) of one launch: every activation
+    read and written once, weights counted once (they stay in L2)."""
+    d, f, F, P, N, L = cfg.d_model, cfg.ffn, cfg.features, cfg.actions, cfg.n_entities, cfg.layers
+    act = 4 if cfg.precision == "f32" else 2          # bf16 activations (f32 on the fp32 path)
+    a8 = 1 if cfg.precision == "fp8" else act         # GEMM A operands (e4m3 on the fp8 path)
+    ln_out = (act * (L - 1) + 4) / L                  # LN output of the block's last GEMM: f32 after the last layer
+    wb = 1 if cfg.precision == "fp8" else act
+    M = float(m_valid)
     if name in ("gemm_qkv", "gemm_f32_qkv"):
-        return "tensor", 2.0 * m_valid * 3 * d * d
+        return 2.0 * M * 3 * d * d, M * (d * a8 + 3 * d * act) + 3 * d * d * wb
     if name in ("gemm_out_resid_ln", "gemm_f32_out_resid"):
-        return "tensor", 2.0 * m_valid * d * d
+        return 2.0 * M * d * d, M * (d * a8 + 8 * d + d * a8) + d * d * wb
     if name in ("gemm_ffn_up_gelu", "gemm_f32_ffn_up"):
-        return "tensor", 2.0 * m_valid * f * d
+        return 2.0 * M * f * d, M * (d * a8 + f * act) + f * d * wb
     if name in ("gemm_ffn_down_resid_ln", "gemm_f32_ffn_down_resid"):
-        return "tensor", 2.0 * m_valid * d * f
+        return 2.0 * M * d * f, M * (f * a8 + 8 * d + d * ln_out) + d * f * wb
+    if name == "ffn_fused":
+        return 4.0 * M * d * f, M * (d * a8 + 8 * d + d * ln_out) + 2 * d * f * wb
     if name == "attention":
-        return "tensor", 4.0 * sq_counts * d
+        return 4.0 * sq_counts * d, M * (3 * d * act + d * act)
     if name == "embed_ln":
-        return "hbm", m_valid * (F * 4 + 2 * d * a8)
+        return 2.0 * M * F * d, M * (F * 4 + 4 * d + d * a8)
     if name == "heads":
         lb = 4 if cfg.logits_dtype == "f32" else 2
-        return "hbm", m_valid * d * act + batch * N * (P * lb + 4) + batch * 4
+        return 2.0 * M * d * (P + 1), M * (4 * d + 4) + batch * N * (P * lb + 4)
     if name == "layernorm_f32":
-        return "hbm", m_valid * d * 8.0
+        return 0.0, M * d * 8.0
     if name == "quantize_e4m3":
-        return "hbm", m_valid * (f + d) / 2 * 3.0
+        return 0.0, M * (f + d) / 2 * 3.0
     if name == "scan_counts":
-        return "hbm", batch * 8.0
-    return "hbm", 0.0
+        return 0.0, batch * 8.0
+    if name == "state_finalize":
+        return 0.0, M * 4.0 + batch * 4.0
+    return 0.0, 0.0
+
+
+def gemm_summary(cfg, kernels: dict, m_valid: int, sq_counts: int, batch: int, tc_peak) -> dict | None:
+    """The block GEMMs together (QKV, out-projection, FFN up and down): their
+    FLOPs over their summed device time, against the measured bf16 peak."""
+    names = [n for n in kernels if n.startswith("gemm_") or n == "ffn_fused"]
+    if not names or not tc_peak:
+        return None
+    flops = sum(kernel_work(cfg, n, m_valid, sq_counts, batch)[0] * kernels[n]["launches"] for n in names)
+    secs = sum(kernels[n]["total_ms"] for n in names) / 1000.0
+    t = flops / secs / 1e12
+    return {"kernels": names, "tflops": round(t, 1), "frac_of_peak": round(t / tc_peak, 4),
+            "note": "FLOPs 2*M_valid*N*K of the four block GEMMs / their CUDA-event time; per-kernel bounds in kernels"}
 
 
 def cpu_baseline(cfg, weights, feats, counts, target_s: float = 12.0) -> dict:
@@ -356,16 +377,28 @@ def run_ours(args, cfg) -> None:
                "synchronous_timing": "ow_policy_forward-equivalent submit + wait per step, one at a time"}
         hp.close()
 
-    # roofline of the dominant kernel
+    # roofline of the dominant kernel: the bound whose roofline time is longer
+    # (algorithmic bytes / measured HBM copy rate vs FLOPs / measured bf16 peak)
     peaks, peak_src = load_peaks()
+    hbm_peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    tc_peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])) * (2.0 if cfg.precision == "fp8" else 1.0)
+    if cfg.precision == "f32":
+        tc_peak = None  # the fp32 path runs on CUDA cores
     kernels = {}
     for name, (n_launch, total_ms) in prof.items():  # from the first `prof_steps` timed steps
-        bound, work = kernel_work(cfg, name, m_valid, sq_counts, B)
+        flops, nbytes = kernel_work(cfg, name, m_valid, sq_counts, B)
         avg_s = total_ms / 1000.0 / max(n_launch, 1)
-        ach = work / avg_s if avg_s > 0 else 0.0
+        gbs = nbytes / avg_s / 1e9 if avg_s > 0 else 0.0
+        tfs = flops / avg_s / 1e12 if avg_s > 0 else 0.0
+        t_hbm = nbytes / (hbm_peak * 1e9)
+        t_tc = flops / (tc_peak * 1e12) if tc_peak else 0.0
+        bound = "tensor" if t_tc > t_hbm else "hbm"
         kernels[name] = {"launches": n_launch, "total_ms": round(total_ms, 4), "avg_us": round(avg_s * 1e6, 2),
-                         "bound": bound, "achieved": round(ach / (1e12 if bound == "tensor" else 1e9), 2),
-                         "unit": "TFLOP/s" if bound == "tensor" else "GB/s"}
+                         "bound": bound, "achieved": round(tfs if bound == "tensor" else gbs, 2),
+                         "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
+                         "tflops": round(tfs, 1), "tensor_frac": round(tfs / tc_peak, 4) if tc_peak else None,
+                         "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm_peak, 4),
+                         "roofline_frac": round(max(t_hbm, t_tc) / avg_s, 4) if avg_s > 0 else None}
     total = sum(k["total_ms"] for k in kernels.values()) or 1.0
     for k in kernels.values():
         k["share"] = round(k["total_ms"] / total, 4)
@@ -373,19 +406,14 @@ def run_ours(args, cfg) -> None:
     roof = None
     if dom_name is not None:
         k = kernels[dom_name]
-        if k["bound"] == "tensor":
-            peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
-            if cfg.precision == "fp8":
-                peak *= 2.0
-        else:
-            peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        peak = tc_peak if k["bound"] == "tensor" else hbm_peak
         traffic, traffic_src = ncu_traffic(args.config, dom_name)
         roof = {"kernel": dom_name, "bound": k["bound"], "achieved": k["achieved"], "peak": peak, "unit": k["unit"],
-                "frac": round(k["achieved"] / peak, 4), "traffic": traffic,
-                "traffic_source": traffic_src,
+                "frac": round(k["achieved"] / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
                 "peak_source": peak_src + (" (fp8 peak = 2x measured bf16)" if cfg.precision == "fp8" else ""),
-                "work_per_launch": "2*M_valid*N*K FLOPs, M_valid = valid tokens of the batch"
-                if k["bound"] == "tensor" else "bytes read + written",
+                "tensor_frac": k["tensor_frac"], "hbm_frac": k["hbm_frac"],
+                "work_per_launch": "algorithmic bytes = every activation read and written once (weights once); "
+                                   "FLOPs = 2*M_valid*N*K, M_valid = valid tokens of the batch",
                 "timed_steps_profiled": prof_steps}
 
     cpu = None
@@ -406,8 +434,7 @@ def run_ours(args, cfg) -> None:
                        "seed": args.seed},
             "e2e": e2e, "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
             "kernels": kernels, "outputs_finite": out_ok,
-            "gemm_tflops_per_gpu": round(cfg.gemm_flops_per_token() * m_valid * args.steps / t_max / 1e12
-                                         * (world / world), 2),
+            "gemm": gemm_summary(cfg, kernels, m_valid, sq_counts, B, tc_peak),
         }
         print(json.dumps(line), flush=True)
     pol.close()
