@@ -644,9 +644,10 @@ def run_true2d(args) -> None:
         mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
         peak = 16.0 * props.multi_processor_count * mhz * 1e6 / 1e9
         roof = {"kernel": "t2_attention", "bound": "mufu", "achieved": round(ach, 1), "peak": round(peak, 1),
-                "unit": "G ex2/s", "frac": round(ach / peak, 4), "traffic": None,
+                "unit": "G exp/s", "frac": round(ach / peak, 4), "traffic": None,
                 "peak_source": f"computed: 16 ex2/clk/SM x {props.multi_processor_count} SMs x {mhz:.0f} MHz "
-                               "(median sampled SM clock); not a measured peak",
+                               "(median sampled SM clock); not a measured peak. A quarter of the exponentials "
+                               "run as a polynomial on the FMA pipe, so the kernel may exceed this MUFU-only rate",
                 "work_per_launch": f"rows^4 x heads = {true2d_ex2_per_request(shape):.0f} exponentials per request"}
     ref_gpu = None
     if rank == 0 and world == 1:

@@ -13,7 +13,9 @@
 //                      memory; the row max is closed-form because scores are
 //                      rank-1 (max_j q*k_j = q*kmax for q >= 0, q*kmin otherwise),
 //                      so softmax and weighted sum take ONE pass over the keys
-//                      (the reference takes two). Attention FFN fused.
+//                      (the reference takes two). A quarter of the exponentials
+//                      run as a polynomial on the FMA pipe, the rest on the
+//                      MUFU. Attention FFN fused.
 //   3. t2_post_collapse: CTA per 4 rows of a request: post-attention matrix layers,
 //                      then the 12-action collapse (:546-647) from shared memory.
 // The model population stays resident in HBM between calls (upload_population);
@@ -184,14 +186,40 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2. full scalar attention + attention FFN, CTA per request, in place on m.
-constexpr int kAttnThreads = 1024;
-constexpr int kQueriesPerThread = 4;  // cells <= 4096 for one pass; larger grids loop
+// 2^x for x <= 0 on the FMA pipe: Cody-Waite style reduction x = n + f with
+// n = rint(x) from the 1.5 * 2^23 shifter and f in [-1/2, 1/2], a degree-4
+// polynomial for 2^f fitted here for minimum relative error on that interval
+// (2.7e-6 in f32 Horner evaluation), then n added to the exponent field with an
+// integer multiply-add. x is clamped to -125 first (2^-125 is far below any
+// softmax term that matters). Nine FMA-pipe instructions, no MUFU.
+__device__ __forceinline__ float exp2_poly(float x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23: x + kShift rounds x to an integer in the low bits
+  x = fmaxf(x, -125.0f);
+  const float t = x + kShift;
+  const float f = x - (t - kShift);
+  float p = fmaf(9.570096619e-03f, f, 5.591785908e-02f);
+  p = fmaf(p, f, 2.402474433e-01f);
+  p = fmaf(p, f, 6.931217909e-01f);
+  p = fmaf(p, f, 9.999992847e-01f);
+  // bits(t) = bits(kShift) + n, and bits(kShift) << 23 wraps to 0, so bits(t) << 23 = n << 23
+  return __uint_as_float(__float_as_uint(t) * 8388608u + __float_as_uint(p));
+}
 
-__global__ void __launch_bounds__(kAttnThreads) t2_attention(const size_t* __restrict__ idx,
-                                                             const float* __restrict__ all_w, int models, T2Dev L,
-                                                             float* __restrict__ m, int* err) {
-  extern __shared__ float2 s_kv[];  // [cells] (k, v)
+// 2. full scalar attention + attention FFN, CTA per request, in place on m.
+// Each of the THREADS threads owns QPT queries; per key, the last NPOLY of them
+// take their exponential from the FMA pipe (exp2_poly), the others from the
+// MUFU (ex2.approx), so the two pipes share the 4,096^2 exponentials of a request.
+constexpr int kAttnThreads = 1024;
+constexpr int kAttnQpt = 4;
+constexpr int kAttnPoly = 1;
+
+template <int THREADS, int QPT, int NPOLY>
+__global__ void __launch_bounds__(THREADS) t2_attention(const size_t* __restrict__ idx,
+                                                        const float* __restrict__ all_w, int models, T2Dev L,
+                                                        float* __restrict__ m, int* err) {
+  constexpr int kAttnThreads = THREADS;
+  constexpr int kQueriesPerThread = QPT;
+  extern __shared__ float2 s_kv[];  // [cells] (k * log2 e, v)
   __shared__ float s_red[2][32];
   const int r = blockIdx.x;
   const float* w = model_of(all_w, idx, models, r, L.total, err);
@@ -245,7 +273,8 @@ __global__ void __launch_bounds__(kAttnThreads) t2_attention(const size_t* __res
         const float2 kv = s_kv[j];
 #pragma unroll
         for (int i = 0; i < kQueriesPerThread; ++i) {
-          const float e = ex2_approx(fmaf(q[i], kv.x, -off[i]));
+          const float x = fmaf(q[i], kv.x, -off[i]);
+          const float e = i >= kQueriesPerThread - NPOLY ? exp2_poly(x) : ex2_approx(x);
           den[i] += e;
           acc[i] = fmaf(e, kv.y, acc[i]);
         }
@@ -265,6 +294,17 @@ __global__ void __launch_bounds__(kAttnThreads) t2_attention(const size_t* __res
       }
     }
   }
+}
+
+// Launches t2_attention for `n` requests.
+cudaError_t launch_t2_attention(const size_t* idx, const float* all_w, int models, const T2Dev& D, float* m, int* err,
+                                unsigned n, cudaStream_t stream) {
+  const size_t smem = static_cast<size_t>(D.cells) * sizeof(float2);
+  auto k = t2_attention<kAttnThreads, kAttnQpt, kAttnPoly>;
+  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  k<<<n, kAttnThreads, smem, stream>>>(idx, all_w, models, D, m, err);
+  return cudaGetLastError();
 }
 
 // 3. matrix layers [mid, layers) + collapse; CTA = 4 rows of one request.
@@ -567,15 +607,12 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
       W.prof_names[W.prof_used++] = name;
     }
   };
-  const size_t smem = L.cells * sizeof(float2);
-  T2_TRY(cudaFuncSetAttribute(t2_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n));
   mark("t2_expand_pre");
   t2_expand_pre<true><<<g1, 256, 0, W.stream>>>(W.in, didx, W.weights, models, D, W.m, W.err);
   T2_TRY(cudaGetLastError());
   mark("t2_attention");
-  t2_attention<<<static_cast<unsigned>(n), kAttnThreads, smem, W.stream>>>(didx, W.weights, models, D, W.m, W.err);
-  T2_TRY(cudaGetLastError());
+  T2_TRY(launch_t2_attention(didx, W.weights, models, D, W.m, W.err, static_cast<unsigned>(n), W.stream));
   const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   mark("t2_post_collapse");
@@ -787,11 +824,7 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(const float* input_ro
   const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(game_count));
   t2_expand_pre<false><<<g1, 256, 0, s>>>(input_rows, nullptr, weights, 1, D, m, err);
   T2_TRY(cudaGetLastError());
-  const size_t smem = L.cells * sizeof(float2);
-  if (smem > 48 * 1024)
-    T2_TRY(cudaFuncSetAttribute(t2_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  t2_attention<<<static_cast<unsigned>(game_count), kAttnThreads, smem, s>>>(nullptr, weights, 1, D, m, err);
-  T2_TRY(cudaGetLastError());
+  T2_TRY(launch_t2_attention(nullptr, weights, 1, D, m, err, static_cast<unsigned>(game_count), s));
   const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(game_count));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   t2_post_collapse<false><<<g3, threads3, 0, s>>>(nullptr, weights, 1, D, m, output_rows, err);
