@@ -213,22 +213,23 @@ __device__ __forceinline__ float ex2_approx_f(float x) {
   return y;
 }
 
-// GELU, erf form: 0.5 v (1 + erf(v / sqrt 2)), with erf from Abramowitz &
-// Stegun, Handbook of Mathematical Functions, eq. 7.1.26 (|error| <= 1.5e-7):
-//   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),  t = 1 / (1 + p z),  z >= 0.
-// With g = 0.5 |v|-side tail, GELU(v) = v - g for v >= 0 and g for v < 0, so
-// the negative branch has no cancellation. Two MUFU ops (rcp, ex2) per value.
+// GELU, erf form: v * Phi(v), Phi(v) = 0.5 (1 + erf(v / sqrt 2)), with erfc
+// from Abramowitz & Stegun, Handbook of Mathematical Functions, eq. 7.1.26
+// (|error| <= 1.5e-7):
+//   erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),  t = 1 / (1 + p z),  z >= 0.
+// With a = |v|, z = a / sqrt 2 and q = a * 0.5 erfc(z) >= 0, GELU(v) = v - q for
+// v >= 0 and -q for v < 0, i.e. max(v, 0) - q, with no cancellation on the
+// negative side. The 1/2 and 1/sqrt 2 factors are folded into the constants.
+// Two MUFU operations (rcp, ex2) per value.
 __device__ __forceinline__ float gelu_erf(float v) {
-  const float z = fabsf(v) * 0.70710678118654752f;
-  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
-  float poly = fmaf(t, 1.061405429f, -1.453152027f);
-  poly = fmaf(t, poly, 1.421413741f);
-  poly = fmaf(t, poly, -0.284496736f);
-  poly = fmaf(t, poly, 0.254829592f);
-  poly *= t;
-  const float e = ex2_approx_f(-(z * z) * 1.4426950408889634f);  // exp(-z^2)
-  const float g = 0.5f * v * poly * e;
-  return v >= 0.0f ? v - g : g;
+  const float a = fabsf(v);
+  const float t = rcp_approx(fmaf(0.3275911f * 0.70710678118654752f, a, 1.0f));
+  float poly = fmaf(t, 0.5f * 1.061405429f, 0.5f * -1.453152027f);
+  poly = fmaf(t, poly, 0.5f * 1.421413741f);
+  poly = fmaf(t, poly, 0.5f * -0.284496736f);
+  poly = fmaf(t, poly, 0.5f * 0.254829592f);
+  const float e = ex2_approx_f((a * a) * (-0.5f * 1.4426950408889634f));  // exp(-v^2 / 2)
+  return fmaxf(v, 0.0f) - a * (poly * t) * e;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
