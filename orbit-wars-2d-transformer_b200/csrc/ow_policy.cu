@@ -529,8 +529,9 @@ cudaError_t launch_attention(const OwPolicy& P, int batch) {
     auto* o = static_cast<__nv_bfloat16*>(P.attn);
     const float sl2 = scale * 1.4426950408889634f;
     const int nmax = c.n_entities <= 32 ? 32 : (c.n_entities <= 64 ? 64 : (c.n_entities <= 96 ? 96 : 128));
-    // largest head group (8, 4, 2, 1) dividing the head count whose staged Q/K/V fit ~110 KB
-    int hg = 8;
+    // head group (4, 2, 1) dividing the head count whose staged Q/K/V fit ~110 KB: 4 heads per CTA
+    // (52 KB at N = 64) let four CTAs share an SM, measured faster at config 2 than 8 (two per SM) or 2
+    int hg = 4;
     while (hg > 1 && (c.heads % hg != 0 || 3 * nmax * (hg * 32 + 8) * 2 > 112 * 1024)) hg /= 2;
     const dim3 g2(batch, c.heads / hg);
     const size_t smem = static_cast<size_t>(3) * nmax * (hg * 32 + 8) * 2;
