@@ -91,7 +91,11 @@ OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_
  * the other when the host buffers are pinned. The host buffers must stay
  * valid until the wait; a third submit before the older one is waited for
  * returns BAD_ARGUMENT. Not thread-safe per handle. ow_policy_forward on a
- * host-IO handle is submit + wait. */
+ * host-IO handle is submit + wait. A host-IO handle on the tensor-core path
+ * keeps a second activation workspace and compute stream when that takes at
+ * most half of the free device memory (ORBIT_WARS_LANES=1 at create turns it
+ * off), so the forwards of two in-flight submissions also run at the same
+ * time, filling each other's idle SMs. */
 OwStatus ow_policy_submit(OwPolicy* policy, const float* features, const int32_t* counts, int32_t batch,
                           void* logits, void* value, int32_t* actions, uint64_t seed, int64_t* ticket);
 OwStatus ow_policy_wait(OwPolicy* policy, int64_t ticket);

@@ -246,6 +246,29 @@ struct OwPolicy {
   };
   static constexpr int kIoSlots = 2;
   IoSlot io[kIoSlots];
+  // Compute lanes: a lane is a compute stream plus its own activation
+  // workspace and tensor maps. The fields above (stream, ws, x, ln, ...,
+  // m_ln, ..., e_y) are the active lane's; lanes[k] keeps each lane's copy.
+  // Host-IO handles get a second lane when it fits in device memory, so the
+  // forwards of the two IO slots can run at the same time.
+  struct Lane {
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    uint8_t* ws = nullptr;
+    size_t ws_bytes = 0;
+    int *counts = nullptr, *offsets = nullptr, *err = nullptr;
+    float* feats = nullptr;
+    void *logits = nullptr, *value = nullptr;
+    int *actions = nullptr, *row_slot = nullptr;
+    float* sval = nullptr;
+    void *x = nullptr, *ln = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr;
+    uint8_t *ln8 = nullptr, *attn8 = nullptr, *h8 = nullptr;
+    float *ln_scale = nullptr, *attn_scale = nullptr, *h_scale = nullptr;
+    CUtensorMap m_ln, m_attn, m_h, e_qkv, e_h, e_x, e_ln, e_y;
+  };
+  Lane lanes[2];
+  int n_lanes = 1;
+  size_t ws_bytes = 0;  // the active lane's workspace size
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   int64_t next_ticket = 0;
   // profiling (ow_policy_profile_begin/_end)
@@ -891,6 +914,7 @@ OwStatus alloc_workspace(OwPolicy& P) {
     o_hs = take(rows * 4);
   }
   const size_t total = align_up(at, 256);
+  P.ws_bytes = total;
   OW_TRY(cudaMalloc(&P.ws, total));
   OW_TRY(cudaMemsetAsync(P.ws, 0, total, P.stream));
   uint8_t* b = P.ws;
@@ -901,7 +925,7 @@ OwStatus alloc_workspace(OwPolicy& P) {
   P.logits = b + o_logits;
   P.value = b + o_value;
   P.actions = reinterpret_cast<int*>(b + o_actions);
-  if (host_io) {
+  if (host_io && P.copy_in == nullptr) {  // the IO slots and copy streams, once per handle
     P.io[0].feats = P.feats;
     P.io[0].counts = P.counts;
     P.io[0].logits = P.logits;
@@ -958,6 +982,64 @@ OwStatus alloc_workspace(OwPolicy& P) {
   return st_ok();
 }
 
+void save_lane(const OwPolicy& P, OwPolicy::Lane& L) {
+  L.stream = P.stream;
+  L.own_stream = P.own_stream;
+  L.ws = P.ws;
+  L.ws_bytes = P.ws_bytes;
+  L.counts = P.counts; L.offsets = P.offsets; L.err = P.err; L.feats = P.feats;
+  L.logits = P.logits; L.value = P.value; L.actions = P.actions; L.row_slot = P.row_slot; L.sval = P.sval;
+  L.x = P.x; L.ln = P.ln; L.qkv = P.qkv; L.attn = P.attn; L.h = P.h; L.y = P.y;
+  L.ln8 = P.ln8; L.attn8 = P.attn8; L.h8 = P.h8;
+  L.ln_scale = P.ln_scale; L.attn_scale = P.attn_scale; L.h_scale = P.h_scale;
+  L.m_ln = P.m_ln; L.m_attn = P.m_attn; L.m_h = P.m_h;
+  L.e_qkv = P.e_qkv; L.e_h = P.e_h; L.e_x = P.e_x; L.e_ln = P.e_ln; L.e_y = P.e_y;
+}
+
+void load_lane(OwPolicy& P, const OwPolicy::Lane& L) {
+  P.stream = L.stream;
+  P.own_stream = L.own_stream;
+  P.ws = L.ws;
+  P.ws_bytes = L.ws_bytes;
+  P.counts = L.counts; P.offsets = L.offsets; P.err = L.err; P.feats = L.feats;
+  P.logits = L.logits; P.value = L.value; P.actions = L.actions; P.row_slot = L.row_slot; P.sval = L.sval;
+  P.x = L.x; P.ln = L.ln; P.qkv = L.qkv; P.attn = L.attn; P.h = L.h; P.y = L.y;
+  P.ln8 = L.ln8; P.attn8 = L.attn8; P.h8 = L.h8;
+  P.ln_scale = L.ln_scale; P.attn_scale = L.attn_scale; P.h_scale = L.h_scale;
+  P.m_ln = L.m_ln; P.m_attn = L.m_attn; P.m_h = L.m_h;
+  P.e_qkv = L.e_qkv; P.e_h = L.e_h; P.e_x = L.e_x; P.e_ln = L.e_ln; P.e_y = L.e_y;
+}
+
+// Lane 0 is the handle's stream and workspace. Host-IO handles on the
+// tensor-core path add a second lane (own stream, own workspace) when its
+// workspace takes at most half of the free device memory, unless
+// ORBIT_WARS_LANES=1.
+OwStatus add_second_lane(OwPolicy& P) {
+  save_lane(P, P.lanes[0]);
+  P.n_lanes = 1;
+  const char* e = std::getenv("ORBIT_WARS_LANES");
+  if (P.cfg.io != OW_IO_HOST || P.cfg.precision == OW_PRECISION_F32 || (e != nullptr && e[0] == '1'))
+    return st_ok();
+  size_t free_b = 0, total_b = 0;
+  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || P.ws_bytes > free_b / 2) return st_ok();
+  cudaStream_t s2 = nullptr;
+  OW_TRY(cudaStreamCreateWithFlags(&s2, cudaStreamNonBlocking));
+  P.stream = s2;
+  P.own_stream = true;
+  P.ws = nullptr;
+  const OwStatus st = alloc_workspace(P);
+  save_lane(P, P.lanes[1]);
+  load_lane(P, P.lanes[0]);
+  if (st.code != OW_STATUS_OK) {
+    if (P.lanes[1].ws) cudaFree(P.lanes[1].ws);
+    cudaStreamDestroy(s2);
+    P.lanes[1] = OwPolicy::Lane{};
+    return st;
+  }
+  P.n_lanes = 2;
+  return st_ok();
+}
+
 void release(OwPolicy* P) {
   if (P == nullptr) return;
   DeviceGuard g(P->device);
@@ -973,6 +1055,16 @@ void release(OwPolicy* P) {
   if (P->copy_in) cudaStreamDestroy(P->copy_in);
   if (P->copy_out) cudaStreamDestroy(P->copy_out);
   for (auto ev : P->prof_events) cudaEventDestroy(ev);
+  for (int k = 1; k < P->n_lanes; ++k) {
+    auto& L = P->lanes[k];
+    if (L.stream) cudaStreamSynchronize(L.stream);
+    if (L.ws) cudaFree(L.ws);
+    if (L.own_stream && L.stream) cudaStreamDestroy(L.stream);
+  }
+  if (P->n_lanes > 1) {  // the active fields may show another lane: free lane 0 through its record
+    P->ws = P->lanes[0].ws;
+    P->stream = P->lanes[0].stream;
+  }
   if (P->ws) cudaFree(P->ws);
   if (P->warena) cudaFree(P->warena);
   if (P->own_stream && P->stream) cudaStreamDestroy(P->stream);
@@ -1066,6 +1158,7 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
   }
   OwStatus s = st_cuda(set_all_gemm_attrs());
   if (s.code == OW_STATUS_OK) s = alloc_workspace(*P);
+  if (s.code == OW_STATUS_OK) s = add_second_lane(*P);
   if (s.code == OW_STATUS_OK) s = upload_weights(*P, weights);
   if (s.code != OW_STATUS_OK) {
     release(P);
@@ -1081,6 +1174,8 @@ OwStatus ow_policy_set_weights(OwPolicy* policy, const float* weights, size_t we
   for (size_t i = 0; i < weight_count; ++i)
     if (!std::isfinite(weights[i])) return st_bad("non-finite weight");
   DeviceGuard g(policy->device);
+  // every lane's forwards read the weight arena: let them finish first
+  for (int k = 0; k < policy->n_lanes; ++k) OW_TRY(cudaStreamSynchronize(policy->lanes[k].stream));
   OW_TRY(cudaStreamSynchronize(policy->stream));
   return upload_weights(*policy, weights);
 }
@@ -1106,20 +1201,18 @@ OwStatus ow_policy_submit(OwPolicy* policy, const float* features, const int32_t
   OW_TRY(cudaMemcpyAsync(sl.feats, features, B * N * c.features * sizeof(float), cudaMemcpyHostToDevice, P.copy_in));
   OW_TRY(cudaMemcpyAsync(sl.counts, counts, B * sizeof(int), cudaMemcpyHostToDevice, P.copy_in));
   OW_TRY(cudaEventRecord(sl.in_done, P.copy_in));
-  // forward on the handle's stream, reading and writing the slot's buffers
-  OW_TRY(cudaStreamWaitEvent(P.stream, sl.in_done, 0));
-  float* saved_feats = P.feats;
-  int* saved_counts = P.counts;
-  int* saved_err = P.err;
+  // forward on the slot's lane (its own stream and workspace when the handle
+  // has two lanes), reading and writing the slot's buffers
+  const int lane = static_cast<int>(P.next_ticket % P.n_lanes);
+  load_lane(P, P.lanes[lane]);
   P.feats = sl.feats;
   P.counts = sl.counts;
   P.err = sl.err;
-  const cudaError_t e = run_blocks(P, batch, seed, sl.logits, sl.value, sl.actions);
-  P.feats = saved_feats;
-  P.counts = saved_counts;
-  P.err = saved_err;
+  cudaError_t e = cudaStreamWaitEvent(P.stream, sl.in_done, 0);
+  if (e == cudaSuccess) e = run_blocks(P, batch, seed, sl.logits, sl.value, sl.actions);
+  if (e == cudaSuccess) e = cudaEventRecord(sl.comp_done, P.stream);
+  load_lane(P, P.lanes[0]);
   OW_TRY(e);
-  OW_TRY(cudaEventRecord(sl.comp_done, P.stream));
   // download
   OW_TRY(cudaStreamWaitEvent(P.copy_out, sl.comp_done, 0));
   if (logits) OW_TRY(cudaMemcpyAsync(logits, sl.logits, lbytes, cudaMemcpyDeviceToHost, P.copy_out));
@@ -1177,6 +1270,9 @@ OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_
 OwStatus ow_policy_synchronize(OwPolicy* policy) {
   if (policy == nullptr) return st_bad("null policy");
   DeviceGuard g(policy->device);
+  for (int k = 1; k < policy->n_lanes; ++k) OW_TRY(cudaStreamSynchronize(policy->lanes[k].stream));
+  if (policy->copy_in != nullptr) OW_TRY(cudaStreamSynchronize(policy->copy_in));
+  if (policy->copy_out != nullptr) OW_TRY(cudaStreamSynchronize(policy->copy_out));
   int herr = 0;
   OW_TRY(cudaMemcpyAsync(&herr, policy->err, sizeof(int), cudaMemcpyDeviceToHost, policy->stream));
   OW_TRY(cudaStreamSynchronize(policy->stream));
