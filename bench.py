@@ -256,7 +256,7 @@ def run_ours(args, cfg) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout (one JSON line)
+        os.environ["NCCL_DEBUG"] = "WARN"  # NCCL prints its version banner on stdout otherwise: one JSON line only
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     from orbit_wars_b200.shard import broadcast_weights, shard_inputs
@@ -323,6 +323,11 @@ def run_ours(args, cfg) -> None:
     value = world * B * args.steps / t_max
     launches = pol.launches_per_forward() * args.steps
     out_ok = bool(torch.isfinite(lg.float()).all().item() and torch.isfinite(vv.float()).all().item())
+    # the device-IO handle's workspace goes before the host-IO handle allocates its own
+    # (config 5's activations take about 112 GB per workspace)
+    pol.close()
+    del f_d, c_d, lg, vv, aa
+    torch.cuda.empty_cache()
 
     # e2e through the host-buffer API (pinned host buffers): the pipelined
     # submit / wait pair, two submissions in flight so one step's upload and
@@ -437,7 +442,6 @@ def run_ours(args, cfg) -> None:
             "gemm": gemm_summary(cfg, kernels, m_valid, sq_counts, B, tc_peak),
         }
         print(json.dumps(line), flush=True)
-    pol.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -592,7 +596,7 @@ def run_true2d(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        os.environ["NCCL_DEBUG"] = "WARN"  # no version banner on stdout
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     shape, per, pop, x, idx = true2d_workload(args)  # replicas: every rank runs the same workload
     lib = CudaTrue2D()

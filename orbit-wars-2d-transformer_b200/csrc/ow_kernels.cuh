@@ -884,6 +884,7 @@ __global__ void __launch_bounds__(128) heads_mma_kernel(const float* __restrict_
                                                         const int* __restrict__ row_slot,
                                                         const float* __restrict__ w_p, const float* __restrict__ b_p,
                                                         const float* __restrict__ w_v, int sample, uint64_t seed,
+                                                        int state_base,
                                                         void* __restrict__ logits, int* __restrict__ actions,
                                                         float* __restrict__ sval) {
   constexpr int WPITCH = D + 16;  // f32 pitch: float4 fragment loads are conflict-free
@@ -947,7 +948,7 @@ __global__ void __launch_bounds__(128) heads_mma_kernel(const float* __restrict_
             float score = v;
             if (sample) {
               const uint4 rr = philox4x32_10(make_uint4(static_cast<uint32_t>(p) >> 2, static_cast<uint32_t>(sj),
-                                                        static_cast<uint32_t>(sb), 0u),
+                                                        static_cast<uint32_t>(sb + state_base), 0u),
                                              static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
               const int w4 = p & 3;
               const uint32_t word = w4 == 0 ? rr.x : (w4 == 1 ? rr.y : (w4 == 2 ? rr.z : rr.w));

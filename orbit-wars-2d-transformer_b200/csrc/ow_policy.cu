@@ -195,6 +195,7 @@ struct OwPolicy {
   bool own_stream = false;
   int num_sms = 148;
   size_t cap_rows = 0;
+  int cap_states = 0;  // states the active lane's workspace holds
 
   // weights (device arena)
   uint8_t* warena = nullptr;
@@ -256,6 +257,8 @@ struct OwPolicy {
     bool own_stream = false;
     uint8_t* ws = nullptr;
     size_t ws_bytes = 0;
+    size_t cap_rows = 0;
+    int cap_states = 0;
     int *counts = nullptr, *offsets = nullptr, *err = nullptr;
     float* feats = nullptr;
     void *logits = nullptr, *value = nullptr;
@@ -268,6 +271,9 @@ struct OwPolicy {
   };
   Lane lanes[2];
   int n_lanes = 1;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;  // device-IO split forward: lane 1 after lane 0's queue, and back
+  bool split_lane = false;  // device IO: lane 1 holds half the capacity and takes the second half of a batch
+  int state_base = 0;       // global index of the forward's first state (Gumbel keys) when a batch is split
   size_t ws_bytes = 0;  // the active lane's workspace size
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   int64_t next_ticket = 0;
@@ -452,7 +458,7 @@ cudaError_t heads_mma_launch(const OwPolicy& P, int batch, uint64_t seed, void* 
   return launch_k(P, heads_mma_kernel<D, NTILE, LB>, grid, 128, smem, static_cast<const float*>(P.y),
            static_cast<const int*>(P.offsets), batch, c.n_entities, c.actions, static_cast<const int*>(P.row_slot),
            static_cast<const float*>(P.wp), static_cast<const float*>(P.bp), static_cast<const float*>(P.wv),
-           c.sample_actions, seed, logits, actions, P.sval);
+           c.sample_actions, seed, P.state_base, logits, actions, P.sval);
 }
 
 template <int D>
@@ -878,10 +884,12 @@ OwStatus upload_weights(OwPolicy& P, const float* w) {
   return st_ok();
 }
 
-OwStatus alloc_workspace(OwPolicy& P) {
+// Activation workspace (and tensor maps) for `cap_states` states on P's stream.
+OwStatus alloc_workspace(OwPolicy& P, int cap_states) {
   const auto& c = P.cfg;
-  const size_t B = c.batch_capacity, N = c.n_entities, rows = B * N;
+  const size_t B = cap_states, N = c.n_entities, rows = B * N;
   P.cap_rows = rows;
+  P.cap_states = cap_states;
   const size_t act = c.precision == OW_PRECISION_F32 ? 4 : 2;
   const size_t d = c.d_model, f = c.ffn;
   size_t at = 0;
@@ -987,6 +995,8 @@ void save_lane(const OwPolicy& P, OwPolicy::Lane& L) {
   L.own_stream = P.own_stream;
   L.ws = P.ws;
   L.ws_bytes = P.ws_bytes;
+  L.cap_rows = P.cap_rows;
+  L.cap_states = P.cap_states;
   L.counts = P.counts; L.offsets = P.offsets; L.err = P.err; L.feats = P.feats;
   L.logits = P.logits; L.value = P.value; L.actions = P.actions; L.row_slot = P.row_slot; L.sval = P.sval;
   L.x = P.x; L.ln = P.ln; L.qkv = P.qkv; L.attn = P.attn; L.h = P.h; L.y = P.y;
@@ -1001,6 +1011,8 @@ void load_lane(OwPolicy& P, const OwPolicy::Lane& L) {
   P.own_stream = L.own_stream;
   P.ws = L.ws;
   P.ws_bytes = L.ws_bytes;
+  P.cap_rows = L.cap_rows;
+  P.cap_states = L.cap_states;
   P.counts = L.counts; P.offsets = L.offsets; P.err = L.err; P.feats = L.feats;
   P.logits = L.logits; P.value = L.value; P.actions = L.actions; P.row_slot = L.row_slot; P.sval = L.sval;
   P.x = L.x; P.ln = L.ln; P.qkv = L.qkv; P.attn = L.attn; P.h = L.h; P.y = L.y;
@@ -1010,24 +1022,28 @@ void load_lane(OwPolicy& P, const OwPolicy::Lane& L) {
   P.e_qkv = L.e_qkv; P.e_h = L.e_h; P.e_x = L.e_x; P.e_ln = L.e_ln; P.e_y = L.e_y;
 }
 
-// Lane 0 is the handle's stream and workspace. Host-IO handles on the
-// tensor-core path add a second lane (own stream, own workspace) when its
-// workspace takes at most half of the free device memory, unless
-// ORBIT_WARS_LANES=1.
+// Lane 0 is the handle's stream and workspace. On the tensor-core path a
+// second lane (own stream, own workspace) is added unless ORBIT_WARS_LANES=1:
+// host-IO handles get a full-capacity lane when it takes at most half of the
+// free device memory (the two IO slots' forwards then run at the same time);
+// device-IO handles get a lane for half the capacity, which takes the second
+// half of each large batch while lane 0 runs the first.
 OwStatus add_second_lane(OwPolicy& P) {
   save_lane(P, P.lanes[0]);
   P.n_lanes = 1;
   const char* e = std::getenv("ORBIT_WARS_LANES");
-  if (P.cfg.io != OW_IO_HOST || P.cfg.precision == OW_PRECISION_F32 || (e != nullptr && e[0] == '1'))
-    return st_ok();
+  if (P.cfg.precision == OW_PRECISION_F32 || (e != nullptr && e[0] == '1')) return st_ok();
+  const bool host = P.cfg.io == OW_IO_HOST;
+  const int cap = host ? P.cfg.batch_capacity : (P.cfg.batch_capacity + 1) / 2;
+  const size_t need = host ? P.ws_bytes : P.ws_bytes / 2;
   size_t free_b = 0, total_b = 0;
-  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || P.ws_bytes > free_b / 2) return st_ok();
+  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || need > free_b / 2) return st_ok();
   cudaStream_t s2 = nullptr;
   OW_TRY(cudaStreamCreateWithFlags(&s2, cudaStreamNonBlocking));
   P.stream = s2;
   P.own_stream = true;
   P.ws = nullptr;
-  const OwStatus st = alloc_workspace(P);
+  const OwStatus st = alloc_workspace(P, cap);
   save_lane(P, P.lanes[1]);
   load_lane(P, P.lanes[0]);
   if (st.code != OW_STATUS_OK) {
@@ -1037,6 +1053,7 @@ OwStatus add_second_lane(OwPolicy& P) {
     return st;
   }
   P.n_lanes = 2;
+  P.split_lane = !host;
   return st_ok();
 }
 
@@ -1055,6 +1072,8 @@ void release(OwPolicy* P) {
   if (P->copy_in) cudaStreamDestroy(P->copy_in);
   if (P->copy_out) cudaStreamDestroy(P->copy_out);
   for (auto ev : P->prof_events) cudaEventDestroy(ev);
+  if (P->fork_ev) cudaEventDestroy(P->fork_ev);
+  if (P->join_ev) cudaEventDestroy(P->join_ev);
   for (int k = 1; k < P->n_lanes; ++k) {
     auto& L = P->lanes[k];
     if (L.stream) cudaStreamSynchronize(L.stream);
@@ -1157,7 +1176,7 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
     P->own_stream = true;
   }
   OwStatus s = st_cuda(set_all_gemm_attrs());
-  if (s.code == OW_STATUS_OK) s = alloc_workspace(*P);
+  if (s.code == OW_STATUS_OK) s = alloc_workspace(*P, config->batch_capacity);
   if (s.code == OW_STATUS_OK) s = add_second_lane(*P);
   if (s.code == OW_STATUS_OK) s = upload_weights(*P, weights);
   if (s.code != OW_STATUS_OK) {
@@ -1256,15 +1275,62 @@ OwStatus ow_policy_forward(OwPolicy* policy, const float* features, const int32_
   }
   // Device IO: features / counts / outputs are device pointers; the pipeline
   // reads the features and counts in place and writes the outputs directly.
+  // With a half-capacity second lane, a batch of 64 states or more is split:
+  // lane 1 runs the second half on its own stream and workspace while lane 0
+  // runs the first, and each fills SMs the other leaves idle (between kernels
+  // and in the last round of row tiles). Rows and states are independent and
+  // the Gumbel keys use the global state index, so the outputs are those of
+  // one unsplit forward. Profiled forwards are not split.
+  const size_t N = c.n_entities;
+  void* lo = logits ? logits : P.logits;
+  void* vo = value ? value : P.value;
+  int32_t* ao = actions ? actions : P.actions;
   float* saved_feats = P.feats;
   int* saved_counts = P.counts;
+  int32_t per_fwd = 0;
+  ow_policy_launches_per_forward(&P, &per_fwd);
+  // profiling records this forward only while event capacity remains (profile_begin's max_forwards)
+  const bool profiling = P.prof_on && P.prof_used + static_cast<size_t>(per_fwd) + 1 < P.prof_events.size();
+  const bool split = P.n_lanes == 2 && P.split_lane && !profiling && batch >= 64 &&
+                     batch - (batch + 1) / 2 <= P.lanes[1].cap_states && (batch + 1) / 2 <= P.lanes[0].cap_states;
+  if (!split) {
+    P.feats = const_cast<float*>(features);
+    P.counts = const_cast<int*>(counts);
+    P.state_base = 0;
+    const cudaError_t e = run_blocks(P, batch, seed, lo, vo, ao);
+    P.feats = saved_feats;
+    P.counts = saved_counts;
+    return st_cuda(e);
+  }
+  const int n0 = (batch + 1) / 2, n1 = batch - n0;
+  const size_t lb = c.logits_dtype == OW_DTYPE_BF16 ? 2 : 4, vb = c.value_dtype == OW_DTYPE_BF16 ? 2 : 4;
+  if (P.fork_ev == nullptr) {
+    OW_TRY(cudaEventCreateWithFlags(&P.fork_ev, cudaEventDisableTiming));
+    OW_TRY(cudaEventCreateWithFlags(&P.join_ev, cudaEventDisableTiming));
+  }
+  // fork: lane 1 starts after everything already queued on the handle's stream,
+  // together with lane 0 (starting lane 1 some kernels later measured slower)
+  OW_TRY(cudaEventRecord(P.fork_ev, P.stream));
+  OW_TRY(cudaStreamWaitEvent(P.lanes[1].stream, P.fork_ev, 0));
   P.feats = const_cast<float*>(features);
   P.counts = const_cast<int*>(counts);
-  const cudaError_t e = run_blocks(P, batch, seed, logits ? logits : P.logits, value ? value : P.value,
-                                   actions ? actions : P.actions);
+  P.state_base = 0;
+  cudaError_t e = run_blocks(P, n0, seed, lo, vo, ao);
   P.feats = saved_feats;
   P.counts = saved_counts;
-  return st_cuda(e);
+  OW_TRY(e);
+  load_lane(P, P.lanes[1]);
+  P.feats = const_cast<float*>(features) + static_cast<size_t>(n0) * N * c.features;
+  P.counts = const_cast<int*>(counts) + n0;
+  P.state_base = n0;
+  e = run_blocks(P, n1, seed, static_cast<uint8_t*>(lo) + static_cast<size_t>(n0) * N * c.actions * lb,
+                 static_cast<uint8_t*>(vo) + static_cast<size_t>(n0) * vb, ao + static_cast<size_t>(n0) * N);
+  if (e == cudaSuccess) e = cudaEventRecord(P.join_ev, P.stream);
+  load_lane(P, P.lanes[0]);
+  P.state_base = 0;
+  OW_TRY(e);
+  // join: work queued after this forward on the handle's stream sees both halves
+  return st_cuda(cudaStreamWaitEvent(P.stream, P.join_ev, 0));
 }
 
 OwStatus ow_policy_synchronize(OwPolicy* policy) {
@@ -1273,13 +1339,17 @@ OwStatus ow_policy_synchronize(OwPolicy* policy) {
   for (int k = 1; k < policy->n_lanes; ++k) OW_TRY(cudaStreamSynchronize(policy->lanes[k].stream));
   if (policy->copy_in != nullptr) OW_TRY(cudaStreamSynchronize(policy->copy_in));
   if (policy->copy_out != nullptr) OW_TRY(cudaStreamSynchronize(policy->copy_out));
-  int herr = 0;
-  OW_TRY(cudaMemcpyAsync(&herr, policy->err, sizeof(int), cudaMemcpyDeviceToHost, policy->stream));
+  int herr[2] = {0, 0};
+  OW_TRY(cudaMemcpyAsync(&herr[0], policy->err, sizeof(int), cudaMemcpyDeviceToHost, policy->stream));
+  if (policy->split_lane)  // the second half of split forwards records its errors in lane 1's word
+    OW_TRY(cudaMemcpyAsync(&herr[1], policy->lanes[1].err, sizeof(int), cudaMemcpyDeviceToHost, policy->stream));
   OW_TRY(cudaStreamSynchronize(policy->stream));
-  if (herr != 0) {
+  const int code = herr[0] != 0 ? herr[0] : herr[1];
+  if (code != 0) {
     cudaMemsetAsync(policy->err, 0, sizeof(int), policy->stream);
+    if (policy->split_lane) cudaMemsetAsync(policy->lanes[1].err, 0, sizeof(int), policy->stream);
     cudaStreamSynchronize(policy->stream);
-    return st_rt(device_error_message(herr));
+    return st_rt(device_error_message(code));
   }
   return st_ok();
 }

@@ -232,3 +232,32 @@ def test_submit_wait_pipeline():
         # the handle keeps working synchronously afterwards
         again = pol.forward(fa, ca, seed=1)
         assert np.array_equal(again[0], ref_a[0])
+
+
+@pytest.mark.parametrize("pid,batch", [(4, 256), (2, 1024)])
+def test_split_device_forward_matches_host(pid, batch):
+    """A device-IO forward of 64+ states runs as two halves on two streams; its
+    outputs equal the unsplit host-IO forward bit for bit, Gumbel-sampled actions
+    included (keys use the global state index)."""
+    torch = pytest.importorskip("torch")
+    cfg = ow.preset(pid).with_(batch=batch)
+    w = ow.make_weights(cfg, seed=8)
+    feats, counts = ow.make_inputs(cfg, batch=batch, seed=9)
+    seed = 0x1234567
+    with ow.EncoderPolicy(cfg, w) as pol:
+        h_lg, h_v, h_a = pol.forward(feats, counts, seed=seed)
+    stream = torch.cuda.Stream()
+    with ow.EncoderPolicy(cfg, w, io="device", stream=stream.cuda_stream) as pol:
+        f = torch.from_numpy(feats).cuda()
+        c = torch.from_numpy(counts).cuda()
+        ldt = torch.bfloat16 if cfg.logits_dtype == "bf16" else torch.float32
+        vdt = torch.bfloat16 if cfg.value_dtype == "bf16" else torch.float32
+        lg = torch.empty((batch, cfg.n_entities, cfg.actions), dtype=ldt, device="cuda")
+        v = torch.empty((batch,), dtype=vdt, device="cuda")
+        a = torch.empty((batch, cfg.n_entities), dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        pol.forward_device(f.data_ptr(), c.data_ptr(), batch, lg.data_ptr(), v.data_ptr(), a.data_ptr(), seed=seed)
+        pol.synchronize()
+        assert np.array_equal(lg.float().cpu().numpy(), h_lg)
+        assert np.array_equal(v.float().cpu().numpy(), h_v)
+        assert np.array_equal(a.cpu().numpy(), h_a)
