@@ -459,6 +459,13 @@ __global__ void __launch_bounds__(256) attention_bf16_kernel(const __nv_bfloat16
 }
 
 // ------------------------------------------------------------------ embedding on tensor cores
+// Both kernels are latency-bound: fewer registers per thread buy more resident
+// warps. Measured at config 2: embed 41 -> 34 us with 64-column passes at 5 CTAs
+// per SM, heads 38 -> 31 us at 6 CTAs per SM.
+constexpr int kEmbedGroupCols = 64;  // output columns per MMA pass of embed_mma_kernel
+constexpr int kEmbedMinBlocks = 5;   // register budget: CTAs of 128 threads per SM
+constexpr int kHeadsMinBlocks = 6;
+
 // Entity embedding + the first block's LayerNorm for the bf16 / fp8 paths.
 // Packed row r is entity j = r - offsets[b] of state b (offsets[b] <= r <
 // offsets[b+1], found by binary search). A warp takes 16 consecutive packed
@@ -468,7 +475,7 @@ __global__ void __launch_bounds__(256) attention_bf16_kernel(const __nv_bfloat16
 // two-pass statistics; rows live across the 4 lanes of a quad), [pass 3 e4m3
 // row absmax], last pass writes x (f32) and the LN output.
 template <int D, int LN_MODE>  // LN_MODE 1: bf16 out; 2: e4m3 out + per-row scale
-__global__ void __launch_bounds__(128) embed_mma_kernel(const float* __restrict__ feats, const int* __restrict__ offsets,
+__global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const float* __restrict__ feats, const int* __restrict__ offsets,
                                                         int batch, int n_entities, int n_feat,
                                                         const __nv_bfloat16* __restrict__ w_e16,  // [D][32] bf16
                                                         const float* __restrict__ b_e,
@@ -476,7 +483,8 @@ __global__ void __launch_bounds__(128) embed_mma_kernel(const float* __restrict_
                                                         float* __restrict__ x, void* __restrict__ ln_out,
                                                         float* __restrict__ ln_scale, int* __restrict__ row_slot) {
   constexpr int WP = 40;  // bf16 pitch of staged rows (32 features + pad: conflict-free ldmatrix)
-  constexpr int CG = D / 128;
+  constexpr int kGW = kEmbedGroupCols;  // output columns per MMA pass (accumulators: kGW / 2 registers)
+  constexpr int CG = D / kGW;
   extern __shared__ __align__(16) uint8_t smem_e[];
   __nv_bfloat16* s_w = reinterpret_cast<__nv_bfloat16*>(smem_e);         // [D][WP]
   __nv_bfloat16* s_f = s_w + D * WP;                                      // [4][16][WP]
@@ -573,18 +581,18 @@ __global__ void __launch_bounds__(128) embed_mma_kernel(const float* __restrict_
       float a0 = 0.f, a1 = 0.f;  // per-pass reductions for rows ra, rb
 #pragma unroll 1
       for (int cg = 0; cg < CG; ++cg) {
-        float acc[16][4];
+        float acc[kGW / 8][4];
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
+        for (int nt = 0; nt < kGW / 8; ++nt) {
           acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
           uint32_t b0, b1, b2, b3;
-          ldsm_x4(smem_u32(s_w + (cg * 128 + nt * 8 + (lane & 7)) * WP + (lane >> 3) * 8), b0, b1, b2, b3);
+          ldsm_x4(smem_u32(s_w + (cg * kGW + nt * 8 + (lane & 7)) * WP + (lane >> 3) * 8), b0, b1, b2, b3);
           mma_bf16_16816(acc[nt], qa[0][0], qa[0][1], qa[0][2], qa[0][3], b0, b1);
           mma_bf16_16816(acc[nt], qa[1][0], qa[1][1], qa[1][2], qa[1][3], b2, b3);
         }
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
-          const int col = cg * 128 + nt * 8 + 2 * t;
+        for (int nt = 0; nt < kGW / 8; ++nt) {
+          const int col = cg * kGW + nt * 8 + 2 * t;
           const float bz0 = s_vec[col], bz1 = s_vec[col + 1];
           const float v00 = acc[nt][0] + bz0, v01 = acc[nt][1] + bz1;  // row ra
           const float v10 = acc[nt][2] + bz0, v11 = acc[nt][3] + bz1;  // row rb
@@ -879,7 +887,7 @@ __device__ __forceinline__ void mma_tf32_1688(float (&c)[4], uint32_t a0, uint32
 }
 
 template <int D, int NTILE, bool LOGITS_BF16>  // NTILE = 8-column tiles covering P logits + the value column
-__global__ void __launch_bounds__(128) heads_mma_kernel(const float* __restrict__ y, const int* __restrict__ offsets,
+__global__ void __launch_bounds__(128, kHeadsMinBlocks) heads_mma_kernel(const float* __restrict__ y, const int* __restrict__ offsets,
                                                         int batch, int n_entities, int n_actions,
                                                         const int* __restrict__ row_slot,
                                                         const float* __restrict__ w_p, const float* __restrict__ b_p,
