@@ -124,8 +124,7 @@ __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf
 // weights are 16-byte aligned (padded device layout) and read as three float4;
 // otherwise (the reference's own layout) as scalars.
 template <bool VEC>
-__device__ __forceinline__ float matrix_cell(float v, const float* __restrict__ w12) {
-  float4 a, b, c;
+__device__ __forceinline__ void load_cell_weights(const float* __restrict__ w12, float4& a, float4& b, float4& c) {
   if (VEC) {
     a = __ldg(reinterpret_cast<const float4*>(w12));
     b = __ldg(reinterpret_cast<const float4*>(w12) + 1);
@@ -135,13 +134,23 @@ __device__ __forceinline__ float matrix_cell(float v, const float* __restrict__ 
     b = make_float4(__ldg(w12 + 4), __ldg(w12 + 5), __ldg(w12 + 6), __ldg(w12 + 7));
     c = make_float4(__ldg(w12 + 8), __ldg(w12 + 9), __ldg(w12 + 10), __ldg(w12 + 11));
   }
-  // a = (w0,w1,w2,w3) b = (w4,w5,w6,w7) c = (w8,w9,w10,w11)
+}
+
+// a = (w0,w1,w2,w3) b = (w4,w5,w6,w7) c = (w8,w9,w10,w11)
+__device__ __forceinline__ float matrix_cell_w(float v, const float4 a, const float4 b, const float4 c) {
   const float ha = tanhf(fmaf(v, a.z, a.w));
   const float hb = tanhf(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
   const float g = sigmoid_f(fmaf(v, b.w, c.x));
   const float u = fmaf(hb, c.y, fmaf(ha, c.z, c.w));
   const float r = fmaf(v, 1.0f + a.x, a.y);
   return tanhf(fmaf(g, u, r));
+}
+
+template <bool VEC>
+__device__ __forceinline__ float matrix_cell(float v, const float* __restrict__ w12) {
+  float4 a, b, c;
+  load_cell_weights<VEC>(w12, a, b, c);
+  return matrix_cell_w(v, a, b, c);
 }
 
 __device__ __forceinline__ const float* model_of(const float* __restrict__ all_w, const size_t* __restrict__ idx,
@@ -184,6 +193,156 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// ---- grouped matrix layers: requests of one model processed together
+// A group is up to kGroup requests that use the same model: entry g of the
+// group table holds (model, request 0, ..., request kGroup-1), -1 for an empty
+// slot. A thread keeps its cell's value for every request of the group in
+// registers and loads each layer's 12 weights once for all of them, so weight
+// traffic drops by the group size; the arithmetic per request is that of
+// matrix_cell, in the same order, so the results are unchanged.
+constexpr int kGroup = 8;
+
+// 1g. expand + matrix layers [0, mid) for one group; thread per cell.
+__global__ void __launch_bounds__(256) t2_expand_pre_g(const float* __restrict__ x, const int* __restrict__ groups,
+                                                       const float* __restrict__ all_w, int models, T2Dev L,
+                                                       float* __restrict__ m, int* err) {
+  const int* gr = groups + static_cast<long long>(blockIdx.y) * (kGroup + 1);
+  const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+  if (cell >= L.cells) return;
+  const int model = gr[0];
+  if (model < 0 || model >= models) {  // the host validates the indices; this only guards the table
+    ow::record_error(err, ow::kErrBadModelIndex);
+    return;
+  }
+  const float* w = all_w + static_cast<long long>(model) * L.total;
+  const int s = cell / L.rows, t = cell % L.rows;
+  const float* pw = w + L.pair;
+  const float tail = w[L.src_emb + s] + w[L.tgt_emb + t] + w[L.pair_emb + cell] + w[L.bias];
+  int req[kGroup];
+  float v[kGroup];
+#pragma unroll
+  for (int i = 0; i < kGroup; ++i) {
+    req[i] = gr[1 + i];
+    float a = 0.0f;
+    if (req[i] >= 0) {
+      const float* xs = x + (static_cast<long long>(req[i]) * L.rows + s) * kFeatures;
+      const float* xt = x + (static_cast<long long>(req[i]) * L.rows + t) * kFeatures;
+#pragma unroll
+      for (int f = 0; f < static_cast<int>(kFeatures); ++f) a = fmaf(xs[f], pw[f], a);
+#pragma unroll
+      for (int f = 0; f < static_cast<int>(kFeatures); ++f) a = fmaf(xt[f], pw[kFeatures + f], a);
+    }
+    a += tail;
+    v[i] = tanhf(a);
+  }
+  const float* mw = w + L.matrix + static_cast<long long>(cell) * kCellWeights;
+  const long long per_layer = static_cast<long long>(L.cells) * kCellWeights;
+  for (int l = 0; l < L.mid; ++l) {
+    float4 a, b, c;
+    load_cell_weights<true>(mw + l * per_layer, a, b, c);
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i) v[i] = matrix_cell_w(v[i], a, b, c);
+  }
+#pragma unroll
+  for (int i = 0; i < kGroup; ++i)
+    if (req[i] >= 0) m[static_cast<long long>(req[i]) * L.cells + cell] = v[i];
+}
+
+// 3g. matrix layers [mid, layers) + collapse for one group: CTA = 4 rows of
+// every request of the group (blockDim = 4 * rows, at most 512 threads).
+__global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict__ groups,
+                                                          const float* __restrict__ all_w, int models, T2Dev L,
+                                                          const float* __restrict__ m, float* __restrict__ out,
+                                                          int* err) {
+  constexpr int kRows = 4;  // rows of each request per CTA
+  __shared__ float s_m[kGroup][kRows][kMaxRows];
+  __shared__ float s_send[kGroup][kRows][kTargets];
+  const int* gr = groups + static_cast<long long>(blockIdx.y) * (kGroup + 1);
+  const int row0 = blockIdx.x * kRows;
+  const int model = gr[0];
+  if (model < 0 || model >= models) {
+    if (threadIdx.x == 0) ow::record_error(err, ow::kErrBadModelIndex);
+    return;
+  }
+  int req[kGroup];
+#pragma unroll
+  for (int i = 0; i < kGroup; ++i) req[i] = gr[1 + i];
+  const float* w = all_w + static_cast<long long>(model) * L.total;
+  const long long per_layer = static_cast<long long>(L.cells) * kCellWeights;
+  for (int i = threadIdx.x; i < kRows * L.rows; i += blockDim.x) {
+    const int lr = i / L.rows, t = i % L.rows;
+    const int row = row0 + lr;
+    if (row >= L.rows) continue;
+    const int cell = row * L.rows + t;
+    float v[kGroup];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g)
+      v[g] = req[g] >= 0 ? m[static_cast<long long>(req[g]) * L.cells + cell] : 0.0f;
+    const float* mw = w + L.matrix + static_cast<long long>(cell) * kCellWeights;
+    for (int l = L.mid; l < L.layers; ++l) {
+      float4 a, b, c;
+      load_cell_weights<true>(mw + l * per_layer, a, b, c);
+#pragma unroll
+      for (int g = 0; g < kGroup; ++g) v[g] = matrix_cell_w(v[g], a, b, c);
+    }
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) s_m[g][lr][t] = v[g];
+  }
+  __syncthreads();
+  // warp per (request, row, action): target softmax -> expected index; send softmax -> sigmoid
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int item = warp; item < kGroup * kRows * static_cast<int>(kTargets); item += nwarps) {
+    const int g = item / (kRows * static_cast<int>(kTargets));
+    const int rest = item % (kRows * static_cast<int>(kTargets));
+    const int lr = rest / kTargets, a = rest % kTargets;
+    const int row = row0 + lr;
+    if (row >= L.rows || req[g] < 0) continue;
+    const float* sc = w + L.scalars + a * kOutScalars;
+    const float* tb = w + L.tbias + static_cast<long long>(a) * L.rows;
+    const float* sb = w + L.sbias + static_cast<long long>(a) * L.rows;
+    const float s0 = sc[0], s1 = sc[1];
+    float tmax = -INFINITY, smax = -INFINITY;
+    for (int t = lane; t < L.rows; t += 32) {
+      tmax = fmaxf(tmax, fmaf(s_m[g][lr][t], s0, tb[t]));
+      smax = fmaxf(smax, fmaf(s_m[g][lr][t], s1, sb[t]));
+    }
+    tmax = ow::warp_max(tmax);
+    smax = ow::warp_max(smax);
+    float tden = 0.0f, tnum = 0.0f, sden = 0.0f, snum = 0.0f;
+    const float inv_last = 1.0f / static_cast<float>(L.rows - 1);
+    for (int t = lane; t < L.rows; t += 32) {
+      const float v = s_m[g][lr][t];
+      const float et = expf(fmaf(v, s0, tb[t]) - tmax);
+      tden += et;
+      tnum = fmaf(et, static_cast<float>(t) * inv_last, tnum);
+      const float es = expf(fmaf(v, s1, sb[t]) - smax);
+      sden += es;
+      snum = fmaf(es, v, snum);
+    }
+    tden = ow::warp_sum(tden);
+    tnum = ow::warp_sum(tnum);
+    sden = ow::warp_sum(sden);
+    snum = ow::warp_sum(snum);
+    if (lane == 0) {
+      const float frac = fminf(fmaxf(tnum / tden, 0.0f), 1.0f);
+      const float logit = fmaf(snum / sden, sc[2], sc[4]);
+      s_send[g][lr][a] = sigmoid_f(logit * sc[3]);
+      out[(static_cast<long long>(req[g]) * L.rows + row) * kOutPerRow + a * 2] = frac;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kGroup * kRows) {
+    const int g = threadIdx.x / kRows, lr = threadIdx.x % kRows, row = row0 + lr;
+    if (row < L.rows && req[g] >= 0) {
+      float sum = 0.0f;
+      for (int a = 0; a < static_cast<int>(kTargets); ++a) sum += s_send[g][lr][a];
+      const float norm = sum > 1.0f ? 1.0f / sum : 1.0f;
+      for (int a = 0; a < static_cast<int>(kTargets); ++a)
+        out[(static_cast<long long>(req[g]) * L.rows + row) * kOutPerRow + a * 2 + 1] = s_send[g][lr][a] * norm;
+    }
+  }
 }
 
 // 2^x for x <= 0 on the FMA pipe: Cody-Waite style reduction x = n + f with
@@ -516,6 +675,9 @@ struct Workspace {
   size_t m_cap = 0;
   size_t* idx = nullptr;
   size_t idx_cap = 0;
+  int* groups = nullptr;  // model groups of the current call: (model, kGroup request indices) each
+  size_t groups_cap = 0;
+  std::vector<int> host_groups;
   int* err = nullptr;
   cudaStream_t stream = nullptr;
   // device timing (orbit_wars_cuda_true2d_profile_begin/_end): an event before
@@ -600,6 +762,24 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
     didx = W.idx;
   }
   const int models = static_cast<int>(W.models);
+  // group the requests by model (counting sort; host-validated indices), kGroup per group
+  std::vector<int>& gt = W.host_groups;
+  gt.clear();
+  {
+    std::vector<int> start(static_cast<size_t>(models) + 1, 0), order(n);
+    for (size_t r = 0; r < n; ++r) ++start[(model_indices != nullptr ? model_indices[r] : 0) + 1];
+    for (int k = 0; k < models; ++k) start[k + 1] += start[k];
+    std::vector<int> fill(start.begin(), start.end() - 1);
+    for (size_t r = 0; r < n; ++r) order[fill[model_indices != nullptr ? model_indices[r] : 0]++] = static_cast<int>(r);
+    for (int k = 0; k < models; ++k)
+      for (int i = start[k]; i < start[k + 1]; i += kGroup) {
+        gt.push_back(k);
+        for (int j = 0; j < kGroup; ++j) gt.push_back(i + j < start[k + 1] ? order[i + j] : -1);
+      }
+  }
+  const size_t n_groups = gt.size() / (kGroup + 1);
+  T2_TRY(ensure(W.groups, W.groups_cap, gt.size()));
+  T2_TRY(cudaMemcpyAsync(W.groups, gt.data(), gt.size() * sizeof(int), cudaMemcpyHostToDevice, W.stream));
   const bool prof = W.prof_on && W.prof_used + 4 <= W.prof_events.size();
   auto mark = [&](const char* name) {
     if (prof) {
@@ -607,16 +787,16 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
       W.prof_names[W.prof_used++] = name;
     }
   };
-  const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n));
+  const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n_groups));
   mark("t2_expand_pre");
-  t2_expand_pre<true><<<g1, 256, 0, W.stream>>>(W.in, didx, W.weights, models, D, W.m, W.err);
+  t2_expand_pre_g<<<g1, 256, 0, W.stream>>>(W.in, W.groups, W.weights, models, D, W.m, W.err);
   T2_TRY(cudaGetLastError());
   mark("t2_attention");
   T2_TRY(launch_t2_attention(didx, W.weights, models, D, W.m, W.err, static_cast<unsigned>(n), W.stream));
-  const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n));
+  const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n_groups));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   mark("t2_post_collapse");
-  t2_post_collapse<true><<<g3, threads3, 0, W.stream>>>(didx, W.weights, models, D, W.m, W.out, W.err);
+  t2_post_collapse_g<<<g3, threads3, 0, W.stream>>>(W.groups, W.weights, models, D, W.m, W.out, W.err);
   T2_TRY(cudaGetLastError());
   mark(nullptr);
   int herr = 0;
