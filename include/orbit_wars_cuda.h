@@ -153,6 +153,44 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(
     OrbitWarsCudaTrue2DShape shape,
     void* stream);
 
+/* Forward + decode on the device -- no counterpart in the reference ABI.
+ * Runs ..._forward_many_resident on the resident population, then the part of
+ * the engine's decoder that needs no geometry (crates/orbit-wars-core/src/
+ * decoder.rs:85-124, target_row_from_fraction :457-461) before anything is
+ * copied back. Per request r and row s (request_count x row_count each):
+ * row_planet_ids[r][s] (-1 = no planet, the encoder's NO_PLANET_ID),
+ * source_owned[r][s] (non-zero when the row's planet belongs to the player),
+ * source_ships[r][s] (its ships). Per (r, s, target slot a), 12 slots:
+ * target_rows = the target row (-1 when the decoder skips the pair) and
+ * ship_counts = floor(ships * clamp(send_fraction, 0, 1)) (0 when skipped).
+ * The engine then runs only its geometry (intercept angles) for the pairs with
+ * target_rows >= 0. output_rows (request_count x row_count x 24, the raw
+ * outputs) may be NULL. A non-finite output of a decoded source returns
+ * RUNTIME_ERROR "non-finite model output", as the decoder's NonFiniteModelOutput. */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_many_resident(
+    const float* input_rows,
+    const size_t* model_indices,
+    const int32_t* row_planet_ids,
+    const uint8_t* source_owned,
+    const float* source_ships,
+    int32_t* target_rows,
+    int32_t* ship_counts,
+    float* output_rows,
+    size_t request_count,
+    OrbitWarsCudaTrue2DShape shape);
+
+/* The same decode on outputs the caller already has (host buffers:
+ * output_rows request_count x row_count x 24, the rest as above). */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_outputs(
+    const float* output_rows,
+    const int32_t* row_planet_ids,
+    const uint8_t* source_owned,
+    const float* source_ships,
+    int32_t* target_rows,
+    int32_t* ship_counts,
+    size_t request_count,
+    size_t row_count);
+
 /* Device timing of the True2D forwards -- no counterpart in the reference ABI;
  * for benchmarks. profile_begin arms CUDA events around each kernel of the next
  * `max_calls` calls of ..._true2d_forward / _forward_many / _forward_many_resident

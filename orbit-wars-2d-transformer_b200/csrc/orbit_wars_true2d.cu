@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -656,6 +657,63 @@ T2Dev ref_layout_dev(const T2Layout& L) {
   return d;
 }
 
+// ---------------------------------------------------------------- device decode
+// The part of the engine's decoder that needs no geometry
+// (crates/orbit-wars-core/src/decoder.rs:85-124, target_row_from_fraction
+// :457-461), on the forward's outputs still in HBM. CTA per request, thread per
+// (source row, target slot). Active rows are the rows whose planet id is not
+// NO_PLANET_ID (-1), in row order (encoder.rs:14-26). A source is decoded only
+// when it is active and owned by the player; then, per slot:
+//   target_row = active[min(floor(clamp(target_fraction, 0, 1) * n_active), n_active - 1)],
+//   skipped when it is the source row;
+//   send = clamp(send_fraction, 0, 1), skipped when send <= 0;
+//   ship_count = floor(ships * send), skipped when < 1.
+// target_rows[r][s][a] is the target row or -1 (skipped), ship_counts the count
+// or 0. A non-finite output of a decoded source raises the device error word,
+// as the decoder returns NonFiniteModelOutput.
+__global__ void __launch_bounds__(512) t2_decode(const float* __restrict__ out, const int32_t* __restrict__ row_ids,
+                                                 const uint8_t* __restrict__ owned, const float* __restrict__ ships,
+                                                 int rows, int32_t* __restrict__ target_rows,
+                                                 int32_t* __restrict__ ship_counts, int* err) {
+  __shared__ int s_active[kMaxRows];
+  __shared__ int s_n;
+  const int r = blockIdx.x;
+  const int32_t* ids = row_ids + static_cast<long long>(r) * rows;
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int i = 0; i < rows; ++i)
+      if (ids[i] != -1) s_active[n++] = i;
+    s_n = n;
+  }
+  __syncthreads();
+  const int n_active = s_n;
+  for (int item = threadIdx.x; item < rows * static_cast<int>(kTargets); item += blockDim.x) {
+    const int src = item / kTargets, a = item % kTargets;
+    const long long o = (static_cast<long long>(r) * rows + src) * kTargets + a;
+    int target = -1, count = 0;
+    if (ids[src] != -1 && owned[static_cast<long long>(r) * rows + src] != 0 && n_active > 0) {
+      const float* pair = out + (static_cast<long long>(r) * rows + src) * kOutPerRow + a * 2;
+      const float tf = pair[0], sf = pair[1];
+      if (!isfinite(tf) || !isfinite(sf)) {
+        ow::record_error(err, ow::kErrNonFiniteOutput);
+      } else {
+        const int scaled = static_cast<int>(floorf(fminf(fmaxf(tf, 0.0f), 1.0f) * static_cast<float>(n_active)));
+        const int trow = s_active[min(scaled, n_active - 1)];
+        const float send = fminf(fmaxf(sf, 0.0f), 1.0f);
+        if (trow != src && send > 0.0f) {
+          const int c = static_cast<int>(floorf(ships[static_cast<long long>(r) * rows + src] * send));
+          if (c >= 1) {
+            target = trow;
+            count = c;
+          }
+        }
+      }
+    }
+    target_rows[o] = target;
+    ship_counts[o] = count;
+  }
+}
+
 // ---------------------------------------------------------------- process-global workspace
 struct Workspace {
   std::mutex mu;
@@ -675,6 +733,12 @@ struct Workspace {
   size_t m_cap = 0;
   size_t* idx = nullptr;
   size_t idx_cap = 0;
+  int32_t* dec_ids = nullptr;  // device decode: row planet ids, owned flags, ships; outputs
+  uint8_t* dec_owned = nullptr;
+  float* dec_ships = nullptr;
+  int32_t* dec_rows = nullptr;
+  int32_t* dec_counts = nullptr;
+  size_t dec_cap = 0;
   int* groups = nullptr;  // model groups of the current call: (model, kGroup request indices) each
   size_t groups_cap = 0;
   std::vector<int> host_groups;
@@ -724,6 +788,7 @@ bool same_shape(const OrbitWarsCudaTrue2DShape& a, const OrbitWarsCudaTrue2DShap
 const char* device_error_text(int code) {
   switch (code) {
     case ow::kErrBadModelIndex: return "model index outside the population";
+    case ow::kErrNonFiniteOutput: return "non-finite model output";
     default: return "device error";
   }
 }
@@ -745,8 +810,17 @@ OrbitWarsCudaStatus upload(Workspace& W, const float* all_w, size_t models, cons
 }
 
 // Runs the forward for `n` requests whose inputs are host buffers.
+// Decode inputs and outputs (host buffers) of orbit_wars_cuda_true2d_decode_many_resident.
+struct DecodeIo {
+  const int32_t* row_ids;
+  const uint8_t* owned;
+  const float* ships;
+  int32_t* target_rows;
+  int32_t* ship_counts;
+};
+
 OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const size_t* model_indices, float* output_rows,
-                                size_t n, const OrbitWarsCudaTrue2DShape& shape) {
+                                size_t n, const OrbitWarsCudaTrue2DShape& shape, const DecodeIo* dec = nullptr) {
   const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
   const T2Dev D = dev_layout(L);
   const size_t in_n = n * L.rows * kFeatures, out_n = n * L.rows * kOutPerRow, m_n = n * L.cells;
@@ -799,8 +873,33 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   t2_post_collapse_g<<<g3, threads3, 0, W.stream>>>(W.groups, W.weights, models, D, W.m, W.out, W.err);
   T2_TRY(cudaGetLastError());
   mark(nullptr);
+  if (dec != nullptr) {
+    const size_t rn = n * L.rows, dn = n * L.rows * kTargets;
+    if (dn > W.dec_cap) {
+      for (void* q : {static_cast<void*>(W.dec_ids), static_cast<void*>(W.dec_owned), static_cast<void*>(W.dec_ships),
+                      static_cast<void*>(W.dec_rows), static_cast<void*>(W.dec_counts)})
+        if (q != nullptr) cudaFree(q);
+      W.dec_ids = nullptr; W.dec_owned = nullptr; W.dec_ships = nullptr; W.dec_rows = nullptr; W.dec_counts = nullptr;
+      W.dec_cap = 0;
+      T2_TRY(cudaMalloc(&W.dec_ids, rn * sizeof(int32_t)));
+      T2_TRY(cudaMalloc(&W.dec_owned, rn));
+      T2_TRY(cudaMalloc(&W.dec_ships, rn * sizeof(float)));
+      T2_TRY(cudaMalloc(&W.dec_rows, dn * sizeof(int32_t)));
+      T2_TRY(cudaMalloc(&W.dec_counts, dn * sizeof(int32_t)));
+      W.dec_cap = dn;
+    }
+    T2_TRY(cudaMemcpyAsync(W.dec_ids, dec->row_ids, rn * sizeof(int32_t), cudaMemcpyHostToDevice, W.stream));
+    T2_TRY(cudaMemcpyAsync(W.dec_owned, dec->owned, rn, cudaMemcpyHostToDevice, W.stream));
+    T2_TRY(cudaMemcpyAsync(W.dec_ships, dec->ships, rn * sizeof(float), cudaMemcpyHostToDevice, W.stream));
+    t2_decode<<<static_cast<unsigned>(n), 512, 0, W.stream>>>(W.out, W.dec_ids, W.dec_owned, W.dec_ships,
+                                                              D.rows, W.dec_rows, W.dec_counts, W.err);
+    T2_TRY(cudaGetLastError());
+    T2_TRY(cudaMemcpyAsync(dec->target_rows, W.dec_rows, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
+    T2_TRY(cudaMemcpyAsync(dec->ship_counts, W.dec_counts, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
+  }
   int herr = 0;
-  T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+  if (output_rows != nullptr)
+    T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
   T2_TRY(cudaMemcpyAsync(&herr, W.err, sizeof(int), cudaMemcpyDeviceToHost, W.stream));
   T2_TRY(cudaStreamSynchronize(W.stream));
   if (herr != 0) return rt(device_error_text(herr));
@@ -948,6 +1047,69 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_many_resident(const float* in
   for (size_t r = 0; r < request_count; ++r)
     if (model_indices[r] >= W.models) return bad("model index out of range");
   return run_forward(W, input_rows, model_indices, output_rows, request_count, shape);
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_many_resident(
+    const float* input_rows, const size_t* model_indices, const int32_t* row_planet_ids,
+    const uint8_t* source_owned, const float* source_ships, int32_t* target_rows, int32_t* ship_counts,
+    float* output_rows, size_t request_count, OrbitWarsCudaTrue2DShape shape) {
+  if (input_rows == nullptr || model_indices == nullptr || row_planet_ids == nullptr || source_owned == nullptr ||
+      source_ships == nullptr || target_rows == nullptr || ship_counts == nullptr || request_count == 0)
+    return bad("invalid true2d decode buffer");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  if (!W.resident) return rt("true2d population is not loaded");
+  if (!same_shape(W.shape, shape)) return bad("true2d shape differs from the resident population");
+  if (request_count > W.request_capacity) return rt("true2d request capacity exceeded");
+  for (size_t r = 0; r < request_count; ++r)
+    if (model_indices[r] >= W.models) return bad("model index out of range");
+  const DecodeIo dec{row_planet_ids, source_owned, source_ships, target_rows, ship_counts};
+  return run_forward(W, input_rows, model_indices, output_rows, request_count, shape, &dec);
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_outputs(const float* output_rows, const int32_t* row_planet_ids,
+                                                          const uint8_t* source_owned, const float* source_ships,
+                                                          int32_t* target_rows, int32_t* ship_counts,
+                                                          size_t request_count, size_t row_count) {
+  if (output_rows == nullptr || row_planet_ids == nullptr || source_owned == nullptr || source_ships == nullptr ||
+      target_rows == nullptr || ship_counts == nullptr || request_count == 0)
+    return bad("invalid true2d decode buffer");
+  if (row_count < kMinRows || row_count > kMaxRows) return bad("invalid row count");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  T2_TRY(ensure_common(W));
+  const size_t out_n = request_count * row_count * kOutPerRow;
+  T2_TRY(ensure(W.out, W.out_cap, out_n));
+  T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
+  T2_TRY(cudaMemcpyAsync(W.out, output_rows, out_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
+  const size_t rn = request_count * row_count, dn = rn * kTargets;
+  if (dn > W.dec_cap) {
+    for (void* q : {static_cast<void*>(W.dec_ids), static_cast<void*>(W.dec_owned), static_cast<void*>(W.dec_ships),
+                    static_cast<void*>(W.dec_rows), static_cast<void*>(W.dec_counts)})
+      if (q != nullptr) cudaFree(q);
+    W.dec_ids = nullptr; W.dec_owned = nullptr; W.dec_ships = nullptr; W.dec_rows = nullptr; W.dec_counts = nullptr;
+    W.dec_cap = 0;
+    T2_TRY(cudaMalloc(&W.dec_ids, rn * sizeof(int32_t)));
+    T2_TRY(cudaMalloc(&W.dec_owned, rn));
+    T2_TRY(cudaMalloc(&W.dec_ships, rn * sizeof(float)));
+    T2_TRY(cudaMalloc(&W.dec_rows, dn * sizeof(int32_t)));
+    T2_TRY(cudaMalloc(&W.dec_counts, dn * sizeof(int32_t)));
+    W.dec_cap = dn;
+  }
+  T2_TRY(cudaMemcpyAsync(W.dec_ids, row_planet_ids, rn * sizeof(int32_t), cudaMemcpyHostToDevice, W.stream));
+  T2_TRY(cudaMemcpyAsync(W.dec_owned, source_owned, rn, cudaMemcpyHostToDevice, W.stream));
+  T2_TRY(cudaMemcpyAsync(W.dec_ships, source_ships, rn * sizeof(float), cudaMemcpyHostToDevice, W.stream));
+  t2_decode<<<static_cast<unsigned>(request_count), 512, 0, W.stream>>>(
+      W.out, W.dec_ids, W.dec_owned, W.dec_ships, static_cast<int>(row_count), W.dec_rows, W.dec_counts, W.err);
+  T2_TRY(cudaGetLastError());
+  T2_TRY(cudaMemcpyAsync(target_rows, W.dec_rows, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
+  T2_TRY(cudaMemcpyAsync(ship_counts, W.dec_counts, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
+  int herr = 0;
+  T2_TRY(cudaMemcpyAsync(&herr, W.err, sizeof(int), cudaMemcpyDeviceToHost, W.stream));
+  T2_TRY(cudaStreamSynchronize(W.stream));
+  if (herr != 0) return rt(device_error_text(herr));
+  return ok();
 }
 
 typedef OrbitWarsCudaStatus (*TrainFn)(const float*, const float*, const int*, const float*, const size_t*, float*,

@@ -21,6 +21,7 @@ enum DeviceError : int {
   kErrWaitTimeout = 1,    // an mbarrier wait exceeded the wall-clock limit
   kErrBadCount = 2,       // an entity count outside [0, N]
   kErrBadModelIndex = 3,  // a model index outside the population
+  kErrNonFiniteOutput = 4,  // a non-finite model output reached the device decode
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait

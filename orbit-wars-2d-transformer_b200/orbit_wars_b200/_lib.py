@@ -84,6 +84,8 @@ SIGNATURES = {
     "orbit_wars_cuda_true2d_upload_population": (Status, [P, SZ, SZ, True2DShapeC]),
     "orbit_wars_cuda_true2d_forward_many_resident": (Status, [P, P, P, SZ, True2DShapeC]),
     "orbit_wars_cuda_true2d_forward_noalloc": (Status, [P, P, P, SZ, True2DShapeC, P]),
+    "orbit_wars_cuda_true2d_decode_many_resident": (Status, [P, P, P, P, P, P, P, P, SZ, True2DShapeC]),
+    "orbit_wars_cuda_true2d_decode_outputs": (Status, [P, P, P, P, P, P, SZ, SZ]),
     "orbit_wars_cuda_true2d_profile_begin": (Status, [C.c_int32]),
     "orbit_wars_cuda_true2d_profile_end": (Status, [C.POINTER(KernelTimingC), C.c_int32, C.POINTER(C.c_int32)]),
     "orbit_wars_cuda_true2d_train_full_attention": (

@@ -126,3 +126,41 @@ class CudaTrue2D:
         n = C.c_int32(0)
         _lib.check("cuda_true2d_profile_end", self.lib.orbit_wars_cuda_true2d_profile_end(arr, cap, C.byref(n)))
         return {arr[i].name.decode(): (int(arr[i].launches), float(arr[i].total_ms)) for i in range(n.value)}
+
+    def _decode_bufs(self, n: int, rows: int, row_planet_ids, source_owned, source_ships):
+        ids = np.ascontiguousarray(row_planet_ids, dtype=np.int32).reshape(n, rows)
+        own = np.ascontiguousarray(source_owned, dtype=np.uint8).reshape(n, rows)
+        ships = np.ascontiguousarray(source_ships, dtype=np.float32).reshape(n, rows)
+        tr = np.empty((n, rows, TARGETS), dtype=np.int32)
+        sc = np.empty((n, rows, TARGETS), dtype=np.int32)
+        return ids, own, ships, tr, sc
+
+    def decode_population_resident(self, input_rows, model_indices, population_size: int, row_planet_ids,
+                                   source_owned, source_ships, shape: True2DShape = True2DShape(),
+                                   with_outputs: bool = False):
+        """Resident forward + device decode: (target_rows, ship_counts[, outputs]) per (request, row, slot);
+        target_rows -1 / ship_counts 0 where the decoder skips (decoder.rs:85-124)."""
+        idx = np.ascontiguousarray(model_indices, dtype=np.uintp)
+        n = idx.size
+        x = _f32(input_rows)
+        if x.size != n * shape.rows * INPUT_FEATURES:
+            raise ValueError("cuda_true2d_decode_input_count_mismatch")
+        if np.any(idx >= population_size):
+            raise ValueError("cuda_true2d_decode_model_index_out_of_range")
+        ids, own, ships, tr, sc = self._decode_bufs(n, shape.rows, row_planet_ids, source_owned, source_ships)
+        out = np.zeros(n * shape.rows * OUTPUT_FEATURES, dtype=np.float32) if with_outputs else None
+        _lib.check("cuda_true2d_decode_many_resident", self.lib.orbit_wars_cuda_true2d_decode_many_resident(
+            x.ctypes.data, idx.ctypes.data, ids.ctypes.data, own.ctypes.data, ships.ctypes.data, tr.ctypes.data,
+            sc.ctypes.data, None if out is None else out.ctypes.data, n, shape.c()))
+        return (tr, sc, out.reshape(n, shape.rows, TARGETS, 2)) if with_outputs else (tr, sc)
+
+    def decode_outputs(self, outputs, row_planet_ids, source_owned, source_ships, rows: int = 64):
+        """Device decode of given outputs [n, rows, 12, 2] -> (target_rows, ship_counts)."""
+        o = _f32(outputs)
+        n = o.size // (rows * OUTPUT_FEATURES)
+        ids, own, ships, tr, sc = self._decode_bufs(n, rows, row_planet_ids, source_owned, source_ships)
+        _lib.check("cuda_true2d_decode_outputs", self.lib.orbit_wars_cuda_true2d_decode_outputs(
+            o.ctypes.data, ids.ctypes.data, own.ctypes.data, ships.ctypes.data, tr.ctypes.data, sc.ctypes.data,
+            n, rows))
+        return tr, sc
+
