@@ -583,6 +583,47 @@ def reference_gpu_true2d(args, shape, pop, x, idx, steps: int) -> dict | None:
             "library": "oracle/_ref/liborbit_wars_cuda_ref.so (reference source, nvcc sm_100a)", "output": out}
 
 
+def true2d_turn(args, lib, shape, steps: int) -> dict:
+    """One policy turn on the device through orbit_wars_cuda_true2d_play_many_resident: seeded game states
+    (host CSR planets) in, decoded (target row, ship count) pairs out; encoder, forward and decode kernels
+    timed by CUDA events. Beside it, the encoder oracle (a C++ restatement of encoder.rs:37-208) on all host
+    threads encodes the same batch: the per-turn host work the device encoder removes
+    (crates/orbit-wars-trainer/src/main.rs:3599-3667 runs encode_state on 12 threads)."""
+    from orbit_wars_b200 import synth
+    from oracle import bind
+    batch, rg, rp = synth.game_batch(args.seed + 1, max(1, args.requests // 3 + 8), players=4)
+    n = min(args.requests, rg.size)
+    rg, rp = rg[:n], rp[:n]
+    idx = (np.arange(n, dtype=np.uint64) * 2654435761 % args.models).astype(np.uintp)
+    for _ in range(3):
+        ids, tr, sc = lib.play_population_resident(batch, rg, rp, idx, args.models, shape)
+    lib.profile_begin(steps)
+    wall = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ids, tr, sc = lib.play_population_resident(batch, rg, rp, idx, args.models, shape)
+        wall.append(time.perf_counter() - t0)
+    prof = lib.profile_end()
+    kern = {k: round(ms * 1000.0 / max(c, 1), 2) for k, (c, ms) in prof.items()}
+    threads = os.cpu_count() or 1
+    bind.encode_batch(batch, rg, rp, threads=threads)
+    t0, reps = time.perf_counter(), 0
+    while time.perf_counter() - t0 < 2.0:
+        bind.encode_batch(batch, rg, rp, threads=threads)
+        reps += 1
+    cpu_rate = n * reps / (time.perf_counter() - t0)
+    enc_us = kern.get("t2_encode", 0.0)
+    h2d = int(batch.planets.nbytes + batch.initial_planets.nbytes + 8 * 3 * (batch.game_count + 1) + 8 * n
+              + (0 if batch.comet_planet_ids is None else batch.comet_planet_ids.nbytes) + 8 * n)
+    return {"value": n * steps / float(np.sum(wall)), "unit": T2_UNIT, "requests": n, "games": batch.game_count,
+            "steps": steps, "timing": "wall clock per synchronous play_many_resident call (host game states in, "
+                                      "row ids + target rows + ship counts out)",
+            "kernel_avg_us": kern, "encode_requests_per_s_device": round(n / (enc_us * 1e-6), 1) if enc_us else None,
+            "encode_requests_per_s_cpu_oracle": round(cpu_rate, 1), "cpu_threads": threads,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(n * shape.rows * 4 * (1 + 2 * 12)),
+            "commands_per_request": round(float((tr >= 0).sum()) / n, 2)}
+
+
 def run_true2d(args) -> None:
     import torch
     import torch.distributed as dist
@@ -660,6 +701,7 @@ def run_true2d(args) -> None:
             ro = ref_gpu.pop("output")
             ref_gpu["max_abs_diff_vs_ours"] = float(np.abs(ro - out.reshape(-1)).max())
             ref_gpu["ours_e2e_over_reference"] = round(e2e["value"] / ref_gpu["value"], 3)
+    turn = true2d_turn(args, lib, shape, steps=min(args.steps, 20)) if rank == 0 and world == 1 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = true2d_cpu_reference(args, shape, pop, per, x, target_s=12.0)
@@ -675,7 +717,7 @@ def run_true2d(args) -> None:
                        "parallelism": f"replicas x{world} (the reference ABI is single-device)",
                        "value_timing": "sum of the three kernels' CUDA events per call (inputs already on the device)"},
             "e2e": e2e, "gpu_launches": 3 * args.steps, "roofline": roof, "cpu_baseline": cpu,
-            "reference_gpu": ref_gpu, "clocks": clocks, "kernels": kernels,
+            "reference_gpu": ref_gpu, "clocks": clocks, "kernels": kernels, "turn": turn,
             "outputs_finite": bool(np.isfinite(out).all()),
         }
         print(json.dumps(line), flush=True)

@@ -153,25 +153,34 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(
     OrbitWarsCudaTrue2DShape shape,
     void* stream);
 
+/* Row flags written by the device encoder and read by the device decode, one
+ * byte per (request, row). */
+#define ORBIT_WARS_ROW_OWNED 1u  /* the row's planet belongs to the player */
+#define ORBIT_WARS_ROW_ABSENT 2u /* the row names a planet no longer on the map */
+
 /* Forward + decode on the device -- no counterpart in the reference ABI.
  * Runs ..._forward_many_resident on the resident population, then the part of
  * the engine's decoder that needs no geometry (crates/orbit-wars-core/src/
  * decoder.rs:85-124, target_row_from_fraction :457-461) before anything is
  * copied back. Per request r and row s (request_count x row_count each):
  * row_planet_ids[r][s] (-1 = no planet, the encoder's NO_PLANET_ID),
- * source_owned[r][s] (non-zero when the row's planet belongs to the player),
- * source_ships[r][s] (its ships). Per (r, s, target slot a), 12 slots:
- * target_rows = the target row (-1 when the decoder skips the pair) and
- * ship_counts = floor(ships * clamp(send_fraction, 0, 1)) (0 when skipped).
- * The engine then runs only its geometry (intercept angles) for the pairs with
- * target_rows >= 0. output_rows (request_count x row_count x 24, the raw
- * outputs) may be NULL. A non-finite output of a decoded source returns
- * RUNTIME_ERROR "non-finite model output", as the decoder's NonFiniteModelOutput. */
+ * row_flags[r][s] (ORBIT_WARS_ROW_OWNED when the row's planet belongs to the
+ * player; ORBIT_WARS_ROW_ABSENT when it is not on the map -- the decoder's
+ * planet_by_id misses, decoder.rs:93 and :112), source_ships[r][s] (its ships).
+ * A source row is decoded when it is active, owned and not absent. Per
+ * (r, s, target slot a), 12 slots: target_rows = the target row (-1 when the
+ * decoder skips the pair: the source row itself, an absent target, send <= 0,
+ * or fewer than one ship) and ship_counts = floor(ships * clamp(send_fraction,
+ * 0, 1)) (0 when skipped). The engine then runs only its geometry (intercept
+ * angles) for the pairs with target_rows >= 0. output_rows (request_count x
+ * row_count x 24, the raw outputs) may be NULL. A non-finite output of a
+ * decoded source returns RUNTIME_ERROR "non-finite model output", as the
+ * decoder's NonFiniteModelOutput. */
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_many_resident(
     const float* input_rows,
     const size_t* model_indices,
     const int32_t* row_planet_ids,
-    const uint8_t* source_owned,
+    const uint8_t* row_flags,
     const float* source_ships,
     int32_t* target_rows,
     int32_t* ship_counts,
@@ -184,17 +193,135 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_many_resident(
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_outputs(
     const float* output_rows,
     const int32_t* row_planet_ids,
-    const uint8_t* source_owned,
+    const uint8_t* row_flags,
     const float* source_ships,
     int32_t* target_rows,
     int32_t* ship_counts,
     size_t request_count,
     size_t row_count);
 
+/* ---- device encoder -- no counterpart in the reference ABI ----------------
+ * crates/orbit-wars-core/src/encoder.rs:37-208 (encode_state) on the device,
+ * for a batch of requests over a batch of game states. */
+
+/* crates/orbit-wars-core/src/types.rs:6-16, field for field (a #[repr(C)]
+ * Planet on the engine side has this layout: 36 bytes). */
+typedef struct OrbitWarsPlanet {
+  int32_t id;
+  int32_t owner;
+  float x;
+  float y;
+  float radius;
+  float ships;
+  float production;
+  float velocity_x;
+  float velocity_y;
+} OrbitWarsPlanet;
+
+/* The AgentConfig fields encode_state reads (crates/orbit-wars-core/src/
+ * config.rs:115-140); orbit_wars_encoder_config_default fills the defaults
+ * of config.rs:1-19. Checked as AgentConfig::validate checks them
+ * (config.rs:335-377): max_rows = initial + comet + padding slots, max_rows
+ * and initial slots positive, 0 < pivot < cap, max_players = 4, the seven
+ * owner classes finite and distinct, board size finite and positive,
+ * fleet_speed_max >= 1; and here also max_rows <= 64 (the model's rows). */
+typedef struct OrbitWarsEncoderConfig {
+  size_t max_rows;
+  size_t initial_planet_slots;
+  size_t comet_slots;
+  size_t padding_slots;
+  float ship_log_pivot;
+  float ship_log_cap;
+  size_t max_players;
+  float owner_class_own;
+  float owner_class_enemy_1;
+  float owner_class_enemy_2;
+  float owner_class_enemy_3;
+  float owner_class_neutral;
+  float owner_class_empty;
+  float owner_class_absent_on_map;
+  float board_size;
+  float fleet_speed_max;
+} OrbitWarsEncoderConfig;
+
+void orbit_wars_encoder_config_default(OrbitWarsEncoderConfig* out);
+
+/* Game states in CSR form (host buffers): game g's current planets are
+ * planets[planet_offsets[g] .. planet_offsets[g + 1]), its initial planets
+ * initial_planets[initial_offsets[g] ..), its comet planet ids
+ * comet_planet_ids[comet_offsets[g] ..); each offsets array has game_count + 1
+ * entries starting at 0. comet_planet_ids and comet_offsets may both be NULL
+ * (no comets, as the trainer encodes: crates/orbit-wars-trainer/src/
+ * main.rs:3633-3639). */
+typedef struct OrbitWarsGameBatch {
+  const OrbitWarsPlanet* planets;
+  const size_t* planet_offsets;
+  const OrbitWarsPlanet* initial_planets;
+  const size_t* initial_offsets;
+  const int32_t* comet_planet_ids;
+  const size_t* comet_offsets;
+  size_t game_count;
+} OrbitWarsGameBatch;
+
+/* encode_errors values: 0 = encoded; then EncodeError (encoder.rs:29-35) in
+ * declaration order. */
+#define ORBIT_WARS_ENCODE_OK 0
+#define ORBIT_WARS_ENCODE_INVALID_CONFIG 1
+#define ORBIT_WARS_ENCODE_INVALID_OWNER_CLASS 2
+#define ORBIT_WARS_ENCODE_MISSING_HOME_PLANET 3
+#define ORBIT_WARS_ENCODE_ROW_OVERFLOW 4
+
+/* Encodes request r = encode_state(game request_games[r]'s planets, initial
+ * planets and comet ids, request_players[r], config) for every request.
+ * Outputs (host buffers, request_count x max_rows each): input_rows x 7 floats
+ * in the order pack_rows_into writes them (crates/orbit-wars-trainer/src/
+ * cuda_true2d.rs:469-487), ready for ..._forward_many_resident;
+ * row_planet_ids; row_flags (ORBIT_WARS_ROW_*); row_ships (the row planet's
+ * current ships, 0 for empty and absent rows; may be NULL); encode_errors
+ * (one per request; may be NULL). A request that fails gets empty rows. When
+ * any request fails the call returns BAD_ARGUMENT naming the first failing
+ * request's error, after filling every output. A bad config returns
+ * BAD_ARGUMENT "invalid encoder config" (EncodeError::InvalidConfig). */
+OrbitWarsCudaStatus orbit_wars_cuda_encode_states(
+    const OrbitWarsGameBatch* games,
+    const uint32_t* request_games,
+    const int32_t* request_players,
+    size_t request_count,
+    const OrbitWarsEncoderConfig* config,
+    float* input_rows,
+    int32_t* row_planet_ids,
+    uint8_t* row_flags,
+    float* row_ships,
+    int32_t* encode_errors);
+
+/* One policy turn on the device: encode (as ..._encode_states), forward on the
+ * resident population (model_indices per request, as ..._forward_many_resident)
+ * and decode (as ..._decode_many_resident), with only the game states going up
+ * and row_planet_ids (request_count x row_count) plus target_rows / ship_counts
+ * (request_count x row_count x 12) coming back. input_rows (request_count x
+ * row_count x 7) and output_rows (x 24) may be NULL; when given they receive
+ * the encoded rows and the raw outputs. config.max_rows must equal
+ * shape.row_count. Errors as the three calls it fuses. */
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_play_many_resident(
+    const OrbitWarsGameBatch* games,
+    const uint32_t* request_games,
+    const int32_t* request_players,
+    const size_t* model_indices,
+    size_t request_count,
+    const OrbitWarsEncoderConfig* config,
+    int32_t* row_planet_ids,
+    int32_t* target_rows,
+    int32_t* ship_counts,
+    int32_t* encode_errors,
+    float* input_rows,
+    float* output_rows,
+    OrbitWarsCudaTrue2DShape shape);
+
 /* Device timing of the True2D forwards -- no counterpart in the reference ABI;
  * for benchmarks. profile_begin arms CUDA events around each kernel of the next
- * `max_calls` calls of ..._true2d_forward / _forward_many / _forward_many_resident
- * (events only, no extra synchronisation). profile_end waits for the library's
+ * `max_calls` calls of ..._true2d_forward / _forward_many / _forward_many_resident /
+ * _decode_many_resident / _play_many_resident (encoder, forward kernels and
+ * decode; events only, no extra synchronisation). profile_end waits for the library's
  * stream and returns, per kernel name, the launches and the summed
  * event-to-event milliseconds; names are static strings. */
 typedef struct OrbitWarsCudaKernelTiming {

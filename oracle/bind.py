@@ -6,6 +6,7 @@ loads it.
 
     policy_forward(cfg, weights, features, counts, f64=True)  encoder policy (SPEC.md)
     true2d_forward(...)                                        True2D (true2d_model.rs restatement)
+    encode_batch(batch, request_games, request_players)        state encoder (encoder.rs restatement)
 """
 from __future__ import annotations
 
@@ -24,6 +25,27 @@ _lib = None
 
 class OwoShape(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("n_entities", "features", "d_model", "heads", "ffn", "layers", "actions")]
+
+
+class OwoEncoderConfig(C.Structure):
+    """The AgentConfig fields the encoder reads (crates/orbit-wars-core/src/config.rs:115-140)."""
+    _fields_ = [("max_rows", C.c_size_t), ("initial_planet_slots", C.c_size_t), ("comet_slots", C.c_size_t),
+                ("padding_slots", C.c_size_t), ("ship_log_pivot", C.c_float), ("ship_log_cap", C.c_float),
+                ("max_players", C.c_size_t), ("owner_class_own", C.c_float), ("owner_class_enemy_1", C.c_float),
+                ("owner_class_enemy_2", C.c_float), ("owner_class_enemy_3", C.c_float),
+                ("owner_class_neutral", C.c_float), ("owner_class_empty", C.c_float),
+                ("owner_class_absent_on_map", C.c_float), ("board_size", C.c_float),
+                ("fleet_speed_max", C.c_float)]
+
+
+def default_encoder_config() -> OwoEncoderConfig:
+    """config.rs:1-19 (MAX_ROWS .. FLEET_SPEED_MAX)."""
+    return OwoEncoderConfig(64, 40, 20, 4, 1000.0, 100000.0, 4, 1.0, 0.75, 0.5, 0.25, 0.0, -0.5, -1.0, 100.0, 6.0)
+
+
+# types.rs:6-16
+PLANET_DTYPE = np.dtype([("id", "<i4"), ("owner", "<i4"), ("x", "<f4"), ("y", "<f4"), ("radius", "<f4"),
+                         ("ships", "<f4"), ("production", "<f4"), ("velocity_x", "<f4"), ("velocity_y", "<f4")])
 
 
 def build(ref: bool = False) -> None:
@@ -61,6 +83,13 @@ def load():
                                        C.c_size_t, C.c_size_t, C.c_size_t, C.c_int]
     lib.owo_trainable_forward.restype = C.c_int
     lib.owo_trainable_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p] + [C.c_size_t] * 5
+    lib.owo_encode_state.restype = C.c_int
+    lib.owo_encode_state.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t,
+                                     C.c_int32, C.POINTER(OwoEncoderConfig), C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_void_p]
+    lib.owo_encode_batch.restype = None
+    lib.owo_encode_batch.argtypes = [C.c_void_p] * 8 + [C.c_size_t, C.POINTER(OwoEncoderConfig)] + [C.c_void_p] * 5 + [
+        C.c_int]
     lib.owo_sinusoid_fill.restype = None
     lib.owo_sinusoid_fill.argtypes = [C.c_void_p, C.c_size_t, C.c_float, C.c_float]
     _lib = lib
@@ -172,3 +201,48 @@ def load_ref_cpu():
     lib.ref_true2d_cpu_reference.restype = None
     lib.ref_true2d_cpu_reference.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
     return lib
+
+
+def _planets(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=PLANET_DTYPE)
+
+
+def encode_state(planets, initial_planets, comet_planet_ids, player: int, cfg: OwoEncoderConfig | None = None):
+    """encode_state (encoder.rs:37-125) for one request -> (rows [R, 7] f32, ids [R] int32, flags [R] uint8,
+    ships [R] f32, error code); error 0 = encoded, else the EncodeError index + 1 with empty rows."""
+    cfg = cfg or default_encoder_config()
+    p, i = _planets(planets), _planets(initial_planets)
+    cm = np.ascontiguousarray(comet_planet_ids if comet_planet_ids is not None else [], dtype=np.int32)
+    R = min(int(cfg.max_rows), 64)
+    rows = np.zeros((R, 7), np.float32)
+    ids = np.zeros(R, np.int32)
+    flags = np.zeros(R, np.uint8)
+    ships = np.zeros(R, np.float32)
+    e = load().owo_encode_state(p.ctypes.data, p.size, i.ctypes.data, i.size, cm.ctypes.data, cm.size, int(player),
+                                C.byref(cfg), rows.ctypes.data, ids.ctypes.data, flags.ctypes.data, ships.ctypes.data)
+    return rows, ids, flags, ships, int(e)
+
+
+def encode_batch(batch, request_games, request_players, cfg: OwoEncoderConfig | None = None, threads: int = 0):
+    """A CSR batch (attributes planets, planet_offsets, initial_planets, initial_offsets, comet_planet_ids,
+    comet_offsets) -> (rows [n, R, 7], ids [n, R], flags [n, R], ships [n, R], errors [n])."""
+    cfg = cfg or default_encoder_config()
+    p, i = _planets(batch.planets), _planets(batch.initial_planets)
+    po = np.ascontiguousarray(batch.planet_offsets, dtype=np.uint64)
+    io = np.ascontiguousarray(batch.initial_offsets, dtype=np.uint64)
+    cm = None if batch.comet_planet_ids is None else np.ascontiguousarray(batch.comet_planet_ids, dtype=np.int32)
+    co = None if batch.comet_offsets is None else np.ascontiguousarray(batch.comet_offsets, dtype=np.uint64)
+    rg = np.ascontiguousarray(request_games, dtype=np.uint32)
+    rp = np.ascontiguousarray(request_players, dtype=np.int32)
+    n = rg.size
+    R = min(int(cfg.max_rows), 64)
+    rows = np.zeros((n, R, 7), np.float32)
+    ids = np.zeros((n, R), np.int32)
+    flags = np.zeros((n, R), np.uint8)
+    ships = np.zeros((n, R), np.float32)
+    errors = np.zeros(n, np.int32)
+    load().owo_encode_batch(p.ctypes.data, po.ctypes.data, i.ctypes.data, io.ctypes.data,
+                            None if cm is None else cm.ctypes.data, None if co is None else co.ctypes.data,
+                            rg.ctypes.data, rp.ctypes.data, n, C.byref(cfg), rows.ctypes.data, ids.ctypes.data,
+                            flags.ctypes.data, ships.ctypes.data, errors.ctypes.data, threads)
+    return rows, ids, flags, ships, errors

@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "ow_common.cuh"
+#include "ow_encode.cuh"
 
 namespace {
 
@@ -663,22 +664,25 @@ T2Dev ref_layout_dev(const T2Layout& L) {
 // :457-461), on the forward's outputs still in HBM. CTA per request, thread per
 // (source row, target slot). Active rows are the rows whose planet id is not
 // NO_PLANET_ID (-1), in row order (encoder.rs:14-26). A source is decoded only
-// when it is active and owned by the player; then, per slot:
+// when it is active, owned by the player and on the map (flags, the encoder's
+// row flags: kRowOwned set, kRowAbsent clear); then, per slot:
 //   target_row = active[min(floor(clamp(target_fraction, 0, 1) * n_active), n_active - 1)],
-//   skipped when it is the source row;
+//   skipped when it is the source row or its planet is absent from the map
+//   (planet_by_id misses, decoder.rs:112-114);
 //   send = clamp(send_fraction, 0, 1), skipped when send <= 0;
 //   ship_count = floor(ships * send), skipped when < 1.
 // target_rows[r][s][a] is the target row or -1 (skipped), ship_counts the count
 // or 0. A non-finite output of a decoded source raises the device error word,
 // as the decoder returns NonFiniteModelOutput.
 __global__ void __launch_bounds__(512) t2_decode(const float* __restrict__ out, const int32_t* __restrict__ row_ids,
-                                                 const uint8_t* __restrict__ owned, const float* __restrict__ ships,
+                                                 const uint8_t* __restrict__ flags, const float* __restrict__ ships,
                                                  int rows, int32_t* __restrict__ target_rows,
                                                  int32_t* __restrict__ ship_counts, int* err) {
   __shared__ int s_active[kMaxRows];
   __shared__ int s_n;
   const int r = blockIdx.x;
   const int32_t* ids = row_ids + static_cast<long long>(r) * rows;
+  const uint8_t* fl = flags + static_cast<long long>(r) * rows;
   if (threadIdx.x == 0) {
     int n = 0;
     for (int i = 0; i < rows; ++i)
@@ -691,7 +695,7 @@ __global__ void __launch_bounds__(512) t2_decode(const float* __restrict__ out, 
     const int src = item / kTargets, a = item % kTargets;
     const long long o = (static_cast<long long>(r) * rows + src) * kTargets + a;
     int target = -1, count = 0;
-    if (ids[src] != -1 && owned[static_cast<long long>(r) * rows + src] != 0 && n_active > 0) {
+    if (ids[src] != -1 && (fl[src] & (enc::kRowOwned | enc::kRowAbsent)) == enc::kRowOwned && n_active > 0) {
       const float* pair = out + (static_cast<long long>(r) * rows + src) * kOutPerRow + a * 2;
       const float tf = pair[0], sf = pair[1];
       if (!isfinite(tf) || !isfinite(sf)) {
@@ -700,7 +704,7 @@ __global__ void __launch_bounds__(512) t2_decode(const float* __restrict__ out, 
         const int scaled = static_cast<int>(floorf(fminf(fmaxf(tf, 0.0f), 1.0f) * static_cast<float>(n_active)));
         const int trow = s_active[min(scaled, n_active - 1)];
         const float send = fminf(fmaxf(sf, 0.0f), 1.0f);
-        if (trow != src && send > 0.0f) {
+        if (trow != src && (fl[trow] & enc::kRowAbsent) == 0 && send > 0.0f) {
           const int c = static_cast<int>(floorf(ships[static_cast<long long>(r) * rows + src] * send));
           if (c >= 1) {
             target = trow;
@@ -733,12 +737,20 @@ struct Workspace {
   size_t m_cap = 0;
   size_t* idx = nullptr;
   size_t idx_cap = 0;
-  int32_t* dec_ids = nullptr;  // device decode: row planet ids, owned flags, ships; outputs
-  uint8_t* dec_owned = nullptr;
+  int32_t* dec_ids = nullptr;  // device decode: row planet ids, row flags, ships; outputs
+  uint8_t* dec_flags = nullptr;
   float* dec_ships = nullptr;
   int32_t* dec_rows = nullptr;
   int32_t* dec_counts = nullptr;
   size_t dec_cap = 0;
+  // device encoder: game states packed into pinned memory, uploaded in one copy
+  unsigned char* enc_host = nullptr;
+  size_t enc_host_cap = 0;
+  unsigned char* enc_dev = nullptr;
+  size_t enc_dev_cap = 0;
+  int32_t* enc_err = nullptr;
+  size_t enc_err_cap = 0;
+  std::vector<int32_t> host_err;
   int* groups = nullptr;  // model groups of the current call: (model, kGroup request indices) each
   size_t groups_cap = 0;
   std::vector<int> host_groups;
@@ -781,6 +793,25 @@ cudaError_t ensure_common(Workspace& W) {
   return cudaSuccess;
 }
 
+// Device buffers of the decode for rn = requests x rows (ids, flags, ships) and
+// rn x 12 outputs.
+cudaError_t ensure_decode(Workspace& W, size_t rn) {
+  const size_t dn = rn * kTargets;
+  if (dn <= W.dec_cap && W.dec_ids != nullptr) return cudaSuccess;
+  for (void* q : {static_cast<void*>(W.dec_ids), static_cast<void*>(W.dec_flags), static_cast<void*>(W.dec_ships),
+                  static_cast<void*>(W.dec_rows), static_cast<void*>(W.dec_counts)})
+    if (q != nullptr) cudaFree(q);
+  W.dec_ids = nullptr; W.dec_flags = nullptr; W.dec_ships = nullptr; W.dec_rows = nullptr; W.dec_counts = nullptr;
+  W.dec_cap = 0;
+  cudaError_t e = cudaMalloc(&W.dec_ids, rn * sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&W.dec_flags, rn);
+  if (e == cudaSuccess) e = cudaMalloc(&W.dec_ships, rn * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&W.dec_rows, dn * sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&W.dec_counts, dn * sizeof(int32_t));
+  if (e == cudaSuccess) W.dec_cap = dn;
+  return e;
+}
+
 bool same_shape(const OrbitWarsCudaTrue2DShape& a, const OrbitWarsCudaTrue2DShape& b) {
   return a.layer_count == b.layer_count && a.row_count == b.row_count && a.head_count == b.head_count;
 }
@@ -809,27 +840,42 @@ OrbitWarsCudaStatus upload(Workspace& W, const float* all_w, size_t models, cons
   return ok();
 }
 
-// Runs the forward for `n` requests whose inputs are host buffers.
-// Decode inputs and outputs (host buffers) of orbit_wars_cuda_true2d_decode_many_resident.
+// Waits for the stream and reports the device error word.
+OrbitWarsCudaStatus finish(Workspace& W) {
+  int herr = 0;
+  T2_TRY(cudaMemcpyAsync(&herr, W.err, sizeof(int), cudaMemcpyDeviceToHost, W.stream));
+  T2_TRY(cudaStreamSynchronize(W.stream));
+  if (herr != 0) return rt(device_error_text(herr));
+  return ok();
+}
+
+// Decode inputs and outputs of orbit_wars_cuda_true2d_decode_many_resident:
+// host buffers, or (row_ids == nullptr) inputs already in W.dec_* (written by
+// the device encoder).
 struct DecodeIo {
   const int32_t* row_ids;
-  const uint8_t* owned;
+  const uint8_t* flags;
   const float* ships;
   int32_t* target_rows;
   int32_t* ship_counts;
 };
 
+// Runs the forward for `n` requests: inputs from the host buffer input_rows, or
+// already in W.in when input_rows is nullptr (written by the device encoder).
 OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const size_t* model_indices, float* output_rows,
-                                size_t n, const OrbitWarsCudaTrue2DShape& shape, const DecodeIo* dec = nullptr) {
+                                size_t n, const OrbitWarsCudaTrue2DShape& shape, const DecodeIo* dec = nullptr,
+                                bool sync = true) {
   const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
   const T2Dev D = dev_layout(L);
   const size_t in_n = n * L.rows * kFeatures, out_n = n * L.rows * kOutPerRow, m_n = n * L.cells;
-  T2_TRY(ensure(W.in, W.in_cap, in_n));
+  if (input_rows != nullptr) T2_TRY(ensure(W.in, W.in_cap, in_n));
   T2_TRY(ensure(W.out, W.out_cap, out_n));
   T2_TRY(ensure(W.m, W.m_cap, m_n));
   T2_TRY(ensure(W.idx, W.idx_cap, n));
-  T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
-  T2_TRY(cudaMemcpyAsync(W.in, input_rows, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
+  if (input_rows != nullptr) {
+    T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
+    T2_TRY(cudaMemcpyAsync(W.in, input_rows, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
+  }
   const size_t* didx = nullptr;
   if (model_indices != nullptr) {
     T2_TRY(cudaMemcpyAsync(W.idx, model_indices, n * sizeof(size_t), cudaMemcpyHostToDevice, W.stream));
@@ -854,7 +900,7 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   const size_t n_groups = gt.size() / (kGroup + 1);
   T2_TRY(ensure(W.groups, W.groups_cap, gt.size()));
   T2_TRY(cudaMemcpyAsync(W.groups, gt.data(), gt.size() * sizeof(int), cudaMemcpyHostToDevice, W.stream));
-  const bool prof = W.prof_on && W.prof_used + 4 <= W.prof_events.size();
+  const bool prof = W.prof_on && W.prof_used + (dec != nullptr ? 6 : 4) <= W.prof_events.size();
   auto mark = [&](const char* name) {
     if (prof) {
       cudaEventRecord(W.prof_events[W.prof_used], W.stream);
@@ -875,34 +921,164 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   mark(nullptr);
   if (dec != nullptr) {
     const size_t rn = n * L.rows, dn = n * L.rows * kTargets;
-    if (dn > W.dec_cap) {
-      for (void* q : {static_cast<void*>(W.dec_ids), static_cast<void*>(W.dec_owned), static_cast<void*>(W.dec_ships),
-                      static_cast<void*>(W.dec_rows), static_cast<void*>(W.dec_counts)})
-        if (q != nullptr) cudaFree(q);
-      W.dec_ids = nullptr; W.dec_owned = nullptr; W.dec_ships = nullptr; W.dec_rows = nullptr; W.dec_counts = nullptr;
-      W.dec_cap = 0;
-      T2_TRY(cudaMalloc(&W.dec_ids, rn * sizeof(int32_t)));
-      T2_TRY(cudaMalloc(&W.dec_owned, rn));
-      T2_TRY(cudaMalloc(&W.dec_ships, rn * sizeof(float)));
-      T2_TRY(cudaMalloc(&W.dec_rows, dn * sizeof(int32_t)));
-      T2_TRY(cudaMalloc(&W.dec_counts, dn * sizeof(int32_t)));
-      W.dec_cap = dn;
+    if (dec->row_ids != nullptr) {
+      T2_TRY(ensure_decode(W, rn));
+      T2_TRY(cudaMemcpyAsync(W.dec_ids, dec->row_ids, rn * sizeof(int32_t), cudaMemcpyHostToDevice, W.stream));
+      T2_TRY(cudaMemcpyAsync(W.dec_flags, dec->flags, rn, cudaMemcpyHostToDevice, W.stream));
+      T2_TRY(cudaMemcpyAsync(W.dec_ships, dec->ships, rn * sizeof(float), cudaMemcpyHostToDevice, W.stream));
     }
-    T2_TRY(cudaMemcpyAsync(W.dec_ids, dec->row_ids, rn * sizeof(int32_t), cudaMemcpyHostToDevice, W.stream));
-    T2_TRY(cudaMemcpyAsync(W.dec_owned, dec->owned, rn, cudaMemcpyHostToDevice, W.stream));
-    T2_TRY(cudaMemcpyAsync(W.dec_ships, dec->ships, rn * sizeof(float), cudaMemcpyHostToDevice, W.stream));
-    t2_decode<<<static_cast<unsigned>(n), 512, 0, W.stream>>>(W.out, W.dec_ids, W.dec_owned, W.dec_ships,
+    mark("t2_decode");
+    t2_decode<<<static_cast<unsigned>(n), 512, 0, W.stream>>>(W.out, W.dec_ids, W.dec_flags, W.dec_ships,
                                                               D.rows, W.dec_rows, W.dec_counts, W.err);
     T2_TRY(cudaGetLastError());
+    mark(nullptr);
     T2_TRY(cudaMemcpyAsync(dec->target_rows, W.dec_rows, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
     T2_TRY(cudaMemcpyAsync(dec->ship_counts, W.dec_counts, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
   }
-  int herr = 0;
   if (output_rows != nullptr)
     T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
-  T2_TRY(cudaMemcpyAsync(&herr, W.err, sizeof(int), cudaMemcpyDeviceToHost, W.stream));
+  if (!sync) return ok();
+  return finish(W);
+}
+
+// ---------------------------------------------------------------- device encoder, host side
+// AgentConfig::validate (crates/orbit-wars-core/src/config.rs:335-377) on the
+// fields the encoder reads, plus the 64-row bound of EncodedState.
+bool encoder_config_ok(const OrbitWarsEncoderConfig& c) {
+  if (c.max_rows != c.initial_planet_slots + c.comet_slots + c.padding_slots) return false;
+  if (c.max_rows == 0 || c.initial_planet_slots == 0 || c.max_rows > static_cast<size_t>(enc::kMaxRows)) return false;
+  if (!(c.ship_log_pivot > 0.0f && c.ship_log_cap > c.ship_log_pivot)) return false;
+  if (c.max_players != 4) return false;  // OWNER_CLASS_PLAYER_SLOTS
+  const float cls[7] = {c.owner_class_own,     c.owner_class_enemy_1, c.owner_class_enemy_2,
+                        c.owner_class_enemy_3, c.owner_class_neutral, c.owner_class_empty,
+                        c.owner_class_absent_on_map};
+  for (int i = 0; i < 7; ++i) {
+    if (!std::isfinite(cls[i])) return false;
+    for (int j = i + 1; j < 7; ++j)
+      if (cls[i] == cls[j]) return false;
+  }
+  if (!(std::isfinite(c.board_size) && c.board_size > 0.0f)) return false;
+  if (!(c.fleet_speed_max >= 1.0f)) return false;
+  return true;
+}
+
+const char* encode_error_text(int code) {
+  switch (code) {
+    case enc::kInvalidConfig: return "encode failed: InvalidConfig";
+    case enc::kInvalidOwnerClass: return "encode failed: InvalidOwnerClass";
+    case enc::kMissingHome: return "encode failed: MissingHomePlanet";
+    case enc::kRowOverflow: return "encode failed: RowOverflow";
+    default: return "encode failed";
+  }
+}
+
+bool offsets_ok(const size_t* off, size_t games, size_t* max_len) {
+  if (off == nullptr || off[0] != 0) return false;
+  size_t m = 0;
+  for (size_t g = 0; g < games; ++g) {
+    if (off[g + 1] < off[g]) return false;
+    m = std::max(m, off[g + 1] - off[g]);
+  }
+  *max_len = m;
+  return true;
+}
+
+// Validates the batch (before any device call), packs it into pinned memory,
+// uploads it in one copy and launches the encoder into W.in (rows), W.dec_ids / dec_flags / dec_ships and
+// W.enc_err, all on W.stream; W.err is cleared first.
+OrbitWarsCudaStatus launch_encode(Workspace& W, const OrbitWarsGameBatch* games, const uint32_t* request_games,
+                                  const int32_t* request_players, size_t n, const OrbitWarsEncoderConfig& cfg) {
+  if (games == nullptr || request_games == nullptr || request_players == nullptr || n == 0 ||
+      games->game_count == 0 || games->planets == nullptr || games->initial_planets == nullptr)
+    return bad("invalid encode buffer");
+  if (!encoder_config_ok(cfg)) return bad("invalid encoder config");
+  const size_t G = games->game_count;
+  const bool comets = games->comet_planet_ids != nullptr || games->comet_offsets != nullptr;
+  size_t max_p = 0, max_i = 0, max_c = 0;
+  if (!offsets_ok(games->planet_offsets, G, &max_p) || !offsets_ok(games->initial_offsets, G, &max_i) ||
+      (comets && (games->comet_planet_ids == nullptr || !offsets_ok(games->comet_offsets, G, &max_c))))
+    return bad("invalid game offsets");
+  for (size_t r = 0; r < n; ++r)
+    if (request_games[r] >= G) return bad("request game out of range");
+  const size_t warp_bytes = enc::warp_smem_bytes(static_cast<int>(std::min<size_t>(max_p, 1 << 20)),
+                                                 static_cast<int>(std::min<size_t>(max_i, 1 << 20)));
+  constexpr size_t kSmemCap = 200 * 1024;
+  if (max_p > 65535 || max_c > 65535 || warp_bytes > kSmemCap) return bad("game too large for the device encoder");
+  const int warps = static_cast<int>(std::min<size_t>(enc::kWarps, kSmemCap / warp_bytes));
+  T2_TRY(ensure_common(W));
+  const size_t np = games->planet_offsets[G], ni = games->initial_offsets[G], nc = comets ? games->comet_offsets[G] : 0;
+  auto up16 = [](size_t b) { return (b + 15) & ~size_t(15); };
+  const size_t o_p = 0, o_i = o_p + up16(np * sizeof(enc::Planet)), o_c = o_i + up16(ni * sizeof(enc::Planet));
+  const size_t o_po = o_c + up16(nc * sizeof(int32_t)), o_io = o_po + up16((G + 1) * 8), o_co = o_io + up16((G + 1) * 8);
+  const size_t o_rg = o_co + up16((G + 1) * 8), o_rp = o_rg + up16(n * 4), total = o_rp + up16(n * 4);
+  if (total > W.enc_host_cap) {
+    if (W.enc_host != nullptr) cudaFreeHost(W.enc_host);
+    W.enc_host = nullptr;
+    W.enc_host_cap = 0;
+    T2_TRY(cudaHostAlloc(reinterpret_cast<void**>(&W.enc_host), total, cudaHostAllocDefault));
+    W.enc_host_cap = total;
+  }
+  T2_TRY(ensure(W.enc_dev, W.enc_dev_cap, total));
+  T2_TRY(ensure(W.enc_err, W.enc_err_cap, n));
+  unsigned char* h = W.enc_host;
+  std::memcpy(h + o_p, games->planets, np * sizeof(enc::Planet));
+  std::memcpy(h + o_i, games->initial_planets, ni * sizeof(enc::Planet));
+  if (nc > 0) std::memcpy(h + o_c, games->comet_planet_ids, nc * sizeof(int32_t));
+  std::memcpy(h + o_po, games->planet_offsets, (G + 1) * 8);
+  std::memcpy(h + o_io, games->initial_offsets, (G + 1) * 8);
+  if (comets) std::memcpy(h + o_co, games->comet_offsets, (G + 1) * 8);
+  std::memcpy(h + o_rg, request_games, n * 4);
+  std::memcpy(h + o_rp, request_players, n * 4);
+  T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
+  T2_TRY(cudaMemcpyAsync(W.enc_dev, h, total, cudaMemcpyHostToDevice, W.stream));
+  const size_t rn = n * cfg.max_rows;
+  T2_TRY(ensure(W.in, W.in_cap, rn * kFeatures));
+  T2_TRY(ensure_decode(W, rn));
+  unsigned char* d = W.enc_dev;
+  enc::Batch b{reinterpret_cast<const enc::Planet*>(d + o_p), reinterpret_cast<const unsigned long long*>(d + o_po),
+               reinterpret_cast<const enc::Planet*>(d + o_i), reinterpret_cast<const unsigned long long*>(d + o_io),
+               comets ? reinterpret_cast<const int32_t*>(d + o_c) : nullptr,
+               comets ? reinterpret_cast<const unsigned long long*>(d + o_co) : nullptr,
+               reinterpret_cast<const uint32_t*>(d + o_rg), reinterpret_cast<const int32_t*>(d + o_rp)};
+  const enc::Cfg c{static_cast<int>(cfg.max_rows), static_cast<int>(cfg.initial_planet_slots),
+                   static_cast<int>(cfg.comet_slots), static_cast<int>(cfg.max_players),
+                   cfg.ship_log_pivot, cfg.ship_log_cap,
+                   cfg.owner_class_own, cfg.owner_class_enemy_1, cfg.owner_class_enemy_2, cfg.owner_class_enemy_3,
+                   cfg.owner_class_neutral, cfg.owner_class_empty, cfg.owner_class_absent_on_map,
+                   cfg.board_size, cfg.fleet_speed_max};
+  const enc::Out o{W.in, W.dec_ids, W.dec_flags, W.dec_ships, W.enc_err};
+  const size_t smem = warp_bytes * warps;
+  if (smem > 48 * 1024)
+    T2_TRY(cudaFuncSetAttribute(enc::encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem)));
+  const bool prof = W.prof_on && W.prof_used + 2 <= W.prof_events.size();
+  if (prof) {
+    cudaEventRecord(W.prof_events[W.prof_used], W.stream);
+    W.prof_names[W.prof_used++] = "t2_encode";
+  }
+  const unsigned blocks = static_cast<unsigned>((n + warps - 1) / warps);
+  enc::encode_kernel<<<blocks, warps * 32, smem, W.stream>>>(b, c, static_cast<int>(n), static_cast<int>(max_p),
+                                                             static_cast<int>(max_i), warps, o);
+  T2_TRY(cudaGetLastError());
+  if (prof) {
+    cudaEventRecord(W.prof_events[W.prof_used], W.stream);
+    W.prof_names[W.prof_used++] = nullptr;
+  }
+  return ok();
+}
+
+// Copies the per-request encode errors back (after the stream is synchronised by
+// the caller) and returns the first failing request's error.
+OrbitWarsCudaStatus encode_result(Workspace& W, size_t n, int32_t* encode_errors) {
+  int32_t* e = encode_errors;
+  if (e == nullptr) {
+    W.host_err.resize(n);
+    e = W.host_err.data();
+  }
+  T2_TRY(cudaMemcpyAsync(e, W.enc_err, n * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
   T2_TRY(cudaStreamSynchronize(W.stream));
-  if (herr != 0) return rt(device_error_text(herr));
+  for (size_t r = 0; r < n; ++r)
+    if (e[r] != enc::kOk) return bad(encode_error_text(e[r]));
   return ok();
 }
 
@@ -1050,10 +1226,10 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_many_resident(const float* in
 }
 
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_many_resident(
-    const float* input_rows, const size_t* model_indices, const int32_t* row_planet_ids,
-    const uint8_t* source_owned, const float* source_ships, int32_t* target_rows, int32_t* ship_counts,
-    float* output_rows, size_t request_count, OrbitWarsCudaTrue2DShape shape) {
-  if (input_rows == nullptr || model_indices == nullptr || row_planet_ids == nullptr || source_owned == nullptr ||
+    const float* input_rows, const size_t* model_indices, const int32_t* row_planet_ids, const uint8_t* row_flags,
+    const float* source_ships, int32_t* target_rows, int32_t* ship_counts, float* output_rows, size_t request_count,
+    OrbitWarsCudaTrue2DShape shape) {
+  if (input_rows == nullptr || model_indices == nullptr || row_planet_ids == nullptr || row_flags == nullptr ||
       source_ships == nullptr || target_rows == nullptr || ship_counts == nullptr || request_count == 0)
     return bad("invalid true2d decode buffer");
   if (!shape_ok(shape)) return bad("invalid true2d shape");
@@ -1064,15 +1240,15 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_many_resident(
   if (request_count > W.request_capacity) return rt("true2d request capacity exceeded");
   for (size_t r = 0; r < request_count; ++r)
     if (model_indices[r] >= W.models) return bad("model index out of range");
-  const DecodeIo dec{row_planet_ids, source_owned, source_ships, target_rows, ship_counts};
+  const DecodeIo dec{row_planet_ids, row_flags, source_ships, target_rows, ship_counts};
   return run_forward(W, input_rows, model_indices, output_rows, request_count, shape, &dec);
 }
 
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_outputs(const float* output_rows, const int32_t* row_planet_ids,
-                                                          const uint8_t* source_owned, const float* source_ships,
+                                                          const uint8_t* row_flags, const float* source_ships,
                                                           int32_t* target_rows, int32_t* ship_counts,
                                                           size_t request_count, size_t row_count) {
-  if (output_rows == nullptr || row_planet_ids == nullptr || source_owned == nullptr || source_ships == nullptr ||
+  if (output_rows == nullptr || row_planet_ids == nullptr || row_flags == nullptr || source_ships == nullptr ||
       target_rows == nullptr || ship_counts == nullptr || request_count == 0)
     return bad("invalid true2d decode buffer");
   if (row_count < kMinRows || row_count > kMaxRows) return bad("invalid row count");
@@ -1084,32 +1260,88 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_decode_outputs(const float* output_ro
   T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
   T2_TRY(cudaMemcpyAsync(W.out, output_rows, out_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
   const size_t rn = request_count * row_count, dn = rn * kTargets;
-  if (dn > W.dec_cap) {
-    for (void* q : {static_cast<void*>(W.dec_ids), static_cast<void*>(W.dec_owned), static_cast<void*>(W.dec_ships),
-                    static_cast<void*>(W.dec_rows), static_cast<void*>(W.dec_counts)})
-      if (q != nullptr) cudaFree(q);
-    W.dec_ids = nullptr; W.dec_owned = nullptr; W.dec_ships = nullptr; W.dec_rows = nullptr; W.dec_counts = nullptr;
-    W.dec_cap = 0;
-    T2_TRY(cudaMalloc(&W.dec_ids, rn * sizeof(int32_t)));
-    T2_TRY(cudaMalloc(&W.dec_owned, rn));
-    T2_TRY(cudaMalloc(&W.dec_ships, rn * sizeof(float)));
-    T2_TRY(cudaMalloc(&W.dec_rows, dn * sizeof(int32_t)));
-    T2_TRY(cudaMalloc(&W.dec_counts, dn * sizeof(int32_t)));
-    W.dec_cap = dn;
-  }
+  T2_TRY(ensure_decode(W, rn));
   T2_TRY(cudaMemcpyAsync(W.dec_ids, row_planet_ids, rn * sizeof(int32_t), cudaMemcpyHostToDevice, W.stream));
-  T2_TRY(cudaMemcpyAsync(W.dec_owned, source_owned, rn, cudaMemcpyHostToDevice, W.stream));
+  T2_TRY(cudaMemcpyAsync(W.dec_flags, row_flags, rn, cudaMemcpyHostToDevice, W.stream));
   T2_TRY(cudaMemcpyAsync(W.dec_ships, source_ships, rn * sizeof(float), cudaMemcpyHostToDevice, W.stream));
   t2_decode<<<static_cast<unsigned>(request_count), 512, 0, W.stream>>>(
-      W.out, W.dec_ids, W.dec_owned, W.dec_ships, static_cast<int>(row_count), W.dec_rows, W.dec_counts, W.err);
+      W.out, W.dec_ids, W.dec_flags, W.dec_ships, static_cast<int>(row_count), W.dec_rows, W.dec_counts, W.err);
   T2_TRY(cudaGetLastError());
   T2_TRY(cudaMemcpyAsync(target_rows, W.dec_rows, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
   T2_TRY(cudaMemcpyAsync(ship_counts, W.dec_counts, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
-  int herr = 0;
-  T2_TRY(cudaMemcpyAsync(&herr, W.err, sizeof(int), cudaMemcpyDeviceToHost, W.stream));
-  T2_TRY(cudaStreamSynchronize(W.stream));
-  if (herr != 0) return rt(device_error_text(herr));
-  return ok();
+  return finish(W);
+}
+
+// config.rs:1-19 defaults of the fields the encoder reads.
+void orbit_wars_encoder_config_default(OrbitWarsEncoderConfig* out) {
+  if (out == nullptr) return;
+  out->max_rows = 64;
+  out->initial_planet_slots = 40;
+  out->comet_slots = 20;
+  out->padding_slots = 4;
+  out->ship_log_pivot = 1000.0f;
+  out->ship_log_cap = 100000.0f;
+  out->max_players = 4;
+  out->owner_class_own = 1.0f;
+  out->owner_class_enemy_1 = 0.75f;
+  out->owner_class_enemy_2 = 0.5f;
+  out->owner_class_enemy_3 = 0.25f;
+  out->owner_class_neutral = 0.0f;
+  out->owner_class_empty = -0.5f;
+  out->owner_class_absent_on_map = -1.0f;
+  out->board_size = 100.0f;
+  out->fleet_speed_max = 6.0f;
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_encode_states(const OrbitWarsGameBatch* games, const uint32_t* request_games,
+                                                  const int32_t* request_players, size_t request_count,
+                                                  const OrbitWarsEncoderConfig* config, float* input_rows,
+                                                  int32_t* row_planet_ids, uint8_t* row_flags, float* row_ships,
+                                                  int32_t* encode_errors) {
+  if (config == nullptr || input_rows == nullptr || row_planet_ids == nullptr || row_flags == nullptr)
+    return bad("invalid encode buffer");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  const OrbitWarsCudaStatus s = launch_encode(W, games, request_games, request_players, request_count, *config);
+  if (s.code != kOk) return s;
+  const size_t rn = request_count * config->max_rows;
+  T2_TRY(cudaMemcpyAsync(input_rows, W.in, rn * kFeatures * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+  T2_TRY(cudaMemcpyAsync(row_planet_ids, W.dec_ids, rn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
+  T2_TRY(cudaMemcpyAsync(row_flags, W.dec_flags, rn, cudaMemcpyDeviceToHost, W.stream));
+  if (row_ships != nullptr)
+    T2_TRY(cudaMemcpyAsync(row_ships, W.dec_ships, rn * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+  return encode_result(W, request_count, encode_errors);
+}
+
+OrbitWarsCudaStatus orbit_wars_cuda_true2d_play_many_resident(
+    const OrbitWarsGameBatch* games, const uint32_t* request_games, const int32_t* request_players,
+    const size_t* model_indices, size_t request_count, const OrbitWarsEncoderConfig* config, int32_t* row_planet_ids,
+    int32_t* target_rows, int32_t* ship_counts, int32_t* encode_errors, float* input_rows, float* output_rows,
+    OrbitWarsCudaTrue2DShape shape) {
+  if (config == nullptr || model_indices == nullptr || row_planet_ids == nullptr || target_rows == nullptr ||
+      ship_counts == nullptr || request_count == 0)
+    return bad("invalid true2d play buffer");
+  if (!shape_ok(shape)) return bad("invalid true2d shape");
+  if (config->max_rows != shape.row_count) return bad("encoder rows differ from the model rows");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  if (!W.resident) return rt("true2d population is not loaded");
+  if (!same_shape(W.shape, shape)) return bad("true2d shape differs from the resident population");
+  if (request_count > W.request_capacity) return rt("true2d request capacity exceeded");
+  for (size_t r = 0; r < request_count; ++r)
+    if (model_indices[r] >= W.models) return bad("model index out of range");
+  OrbitWarsCudaStatus s = launch_encode(W, games, request_games, request_players, request_count, *config);
+  if (s.code != kOk) return s;
+  const size_t rn = request_count * shape.row_count;
+  const DecodeIo dec{nullptr, nullptr, nullptr, target_rows, ship_counts};
+  s = run_forward(W, nullptr, model_indices, output_rows, request_count, shape, &dec, false);
+  if (s.code != kOk) return s;
+  T2_TRY(cudaMemcpyAsync(row_planet_ids, W.dec_ids, rn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
+  if (input_rows != nullptr)
+    T2_TRY(cudaMemcpyAsync(input_rows, W.in, rn * kFeatures * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+  const OrbitWarsCudaStatus e = encode_result(W, request_count, encode_errors);
+  const OrbitWarsCudaStatus f = finish(W);
+  return e.code != kOk ? e : f;
 }
 
 typedef OrbitWarsCudaStatus (*TrainFn)(const float*, const float*, const int*, const float*, const size_t*, float*,
@@ -1177,7 +1409,7 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_profile_begin(int32_t max_calls) {
   if (max_calls <= 0 || max_calls > 100000) return bad("max_calls must be in [1, 100000]");
   Workspace& W = ws();
   std::lock_guard<std::mutex> lock(W.mu);
-  const size_t need = static_cast<size_t>(max_calls) * 4;
+  const size_t need = static_cast<size_t>(max_calls) * 8;  // encode, three forward kernels, decode
   while (W.prof_events.size() < need) {
     cudaEvent_t ev;
     T2_TRY(cudaEventCreate(&ev));

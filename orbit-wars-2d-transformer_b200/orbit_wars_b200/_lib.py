@@ -49,6 +49,24 @@ class TrainingConfigC(C.Structure):
                 ("owner_class_absent_on_map", C.c_float)]
 
 
+class EncoderConfigC(C.Structure):
+    """OrbitWarsEncoderConfig (include/orbit_wars_cuda.h)."""
+    _fields_ = [("max_rows", C.c_size_t), ("initial_planet_slots", C.c_size_t), ("comet_slots", C.c_size_t),
+                ("padding_slots", C.c_size_t), ("ship_log_pivot", C.c_float), ("ship_log_cap", C.c_float),
+                ("max_players", C.c_size_t), ("owner_class_own", C.c_float), ("owner_class_enemy_1", C.c_float),
+                ("owner_class_enemy_2", C.c_float), ("owner_class_enemy_3", C.c_float),
+                ("owner_class_neutral", C.c_float), ("owner_class_empty", C.c_float),
+                ("owner_class_absent_on_map", C.c_float), ("board_size", C.c_float),
+                ("fleet_speed_max", C.c_float)]
+
+
+class GameBatchC(C.Structure):
+    """OrbitWarsGameBatch (include/orbit_wars_cuda.h): CSR game states."""
+    _fields_ = [("planets", C.c_void_p), ("planet_offsets", C.c_void_p), ("initial_planets", C.c_void_p),
+                ("initial_offsets", C.c_void_p), ("comet_planet_ids", C.c_void_p), ("comet_offsets", C.c_void_p),
+                ("game_count", C.c_size_t)]
+
+
 class KernelTimingC(C.Structure):
     _fields_ = [("name", C.c_char_p), ("launches", C.c_int32), ("total_ms", C.c_float)]
 
@@ -86,6 +104,11 @@ SIGNATURES = {
     "orbit_wars_cuda_true2d_forward_noalloc": (Status, [P, P, P, SZ, True2DShapeC, P]),
     "orbit_wars_cuda_true2d_decode_many_resident": (Status, [P, P, P, P, P, P, P, P, SZ, True2DShapeC]),
     "orbit_wars_cuda_true2d_decode_outputs": (Status, [P, P, P, P, P, P, SZ, SZ]),
+    "orbit_wars_encoder_config_default": (None, [C.POINTER(EncoderConfigC)]),
+    "orbit_wars_cuda_encode_states": (Status, [C.POINTER(GameBatchC), P, P, SZ, C.POINTER(EncoderConfigC), P, P, P, P,
+                                               P]),
+    "orbit_wars_cuda_true2d_play_many_resident": (
+        Status, [C.POINTER(GameBatchC), P, P, P, SZ, C.POINTER(EncoderConfigC), P, P, P, P, P, P, True2DShapeC]),
     "orbit_wars_cuda_true2d_profile_begin": (Status, [C.c_int32]),
     "orbit_wars_cuda_true2d_profile_end": (Status, [C.POINTER(KernelTimingC), C.c_int32, C.POINTER(C.c_int32)]),
     "orbit_wars_cuda_true2d_train_full_attention": (

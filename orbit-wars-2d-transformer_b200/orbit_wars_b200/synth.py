@@ -155,3 +155,82 @@ def true2d_requests(seed: int, requests: int, rows: int, models: int) -> tuple[n
     idx = (u01(seed, TENSOR_TRUE2D_MODELS, np.arange(requests, dtype=np.uint64)) * models).astype(np.uintp)
     return x, np.minimum(idx, models - 1).astype(np.uintp)
 
+
+
+def game_batch(seed: int, games: int, players: int = 4, min_groups: int = 5, max_groups: int = 10,
+               comet_prob: float = 0.5, absent_prob: float = 0.02):
+    """Seeded Orbit Wars-shaped game states for the device encoder -> (GameBatch, request_games, request_players).
+
+    Per game: 5..10 planet groups (config.rs MAP_MIN/MAX_PLANET_GROUPS), each one planet mirrored into the
+    four quadrants of the 100 x 100 board outside the sun (so equal distances, and the encoder's tie order,
+    are common); 40% of groups orbit the centre at 0.03 rad per turn (DEFAULT_ANGULAR_VELOCITY) and are
+    shown rotated to a random turn with their tangential velocity; owners and log-uniform ships (0 .. 2e5,
+    across SHIP_LOG_PIVOT and SHIP_LOG_CAP) are random; player p's home is group 0, quadrant p. With
+    probability comet_prob a group of four comets (speed 4, some above fleet_speed_max) is on the map, its
+    ids listed in a shuffled comet list that also names a departed comet. absent_prob of the non-home
+    initial planets are missing from the current planets (absent_on_map rows). One request per
+    (game, player) for every player that owns a planet.
+    """
+    from .games import GameBatch, PLANET_DTYPE
+
+    rng = np.random.default_rng(seed)
+    quadrant = ((1, 1), (-1, 1), (1, -1), (-1, -1))
+    cur_parts, init_parts, comet_parts = [], [], []
+    req_g, req_p = [], []
+    for g in range(games):
+        groups = int(rng.integers(min_groups, max_groups + 1))
+        step = int(rng.integers(0, 500))
+        init, cur = [], []
+        for k in range(groups):
+            while True:
+                dx, dy = rng.uniform(8.0, 45.0, 2)
+                if np.hypot(dx, dy) > 17.0:
+                    break
+            radius = float(rng.uniform(1.0, 3.0))
+            prod = float(rng.integers(1, 6))
+            ships0 = float(rng.integers(5, 40))
+            orbit = k > 0 and rng.random() < 0.4
+            for q, (sx, sy) in enumerate(quadrant):
+                pid = 4 * k + q
+                x0, y0 = 50.0 + sx * dx, 50.0 + sy * dy
+                owner0 = q if (k == 0 and q < players and g % 2 == 0) else -1
+                init.append((pid, owner0, x0, y0, radius, ships0, prod, 0.0, 0.0))
+                x, y, vx, vy = x0, y0, 0.0, 0.0
+                if orbit:
+                    a = 0.03 * step
+                    ca, sa = np.cos(a), np.sin(a)
+                    rx, ry = x0 - 50.0, y0 - 50.0
+                    x, y = 50.0 + ca * rx - sa * ry, 50.0 + sa * rx + ca * ry
+                    vx, vy = -0.03 * (y - 50.0), 0.03 * (x - 50.0)
+                if k == 0 and q < players:
+                    owner = q
+                else:
+                    owner = int(rng.choice([-1, -1, -1] + list(range(players))))
+                ships = float(np.expm1(rng.uniform(0.0, np.log(2e5)))) if rng.random() > 0.05 else 0.0
+                if k > 0 and rng.random() < absent_prob:
+                    continue
+                cur.append((pid, owner, x, y, radius, ships, prod, vx, vy))
+        comets = []
+        if rng.random() < comet_prob:
+            base = 1000 + 10 * int(rng.integers(0, 50))
+            speed = 4.0 if rng.random() < 0.7 else 7.5
+            for q, (sx, sy) in enumerate(quadrant):
+                cx, cy = rng.uniform(0.0, 100.0, 2)
+                ang = rng.uniform(0, 2 * np.pi)
+                cur.append((base + q, int(rng.choice([-1, -1] + list(range(players)))), cx, cy, 1.0,
+                            float(rng.integers(0, 60)), 1.0, speed * np.cos(ang), speed * np.sin(ang)))
+            comets = [base + q for q in range(4)] + [base + 9]
+            rng.shuffle(comets)
+        cur_parts.append(np.array(cur, dtype=PLANET_DTYPE))
+        init_parts.append(np.array(init, dtype=PLANET_DTYPE))
+        comet_parts.append(np.array(comets, dtype=np.int32))
+        owners = {int(p[1]) for p in cur}
+        for p in range(players):
+            if p in owners:
+                req_g.append(g)
+                req_p.append(p)
+    batch = GameBatch.from_games(list(zip(cur_parts, init_parts, comet_parts)))
+    if batch.comet_planet_ids is None:
+        batch.comet_planet_ids = np.zeros(0, np.int32)
+        batch.comet_offsets = np.zeros(games + 1, np.uint64)
+    return batch, np.array(req_g, np.uint32), np.array(req_p, np.int32)

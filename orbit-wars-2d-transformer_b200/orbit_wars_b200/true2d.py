@@ -14,6 +14,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
+from .games import ENCODE_ERRORS, GameBatch, default_config
 
 INPUT_FEATURES = 7        # config.rs TRUE2D_INPUT_FEATURES
 TARGETS = 12              # TRUE2D_ACTION_TARGETS_PER_SOURCE
@@ -121,25 +122,26 @@ class CudaTrue2D:
 
     def profile_end(self) -> dict:
         """{kernel: (launches, total_ms)} over the calls since profile_begin."""
-        cap = 8
+        cap = 16
         arr = (_lib.KernelTimingC * cap)()
         n = C.c_int32(0)
         _lib.check("cuda_true2d_profile_end", self.lib.orbit_wars_cuda_true2d_profile_end(arr, cap, C.byref(n)))
         return {arr[i].name.decode(): (int(arr[i].launches), float(arr[i].total_ms)) for i in range(n.value)}
 
-    def _decode_bufs(self, n: int, rows: int, row_planet_ids, source_owned, source_ships):
+    def _decode_bufs(self, n: int, rows: int, row_planet_ids, row_flags, source_ships):
         ids = np.ascontiguousarray(row_planet_ids, dtype=np.int32).reshape(n, rows)
-        own = np.ascontiguousarray(source_owned, dtype=np.uint8).reshape(n, rows)
+        own = np.ascontiguousarray(row_flags, dtype=np.uint8).reshape(n, rows)
         ships = np.ascontiguousarray(source_ships, dtype=np.float32).reshape(n, rows)
         tr = np.empty((n, rows, TARGETS), dtype=np.int32)
         sc = np.empty((n, rows, TARGETS), dtype=np.int32)
         return ids, own, ships, tr, sc
 
     def decode_population_resident(self, input_rows, model_indices, population_size: int, row_planet_ids,
-                                   source_owned, source_ships, shape: True2DShape = True2DShape(),
+                                   row_flags, source_ships, shape: True2DShape = True2DShape(),
                                    with_outputs: bool = False):
         """Resident forward + device decode: (target_rows, ship_counts[, outputs]) per (request, row, slot);
-        target_rows -1 / ship_counts 0 where the decoder skips (decoder.rs:85-124)."""
+        target_rows -1 / ship_counts 0 where the decoder skips (decoder.rs:85-124). row_flags per row:
+        ROW_OWNED (the planet belongs to the player) | ROW_ABSENT (the planet is not on the map)."""
         idx = np.ascontiguousarray(model_indices, dtype=np.uintp)
         n = idx.size
         x = _f32(input_rows)
@@ -147,20 +149,91 @@ class CudaTrue2D:
             raise ValueError("cuda_true2d_decode_input_count_mismatch")
         if np.any(idx >= population_size):
             raise ValueError("cuda_true2d_decode_model_index_out_of_range")
-        ids, own, ships, tr, sc = self._decode_bufs(n, shape.rows, row_planet_ids, source_owned, source_ships)
+        ids, own, ships, tr, sc = self._decode_bufs(n, shape.rows, row_planet_ids, row_flags, source_ships)
         out = np.zeros(n * shape.rows * OUTPUT_FEATURES, dtype=np.float32) if with_outputs else None
         _lib.check("cuda_true2d_decode_many_resident", self.lib.orbit_wars_cuda_true2d_decode_many_resident(
             x.ctypes.data, idx.ctypes.data, ids.ctypes.data, own.ctypes.data, ships.ctypes.data, tr.ctypes.data,
             sc.ctypes.data, None if out is None else out.ctypes.data, n, shape.c()))
         return (tr, sc, out.reshape(n, shape.rows, TARGETS, 2)) if with_outputs else (tr, sc)
 
-    def decode_outputs(self, outputs, row_planet_ids, source_owned, source_ships, rows: int = 64):
+    def decode_outputs(self, outputs, row_planet_ids, row_flags, source_ships, rows: int = 64):
         """Device decode of given outputs [n, rows, 12, 2] -> (target_rows, ship_counts)."""
         o = _f32(outputs)
         n = o.size // (rows * OUTPUT_FEATURES)
-        ids, own, ships, tr, sc = self._decode_bufs(n, rows, row_planet_ids, source_owned, source_ships)
+        ids, own, ships, tr, sc = self._decode_bufs(n, rows, row_planet_ids, row_flags, source_ships)
         _lib.check("cuda_true2d_decode_outputs", self.lib.orbit_wars_cuda_true2d_decode_outputs(
             o.ctypes.data, ids.ctypes.data, own.ctypes.data, ships.ctypes.data, tr.ctypes.data, sc.ctypes.data,
             n, rows))
         return tr, sc
 
+
+    # ---- device encoder (encoder.rs:37-208) ----------------------------------------------------------------
+    @staticmethod
+    def _requests(request_games, request_players):
+        rg = np.ascontiguousarray(request_games, dtype=np.uint32)
+        rp = np.ascontiguousarray(request_players, dtype=np.int32)
+        if rg.shape != rp.shape or rg.ndim != 1:
+            raise ValueError("encode_request_shape_mismatch")
+        return rg, rp
+
+    def encode_states(self, batch: GameBatch, request_games, request_players, config=None, strict: bool = True):
+        """encode_state for every request on the device -> EncodedRows(rows [n, R, 7], row_planet_ids [n, R],
+        row_flags [n, R], row_ships [n, R], errors [n]). strict: raise when a request fails to encode
+        (the call's BAD_ARGUMENT); otherwise return its empty rows with its error code."""
+        cfg = config if config is not None else default_config()
+        rg, rp = self._requests(request_games, request_players)
+        n, R = rg.size, int(cfg.max_rows)
+        rows = np.empty((n, R, INPUT_FEATURES), np.float32)
+        ids = np.empty((n, R), np.int32)
+        flags = np.empty((n, R), np.uint8)
+        ships = np.empty((n, R), np.float32)
+        errors = np.empty(n, np.int32)
+        bc = batch.c()
+        st = self.lib.orbit_wars_cuda_encode_states(C.byref(bc), rg.ctypes.data, rp.ctypes.data, n, C.byref(cfg),
+                                                    rows.ctypes.data, ids.ctypes.data, flags.ctypes.data,
+                                                    ships.ctypes.data, errors.ctypes.data)
+        if st.code != 0 and (strict or not (st.message or b"").startswith(b"encode failed")):
+            _lib.check("cuda_encode_states", st)
+        return EncodedRows(rows, ids, flags, ships, errors)
+
+    def play_population_resident(self, batch: GameBatch, request_games, request_players, model_indices,
+                                 population_size: int, shape: True2DShape = True2DShape(), config=None,
+                                 with_rows: bool = False, with_outputs: bool = False):
+        """Encode + resident forward + decode on the device, one call:
+        (row_planet_ids [n, R], target_rows [n, R, 12], ship_counts [n, R, 12][, rows][, outputs])."""
+        cfg = config if config is not None else default_config()
+        rg, rp = self._requests(request_games, request_players)
+        idx = np.ascontiguousarray(model_indices, dtype=np.uintp)
+        n, R = rg.size, shape.rows
+        if idx.size != n:
+            raise ValueError("cuda_true2d_play_model_index_count_mismatch")
+        if np.any(idx >= population_size):
+            raise ValueError("cuda_true2d_play_model_index_out_of_range")
+        ids = np.empty((n, R), np.int32)
+        tr = np.empty((n, R, TARGETS), np.int32)
+        sc = np.empty((n, R, TARGETS), np.int32)
+        rows = np.empty((n, R, INPUT_FEATURES), np.float32) if with_rows else None
+        out = np.empty((n, R, TARGETS, 2), np.float32) if with_outputs else None
+        bc = batch.c()
+        _lib.check("cuda_true2d_play_many_resident", self.lib.orbit_wars_cuda_true2d_play_many_resident(
+            C.byref(bc), rg.ctypes.data, rp.ctypes.data, idx.ctypes.data, n, C.byref(cfg), ids.ctypes.data,
+            tr.ctypes.data, sc.ctypes.data, None, None if rows is None else rows.ctypes.data,
+            None if out is None else out.ctypes.data, shape.c()))
+        res = (ids, tr, sc)
+        if with_rows:
+            res += (rows,)
+        if with_outputs:
+            res += (out,)
+        return res
+
+
+@dataclass
+class EncodedRows:
+    rows: np.ndarray
+    row_planet_ids: np.ndarray
+    row_flags: np.ndarray
+    row_ships: np.ndarray
+    errors: np.ndarray
+
+    def error_names(self) -> list[str]:
+        return [ENCODE_ERRORS[int(e)] for e in self.errors]

@@ -19,7 +19,7 @@ def declared_symbols():
     names = set()
     for h in (REPO / "include").glob("*.h"):
         txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
-        names |= set(re.findall(r"\b((?:ow_policy|ow_selftest|orbit_wars_cuda)_\w+)\s*\(", txt))
+        names |= set(re.findall(r"\b((?:ow_policy|ow_selftest|orbit_wars)_\w+)\s*\(", txt))
     return sorted(names)
 
 

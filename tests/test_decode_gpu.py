@@ -42,11 +42,13 @@ def test_reference_decoder_known_answers():
 
 
 def random_decode_inputs(rng, n, rows=64):
+    """Row flags: 1 = owned by the player, 2 = not on the map (both set is contradictory and never decoded)."""
     ids = np.where(rng.random((n, rows)) < 0.6, rng.integers(0, 50, (n, rows)), -1).astype(np.int32)
     ids[0, :] = -1  # a request with no planet at all
     owned = (rng.random((n, rows)) < 0.5).astype(np.uint8)
+    absent = (rng.random((n, rows)) < 0.1).astype(np.uint8)
     ships = (rng.random((n, rows)) * 120.0).astype(np.float32)
-    return ids, owned, ships
+    return ids, owned | (absent << 1), ships
 
 
 def test_decode_outputs_matches_restatement():
@@ -77,6 +79,21 @@ def test_decode_many_resident_matches_forward_and_restatement():
     assert np.array_equal(tr, rtr) and np.array_equal(sc, rsc)
     tr2, sc2 = lib.decode_population_resident(x, idx, models, ids, owned, ships, SHAPE)
     assert np.array_equal(tr2, tr) and np.array_equal(sc2, sc)
+
+
+def test_absent_target_and_source_are_skipped():
+    """decoder.rs:93-95 and :112-114: a source or target whose planet is not on the map gives no command."""
+    out, ids, owned, ships = scenario(10.0, 0.75, 0.5)
+    flags = owned.copy()
+    flags[0, 1] = 2  # the target planet (row 1) left the map
+    tr, sc = ow.CudaTrue2D().decode_outputs(out, ids, flags, ships)
+    assert (tr >= 0).sum() == 0 and sc.sum() == 0
+    rtr, _ = dec.decode(out, ids, flags, ships)
+    assert (rtr >= 0).sum() == 0
+    flags = owned.copy()
+    flags[0, 0] = 3  # owned but absent: no source
+    tr, _ = ow.CudaTrue2D().decode_outputs(out, ids, flags, ships)
+    assert (tr >= 0).sum() == 0
 
 
 def test_non_finite_output_is_rejected():
