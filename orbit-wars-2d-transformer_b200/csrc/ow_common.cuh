@@ -200,6 +200,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// The same wait, with the loaded registers as operands: their uses cannot be
+// scheduled above it (a load of the next chunk may be in flight meanwhile).
+__device__ __forceinline__ void tmem_ld_wait_dep(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- numerics
@@ -231,6 +243,27 @@ __device__ __forceinline__ float gelu_erf(float v) {
   poly = fmaf(t, poly, 0.5f * 0.254829592f);
   const float e = ex2_approx_f((a * a) * (-0.5f * 1.4426950408889634f));  // exp(-v^2 / 2)
   return fmaxf(v, 0.0f) - a * (poly * t) * e;
+}
+
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU for the bf16 / e4m3 epilogues, whose outputs are bf16: v * Phi(v) with
+//   Phi(v) ~= 0.5 (1 + tanh(v (c0 + c1 v^2))),
+// c0 and c1 fitted here to the normal CDF by minimax over [0, 8] (|error| <=
+// 1.42e-4; Phi(-v) = 1 - Phi(v) holds exactly in the form), and the hardware
+// tanh (tanh.approx.f32, relative error <= 2^-10.99): |Phi error| <= 3.9e-4,
+// within half a bf16 ulp of the output for v >= -1. One MUFU operation and five
+// FMA-pipe operations per value; the erf form above takes two and about eleven,
+// which made the FFN up-projection's epilogue issue-bound. The f32 path keeps
+// the erf form.
+__device__ __forceinline__ float gelu_bf16(float v) {
+  const float z = v * fmaf(v * v, 0.03529402f, 0.79878396f);
+  const float hv = 0.5f * v;
+  return fmaf(hv, tanh_approx(z), hv);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -271,6 +304,36 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(x), "r"(y), "r"(smem_u32(smem_src))
+               : "memory");
+}
+// L2 eviction priorities for TMA copies (createpolicy; the hint travels with
+// the copy): evict_last keeps a tensor in L2 from one kernel to the next (the
+// f32 residual stream, 4 bytes per value, read and rewritten by every
+// LayerNorm epilogue); evict_first lets a streamed tensor leave first (the FFN
+// hidden activations, written once and read once).
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], "
+      "[%4], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* smem_src, int x, int y,
+                                                  uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(smem_src)), "l"(policy)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }

@@ -164,6 +164,10 @@ bool make_ln_map(CUtensorMap* map, const void* base, MapType t, uint64_t inner, 
   const uint32_t elt = t == kMapF32 ? 4 : (t == kMapBf16 ? 2 : 1);
   return make_map_box(map, base, t, inner, rows, 32 * elt, 32);
 }
+// Bias / GELU epilogue output map (bf16): chunk_cols columns x 32 rows.
+bool make_out_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, int chunk_cols) {
+  return make_map_box(map, base, kMapBf16, inner, rows, static_cast<uint32_t>(chunk_cols) * 2, 32);
+}
 // K-major GEMM operand map (bf16 or e4m3), box = 128 bytes x box_rows.
 bool make_kmajor_map(CUtensorMap* map, const void* base, bool e4m3, uint64_t inner, uint64_t rows, uint32_t box_rows) {
   return make_map_128b(map, base, e4m3 ? kMapU8 : kMapBf16, inner, rows, box_rows);
@@ -728,6 +732,7 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       w.ln_scale = P.ln_scale;
       w.a_scale = P.h_scale;
       w.b_scale = W.s2;
+      w.a_stream = 1;  // h is read once here
       OW_STEP("gemm_ffn_down_resid_ln",
               launch_gemm_resid_ln(P, P.m_h, W.m2, P.e_x, last ? P.e_y : P.e_ln, w, fp8));
     }
@@ -980,7 +985,8 @@ OwStatus alloc_workspace(OwPolicy& P, int cap_states) {
     else
       ok = make_kmajor_map(&P.m_ln, P.ln, false, d, rows, 128) && make_kmajor_map(&P.m_attn, P.attn, false, d, rows, 128) &&
            make_kmajor_map(&P.m_h, P.h, false, f, rows, 128);
-    ok = ok && make_ln_map(&P.e_qkv, P.qkv, kMapBf16, 3 * d, rows) && make_ln_map(&P.e_h, P.h, kMapBf16, f, rows) &&
+    ok = ok && make_out_map(&P.e_qkv, P.qkv, 3 * d, rows, ow::EpiWarps<ow::kEpiBias>::kChunkCols) &&
+         make_out_map(&P.e_h, P.h, f, rows, ow::EpiWarps<ow::kEpiBiasGelu>::kChunkCols) &&
          make_map_128b(&P.e_x, P.x, kMapF32, d, rows, 32) &&
          make_ln_map(&P.e_y, P.y, kMapF32, d, rows) &&
          (e4 ? make_ln_map(&P.e_ln, P.ln8, kMapU8, d, rows) : make_ln_map(&P.e_ln, P.ln, kMapBf16, d, rows));
@@ -1446,7 +1452,8 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
     const MapType lt = ln_mode == kLnF32 ? kMapF32 : (ln_mode == kLnE4m3 ? kMapU8 : kMapBf16);
     mok = make_map_128b(&mo, resid, kMapF32, n, m, 32) && make_ln_map(&ml, ln_out, lt, n, m);
   } else {
-    mok = make_ln_map(&mo, out, kMapBf16, n, m);
+    mok = make_out_map(&mo, out, n, m, epilogue == kEpiBias ? ow::EpiWarps<ow::kEpiBias>::kChunkCols
+                                                             : ow::EpiWarps<ow::kEpiBiasGelu>::kChunkCols);
     ml = mo;
   }
   if (!mok) return st_rt("cuTensorMapEncodeTiled failed for an epilogue buffer");

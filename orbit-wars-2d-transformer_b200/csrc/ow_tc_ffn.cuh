@@ -310,10 +310,10 @@ __global__ void __launch_bounds__(TcFfnShape<D>::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
           const float4 bv = *reinterpret_cast<const float4*>(bias + i);
-          const float v0 = gelu_erf(__uint_as_float(r[i]) + bv.x);
-          const float v1 = gelu_erf(__uint_as_float(r[i + 1]) + bv.y);
-          const float v2 = gelu_erf(__uint_as_float(r[i + 2]) + bv.z);
-          const float v3 = gelu_erf(__uint_as_float(r[i + 3]) + bv.w);
+          const float v0 = gelu_bf16(__uint_as_float(r[i]) + bv.x);
+          const float v1 = gelu_bf16(__uint_as_float(r[i + 1]) + bv.y);
+          const float v2 = gelu_bf16(__uint_as_float(r[i + 2]) + bv.z);
+          const float v3 = gelu_bf16(__uint_as_float(r[i + 3]) + bv.w);
           pk[i / 2] = pack_bf16x2(v0, v1);
           pk[i / 2 + 1] = pack_bf16x2(v2, v3);
         }

@@ -27,7 +27,8 @@
 // Epilogues:
 //   kEpiBias       out = bf16(acc*s + bias)                        (QKV projection)
 //   kEpiBiasGelu   out = bf16(gelu(acc*s + bias))                  (FFN up-projection)
-// map_o is the output map (bf16, box 64 x 32) for the bias epilogues and the
+// map_o is the output map (bf16, box EpiWarps<EPI>::kChunkCols x 32 rows, in
+// the swizzle of that row width) for the bias epilogues and the
 // f32 residual map (box 32 x 32) for the LayerNorm epilogue; map_l is the
 // LayerNorm output map (box 128 B x 32 rows of its dtype).
 //   kEpiResidLn    x   = x + acc*s + bias in place (fp32 residual stream),
@@ -62,14 +63,32 @@ struct TcGemmParams {
   const float* a_scale;   // [rows] (e4m3 operands only)
   const float* b_scale;   // [n]    (e4m3 operands only)
   int* err;
+  int a_stream;           // A is read once and not again (the FFN hidden activations): load it evict_first
 };
 
 constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 
+#ifndef OW_BIAS_EPI_WARPS
+#define OW_BIAS_EPI_WARPS 16
+#endif
+#ifndef OW_BIAS_CHUNK_COLS
+#define OW_BIAS_CHUNK_COLS 32
+#endif
+#ifndef OW_GELU_EPI_WARPS
+#define OW_GELU_EPI_WARPS 16
+#endif
+#ifndef OW_GELU_CHUNK_COLS
+#define OW_GELU_CHUNK_COLS 32
+#endif
+
+// Epilogue warps per CTA and, for the bias / GELU epilogues, the columns of one
+// output chunk (one TMA store box of 32 rows: 32 columns = 64 B rows, 64 = 128 B).
 template <int EPI>
 struct EpiWarps {
-  static constexpr int kCount = EPI == kEpiResidLn ? 8 : 16;
+  static constexpr int kCount = EPI == kEpiResidLn ? 8 : (EPI == kEpiBias ? OW_BIAS_EPI_WARPS : OW_GELU_EPI_WARPS);
   static constexpr int kThreads = 64 + 32 * kCount;
+  static constexpr int kChunkCols = EPI == kEpiBias ? OW_BIAS_CHUNK_COLS : OW_GELU_CHUNK_COLS;
+  static_assert(kChunkCols == 32 || kChunkCols == 64, "output chunks of 64 B or 128 B rows");
 };
 
 template <int BLOCK_N, int EPI>
@@ -95,8 +114,8 @@ struct TcGemmShape {
   // staging tiles (4 KB) per epilogue warp, used by the TMA loads of the
   // residual and the TMA stores of the outputs: 2, or 1 at d = 512 (budget)
   static constexpr int kTilesPerWarp = (EPI == kEpiResidLn && BLOCK_N > 384) ? 1 : 2;
-  // bias/GELU epilogues stage 32 rows x 32 bf16 columns (64 B rows); LayerNorm 32 x 128 B
-  static constexpr int kTileBytes = EPI == kEpiResidLn ? 4096 : 2048;
+  // bias/GELU epilogues stage 32 rows x kChunkCols bf16 columns; LayerNorm 32 x 128 B
+  static constexpr int kTileBytes = EPI == kEpiResidLn ? 4096 : 32 * EpiWarps<EPI>::kChunkCols * 2;
   static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * kTilesPerWarp * kTileBytes;
   // LayerNorm: per-row partial statistics exchanged between the two warps of a
   // lane quadrant: [2 parities][8 warps][32 lanes] x (mean, M2, amax, pad)
@@ -146,6 +165,31 @@ __device__ __forceinline__ void pair_sync(uint64_t* bar, uint32_t& phase, volati
 // are merged exactly (Chan et al.) through `st` and the pair's mbarrier
 // (64 arrivals, bounded wait). Pass 2: x and the LN output leave by TMA
 // stores from the warp's staging tiles.
+// One 32-column chunk of LayerNorm output of this thread's row into a staging
+// tile, in the box layout of its dtype (bf16: 64 B rows, e4m3: 32 B, f32: 128 B).
+__device__ __forceinline__ void ln_to_staging(const float (&y)[32], uint8_t* lt, int lane, int ln_mode,
+                                              float inv_scale) {
+  if (ln_mode == kLnE4m3) {
+    uint32_t q8[8];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale, y[i + 3] * inv_scale);
+    *xpose_slot32(lt, lane, 0) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+    *xpose_slot32(lt, lane, 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
+  } else if (ln_mode == kLnF32) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *xpose_slot(lt, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
+                                            __float_as_uint(y[4 * q + 2]), __float_as_uint(y[4 * q + 3]));
+  } else {
+    uint32_t yo[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) *xpose_slot64(lt, lane, q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
+  }
+}
+
 template <int BLOCK_N, bool FP8, int NT>
 __device__ __forceinline__ void resid_ln_epilogue(uint32_t tbase, uint8_t* tiles, uint64_t* my_xbar, uint32_t& xbits,
                                                   float4* st, const float* s_bias, const float* s_bscale,
@@ -158,16 +202,22 @@ __device__ __forceinline__ void resid_ln_epilogue(uint32_t tbase, uint8_t* tiles
   constexpr int kChunks = HW / 32;
   const int half = ew >> 2;
   const int cbase = half * HW;
-  float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
+  // shifted sums in four interleaved partials (shorter dependency chains);
+  // the next chunk's TMEM load is in flight while a chunk is processed
+  float shift = 0.0f;
+  float s1p[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s2p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   bool ok = true;
-#pragma unroll 1
+  uint32_t ra[32], rb[32];
+  tmem_ld32(tbase + cbase, ra);
+#pragma unroll
   for (int c = 0; c < kChunks; ++c) {
-    uint32_t r[32];
-    tmem_ld32(tbase + cbase + c * 32, r);
+    uint32_t(&r)[32] = (c & 1) ? rb : ra;
+    uint32_t(&rn)[32] = (c & 1) ? ra : rb;
     const int b = c % NT;
     if (!mbar_wait(&my_xbar[b], (xbits >> b) & 1u, abort_flag, p.err)) ok = false;
     xbits ^= 1u << b;
-    tmem_ld_wait();
+    tmem_ld_wait_dep(r);
+    if (c + 1 < kChunks) tmem_ld32(tbase + cbase + (c + 1) * 32, rn);
     float xv[32];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -192,8 +242,8 @@ __device__ __forceinline__ void resid_ln_epilogue(uint32_t tbase, uint8_t* tiles
         v += b4[j] + xv[i + j];
         if (c == 0 && i + j == 0) shift = v;
         const float dv = v - shift;
-        s1 += dv;
-        s2 = fmaf(dv, dv, s2);
+        s1p[j] += dv;
+        s2p[j] = fmaf(dv, dv, s2p[j]);
         r[i + j] = __float_as_uint(v);
       }
     }
@@ -207,9 +257,11 @@ __device__ __forceinline__ void resid_ln_epilogue(uint32_t tbase, uint8_t* tiles
     __syncwarp();
     if (lane == 0 && c + NT < kChunks && ok) {
       mbar_arrive_expect_tx(&my_xbar[b], 4096);
-      tma_load_2d(tiles + b * 4096, map_o, &my_xbar[b], cbase + (c + NT) * 32, row_base);
+      tma_load_2d_hint(tiles + b * 4096, map_o, &my_xbar[b], cbase + (c + NT) * 32, row_base, l2_evict_last());
     }
   }
+  const float s1 = (s1p[0] + s1p[1]) + (s1p[2] + s1p[3]);
+  const float s2 = (s2p[0] + s2p[1]) + (s2p[2] + s2p[3]);
   tmem_st_wait();
   // merge the two halves' statistics (same operation order in both warps)
   const float mh = shift + s1 * (1.0f / HW);
@@ -244,70 +296,81 @@ __device__ __forceinline__ void resid_ln_epilogue(uint32_t tbase, uint8_t* tiles
     inv_scale = 1.0f / scale;
     if (live && half == 0) p.ln_scale[m] = scale;
   }
+  if constexpr (NT >= 2) {
+    // x (staging tile 0) and the LN output (tile 1) of a chunk leave in one bulk
+    // group behind one proxy fence; the next chunk waits for that group's reads
+    uint8_t* xt = tiles;
+    uint8_t* lt = tiles + 4096;
+    uint32_t qa[32], qb[32];
+    tmem_ld32(tbase + cbase, qa);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      uint32_t(&r)[32] = (c & 1) ? qb : qa;
+      uint32_t(&rn)[32] = (c & 1) ? qa : qb;
+      const int col0 = cbase + c * 32;
+      if (lane == 0) bulk_wait_read<0>();
+      tmem_ld_wait_dep(r);
+      if (c + 1 < kChunks) tmem_ld32(tbase + cbase + (c + 1) * 32, rn);
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < 8; ++q) *xpose_slot(xt, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+      float y[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 gv = *reinterpret_cast<const float4*>(s_g + col0 + i);
+        const float4 bv = *reinterpret_cast<const float4*>(s_b + col0 + i);
+        y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
+        y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
+        y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
+        y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
+      }
+      ln_to_staging(y, lt, lane, p.ln_mode, inv_scale);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d_hint(map_o, xt, col0, row_base, l2_evict_last());
+        tma_store_2d(map_l, lt, col0, row_base);
+        bulk_commit();
+      }
+    }
+  } else {
+    // one staging tile (d = 512): x, then the LN output, each behind its own fence
+    uint8_t* t = tiles;
 #pragma unroll 1
-  for (int c = 0; c < kChunks; ++c) {
-    const int col0 = cbase + c * 32;
-    uint32_t r[32];
-    tmem_ld32(tbase + col0, r);
-    // x (f32, 128 B box rows): the tile's previous store must have read it
-    uint8_t* xt = tiles + 0;
-    uint8_t* lt = tiles + (NT - 1) * 4096;
-    if (lane == 0) {
-      if (NT == 2) bulk_wait_read<1>();
-      else bulk_wait_read<0>();
-    }
-    tmem_ld_wait();
-    __syncwarp();
+    for (int c = 0; c < kChunks; ++c) {
+      const int col0 = cbase + c * 32;
+      uint32_t r[32];
+      tmem_ld32(tbase + col0, r);
+      if (lane == 0) bulk_wait_read<0>();
+      tmem_ld_wait_dep(r);
+      __syncwarp();
 #pragma unroll
-    for (int q = 0; q < 8; ++q) *xpose_slot(xt, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(map_o, xt, col0, row_base);
-      bulk_commit();
-    }
-    float y[32];
+      for (int q = 0; q < 8; ++q) *xpose_slot(t, lane, q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d_hint(map_o, t, col0, row_base, l2_evict_last());
+        bulk_commit();
+      }
+      float y[32];
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float4 gv = *reinterpret_cast<const float4*>(s_g + col0 + i);
-      const float4 bv = *reinterpret_cast<const float4*>(s_b + col0 + i);
-      y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
-      y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
-      y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
-      y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
-    }
-    // LN output: 32 columns = one 32 x (32*elt) B box in the matching swizzle
-    if (lane == 0) {
-      if (NT == 2) bulk_wait_read<1>();
-      else bulk_wait_read<0>();
-    }
-    __syncwarp();
-    if (p.ln_mode == kLnE4m3) {
-      uint32_t q8[8];
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        q8[i / 4] = pack_e4m3x4(y[i] * inv_scale, y[i + 1] * inv_scale, y[i + 2] * inv_scale,
-                                y[i + 3] * inv_scale);
-      *xpose_slot32(lt, lane, 0) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
-      *xpose_slot32(lt, lane, 1) = make_uint4(q8[4], q8[5], q8[6], q8[7]);
-    } else if (p.ln_mode == kLnF32) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        *xpose_slot(lt, lane, q) = make_uint4(__float_as_uint(y[4 * q]), __float_as_uint(y[4 * q + 1]),
-                                              __float_as_uint(y[4 * q + 2]), __float_as_uint(y[4 * q + 3]));
-    } else {
-      uint32_t yo[16];
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) yo[i / 2] = pack_bf16x2(y[i], y[i + 1]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *xpose_slot64(lt, lane, q) = make_uint4(yo[4 * q], yo[4 * q + 1], yo[4 * q + 2], yo[4 * q + 3]);
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(map_l, lt, col0, row_base);
-      bulk_commit();
+      for (int i = 0; i < 32; i += 4) {
+        const float4 gv = *reinterpret_cast<const float4*>(s_g + col0 + i);
+        const float4 bv = *reinterpret_cast<const float4*>(s_b + col0 + i);
+        y[i] = (__uint_as_float(r[i]) - mean) * rstd * gv.x + bv.x;
+        y[i + 1] = (__uint_as_float(r[i + 1]) - mean) * rstd * gv.y + bv.y;
+        y[i + 2] = (__uint_as_float(r[i + 2]) - mean) * rstd * gv.z + bv.z;
+        y[i + 3] = (__uint_as_float(r[i + 3]) - mean) * rstd * gv.w + bv.w;
+      }
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+      ln_to_staging(y, t, lane, p.ln_mode, inv_scale);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(map_l, t, col0, row_base);
+        bulk_commit();
+      }
     }
   }
 }
@@ -391,6 +454,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const uint64_t a_policy = l2_evict_first();
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * S::kBlockM;
         const int n0 = (tile % n_tiles) * BLOCK_N;
@@ -401,7 +465,10 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           }
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
           const int kx = kb * (FP8 ? 128 : 64);
-          tma_load_2d(sa + stage * S::kATileBytes, &map_a, &full[stage], kx, m0);
+          if (p.a_stream)
+            tma_load_2d_hint(sa + stage * S::kATileBytes, &map_a, &full[stage], kx, m0, a_policy);
+          else
+            tma_load_2d(sa + stage * S::kATileBytes, &map_a, &full[stage], kx, m0);
 #pragma unroll
           for (int c = 0; c < S::kBoxCount; ++c)
             tma_load_2d(sb + stage * S::kBTileBytes + c * S::kBoxRows * S::kRowBytes, &map_w, &full[stage], kx,
@@ -484,7 +551,8 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
 #pragma unroll
           for (int b = 0; b < S::kTilesPerWarp; ++b) {
             mbar_arrive_expect_tx(&my_xbar[b], 4096);
-            tma_load_2d(tiles + b * 4096, &map_o, &my_xbar[b], (ew >> 2) * (BLOCK_N / 2) + b * 32, rb);
+            tma_load_2d_hint(tiles + b * 4096, &map_o, &my_xbar[b], (ew >> 2) * (BLOCK_N / 2) + b * 32, rb,
+                             l2_evict_last());
           }
         }
         __syncwarp();
@@ -500,16 +568,18 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       const float a_s = (FP8 && live) ? p.a_scale[m] : 1.0f;
 
       if (EPI == kEpiBias || EPI == kEpiBiasGelu) {
-        static_assert(kCols % 32 == 0, "32-column epilogue chunks");
+        constexpr int CW = EpiWarps<EPI>::kChunkCols;
+        static_assert(kCols % CW == 0, "whole epilogue chunks");
 #pragma unroll 1
-        for (int c = col0; c < col0 + kCols && any; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c, r);
+        for (int c = col0; c < col0 + kCols && any; c += CW) {
+          uint32_t r[CW];
+#pragma unroll
+          for (int h = 0; h < CW / 32; ++h) tmem_ld32(tbase + c + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
           if (lane == 0) bulk_wait_read<1>();  // the store that last used this tile has read it
           tmem_ld_wait();
-          uint32_t packed[16];
+          uint32_t packed[CW / 2];
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
+          for (int i = 0; i < CW; i += 4) {
             const float4 bv = *reinterpret_cast<const float4*>(s_bias + n0 + c + i);
             float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
             float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
@@ -525,10 +595,10 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
             v2 += bv.z;
             v3 += bv.w;
             if (EPI == kEpiBiasGelu) {
-              v0 = gelu_erf(v0);
-              v1 = gelu_erf(v1);
-              v2 = gelu_erf(v2);
-              v3 = gelu_erf(v3);
+              v0 = gelu_bf16(v0);
+              v1 = gelu_bf16(v1);
+              v2 = gelu_bf16(v2);
+              v3 = gelu_bf16(v3);
             }
             packed[i / 2] = pack_bf16x2(v0, v1);
             packed[i / 2 + 1] = pack_bf16x2(v2, v3);
@@ -536,12 +606,20 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           uint8_t* ot = tiles + (out_k & 1) * S::kTileBytes;
           __syncwarp();
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *xpose_slot64(ot, lane, q) = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          for (int q = 0; q < CW / 8; ++q) {
+            const uint4 v = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            if (CW == 64)
+              *xpose_slot(ot, lane, q) = v;
+            else
+              *xpose_slot64(ot, lane, q) = v;
+          }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&map_o, ot, n0 + c, row_base);
+            if (EPI == kEpiBiasGelu)
+              tma_store_2d_hint(&map_o, ot, n0 + c, row_base, l2_evict_first());
+            else
+              tma_store_2d(&map_o, ot, n0 + c, row_base);
             bulk_commit();
           }
           ++out_k;
