@@ -470,10 +470,11 @@ constexpr int kHeadsMinBlocks = 6;
 // Packed row r is entity j = r - offsets[b] of state b (offsets[b] <= r <
 // offsets[b+1], found by binary search). A warp takes 16 consecutive packed
 // rows: features (f32 -> bf16) times W_e^T (K = 32 features) on m16n8k16
-// tensor cores, 128 output columns at a time. The MMA is cheap enough to be
-// recomputed per pass: pass 1 row means, pass 2 centred variances (exact
-// two-pass statistics; rows live across the 4 lanes of a quad), [pass 3 e4m3
-// row absmax], last pass writes x (f32) and the LN output.
+// tensor cores, kEmbedGroupCols output columns at a time. The MMA is
+// recomputed per pass rather than held: pass 1 row statistics (each lane sums
+// its columns shifted by its first value; the four lanes of a quad, which
+// share a row, merge mean and M2 exactly, Chan et al.), [pass 2 e4m3 row
+// absmax], last pass writes x (f32) and the LN output.
 template <int D, int LN_MODE>  // LN_MODE 1: bf16 out; 2: e4m3 out + per-row scale
 __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const float* __restrict__ feats, const int* __restrict__ offsets,
                                                         int batch, int n_entities, int n_feat,
@@ -575,7 +576,8 @@ __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const f
     __syncwarp();  // sf is rewritten by the next block of this warp
     const int ra = r0 + gq, rb = r0 + gq + 8;
     float mean0 = 0.f, mean1 = 0.f, rstd0 = 1.f, rstd1 = 1.f, inv0 = 1.f, inv1 = 1.f;
-    constexpr int kPasses = LN_MODE == 2 ? 4 : 3;
+    float sh0 = 0.f, sh1 = 0.f, q0 = 0.f, q1 = 0.f;  // statistics pass: shifts, shifted sums of squares
+    constexpr int kPasses = LN_MODE == 2 ? 3 : 2;
 #pragma unroll 1
     for (int pass = 0; pass < kPasses; ++pass) {
       float a0 = 0.f, a1 = 0.f;  // per-pass reductions for rows ra, rb
@@ -597,17 +599,21 @@ __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const f
           const float v00 = acc[nt][0] + bz0, v01 = acc[nt][1] + bz1;  // row ra
           const float v10 = acc[nt][2] + bz0, v11 = acc[nt][3] + bz1;  // row rb
           if (pass == 0) {
-            a0 += v00 + v01;
-            a1 += v10 + v11;
-          } else if (pass == 1) {
-            a0 += (v00 - mean0) * (v00 - mean0) + (v01 - mean0) * (v01 - mean0);
-            a1 += (v10 - mean1) * (v10 - mean1) + (v11 - mean1) * (v11 - mean1);
+            if (cg == 0 && nt == 0) {
+              sh0 = v00;
+              sh1 = v10;
+            }
+            const float d00 = v00 - sh0, d01 = v01 - sh0, d10 = v10 - sh1, d11 = v11 - sh1;
+            a0 += d00 + d01;
+            a1 += d10 + d11;
+            q0 = fmaf(d00, d00, fmaf(d01, d01, q0));
+            q1 = fmaf(d10, d10, fmaf(d11, d11, q1));
           } else {
             const float g0 = s_vec[D + col], g1 = s_vec[D + col + 1];
             const float e0 = s_vec[2 * D + col], e1 = s_vec[2 * D + col + 1];
             const float y00 = (v00 - mean0) * rstd0 * g0 + e0, y01 = (v01 - mean0) * rstd0 * g1 + e1;
             const float y10 = (v10 - mean1) * rstd1 * g0 + e0, y11 = (v11 - mean1) * rstd1 * g1 + e1;
-            if (LN_MODE == 2 && pass == 2) {
+            if (LN_MODE == 2 && pass == 1) {
               a0 = fmaxf(a0, fmaxf(fabsf(y00), fabsf(y01)));
               a1 = fmaxf(a1, fmaxf(fabsf(y10), fabsf(y11)));
             } else {
@@ -634,7 +640,7 @@ __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const f
         }
       }
       // reduce over the quad (the 4 lanes sharing rows ra, rb)
-      if (LN_MODE == 2 && pass == 2) {
+      if (LN_MODE == 2 && pass == 1) {
         a0 = fmaxf(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
         a0 = fmaxf(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
         a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
@@ -644,18 +650,27 @@ __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const f
         inv1 = 1.0f / sc1;
         if (t == 0 && ra < M) ln_scale[ra] = sc0;
         if (t == 0 && rb < M) ln_scale[rb] = sc1;
-      } else if (pass < 2) {
-        a0 += __shfl_xor_sync(0xffffffffu, a0, 1);
-        a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
-        if (pass == 0) {
-          mean0 = a0 * (1.0f / D);
-          mean1 = a1 * (1.0f / D);
-        } else {
-          rstd0 = rsqrtf(a0 * (1.0f / D) + 1e-5f);
-          rstd1 = rsqrtf(a1 * (1.0f / D) + 1e-5f);
+      } else if (pass == 0) {
+        // per lane: mean and M2 over its D/4 columns; merged over the quad in two
+        // steps of equal counts (the same operations in every lane of the quad)
+        float cnt = static_cast<float>(D / 4);
+        float m0 = sh0 + a0 / cnt, m1 = sh1 + a1 / cnt;
+        float M0 = fmaxf(q0 - a0 * a0 / cnt, 0.0f), M1 = fmaxf(q1 - a1 * a1 / cnt, 0.0f);
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+          const float om0 = __shfl_xor_sync(0xffffffffu, m0, o), oM0 = __shfl_xor_sync(0xffffffffu, M0, o);
+          const float om1 = __shfl_xor_sync(0xffffffffu, m1, o), oM1 = __shfl_xor_sync(0xffffffffu, M1, o);
+          const float e0 = om0 - m0, e1 = om1 - m1;
+          M0 = (M0 + oM0) + e0 * e0 * (0.5f * cnt);
+          M1 = (M1 + oM1) + e1 * e1 * (0.5f * cnt);
+          m0 = 0.5f * (m0 + om0);
+          m1 = 0.5f * (m1 + om1);
+          cnt *= 2.0f;
         }
+        mean0 = m0;
+        mean1 = m1;
+        rstd0 = rsqrtf(M0 * (1.0f / D) + 1e-5f);
+        rstd1 = rsqrtf(M1 * (1.0f / D) + 1e-5f);
       }
     }
   }
@@ -897,12 +912,27 @@ __global__ void __launch_bounds__(128, kHeadsMinBlocks) heads_mma_kernel(const f
                                                         float* __restrict__ sval) {
   constexpr int WPITCH = D + 16;  // f32 pitch: float4 fragment loads are conflict-free
   extern __shared__ __align__(16) float s_wh[];  // [NTILE*8][WPITCH]
-  for (int i = threadIdx.x; i < NTILE * 8 * D; i += blockDim.x) {
-    const int n = i / D, k = i % D;
-    float v = 0.0f;
-    if (n < n_actions) v = w_p[n * D + k];
-    else if (n == n_actions) v = w_v[k];
-    s_wh[n * WPITCH + k] = v;
+  {
+    // batched 16-byte copies, every load of the batch issued before any store
+    // (a load-store loop here cost one L2 round trip per element per thread)
+    constexpr int kQuads = NTILE * 8 * D / 4;
+    constexpr int kPer = (kQuads + 127) / 128;
+    float4 v[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = threadIdx.x + 128 * k;
+      const int n = (4 * i) / D, kk = (4 * i) % D;
+      v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < kQuads) {
+        if (n < n_actions) v[k] = *reinterpret_cast<const float4*>(w_p + n * D + kk);
+        else if (n == n_actions) v[k] = *reinterpret_cast<const float4*>(w_v + kk);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = threadIdx.x + 128 * k;
+      if (i < kQuads) *reinterpret_cast<float4*>(s_wh + ((4 * i) / D) * WPITCH + (4 * i) % D) = v[k];
+    }
   }
   pdl_wait();  // the head weights above are constant; y comes from the last block
   __syncthreads();

@@ -407,9 +407,9 @@ cudaError_t launch_embed(const OwPolicy& P, int batch) {
   } else {
     constexpr int D = DPL * 32;
     const size_t esmem = static_cast<size_t>(D) * 40 * 2 + 4 * 16 * 40 * 2 + 3 * D * sizeof(float);
-    // a warp takes 16 packed rows at a time: enough CTAs (8 fit per SM) for about one block per warp
+    // a warp takes 16 packed rows at a time; one wave of resident CTAs, each staging W_e once
     const int eg = static_cast<int>(std::max<size_t>(1, std::min<size_t>((P.cap_rows + 63) / 64,
-                                                                          static_cast<size_t>(P.num_sms) * 8)));
+                                                                          static_cast<size_t>(P.num_sms) * kEmbedMinBlocks)));
     if (c.precision == OW_PRECISION_BF16) {
       auto k = embed_mma_kernel<D, 1>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
@@ -456,9 +456,9 @@ cudaError_t heads_mma_launch(const OwPolicy& P, int batch, uint64_t seed, void* 
   const size_t smem = static_cast<size_t>(NTILE) * 8 * (D + 16) * sizeof(float);
   cudaFuncSetAttribute(heads_mma_kernel<D, NTILE, LB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  // a warp takes 16 packed rows at a time: enough CTAs (8 fit per SM) for about one block per warp
+  // a warp takes 16 packed rows at a time; one wave of resident CTAs, each staging the head weights once
   const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((P.cap_rows + 63) / 64,
-                                                                         static_cast<size_t>(P.num_sms) * 8)));
+                                                                         static_cast<size_t>(P.num_sms) * kHeadsMinBlocks)));
   return launch_k(P, heads_mma_kernel<D, NTILE, LB>, grid, 128, smem, static_cast<const float*>(P.y),
            static_cast<const int*>(P.offsets), batch, c.n_entities, c.actions, static_cast<const int*>(P.row_slot),
            static_cast<const float*>(P.wp), static_cast<const float*>(P.bp), static_cast<const float*>(P.wv),
