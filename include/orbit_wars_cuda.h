@@ -114,10 +114,15 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_many_resident(
     size_t request_count,
     OrbitWarsCudaTrue2DShape shape);
 
-/* orbit_wars_cuda.h:82-92; .cu:2823-3330 -- training is not part of the
- * policy forward. The call is forwarded to the library named by
- * ORBIT_WARS_CUDA_TRAIN_LIB_PATH (for example the reference's own build),
- * else it returns RUNTIME_ERROR "training not provided". */
+/* orbit_wars_cuda.h:82-92; .cu:2823-3330 -- one full-batch SGD step per
+ * model: all_weights (model_count x weight count, host buffer) is updated in
+ * place with w -= learning_rate * (sum over the model's samples of the loss
+ * gradient) / (the model's sample count). Per sample: input rows (rows x 7),
+ * the outputs it produced (rows x 24), an int reward and rows x 12 target
+ * action rewards. Samples are processed in chunks of at most
+ * batch_sample_count; the result does not depend on the chunking beyond f32
+ * rounding. BAD_ARGUMENT "invalid true2d training batch" or "true2d training
+ * model index out of range" as the reference. */
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
     const float* input_rows,
     const float* output_rows,

@@ -24,8 +24,6 @@
 
 #include "orbit_wars_cuda.h"
 
-#include <dlfcn.h>
-
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -718,6 +716,8 @@ __global__ void __launch_bounds__(512) t2_decode(const float* __restrict__ out, 
   }
 }
 
+#include "ow_t2_train.cuh"
+
 // ---------------------------------------------------------------- process-global workspace
 struct Workspace {
   std::mutex mu;
@@ -1082,6 +1082,167 @@ OrbitWarsCudaStatus encode_result(Workspace& W, size_t n, int32_t* encode_errors
   return ok();
 }
 
+
+// ---------------------------------------------------------------- training step, host side
+// One full-batch SGD step (orbit_wars_cuda.cu:2823-3330): samples are sorted by
+// model (stable counting sort) and processed in chunks of at most
+// batch_sample_count; every chunk runs forward with history, loss, backward and
+// adds its gradients to the per-model sums; the update is applied once at the end.
+OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const float* output_rows, const int* rewards,
+                               const float* target_action_rewards, const size_t* model_indices, float* all_weights,
+                               size_t sample_count, size_t model_count, const OrbitWarsCudaTrue2DShape& shape,
+                               const OrbitWarsCudaTrue2DTrainingConfig& tc) {
+  const T2Layout Ly = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
+  const T2Dev D = ref_layout_dev(Ly);
+  const size_t rows = Ly.rows, cells = Ly.cells, layers = Ly.layers, heads = Ly.heads, total = Ly.total;
+  const size_t n_out = 2 * rows * kTargets + kOutScalars * kTargets;
+  const size_t cap = std::min<size_t>(std::min<size_t>(tc.batch_sample_count, sample_count), 65535);
+  // order: samples sorted by model; counts per model over the whole call
+  std::vector<int> count(model_count, 0), order(sample_count);
+  for (size_t i = 0; i < sample_count; ++i) ++count[model_indices[i]];
+  {
+    std::vector<size_t> fill(model_count + 1, 0);
+    for (size_t m = 0; m < model_count; ++m) fill[m + 1] = fill[m] + static_cast<size_t>(count[m]);
+    for (size_t i = 0; i < sample_count; ++i) order[fill[model_indices[i]]++] = static_cast<int>(i);
+  }
+  // device buffers (freed on every exit path)
+  std::vector<void*> owned;
+  auto alloc = [&](void** p, size_t bytes) -> cudaError_t {
+    const cudaError_t e = cudaMalloc(p, std::max<size_t>(bytes, 4));
+    if (e == cudaSuccess) owned.push_back(*p);
+    return e;
+  };
+  struct Freer {
+    std::vector<void*>& v;
+    ~Freer() {
+      for (void* q : v) cudaFree(q);
+    }
+  } freer{owned};
+  float *dw, *dg, *dx, *dout, *dtar, *hist, *grad, *attv, *attg, *stats, *gpart, *opart, *hpart, *igrad, *cpart, *hcta;
+  int *drew, *dmodel, *dmstart, *dcount;
+  const size_t ctas = (cells + 255) / 256;
+  T2_TRY(alloc(reinterpret_cast<void**>(&dw), model_count * total * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&dg), model_count * total * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&dcount), model_count * sizeof(int)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&dx), cap * rows * kFeatures * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&dout), cap * rows * kOutPerRow * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&dtar), cap * rows * kTargets * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&drew), cap * sizeof(int)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&dmodel), cap * sizeof(int)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&dmstart), (model_count + 1) * sizeof(int)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&hist), cap * (layers + 2) * cells * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&grad), cap * (layers + 2) * cells * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&attv), cap * cells * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&attg), cap * cells * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&stats), cap * heads * 3 * cells * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&gpart), cap * kTargets * cells * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&opart), cap * n_out * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&hpart), cap * heads * 8 * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&igrad), cap * heads * cells * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&cpart), model_count * cells * 16 * sizeof(float)));
+  T2_TRY(alloc(reinterpret_cast<void**>(&hcta), cap * ctas * 8 * sizeof(float)));
+  cudaStream_t st = W.stream;
+  T2_TRY(cudaMemcpyAsync(dw, all_weights, model_count * total * sizeof(float), cudaMemcpyHostToDevice, st));
+  T2_TRY(cudaMemsetAsync(dg, 0, model_count * total * sizeof(float), st));
+  T2_TRY(cudaMemcpyAsync(dcount, count.data(), model_count * sizeof(int), cudaMemcpyHostToDevice, st));
+  // shared memory: the mid state (forward) and five per-cell vectors (backward) when they fit
+  const size_t fwd_smem = cells * sizeof(float), bwd_smem = 5 * cells * sizeof(float);
+  const int fwd_sm = fwd_smem <= 200 * 1024, bwd_sm = bwd_smem <= 200 * 1024;
+  if (fwd_sm && fwd_smem > 48 * 1024)
+    T2_TRY(cudaFuncSetAttribute(t2tr::fwd_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(fwd_smem)));
+  if (bwd_sm && bwd_smem > 48 * 1024)
+    T2_TRY(cudaFuncSetAttribute(t2tr::bwd_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(bwd_smem)));
+  // staged chunk inputs in sorted order
+  std::vector<float> hx(cap * rows * kFeatures), hout(cap * rows * kOutPerRow), htar(cap * rows * kTargets);
+  std::vector<int> hrew(cap), hmodel(cap), hmstart(model_count + 1);
+  t2tr::Tr t{};
+  t.L = D;
+  t.w = dw;
+  t.g = dg;
+  t.x = dx;
+  t.out = dout;
+  t.rewards = drew;
+  t.tar = dtar;
+  t.model = dmodel;
+  t.mstart = dmstart;
+  t.models = static_cast<int>(model_count);
+  t.hist = hist;
+  t.grad = grad;
+  t.attv = attv;
+  t.att_grad = attg;
+  t.stats = stats;
+  t.gpart = gpart;
+  t.opart = opart;
+  t.hpart = hpart;
+  t.igrad = igrad;
+  t.cpart = cpart;
+  t.owner_own = tc.owner_class_own;
+  t.owner_empty = tc.owner_class_empty;
+  t.owner_absent = tc.owner_class_absent_on_map;
+  t.reward_normalizer = tc.reward_normalizer;
+  t.send_threshold = tc.send_threshold;
+  t.learning_rate = tc.learning_rate;
+  const unsigned cb = static_cast<unsigned>(ctas);
+  const unsigned mid = static_cast<unsigned>(D.mid);
+  for (size_t off = 0; off < sample_count; off += cap) {
+    const size_t n = std::min(cap, sample_count - off);
+    std::fill(hmstart.begin(), hmstart.end(), 0);
+    for (size_t k = 0; k < n; ++k) {
+      const size_t i = static_cast<size_t>(order[off + k]);
+      std::memcpy(&hx[k * rows * kFeatures], input_rows + i * rows * kFeatures, rows * kFeatures * sizeof(float));
+      std::memcpy(&hout[k * rows * kOutPerRow], output_rows + i * rows * kOutPerRow, rows * kOutPerRow * sizeof(float));
+      std::memcpy(&htar[k * rows * kTargets], target_action_rewards + i * rows * kTargets, rows * kTargets * sizeof(float));
+      hrew[k] = rewards[i];
+      hmodel[k] = static_cast<int>(model_indices[i]);
+      ++hmstart[model_indices[i] + 1];
+    }
+    for (size_t m = 0; m < model_count; ++m) hmstart[m + 1] += hmstart[m];
+    T2_TRY(cudaMemcpyAsync(dx, hx.data(), n * rows * kFeatures * sizeof(float), cudaMemcpyHostToDevice, st));
+    T2_TRY(cudaMemcpyAsync(dout, hout.data(), n * rows * kOutPerRow * sizeof(float), cudaMemcpyHostToDevice, st));
+    T2_TRY(cudaMemcpyAsync(dtar, htar.data(), n * rows * kTargets * sizeof(float), cudaMemcpyHostToDevice, st));
+    T2_TRY(cudaMemcpyAsync(drew, hrew.data(), n * sizeof(int), cudaMemcpyHostToDevice, st));
+    T2_TRY(cudaMemcpyAsync(dmodel, hmodel.data(), n * sizeof(int), cudaMemcpyHostToDevice, st));
+    T2_TRY(cudaMemcpyAsync(dmstart, hmstart.data(), (model_count + 1) * sizeof(int), cudaMemcpyHostToDevice, st));
+    T2_TRY(cudaMemsetAsync(grad, 0, n * (layers + 2) * cells * sizeof(float), st));
+    t.n = static_cast<int>(n);
+    const dim3 gs(cb, static_cast<unsigned>(n)), gm(cb, static_cast<unsigned>(model_count));
+    // forward with history
+    t2tr::fwd_matrix<<<gs, 256, 0, st>>>(t, 0, static_cast<int>(mid), 1);
+    t2tr::fwd_attention<<<gs, 256, fwd_sm ? fwd_smem : 0, st>>>(t, fwd_sm);
+    t2tr::fwd_matrix<<<gs, 256, 0, st>>>(t, static_cast<int>(mid), static_cast<int>(layers), 0);
+    // loss
+    t2tr::loss_backward<<<dim3(static_cast<unsigned>(kTargets), static_cast<unsigned>(n)),
+                          static_cast<unsigned>((rows + 31) / 32 * 32), 0, st>>>(t);
+    t2tr::sum_actions<<<gs, 256, 0, st>>>(t);
+    // backward
+    for (int l = static_cast<int>(layers) - 1; l >= static_cast<int>(mid); --l) t2tr::bwd_matrix<<<gm, 256, 0, st>>>(t, l);
+    t2tr::bwd_apply<<<gm, 256, 0, st>>>(t);
+    t2tr::reduce_shared<<<static_cast<unsigned>(model_count), 32, 0, st>>>(t);
+    for (int h = 0; h < static_cast<int>(heads); ++h) {
+      t2tr::bwd_attention<<<gs, 256, bwd_sm ? bwd_smem : 0, st>>>(t, h, hcta, bwd_sm);
+      t2tr::sum_heads<<<gs, 256, 0, st>>>(t, h, hcta, static_cast<int>(ctas));
+    }
+    t2tr::reduce_heads<<<static_cast<unsigned>(model_count), static_cast<unsigned>(heads * 8), 0, st>>>(t);
+    for (int l = static_cast<int>(mid) - 1; l >= 0; --l) t2tr::bwd_matrix<<<gm, 256, 0, st>>>(t, l);
+    t2tr::bwd_expand<<<gm, 256, 0, st>>>(t);
+    t2tr::reduce_expand<<<static_cast<unsigned>(model_count), 128, 0, st>>>(t);
+    t2tr::reduce_output<<<dim3(static_cast<unsigned>((n_out + 127) / 128), static_cast<unsigned>(model_count)), 128, 0,
+                          st>>>(t);
+    T2_TRY(cudaGetLastError());
+    // the host staging vectors are rewritten by the next chunk
+    T2_TRY(cudaStreamSynchronize(st));
+  }
+  const long long all = static_cast<long long>(model_count) * static_cast<long long>(total);
+  t2tr::apply_sgd<<<static_cast<unsigned>((all + 255) / 256), 256, 0, st>>>(dw, dg, dcount, static_cast<int>(model_count),
+                                                                          static_cast<long long>(total), tc.learning_rate);
+  T2_TRY(cudaGetLastError());
+  T2_TRY(cudaMemcpyAsync(all_weights, dw, model_count * total * sizeof(float), cudaMemcpyDeviceToHost, st));
+  T2_TRY(cudaStreamSynchronize(st));
+  return ok();
+}
+
 }  // namespace
 
 extern "C" {
@@ -1344,33 +1505,25 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_play_many_resident(
   return e.code != kOk ? e : f;
 }
 
-typedef OrbitWarsCudaStatus (*TrainFn)(const float*, const float*, const int*, const float*, const size_t*, float*,
-                                       size_t, size_t, OrbitWarsCudaTrue2DShape, OrbitWarsCudaTrue2DTrainingConfig);
-
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
     const float* input_rows, const float* output_rows, const int* rewards, const float* target_action_rewards,
     const size_t* model_indices, float* all_weights, size_t sample_count, size_t model_count,
     OrbitWarsCudaTrue2DShape shape, OrbitWarsCudaTrue2DTrainingConfig training_config) {
+  // argument checks of orbit_wars_cuda.cu:2834-2850
+  const OrbitWarsCudaTrue2DTrainingConfig& tc = training_config;
+  const bool config_ok = tc.batch_sample_count > 0 && tc.learning_rate > 0.0f && tc.reward_normalizer > 0.0f &&
+                         tc.send_threshold >= 0.0f && tc.send_threshold <= 1.0f;
   if (input_rows == nullptr || output_rows == nullptr || rewards == nullptr || target_action_rewards == nullptr ||
-      model_indices == nullptr || all_weights == nullptr || sample_count == 0 || model_count == 0)
-    return bad("invalid true2d training buffer");
-  if (!shape_ok(shape)) return bad("invalid true2d shape");
-  const char* path = std::getenv("ORBIT_WARS_CUDA_TRAIN_LIB_PATH");
-  if (path == nullptr || *path == '\0') return rt("training not provided");
-  static std::mutex mu;
-  static TrainFn fn = nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (fn == nullptr) {
-    void* h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
-    if (h == nullptr) return rt("training library could not be opened");
-    fn = reinterpret_cast<TrainFn>(dlsym(h, "orbit_wars_cuda_true2d_train_full_attention"));
-    if (fn == nullptr || fn == &orbit_wars_cuda_true2d_train_full_attention) {
-      fn = nullptr;
-      return rt("training library lacks the training symbol");
-    }
-  }
-  return fn(input_rows, output_rows, rewards, target_action_rewards, model_indices, all_weights, sample_count,
-            model_count, shape, training_config);
+      model_indices == nullptr || all_weights == nullptr || sample_count == 0 || model_count == 0 ||
+      !shape_ok(shape) || !config_ok)
+    return bad("invalid true2d training batch");
+  for (size_t i = 0; i < sample_count; ++i)
+    if (model_indices[i] >= model_count) return bad("true2d training model index out of range");
+  Workspace& W = ws();
+  std::lock_guard<std::mutex> lock(W.mu);
+  T2_TRY(ensure_common(W));
+  return train_step(W, input_rows, output_rows, rewards, target_action_rewards, model_indices, all_weights,
+                    sample_count, model_count, shape, tc);
 }
 
 // Allocation-free variant of orbit_wars_cuda_true2d_forward (no counterpart in

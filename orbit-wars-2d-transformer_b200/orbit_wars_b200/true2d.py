@@ -167,6 +167,28 @@ class CudaTrue2D:
         return tr, sc
 
 
+    # ---- training step (orbit_wars_cuda.cu:2823-3330) ---------------------------------------------------------
+    def train_full_attention(self, input_rows, output_rows, rewards, target_action_rewards, model_indices,
+                             all_weights, shape: True2DShape = True2DShape(), batch_sample_count: int = 64,
+                             learning_rate: float = 1e-3, reward_normalizer: float = 1.0, send_threshold: float = 0.5,
+                             owner_class_own: float = 1.0, owner_class_empty: float = -0.5,
+                             owner_class_absent_on_map: float = -1.0) -> np.ndarray:
+        """One SGD step; returns the updated weights (models x parameter_count) as a new array."""
+        x = _f32(input_rows)
+        o = _f32(output_rows)
+        r = np.ascontiguousarray(rewards, dtype=np.int32)
+        tar = _f32(target_action_rewards)
+        idx = np.ascontiguousarray(model_indices, dtype=np.uintp)
+        w = np.array(all_weights, dtype=np.float32, copy=True, order="C")
+        n = idx.size
+        models = w.size // shape.parameter_count()
+        cfg = _lib.TrainingConfigC(batch_sample_count, learning_rate, reward_normalizer, send_threshold,
+                                   owner_class_own, owner_class_empty, owner_class_absent_on_map)
+        _lib.check("cuda_true2d_train_full_attention", self.lib.orbit_wars_cuda_true2d_train_full_attention(
+            x.ctypes.data, o.ctypes.data, r.ctypes.data, tar.ctypes.data, idx.ctypes.data, w.ctypes.data, n, models,
+            shape.c(), cfg))
+        return w.reshape(models, shape.parameter_count())
+
     # ---- device encoder (encoder.rs:37-208) ----------------------------------------------------------------
     @staticmethod
     def _requests(request_games, request_players):
