@@ -624,6 +624,59 @@ def true2d_turn(args, lib, shape, steps: int) -> dict:
             "commands_per_request": round(float((tr >= 0).sum()) / n, 2)}
 
 
+def true2d_train(args, lib, shape, samples: int = 64, models: int = 8, steps: int = 3) -> dict:
+    """The training step (orbit_wars_cuda_true2d_train_full_attention) on seeded engine-shaped samples: ours
+    and, when built, the reference's own CUDA library on the same samples and weights (wall clock per
+    synchronous call, host buffers, as the engine calls it), with the agreement of the weight updates."""
+    import ctypes as C
+    from orbit_wars_b200 import _lib, synth
+    rng = np.random.default_rng(args.seed + 7)
+    R = shape.rows
+    x = rng.uniform(-1.0, 1.0, (samples, R, 7)).astype(np.float32)
+    classes = np.array([1.0, 0.75, 0.5, 0.25, 0.0, -1.0], np.float32)
+    for i in range(samples):
+        act = int(rng.integers(8, R + 1))
+        x[i, :act, 0] = rng.choice(classes, act, p=[0.3, 0.15, 0.1, 0.1, 0.25, 0.1])
+        x[i, act:, 0] = -0.5
+        x[i, act:, 1:] = 0.0
+    out = rng.uniform(0.0, 1.0, (samples, R, 24)).astype(np.float32)
+    rewards = rng.integers(-2, 3, samples).astype(np.int32)
+    tar = (rng.standard_normal((samples, R, 12)) * 0.2).astype(np.float32)
+    idx = (np.arange(samples) % models).astype(np.uintp)
+    w = synth.true2d_population(args.seed, models, shape.parameter_count())
+    kw = dict(batch_sample_count=samples, learning_rate=0.01, reward_normalizer=2.0, send_threshold=0.5)
+    lib.train_full_attention(x, out, rewards, tar, idx, w, shape, **kw)
+    wall = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ours = lib.train_full_attention(x, out, rewards, tar, idx, w, shape, **kw)
+        wall.append(time.perf_counter() - t0)
+    res = {"value": samples * steps / float(np.sum(wall)), "unit": "samples/s", "samples": samples, "models": models,
+           "steps": steps, "timing": "wall clock per synchronous train_full_attention call (host buffers)"}
+    path = REPO / "oracle" / "_ref" / "liborbit_wars_cuda_ref.so"
+    if path.exists():
+        ref = C.CDLL(str(path), mode=2)
+        fn = ref.orbit_wars_cuda_true2d_train_full_attention
+        fn.restype = _lib.Status
+        fn.argtypes = [C.c_void_p] * 6 + [C.c_size_t, C.c_size_t, _lib.True2DShapeC, _lib.TrainingConfigC]
+        cfg = _lib.TrainingConfigC(samples, 0.01, 2.0, 0.5, 1.0, -0.5, -1.0)
+        rwall = []
+        for k in range(2):
+            wr = np.array(w, dtype=np.float32, copy=True)
+            t0 = time.perf_counter()
+            _lib.check("reference training", fn(x.ctypes.data, out.ctypes.data, rewards.ctypes.data, tar.ctypes.data,
+                                                idx.ctypes.data, wr.ctypes.data, samples, models, shape.c(), cfg))
+            if k > 0:
+                rwall.append(time.perf_counter() - t0)
+        d_ref = wr.reshape(models, -1) - w.reshape(models, -1)
+        d_ours = ours - w.reshape(models, -1)
+        res["reference_value"] = samples * len(rwall) / float(np.sum(rwall))
+        res["ours_over_reference"] = round(res["value"] / res["reference_value"], 2)
+        res["update_rel_err_vs_reference"] = float(np.abs(d_ours - d_ref).max() / np.abs(d_ref).max())
+        res["reference_library"] = "oracle/_ref/liborbit_wars_cuda_ref.so (reference source, nvcc sm_100a)"
+    return res
+
+
 def run_true2d(args) -> None:
     import torch
     import torch.distributed as dist
@@ -702,6 +755,7 @@ def run_true2d(args) -> None:
             ref_gpu["max_abs_diff_vs_ours"] = float(np.abs(ro - out.reshape(-1)).max())
             ref_gpu["ours_e2e_over_reference"] = round(e2e["value"] / ref_gpu["value"], 3)
     turn = true2d_turn(args, lib, shape, steps=min(args.steps, 20)) if rank == 0 and world == 1 else None
+    train = true2d_train(args, lib, shape) if rank == 0 and world == 1 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = true2d_cpu_reference(args, shape, pop, per, x, target_s=12.0)
@@ -717,7 +771,7 @@ def run_true2d(args) -> None:
                        "parallelism": f"replicas x{world} (the reference ABI is single-device)",
                        "value_timing": "sum of the three kernels' CUDA events per call (inputs already on the device)"},
             "e2e": e2e, "gpu_launches": 3 * args.steps, "roofline": roof, "cpu_baseline": cpu,
-            "reference_gpu": ref_gpu, "clocks": clocks, "kernels": kernels, "turn": turn,
+            "reference_gpu": ref_gpu, "clocks": clocks, "kernels": kernels, "turn": turn, "train": train,
             "outputs_finite": bool(np.isfinite(out).all()),
         }
         print(json.dumps(line), flush=True)
