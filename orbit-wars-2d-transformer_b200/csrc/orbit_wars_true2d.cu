@@ -30,6 +30,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "ow_common.cuh"
@@ -751,6 +752,11 @@ struct Workspace {
   int32_t* enc_err = nullptr;
   size_t enc_err_cap = 0;
   std::vector<int32_t> host_err;
+  // training step: one device arena and the pinned staging of the weights, kept between calls
+  unsigned char* train_arena = nullptr;
+  size_t train_cap = 0;
+  unsigned char* train_pin = nullptr;
+  size_t train_pin_cap = 0;
   int* groups = nullptr;  // model groups of the current call: (model, kGroup request indices) each
   size_t groups_cap = 0;
   std::vector<int> host_groups;
@@ -1084,6 +1090,25 @@ OrbitWarsCudaStatus encode_result(Workspace& W, size_t n, int32_t* encode_errors
 
 
 // ---------------------------------------------------------------- training step, host side
+// memcpy split over up to 8 host threads (pageable <-> pinned staging).
+void par_copy(unsigned char* dst, const unsigned char* src, size_t bytes) {
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t threads = std::min<size_t>({8, hw, std::max<size_t>(1, bytes >> 20)});
+  if (threads <= 1) {
+    std::memcpy(dst, src, bytes);
+    return;
+  }
+  const size_t per = (bytes + threads - 1) / threads;
+  std::vector<std::thread> pool;
+  for (size_t k = 1; k < threads; ++k) {
+    const size_t o = k * per;
+    if (o >= bytes) break;
+    pool.emplace_back([=] { std::memcpy(dst + o, src + o, std::min(per, bytes - o)); });
+  }
+  std::memcpy(dst, src, std::min(per, bytes));
+  for (auto& th : pool) th.join();
+}
+
 // One full-batch SGD step (orbit_wars_cuda.cu:2823-3330): samples are sorted by
 // model (stable counting sort) and processed in chunks of at most
 // batch_sample_count; every chunk runs forward with history, loss, backward and
@@ -1106,43 +1131,81 @@ OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const floa
     for (size_t i = 0; i < sample_count; ++i) order[fill[model_indices[i]]++] = static_cast<int>(i);
   }
   // device buffers (freed on every exit path)
-  std::vector<void*> owned;
-  auto alloc = [&](void** p, size_t bytes) -> cudaError_t {
-    const cudaError_t e = cudaMalloc(p, std::max<size_t>(bytes, 4));
-    if (e == cudaSuccess) owned.push_back(*p);
-    return e;
-  };
-  struct Freer {
-    std::vector<void*>& v;
-    ~Freer() {
-      for (void* q : v) cudaFree(q);
-    }
-  } freer{owned};
-  float *dw, *dg, *dx, *dout, *dtar, *hist, *grad, *attv, *attg, *stats, *gpart, *opart, *hpart, *igrad, *cpart, *hcta;
-  int *drew, *dmodel, *dmstart, *dcount;
+  // one device arena for every buffer of the step, kept between calls and
+  // grown when a call needs more (the population's buffers are separate)
   const size_t ctas = (cells + 255) / 256;
-  T2_TRY(alloc(reinterpret_cast<void**>(&dw), model_count * total * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&dg), model_count * total * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&dcount), model_count * sizeof(int)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&dx), cap * rows * kFeatures * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&dout), cap * rows * kOutPerRow * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&dtar), cap * rows * kTargets * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&drew), cap * sizeof(int)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&dmodel), cap * sizeof(int)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&dmstart), (model_count + 1) * sizeof(int)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&hist), cap * (layers + 2) * cells * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&grad), cap * (layers + 2) * cells * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&attv), cap * cells * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&attg), cap * cells * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&stats), cap * heads * 3 * cells * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&gpart), cap * kTargets * cells * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&opart), cap * n_out * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&hpart), cap * heads * 8 * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&igrad), cap * heads * cells * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&cpart), model_count * cells * 16 * sizeof(float)));
-  T2_TRY(alloc(reinterpret_cast<void**>(&hcta), cap * ctas * 8 * sizeof(float)));
+  size_t need = 0;
+  auto carve = [&](size_t bytes) {
+    const size_t o = need;
+    need += (std::max<size_t>(bytes, 4) + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t o_w = carve(model_count * total * sizeof(float)), o_g = carve(model_count * total * sizeof(float));
+  const size_t o_count = carve(model_count * sizeof(int)), o_x = carve(cap * rows * kFeatures * sizeof(float));
+  const size_t o_out = carve(cap * rows * kOutPerRow * sizeof(float)), o_tar = carve(cap * rows * kTargets * sizeof(float));
+  const size_t o_rew = carve(cap * sizeof(int)), o_model = carve(cap * sizeof(int));
+  const size_t o_mstart = carve((model_count + 1) * sizeof(int));
+  const size_t o_hist = carve(cap * (layers + 2) * cells * sizeof(float));
+  const size_t o_grad = carve(cap * (layers + 2) * cells * sizeof(float));
+  const size_t o_attv = carve(cap * cells * sizeof(float)), o_attg = carve(cap * cells * sizeof(float));
+  const size_t o_stats = carve(cap * heads * 3 * cells * sizeof(float));
+  const size_t o_gpart = carve(cap * kTargets * cells * sizeof(float)), o_opart = carve(cap * n_out * sizeof(float));
+  const size_t o_hpart = carve(cap * heads * 8 * sizeof(float)), o_igrad = carve(cap * heads * cells * sizeof(float));
+  const size_t o_cpart = carve(model_count * cells * 16 * sizeof(float)), o_hcta = carve(cap * ctas * 8 * sizeof(float));
+  if (need > W.train_cap || W.train_arena == nullptr) {
+    if (W.train_arena != nullptr) cudaFree(W.train_arena);
+    W.train_arena = nullptr;
+    W.train_cap = 0;
+    T2_TRY(cudaMalloc(reinterpret_cast<void**>(&W.train_arena), need));
+    W.train_cap = need;
+  }
+  unsigned char* ab = W.train_arena;
+  float* dw = reinterpret_cast<float*>(ab + o_w);
+  float* dg = reinterpret_cast<float*>(ab + o_g);
+  int* dcount = reinterpret_cast<int*>(ab + o_count);
+  float* dx = reinterpret_cast<float*>(ab + o_x);
+  float* dout = reinterpret_cast<float*>(ab + o_out);
+  float* dtar = reinterpret_cast<float*>(ab + o_tar);
+  int* drew = reinterpret_cast<int*>(ab + o_rew);
+  int* dmodel = reinterpret_cast<int*>(ab + o_model);
+  int* dmstart = reinterpret_cast<int*>(ab + o_mstart);
+  float* hist = reinterpret_cast<float*>(ab + o_hist);
+  float* grad = reinterpret_cast<float*>(ab + o_grad);
+  float* attv = reinterpret_cast<float*>(ab + o_attv);
+  float* attg = reinterpret_cast<float*>(ab + o_attg);
+  float* stats = reinterpret_cast<float*>(ab + o_stats);
+  float* gpart = reinterpret_cast<float*>(ab + o_gpart);
+  float* opart = reinterpret_cast<float*>(ab + o_opart);
+  float* hpart = reinterpret_cast<float*>(ab + o_hpart);
+  float* igrad = reinterpret_cast<float*>(ab + o_igrad);
+  float* cpart = reinterpret_cast<float*>(ab + o_cpart);
+  float* hcta = reinterpret_cast<float*>(ab + o_hcta);
+  // pinned staging of the weights, kept between calls
+  const size_t wbytes = model_count * total * sizeof(float);
+  if (wbytes > W.train_pin_cap || W.train_pin == nullptr) {
+    if (W.train_pin != nullptr) cudaFreeHost(W.train_pin);
+    W.train_pin = nullptr;
+    W.train_pin_cap = 0;
+    T2_TRY(cudaHostAlloc(reinterpret_cast<void**>(&W.train_pin), wbytes, cudaHostAllocDefault));
+    W.train_pin_cap = wbytes;
+  }
   cudaStream_t st = W.stream;
-  T2_TRY(cudaMemcpyAsync(dw, all_weights, model_count * total * sizeof(float), cudaMemcpyHostToDevice, st));
+  // device timing (profile_begin / profile_end): copies and kernel phases
+  auto mark = [&](const char* name) {
+    if (W.prof_on && W.prof_used < W.prof_events.size()) {
+      cudaEventRecord(W.prof_events[W.prof_used], st);
+      W.prof_names[W.prof_used++] = name;
+    }
+  };
+  mark("train_weights_h2d");
+  // weights up in 16 MB pieces: a piece is copied into pinned memory by host
+  // threads while the previous piece's DMA runs
+  constexpr size_t kPiece = size_t(16) << 20;
+  for (size_t o = 0; o < wbytes; o += kPiece) {
+    const size_t b = std::min(kPiece, wbytes - o);
+    par_copy(W.train_pin + o, reinterpret_cast<const unsigned char*>(all_weights) + o, b);
+    T2_TRY(cudaMemcpyAsync(reinterpret_cast<unsigned char*>(dw) + o, W.train_pin + o, b, cudaMemcpyHostToDevice, st));
+  }
   T2_TRY(cudaMemsetAsync(dg, 0, model_count * total * sizeof(float), st));
   T2_TRY(cudaMemcpyAsync(dcount, count.data(), model_count * sizeof(int), cudaMemcpyHostToDevice, st));
   // shared memory: the mid state (forward) and five per-cell vectors (backward) when they fit
@@ -1199,6 +1262,7 @@ OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const floa
       ++hmstart[model_indices[i] + 1];
     }
     for (size_t m = 0; m < model_count; ++m) hmstart[m + 1] += hmstart[m];
+    mark("train_samples_h2d");
     T2_TRY(cudaMemcpyAsync(dx, hx.data(), n * rows * kFeatures * sizeof(float), cudaMemcpyHostToDevice, st));
     T2_TRY(cudaMemcpyAsync(dout, hout.data(), n * rows * kOutPerRow * sizeof(float), cudaMemcpyHostToDevice, st));
     T2_TRY(cudaMemcpyAsync(dtar, htar.data(), n * rows * kTargets * sizeof(float), cudaMemcpyHostToDevice, st));
@@ -1209,15 +1273,19 @@ OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const floa
     t.n = static_cast<int>(n);
     const dim3 gs(cb, static_cast<unsigned>(n)), gm(cb, static_cast<unsigned>(model_count));
     // forward with history
+    mark("train_forward");
     t2tr::fwd_matrix<<<gs, 256, 0, st>>>(t, 0, static_cast<int>(mid), 1);
     t2tr::fwd_attention<<<gs, 256, fwd_sm ? fwd_smem : 0, st>>>(t, fwd_sm);
     t2tr::fwd_matrix<<<gs, 256, 0, st>>>(t, static_cast<int>(mid), static_cast<int>(layers), 0);
     // loss
+    mark("train_loss");
     t2tr::loss_backward<<<dim3(static_cast<unsigned>(kTargets), static_cast<unsigned>(n)),
                           static_cast<unsigned>((rows + 31) / 32 * 32), 0, st>>>(t);
     t2tr::sum_actions<<<gs, 256, 0, st>>>(t);
     // backward
+    mark("train_backward_matrix");
     for (int l = static_cast<int>(layers) - 1; l >= static_cast<int>(mid); --l) t2tr::bwd_matrix<<<gm, 256, 0, st>>>(t, l);
+    mark("train_backward_attention");
     t2tr::bwd_apply<<<gm, 256, 0, st>>>(t);
     t2tr::reduce_shared<<<static_cast<unsigned>(model_count), 32, 0, st>>>(t);
     for (int h = 0; h < static_cast<int>(heads); ++h) {
@@ -1225,20 +1293,42 @@ OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const floa
       t2tr::sum_heads<<<gs, 256, 0, st>>>(t, h, hcta, static_cast<int>(ctas));
     }
     t2tr::reduce_heads<<<static_cast<unsigned>(model_count), static_cast<unsigned>(heads * 8), 0, st>>>(t);
+    mark("train_backward_matrix");
     for (int l = static_cast<int>(mid) - 1; l >= 0; --l) t2tr::bwd_matrix<<<gm, 256, 0, st>>>(t, l);
+    mark("train_backward_expand_reduce");
     t2tr::bwd_expand<<<gm, 256, 0, st>>>(t);
     t2tr::reduce_expand<<<static_cast<unsigned>(model_count), 128, 0, st>>>(t);
     t2tr::reduce_output<<<dim3(static_cast<unsigned>((n_out + 127) / 128), static_cast<unsigned>(model_count)), 128, 0,
                           st>>>(t);
     T2_TRY(cudaGetLastError());
+    mark(nullptr);
     // the host staging vectors are rewritten by the next chunk
     T2_TRY(cudaStreamSynchronize(st));
   }
   const long long all = static_cast<long long>(model_count) * static_cast<long long>(total);
+  mark("train_sgd_d2h");
   t2tr::apply_sgd<<<static_cast<unsigned>((all + 255) / 256), 256, 0, st>>>(dw, dg, dcount, static_cast<int>(model_count),
                                                                           static_cast<long long>(total), tc.learning_rate);
   T2_TRY(cudaGetLastError());
-  T2_TRY(cudaMemcpyAsync(all_weights, dw, model_count * total * sizeof(float), cudaMemcpyDeviceToHost, st));
+  // weights down in pieces: each piece leaves pinned memory by host threads as soon as its DMA is done
+  std::vector<cudaEvent_t> piece_ev;
+  for (size_t o = 0; o < wbytes; o += kPiece) {
+    const size_t b = std::min(kPiece, wbytes - o);
+    T2_TRY(cudaMemcpyAsync(W.train_pin + o, reinterpret_cast<unsigned char*>(dw) + o, b, cudaMemcpyDeviceToHost, st));
+    cudaEvent_t ev;
+    T2_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    piece_ev.push_back(ev);
+    T2_TRY(cudaEventRecord(ev, st));
+  }
+  mark(nullptr);
+  cudaError_t e = cudaSuccess;
+  for (size_t k = 0, o = 0; k < piece_ev.size(); ++k, o += kPiece) {
+    if (e == cudaSuccess) e = cudaEventSynchronize(piece_ev[k]);
+    if (e == cudaSuccess)
+      par_copy(reinterpret_cast<unsigned char*>(all_weights) + o, W.train_pin + o, std::min(kPiece, wbytes - o));
+    cudaEventDestroy(piece_ev[k]);
+  }
+  T2_TRY(e);
   T2_TRY(cudaStreamSynchronize(st));
   return ok();
 }

@@ -403,7 +403,7 @@ __device__ __forceinline__ void attention_task(const __nv_bfloat16* sq, const __
 // keeps ldmatrix conflict-free. Each (head, 16-query block) task runs exactly
 // the state's ceil(count/16) key blocks.
 template <int NMAX, int HG>
-__global__ void __launch_bounds__(256) attention_bf16_kernel(const __nv_bfloat16* __restrict__ qkv,
+__global__ void __launch_bounds__(256, 4) attention_bf16_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                               __nv_bfloat16* __restrict__ out,
                                                               const int* __restrict__ offsets, int d,
                                                               float scale_log2) {

@@ -26,7 +26,9 @@
 //     whole mid state and the per-query statistics of its head in shared memory;
 //   * reductions over cells or samples go through per-sample partial buffers.
 // The arithmetic follows the reference's formulas; sums are taken in a
-// different order, so results agree to f32 rounding, not bit for bit.
+// different order, and the O(cells^2) attention loops use the fast exponential
+// (__expf, a few ulp) and a reciprocal of each denominator, so results agree to
+// f32 rounding, not bit for bit.
 #pragma once
 
 namespace t2tr {
@@ -52,7 +54,7 @@ struct Tr {
   float* grad;             // [n][layers + 2][cells] their gradients
   float* attv;             // [n][cells] combined attention context
   float* att_grad;         // [n][cells]
-  float* stats;            // [n][heads][3][cells] per query: max score, denominator, weighted average
+  float* stats;            // [n][heads][3][cells] per query: max score, 1 / denominator, weighted average
   float* gpart;            // [n][12][cells] final-state gradient per action
   float* opart;            // [n][2 * rows * 12 + 60] output-weight gradients per sample
   float* hpart;            // [n][heads][8] head-weight gradients per sample (7 used)
@@ -161,14 +163,14 @@ __global__ void __launch_bounds__(256) fwd_attention(Tr t, int use_smem) {
     float den = 0.0f, wv = 0.0f;
     for (int j = 0; j < cells; ++j) {
       const float kv = s_v[j];
-      const float a = expf(query * (kv * ks + kb) - mx);
+      const float a = __expf(query * (kv * ks + kb) - mx);
       den += a;
       wv += a * (kv * vs + vb);
     }
     const float wavg = wv / den;
     float* st = t.stats + (static_cast<long long>(s) * t.L.heads + h) * 3 * cells;
     st[q] = mx;
-    st[cells + q] = den;
+    st[cells + q] = 1.0f / den;  // kept as the reciprocal: the backward multiplies
     st[2 * cells + q] = wavg;
     ctx += wavg * os;
   }
@@ -469,7 +471,7 @@ __global__ void __launch_bounds__(256) bwd_attention(Tr t, int h, float* hcta, i
         const float kv = s_v[j];
         const float key = kv * ks + kb;
         const float val = kv * vs + vb;
-        const float p = expf(qc * key - mx) / den;
+        const float p = __expf(qc * key - mx) * den;  // den holds 1 / denominator
         d_query += d_wavg * p * (val - wa) * key;
       }
       go = d_att_c * wa;
@@ -482,7 +484,7 @@ __global__ void __launch_bounds__(256) bwd_attention(Tr t, int h, float* hcta, i
       const float d_att = s_dg[i];
       if (d_att == 0.0f) continue;
       const float qv = s_v[i] * qs + qb;
-      const float p = expf(qv * key_c - s_mx[i]) / s_den[i];
+      const float p = __expf(qv * key_c - s_mx[i]) * s_den[i];  // s_den holds 1 / denominator
       const float d_wavg = d_att * os;
       const float d_val = d_wavg * p;
       const float d_key = d_wavg * p * (val_c - s_wa[i]) * qv;

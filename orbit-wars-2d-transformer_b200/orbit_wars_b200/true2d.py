@@ -172,14 +172,21 @@ class CudaTrue2D:
                              all_weights, shape: True2DShape = True2DShape(), batch_sample_count: int = 64,
                              learning_rate: float = 1e-3, reward_normalizer: float = 1.0, send_threshold: float = 0.5,
                              owner_class_own: float = 1.0, owner_class_empty: float = -0.5,
-                             owner_class_absent_on_map: float = -1.0) -> np.ndarray:
-        """One SGD step; returns the updated weights (models x parameter_count) as a new array."""
+                             owner_class_absent_on_map: float = -1.0, inplace: bool = False) -> np.ndarray:
+        """One SGD step; returns the updated weights (models x parameter_count): a new array, or with
+        inplace=True the given float32 C-contiguous array itself, updated where it lies (as the engine's
+        host buffer is)."""
         x = _f32(input_rows)
         o = _f32(output_rows)
         r = np.ascontiguousarray(rewards, dtype=np.int32)
         tar = _f32(target_action_rewards)
         idx = np.ascontiguousarray(model_indices, dtype=np.uintp)
-        w = np.array(all_weights, dtype=np.float32, copy=True, order="C")
+        if inplace:
+            w = all_weights
+            if not (isinstance(w, np.ndarray) and w.dtype == np.float32 and w.flags.c_contiguous):
+                raise ValueError("inplace training needs a float32 C-contiguous weight array")
+        else:
+            w = np.array(all_weights, dtype=np.float32, copy=True, order="C")
         n = idx.size
         models = w.size // shape.parameter_count()
         cfg = _lib.TrainingConfigC(batch_sample_count, learning_rate, reward_normalizer, send_threshold,
