@@ -752,6 +752,11 @@ struct Workspace {
   int32_t* enc_err = nullptr;
   size_t enc_err_cap = 0;
   std::vector<int32_t> host_err;
+  // pinned staging of the host-buffer forward's input rows and output rows
+  unsigned char* pin_in = nullptr;
+  size_t pin_in_cap = 0;
+  unsigned char* pin_out = nullptr;
+  size_t pin_out_cap = 0;
   // training step: one device arena and the pinned staging of the weights, kept between calls
   unsigned char* train_arena = nullptr;
   size_t train_cap = 0;
@@ -846,6 +851,35 @@ OrbitWarsCudaStatus upload(Workspace& W, const float* all_w, size_t models, cons
   return ok();
 }
 
+// memcpy split over up to 8 host threads (pageable <-> pinned staging).
+void par_copy(unsigned char* dst, const unsigned char* src, size_t bytes) {
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t threads = std::min<size_t>({8, hw, std::max<size_t>(1, bytes >> 20)});
+  if (threads <= 1) {
+    std::memcpy(dst, src, bytes);
+    return;
+  }
+  const size_t per = (bytes + threads - 1) / threads;
+  std::vector<std::thread> pool;
+  for (size_t k = 1; k < threads; ++k) {
+    const size_t o = k * per;
+    if (o >= bytes) break;
+    pool.emplace_back([=] { std::memcpy(dst + o, src + o, std::min(per, bytes - o)); });
+  }
+  std::memcpy(dst, src, std::min(per, bytes));
+  for (auto& th : pool) th.join();
+}
+
+cudaError_t ensure_pinned(unsigned char*& p, size_t& cap, size_t bytes) {
+  if (bytes <= cap && p != nullptr) return cudaSuccess;
+  if (p != nullptr) cudaFreeHost(p);
+  p = nullptr;
+  cap = 0;
+  const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&p), std::max<size_t>(bytes, 16), cudaHostAllocDefault);
+  if (e == cudaSuccess) cap = bytes;
+  return e;
+}
+
 // Waits for the stream and reports the device error word.
 OrbitWarsCudaStatus finish(Workspace& W) {
   int herr = 0;
@@ -880,7 +914,11 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   T2_TRY(ensure(W.idx, W.idx_cap, n));
   if (input_rows != nullptr) {
     T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
-    T2_TRY(cudaMemcpyAsync(W.in, input_rows, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
+    // host rows go through pinned memory: host threads copy, then one DMA (the
+    // previous call's copies are done: every host-buffer call ends synchronised)
+    T2_TRY(ensure_pinned(W.pin_in, W.pin_in_cap, in_n * sizeof(float)));
+    par_copy(W.pin_in, reinterpret_cast<const unsigned char*>(input_rows), in_n * sizeof(float));
+    T2_TRY(cudaMemcpyAsync(W.in, W.pin_in, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
   }
   const size_t* didx = nullptr;
   if (model_indices != nullptr) {
@@ -941,10 +979,20 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
     T2_TRY(cudaMemcpyAsync(dec->target_rows, W.dec_rows, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
     T2_TRY(cudaMemcpyAsync(dec->ship_counts, W.dec_counts, dn * sizeof(int32_t), cudaMemcpyDeviceToHost, W.stream));
   }
-  if (output_rows != nullptr)
-    T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
-  if (!sync) return ok();
-  return finish(W);
+  if (!sync) {
+    if (output_rows != nullptr)
+      T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+    return ok();
+  }
+  // outputs through pinned memory: one DMA, then host threads copy once the stream is done
+  if (output_rows != nullptr) {
+    T2_TRY(ensure_pinned(W.pin_out, W.pin_out_cap, out_n * sizeof(float)));
+    T2_TRY(cudaMemcpyAsync(W.pin_out, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+  }
+  const OrbitWarsCudaStatus st = finish(W);
+  if (output_rows != nullptr && st.code == kOk)
+    par_copy(reinterpret_cast<unsigned char*>(output_rows), W.pin_out, out_n * sizeof(float));
+  return st;
 }
 
 // ---------------------------------------------------------------- device encoder, host side
@@ -1090,24 +1138,6 @@ OrbitWarsCudaStatus encode_result(Workspace& W, size_t n, int32_t* encode_errors
 
 
 // ---------------------------------------------------------------- training step, host side
-// memcpy split over up to 8 host threads (pageable <-> pinned staging).
-void par_copy(unsigned char* dst, const unsigned char* src, size_t bytes) {
-  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-  const size_t threads = std::min<size_t>({8, hw, std::max<size_t>(1, bytes >> 20)});
-  if (threads <= 1) {
-    std::memcpy(dst, src, bytes);
-    return;
-  }
-  const size_t per = (bytes + threads - 1) / threads;
-  std::vector<std::thread> pool;
-  for (size_t k = 1; k < threads; ++k) {
-    const size_t o = k * per;
-    if (o >= bytes) break;
-    pool.emplace_back([=] { std::memcpy(dst + o, src + o, std::min(per, bytes - o)); });
-  }
-  std::memcpy(dst, src, std::min(per, bytes));
-  for (auto& th : pool) th.join();
-}
 
 // One full-batch SGD step (orbit_wars_cuda.cu:2823-3330): samples are sorted by
 // model (stable counting sort) and processed in chunks of at most
