@@ -676,7 +676,7 @@ def true2d_train(args, lib, shape, samples: int = 64, models: int = 8, steps: in
         fn.argtypes = [C.c_void_p] * 6 + [C.c_size_t, C.c_size_t, _lib.True2DShapeC, _lib.TrainingConfigC]
         cfg = _lib.TrainingConfigC(samples, 0.01, 2.0, 0.5, 1.0, -0.5, -1.0)
         rwall = []
-        for k in range(2):
+        for k in range(4):
             wr = np.array(w, dtype=np.float32, copy=True)  # outside the timed region
             t0 = time.perf_counter()
             _lib.check("reference training", fn(x.ctypes.data, out.ctypes.data, rewards.ctypes.data, tar.ctypes.data,

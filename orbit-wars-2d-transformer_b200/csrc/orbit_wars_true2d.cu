@@ -1247,6 +1247,13 @@ OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const floa
   if (bwd_sm && bwd_smem > 48 * 1024)
     T2_TRY(cudaFuncSetAttribute(t2tr::bwd_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(bwd_smem)));
+  // the prepared-term backward (512 threads, six floats per cell) where it fits
+  const size_t prep_smem = 6 * cells * sizeof(float);
+  const bool prep_sm = prep_smem <= 200 * 1024;
+  const unsigned cb512 = static_cast<unsigned>((cells + 511) / 512);
+  if (prep_sm && prep_smem > 48 * 1024)
+    T2_TRY(cudaFuncSetAttribute(t2tr::bwd_attention_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(prep_smem)));
   // staged chunk inputs in sorted order
   std::vector<float> hx(cap * rows * kFeatures), hout(cap * rows * kOutPerRow), htar(cap * rows * kTargets);
   std::vector<int> hrew(cap), hmodel(cap), hmstart(model_count + 1);
@@ -1319,8 +1326,13 @@ OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const floa
     t2tr::bwd_apply<<<gm, 256, 0, st>>>(t);
     t2tr::reduce_shared<<<static_cast<unsigned>(model_count), 32, 0, st>>>(t);
     for (int h = 0; h < static_cast<int>(heads); ++h) {
-      t2tr::bwd_attention<<<gs, 256, bwd_sm ? bwd_smem : 0, st>>>(t, h, hcta, bwd_sm);
-      t2tr::sum_heads<<<gs, 256, 0, st>>>(t, h, hcta, static_cast<int>(ctas));
+      if (prep_sm) {
+        t2tr::bwd_attention_smem<<<dim3(cb512, static_cast<unsigned>(n)), 512, prep_smem, st>>>(t, h, hcta);
+        t2tr::sum_heads<<<gs, 256, 0, st>>>(t, h, hcta, static_cast<int>(cb512));
+      } else {
+        t2tr::bwd_attention<<<gs, 256, bwd_sm ? bwd_smem : 0, st>>>(t, h, hcta, bwd_sm);
+        t2tr::sum_heads<<<gs, 256, 0, st>>>(t, h, hcta, static_cast<int>(ctas));
+      }
     }
     t2tr::reduce_heads<<<static_cast<unsigned>(model_count), static_cast<unsigned>(heads * 8), 0, st>>>(t);
     mark("train_backward_matrix");

@@ -512,6 +512,91 @@ __global__ void __launch_bounds__(256) bwd_attention(Tr t, int h, float* hcta, i
   }
 }
 
+// The same attention backward with the per-cell terms prepared once per CTA in
+// shared memory (6 x cells floats), 512 threads per CTA:
+//   s_kv[j] = (key_j, value_j)
+//   s_q[i]  = (query_i, max_i, d_att_i * out_scale / denominator_i, wavg_i)
+// so that both O(cells^2) loops read one broadcast vector per step and spend
+// one exponential, three multiply-adds and a subtraction on it:
+//   d_query_c = s_q[c].z * sum_j e^(q_c k_j - max_c) (v_j - wavg_c) k_j
+//   for key c: sum_v = sum_i s_q[i].z e^(q_i k_c - max_i)
+//              sum_k = sum_i s_q[i].z e^(q_i k_c - max_i) (v_c - wavg_i) q_i
+// and the value / key weight terms are sum_v, sum_k times (cell value, 1).
+__global__ void __launch_bounds__(512) bwd_attention_smem(Tr t, int h, float* hcta) {
+  extern __shared__ float4 smq[];
+  const int cells = t.L.cells;
+  __shared__ float s_red[16][8];
+  const int s = blockIdx.y;
+  const int m = t.model[s];
+  const float* hw = t.w + static_cast<long long>(m) * t.L.total + t.L.attn + h * 7;
+  const float qs = hw[0], qb = hw[1], ks = hw[2], kb = hw[3], vs = hw[4], vb = hw[5], os = hw[6];
+  const float* mv = t.hist + hoff(t, s, t.L.mid);
+  const float* st = t.stats + (static_cast<long long>(s) * t.L.heads + h) * 3 * cells;
+  const float* ag = t.att_grad + static_cast<long long>(s) * cells;
+  float4* s_q = smq;
+  float2* s_kv = reinterpret_cast<float2*>(smq + cells);
+  for (int i = threadIdx.x; i < cells; i += blockDim.x) {
+    const float v = mv[i];
+    s_kv[i] = make_float2(v * ks + kb, v * vs + vb);
+    s_q[i] = make_float4(v * qs + qb, st[i], ag[i] * os * st[cells + i], st[2 * cells + i]);
+  }
+  __syncthreads();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  float gq_s = 0.f, gq_b = 0.f, gk_s = 0.f, gk_b = 0.f, gv_s = 0.f, gv_b = 0.f, go = 0.f;
+  if (c < cells) {
+    const float cv = mv[c];
+    const float4 qc = s_q[c];
+    const float2 kvc = s_kv[c];
+    const float d_att_c = ag[c];
+    float input_g = 0.0f;
+    if (d_att_c != 0.0f) {
+      float a0 = 0.0f, a1 = 0.0f;
+      int j = 0;
+      for (; j + 1 < cells; j += 2) {
+        const float2 p0 = s_kv[j], p1 = s_kv[j + 1];
+        a0 += __expf(qc.x * p0.x - qc.y) * (p0.y - qc.w) * p0.x;
+        a1 += __expf(qc.x * p1.x - qc.y) * (p1.y - qc.w) * p1.x;
+      }
+      if (j < cells) {
+        const float2 p0 = s_kv[j];
+        a0 += __expf(qc.x * p0.x - qc.y) * (p0.y - qc.w) * p0.x;
+      }
+      const float d_query = qc.z * (a0 + a1);
+      go = d_att_c * qc.w;
+      gq_s = d_query * cv;
+      gq_b = d_query;
+      input_g += d_query * qs;
+    }
+    float sum_v = 0.0f, sum_k = 0.0f;
+    for (int i = 0; i < cells; ++i) {
+      const float4 y = s_q[i];
+      if (y.z == 0.0f) continue;  // the same i in every lane: a uniform branch
+      const float d = y.z * __expf(y.x * kvc.x - y.y);
+      sum_v += d;
+      sum_k += d * (kvc.y - y.w) * y.x;
+    }
+    gv_s = sum_v * cv;
+    gv_b = sum_v;
+    gk_s = sum_k * cv;
+    gk_b = sum_k;
+    input_g += sum_v * vs + sum_k * ks;
+    t.igrad[(static_cast<long long>(s) * t.L.heads + h) * cells + c] = input_g;
+  }
+  float v7[7] = {gq_s, gq_b, gk_s, gk_b, gv_s, gv_b, go};
+#pragma unroll
+  for (int k = 0; k < 7; ++k)
+    for (int o = 16; o > 0; o >>= 1) v7[k] += __shfl_xor_sync(0xffffffffu, v7[k], o);
+  if ((threadIdx.x & 31) == 0)
+#pragma unroll
+    for (int k = 0; k < 7; ++k) s_red[threadIdx.x >> 5][k] = v7[k];
+  __syncthreads();
+  if (threadIdx.x < 7) {
+    float r = 0.0f;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) r += s_red[i][threadIdx.x];
+    hcta[(static_cast<long long>(s) * gridDim.x + blockIdx.x) * 8 + threadIdx.x] = r;
+  }
+}
+
 // head-weight terms per sample (sum over the sample's CTAs in order) and the
 // mid-state gradient (sum over heads in order)
 __global__ void __launch_bounds__(256) sum_heads(Tr t, int h, const float* hcta, int ctas) {
