@@ -145,7 +145,7 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
  * (games x rows x 24) are DEVICE pointers, the call is enqueued on `stream`
  * (NULL: the legacy default stream) and returns without waiting.
  * Scratch is a fixed 1 MiB device array inside the library, held by every GPU
- * that loads it until exit: game_count * row_count^2 must be <= 262,080
+ * that loads it until exit: game_count * (row_count^2 + 1) must be <= 262,080
  * (63 requests at 64 rows), else BAD_ARGUMENT. The first call on a device
  * resolves the array's device address; make that first call before any stream
  * capture. All calls share the array: calls that overlap on the GPU (other

@@ -366,32 +366,275 @@ __device__ __forceinline__ float exp2_poly(float x) {
 }
 
 // 2. full scalar attention + attention FFN, CTA per request, in place on m.
-// Each of the THREADS threads owns QPT queries; per key, the last NPOLY of them
-// take their exponential from the FMA pipe (exp2_poly), the others from the
-// MUFU (ex2.approx), so the two pipes share the 4,096^2 exponentials of a request.
+//
+// The scores of a head are rank one: q_i k_j with q_i = m_i wq + bq and
+// k_j = m_j wk + bk, so softmax_j(q_i k_j) = softmax_j(a_i m_j) with
+// a_i = q_i wk, and the head's weighted value is
+//   wavg_i = wv E_i[m] + bv,   E_i[m] = sum_j m_j e^(a_i m_j) / sum_j e^(a_i m_j).
+// Two kernels compute it.
+//
+// 2a. t2_attention_moments (the usual path). With c, h the centre and
+// half-width of the request's cell values, x_j = (m_j - c) / h lies in
+// [-1, 1] and b_i = a_i h. The generating function of the modified Bessel
+// functions (Abramowitz & Stegun 9.6.34 with cos t = x) gives, for every real b,
+//   e^(b x) = I_0(b) + 2 sum_{k>=1} I_k(b) T_k(x)          (T_k: Chebyshev)
+// so with the request's Chebyshev moments mu_k = sum_j T_k(x_j) and
+// nu_k = sum_j x_j T_k(x_j) = (mu_{k+1} + mu_{|k-1|}) / 2,
+//   sum_j e^(b x_j)     = I_0 mu_0 + 2 sum_k I_k mu_k
+//   sum_j x_j e^(b x_j) = I_0 nu_0 + 2 sum_k I_k nu_k
+// and E_i[m] = c + h (second / first). The I_k(b_i) come from Miller's
+// backward recurrence I_{k-1} = I_{k+1} + (2k / b) I_k started at k = P with
+// arbitrary scale (the scale cancels in the ratio), in double precision.
+// The series is cut at P = ceil(8.5 sqrt(|b|max) + 7): over |b| in [1e-12, 1e3]
+// the dropped terms sum to at most 1e-16 of e^|b| (checked against tabulated
+// e^-|b| I_k(|b|)), and every term of the first sum is at most e^|b| while the
+// sum is at least e^|b| (a cell sits at each end of [-1, 1]), so the ratio is
+// good to double rounding, far below the f32 rounding of a direct sum. Work per
+// request and head: O(cells x P) for the moments and for the recurrences,
+// instead of cells^2 exponentials. A request whose |b|max exceeds
+// kMomentBetaMax on some head, or with more than 512 x 8 cells, is flagged for:
+//
+// 2b. t2_attention (direct): one pass over the keys in shared memory with the
+// exact closed-form row max of the rank-1 scores; each of the THREADS threads
+// owns QPT queries and, per key, the last NPOLY of them take their exponential
+// from the FMA pipe (exp2_poly), the others from the MUFU (ex2.approx). The
+// request's cell values are staged in shared memory first, so a grid of more
+// than QPT x THREADS cells (several query chunks) reads the attention's
+// inputs, not the outputs of an earlier chunk. Requests that 2a took return
+// at once.
 constexpr int kAttnThreads = 1024;
 constexpr int kAttnQpt = 4;
 constexpr int kAttnPoly = 1;
+constexpr int kMomThreads = 512;
+constexpr int kMomQpt = 8;
+constexpr int kMomentMax = 192;              // highest Chebyshev order used by the recurrence
+constexpr double kMomentBetaMax = 470.0;     // ceil(8.5 sqrt(470) + 7) = 192
+constexpr double kMomentBetaLinear = 1e-6;   // below: first order in b, relative error O(b^2)
 
+__device__ __forceinline__ int moment_order(double beta) {
+  const int p = static_cast<int>(ceil(8.5 * sqrt(beta) + 7.0));
+  return (p + 3) & ~3;  // a multiple of 4: the recurrence checks its scale every 4 steps
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// |b|max of a head: q is affine in m, so its largest magnitude sits at an end of [lo, hi]
+__device__ __forceinline__ double head_beta_max(const float* hw, float lo, float hi, double mh) {
+  const double qmax = fmax(fabs(static_cast<double>(fmaf(lo, hw[0], hw[1]))),
+                           fabs(static_cast<double>(fmaf(hi, hw[0], hw[1]))));
+  return qmax * fabs(static_cast<double>(hw[2])) * mh;
+}
+
+// E[m] for two queries from the moments (mu_k, nu_k), k = 0 .. P: Miller's
+// backward recurrence from k = P (z_{P+1} = 0, z_P = 1) for each query, the two
+// sums accumulated on the way down, rescaled together every four steps.
+__device__ __forceinline__ void moment_pair(const double2* __restrict__ s_mn, int P, float m0, float m1, float wq,
+                                            float bq, float wk, double mc, double mh, double& em0, double& em1) {
+  double bb[2], step[2], z[2], z1[2], sf[2], sp[2];
+  const float mq[2] = {m0, m1};
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    bb[i] = static_cast<double>(fmaf(mq[i], wq, bq)) * static_cast<double>(wk) * mh;
+    step[i] = fabs(bb[i]) >= kMomentBetaLinear ? 2.0 / bb[i] : 0.0;
+    z[i] = 1.0;
+    z1[i] = 0.0;
+    sf[i] = 0.0;
+    sp[i] = 0.0;
+  }
+  // k = P .. 1, four steps between scale checks (P is a multiple of 4)
+  for (int k = P; k > 0; k -= 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const double2 mn = s_mn[k - u];
+      const double kk = static_cast<double>(k - u);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        sf[i] = fma(z[i], mn.x, sf[i]);
+        sp[i] = fma(z[i], mn.y, sp[i]);
+        const double zn = fma(kk * step[i], z[i], z1[i]);
+        z1[i] = z[i];
+        z[i] = zn;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if (fabs(z[i]) > 1e180) {  // growth per step is at most 1 + 2P / 1e-6 < 4e8
+        z[i] *= 1e-180;
+        z1[i] *= 1e-180;
+        sf[i] *= 1e-180;
+        sp[i] *= 1e-180;
+      }
+    }
+  }
+  const double2 mn0 = s_mn[0];
+  const double mu1 = s_mn[1].x, mu2 = s_mn[2].x;
+  double em[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    double ratio;
+    if (!(fabs(bb[i]) >= kMomentBetaLinear)) {
+      // e^(b x) = 1 + b x + O(b^2): sum x e^(bx) / sum e^(bx) to first order (sum x^2 = (mu_0 + mu_2) / 2)
+      ratio = fma(bb[i], 0.5 * (mn0.x + mu2), mn0.y) / fma(bb[i], mu1, mn0.x);
+    } else {
+      ratio = fma(z[i], mn0.y, 2.0 * sp[i]) / fma(z[i], mn0.x, 2.0 * sf[i]);
+    }
+    em[i] = fma(mh, ratio, mc);
+  }
+  em0 = em[0];
+  em1 = em[1];
+}
+
+// 2a. CTA per request, THREADS threads of QPT cells each; direct[r] = 1 when
+// the request is left to 2b, 0 when it is done here.
+template <int THREADS, int QPT>
+__global__ void __launch_bounds__(THREADS) t2_attention_moments(const size_t* __restrict__ idx,
+                                                                const float* __restrict__ all_w, int models, T2Dev L,
+                                                                float* __restrict__ m, int* err,
+                                                                int* __restrict__ direct) {
+  constexpr int kWarps = THREADS / 32;
+  __shared__ float s_red[2][kWarps];
+  __shared__ double2 s_mn[kMomentMax + 2];  // (mu_k, nu_k)
+  __shared__ double s_part[kWarps][8];
+  const int r = blockIdx.x;
+  if (L.cells > THREADS * QPT) {
+    if (threadIdx.x == 0) direct[r] = 1;
+    return;
+  }
+  const float* w = model_of(all_w, idx, models, r, L.total, err);
+  const float* aw = w + L.attn;
+  float* mr = m + static_cast<long long>(r) * L.cells;
+  float mv[QPT];
+  float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < QPT; ++i) {
+    const int c = i * THREADS + threadIdx.x;
+    mv[i] = c < L.cells ? mr[c] : 0.0f;
+    if (c < L.cells) {
+      lo = fminf(lo, mv[i]);
+      hi = fmaxf(hi, mv[i]);
+    }
+  }
+  hi = ow::warp_max(hi);
+  lo = -ow::warp_max(-lo);
+  if ((threadIdx.x & 31) == 0) {
+    s_red[0][threadIdx.x >> 5] = hi;
+    s_red[1][threadIdx.x >> 5] = lo;
+  }
+  __syncthreads();
+  hi = s_red[0][0];
+  lo = s_red[1][0];
+  for (int i = 1; i < kWarps; ++i) {
+    hi = fmaxf(hi, s_red[0][i]);
+    lo = fminf(lo, s_red[1][i]);
+  }
+  // centre and half-width (exact in double: f32 sums and halves)
+  const double mc = 0.5 * (static_cast<double>(lo) + static_cast<double>(hi));
+  const double mh = 0.5 * (static_cast<double>(hi) - static_cast<double>(lo));
+  bool take = true;  // the same in every thread
+  for (int h = 0; h < L.heads; ++h) take = take && head_beta_max(aw + h * kHeadWeights, lo, hi, mh) <= kMomentBetaMax;
+  if (threadIdx.x == 0) direct[r] = take ? 0 : 1;
+  if (!take) return;
+  float ctx[QPT];
+#pragma unroll
+  for (int i = 0; i < QPT; ++i) ctx[i] = 0.0f;
+  for (int h = 0; h < L.heads; ++h) {
+    const float* hw = aw + h * kHeadWeights;
+    const float wq = hw[0], bq = hw[1], wk = hw[2], wv = hw[4], bv = hw[5], wo = hw[6];
+    float wavg[QPT];
+    if (!(mh > 0.0)) {
+      // one cell value: every weight is equal, E[m] = that value
+#pragma unroll
+      for (int i = 0; i < QPT; ++i) wavg[i] = fmaf(lo, wv, bv);
+    } else {
+      const int P = moment_order(head_beta_max(hw, lo, hi, mh));  // mu_0 .. mu_{P+1}
+      const double inv_h = 1.0 / mh;
+      double x[QPT], tp[QPT], tc[QPT];
+#pragma unroll
+      for (int i = 0; i < QPT; ++i) {
+        const bool valid = i * THREADS + static_cast<int>(threadIdx.x) < L.cells;
+        x[i] = valid ? (static_cast<double>(mv[i]) - mc) * inv_h : 0.0;
+        tp[i] = x[i];               // T_{-1} = T_1
+        tc[i] = valid ? 1.0 : 0.0;  // T_0 (0 for a padding slot: its T_k stay 0)
+      }
+      __syncthreads();  // the previous head is done with s_mn and s_part
+      for (int kb = 0; kb <= P + 1; kb += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          double sum = 0.0;
+#pragma unroll
+          for (int i = 0; i < QPT; ++i) {
+            sum += tc[i];
+            const double tn = fma(2.0 * x[i], tc[i], -tp[i]);
+            tp[i] = tc[i];
+            tc[i] = tn;
+          }
+          sum = warp_sum_d(sum);
+          if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5][u] = sum;
+        }
+        __syncthreads();
+        if (threadIdx.x < 8 && kb + static_cast<int>(threadIdx.x) <= P + 1) {
+          double mu = 0.0;
+          for (int wi = 0; wi < kWarps; ++wi) mu += s_part[wi][threadIdx.x];
+          s_mn[kb + threadIdx.x].x = mu;
+        }
+        __syncthreads();
+      }
+      for (int k = threadIdx.x; k <= P; k += THREADS) s_mn[k].y = k == 0 ? s_mn[1].x : 0.5 * (s_mn[k + 1].x + s_mn[k - 1].x);
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < QPT; i += 2) {
+        double e0, e1;
+        moment_pair(s_mn, P, mv[i], mv[i + 1], wq, bq, wk, mc, mh, e0, e1);
+        wavg[i] = static_cast<float>(fma(e0, static_cast<double>(wv), static_cast<double>(bv)));
+        wavg[i + 1] = static_cast<float>(fma(e1, static_cast<double>(wv), static_cast<double>(bv)));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < QPT; ++i) ctx[i] = fmaf(wavg[i], wo, ctx[i]);
+  }
+  // attention FFN; each thread rewrites only the cells it read
+  const float* s = aw + L.heads * kHeadWeights;
+#pragma unroll
+  for (int i = 0; i < QPT; ++i) {
+    const int c = i * THREADS + threadIdx.x;
+    if (c < L.cells) {
+      const float rr = fmaf(mv[i], s[0], ctx[i] + s[1]);
+      const float hid = tanhf(fmaf(rr, s[2], s[3]));
+      mr[c] = tanhf(fmaf(hid, s[4], rr + s[5]));
+    }
+  }
+}
+
+// 2b. direct attention for the requests 2a flagged.
 template <int THREADS, int QPT, int NPOLY>
 __global__ void __launch_bounds__(THREADS) t2_attention(const size_t* __restrict__ idx,
                                                         const float* __restrict__ all_w, int models, T2Dev L,
-                                                        float* __restrict__ m, int* err) {
+                                                        float* __restrict__ m, int* err,
+                                                        const int* __restrict__ direct) {
   constexpr int kAttnThreads = THREADS;
   constexpr int kQueriesPerThread = QPT;
-  extern __shared__ float2 s_kv[];  // [cells] (k * log2 e, v)
+  extern __shared__ float4 s_dyn[];
+  float2* s_kv = reinterpret_cast<float2*>(s_dyn);        // [cells] (k * log2 e, v)
+  float* s_m = reinterpret_cast<float*>(s_kv + L.cells);  // [cells] the attention's input
   __shared__ float s_red[2][32];
   const int r = blockIdx.x;
+  if (direct[r] == 0) return;
   const float* w = model_of(all_w, idx, models, r, L.total, err);
   const float* aw = w + L.attn;
   float* mr = m + static_cast<long long>(r) * L.cells;
   const float kLog2e = 1.4426950408889634f;
+  for (int c = threadIdx.x; c < L.cells; c += kAttnThreads) s_m[c] = mr[c];
   for (int base = 0; base < L.cells; base += kAttnThreads * kQueriesPerThread) {
     float mv[kQueriesPerThread], ctx[kQueriesPerThread];
+    __syncthreads();  // s_m staged
 #pragma unroll
     for (int i = 0; i < kQueriesPerThread; ++i) {
       const int c = base + i * kAttnThreads + threadIdx.x;
-      mv[i] = c < L.cells ? mr[c] : 0.0f;
+      mv[i] = c < L.cells ? s_m[c] : 0.0f;
       ctx[i] = 0.0f;
     }
     for (int h = 0; h < L.heads; ++h) {
@@ -400,7 +643,7 @@ __global__ void __launch_bounds__(THREADS) t2_attention(const size_t* __restrict
       __syncthreads();  // previous head / chunk done with s_kv
       float kmax = -INFINITY, kmin = INFINITY;
       for (int c = threadIdx.x; c < L.cells; c += kAttnThreads) {
-        const float cv = mr[c];
+        const float cv = s_m[c];
         const float k = fmaf(cv, wk, bk);
         s_kv[c] = make_float2(k * kLog2e, fmaf(cv, wv, bv));
         kmax = fmaxf(kmax, k);
@@ -443,7 +686,6 @@ __global__ void __launch_bounds__(THREADS) t2_attention(const size_t* __restrict
       for (int i = 0; i < kQueriesPerThread; ++i) ctx[i] = fmaf(acc[i] / den[i], wo, ctx[i]);
     }
     const float* s = aw + L.heads * kHeadWeights;
-    __syncthreads();  // every thread has read the keys of this chunk before m is overwritten
 #pragma unroll
     for (int i = 0; i < kQueriesPerThread; ++i) {
       const int c = base + i * kAttnThreads + threadIdx.x;
@@ -456,14 +698,18 @@ __global__ void __launch_bounds__(THREADS) t2_attention(const size_t* __restrict
   }
 }
 
-// Launches t2_attention for `n` requests.
+// Launches the attention for `n` requests: 2a over every request, then 2b,
+// whose CTAs return at once for the requests 2a took. direct: n ints of scratch.
 cudaError_t launch_t2_attention(const size_t* idx, const float* all_w, int models, const T2Dev& D, float* m, int* err,
-                                unsigned n, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(D.cells) * sizeof(float2);
-  auto k = t2_attention<kAttnThreads, kAttnQpt, kAttnPoly>;
-  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+                                int* direct, unsigned n, cudaStream_t stream) {
+  t2_attention_moments<kMomThreads, kMomQpt><<<n, kMomThreads, 0, stream>>>(idx, all_w, models, D, m, err, direct);
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  k<<<n, kAttnThreads, smem, stream>>>(idx, all_w, models, D, m, err);
+  const size_t smem = static_cast<size_t>(D.cells) * (sizeof(float2) + sizeof(float));
+  auto k = t2_attention<kAttnThreads, kAttnQpt, kAttnPoly>;
+  e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  k<<<n, kAttnThreads, smem, stream>>>(idx, all_w, models, D, m, err, direct);
   return cudaGetLastError();
 }
 
@@ -618,8 +864,9 @@ __global__ void copy_kernel(const float4* __restrict__ in, float4* __restrict__ 
 // ---------------------------------------------------------------- allocation-free forward
 // Scratch of orbit_wars_cuda_true2d_forward_noalloc: a fixed device array
 // every GPU that loads this library holds until exit (1 MiB). The first 256
-// bytes hold the error word; the rest holds the per-request cell matrices
-// (game_count * rows^2 floats at most kNoAllocCells).
+// bytes hold the error word; the rest holds the per-request cell matrices and
+// one path flag per request for the attention (game_count * (rows^2 + 1)
+// floats at most kNoAllocCells).
 constexpr size_t kNoAllocFloats = size_t(1) << 18;
 constexpr size_t kNoAllocHeaderFloats = 64;
 constexpr size_t kNoAllocCells = kNoAllocFloats - kNoAllocHeaderFloats;  // 262,080 cells
@@ -910,7 +1157,7 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   const size_t in_n = n * L.rows * kFeatures, out_n = n * L.rows * kOutPerRow, m_n = n * L.cells;
   if (input_rows != nullptr) T2_TRY(ensure(W.in, W.in_cap, in_n));
   T2_TRY(ensure(W.out, W.out_cap, out_n));
-  T2_TRY(ensure(W.m, W.m_cap, m_n));
+  T2_TRY(ensure(W.m, W.m_cap, m_n + n));  // cell matrices, then the attention's per-request path flags
   T2_TRY(ensure(W.idx, W.idx_cap, n));
   if (input_rows != nullptr) {
     T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
@@ -956,7 +1203,8 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   t2_expand_pre_g<<<g1, 256, 0, W.stream>>>(W.in, W.groups, W.weights, models, D, W.m, W.err);
   T2_TRY(cudaGetLastError());
   mark("t2_attention");
-  T2_TRY(launch_t2_attention(didx, W.weights, models, D, W.m, W.err, static_cast<unsigned>(n), W.stream));
+  T2_TRY(launch_t2_attention(didx, W.weights, models, D, W.m, W.err, reinterpret_cast<int*>(W.m + m_n),
+                                  static_cast<unsigned>(n), W.stream));
   const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n_groups));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   mark("t2_post_collapse");
@@ -1495,7 +1743,7 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_upload_population(const float* all_we
   const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
   T2_TRY(ensure(W.in, W.in_cap, request_capacity * L.rows * kFeatures));
   T2_TRY(ensure(W.out, W.out_cap, request_capacity * L.rows * kOutPerRow));
-  T2_TRY(ensure(W.m, W.m_cap, request_capacity * L.cells));
+  T2_TRY(ensure(W.m, W.m_cap, request_capacity * (L.cells + 1)));
   T2_TRY(ensure(W.idx, W.idx_cap, request_capacity));
   W.request_capacity = request_capacity;
   return from_cuda(cudaStreamSynchronize(W.stream));
@@ -1668,8 +1916,8 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(const float* input_ro
     return bad("invalid true2d buffer");
   if (!shape_ok(shape)) return bad("invalid true2d shape");
   const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
-  if (game_count > kNoAllocCells / L.cells)
-    return bad("game_count x row_count^2 exceeds the allocation-free scratch (262080 cells)");
+  if (game_count > kNoAllocCells / (L.cells + 1))
+    return bad("game_count x (row_count^2 + 1) exceeds the allocation-free scratch (262080 floats)");
   int dev = 0;
   T2_TRY(cudaGetDevice(&dev));
   float* scratch = nullptr;
@@ -1683,7 +1931,8 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(const float* input_ro
   const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(game_count));
   t2_expand_pre<false><<<g1, 256, 0, s>>>(input_rows, nullptr, weights, 1, D, m, err);
   T2_TRY(cudaGetLastError());
-  T2_TRY(launch_t2_attention(nullptr, weights, 1, D, m, err, static_cast<unsigned>(game_count), s));
+  T2_TRY(launch_t2_attention(nullptr, weights, 1, D, m, err, reinterpret_cast<int*>(m + game_count * L.cells),
+                                  static_cast<unsigned>(game_count), s));
   const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(game_count));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   t2_post_collapse<false><<<g3, threads3, 0, s>>>(nullptr, weights, 1, D, m, output_rows, err);

@@ -68,6 +68,65 @@ def test_heads_and_rows_variants(oracle):
         assert np.abs(out - ref).max() <= GATE, (layers, rows, heads)
 
 
+def attn_offset(layers, rows):
+    """Offset of the attention weights in the True2D weight vector (true2d_model.rs:111-126): input_pair[14],
+    src_emb[rows], tgt_emb[rows], pair_emb[rows^2], expand_bias[1], matrix[layers x rows^2 x 12]."""
+    return 14 + 2 * rows + rows * rows + 1 + layers * rows * rows * 12
+
+
+def test_attention_paths_match_oracle(oracle):
+    """One batch whose requests take the Chebyshev-moment attention (|b|max from about 1e-8 to a few
+    hundred) and the direct attention (|b|max beyond 470), against the oracle's direct f32 softmax."""
+    layers, rows, heads = 4, 64, 2
+    shape = ow.True2DShape(layers, rows, heads)
+    per = shape.parameter_count()
+    rng = np.random.default_rng(7)
+    base = (rng.standard_normal(per) * 0.3).astype(np.float32)
+    a0 = attn_offset(layers, rows)
+    scales = (1e-4, 0.3, 2.0, 6.0, 14.0, 60.0)  # wq, bq, wk of each head: |b|max ~ 2 scale^2 h
+    pop = []
+    for sc in scales:
+        w = base.copy()
+        for h in range(heads):
+            w[a0 + 7 * h:a0 + 7 * h + 3] = sc * rng.uniform(0.5, 1.0, 3) * rng.choice([-1.0, 1.0], 3)
+        pop.append(w)
+    pop = np.concatenate(pop)
+    n = 2 * len(scales)
+    x = rng.uniform(-1, 1, (n, rows, 7)).astype(np.float32)
+    idx = (np.arange(n) % len(scales)).astype(np.uintp)
+    ref = oracle.true2d_forward(x, pop, model_indices=idx, layers=layers, rows=rows, heads=heads)
+    out = ow.CudaTrue2D().forward_population_packed(x, idx, pop, shape).reshape(-1)
+    err = np.abs(out - ref).reshape(n, -1).max(axis=1)
+    assert np.all(np.isfinite(out))
+    assert err.max() <= GATE, err
+
+
+def test_rows_beyond_one_query_chunk(oracle):
+    """More cells than one CTA's 4,096 queries (80 and 128 rows): the direct attention runs several query
+    chunks, all over keys staged before any chunk writes its outputs."""
+    rng = np.random.default_rng(11)
+    for layers, rows, heads in ((3, 80, 1), (2, 128, 2)):
+        shape = ow.True2DShape(layers, rows, heads)
+        w = (rng.standard_normal(shape.parameter_count()) * 0.3).astype(np.float32)
+        x = rng.uniform(-1, 1, size=(2, rows, 7)).astype(np.float32)
+        ref = oracle.true2d_forward(x, w, layers=layers, rows=rows, heads=heads)
+        out = ow.CudaTrue2D().forward_packed(x, w, 2, shape).reshape(-1)
+        assert np.abs(out - ref).max() <= GATE, (layers, rows, heads)
+
+
+def test_constant_mid_state(oracle):
+    """Zero expand and matrix weights leave every cell at 0: one cell value, so every softmax weight is equal."""
+    shape = ow.True2DShape(3, 16, 2)
+    rng = np.random.default_rng(3)
+    w = np.zeros(shape.parameter_count(), np.float32)
+    a0 = attn_offset(3, 16)
+    w[a0:] = rng.standard_normal(w.size - a0).astype(np.float32) * 0.5
+    x = rng.uniform(-1, 1, size=(2, 16, 7)).astype(np.float32)
+    ref = oracle.true2d_forward(x, w, layers=3, rows=16, heads=2)
+    out = ow.CudaTrue2D().forward_packed(x, w, 2, shape).reshape(-1)
+    assert np.abs(out - ref).max() <= 1e-6
+
+
 def test_resident_errors():
     lib = _lib.load_library()
     x = np.zeros(64 * 7, np.float32)

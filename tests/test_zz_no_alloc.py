@@ -52,7 +52,7 @@ def test_noalloc_matches_allocating_entry_point_two_calls():
 
 def test_noalloc_rejects_work_beyond_the_scratch():
     lib = _lib.load_library()
-    games = 64  # 64 x 64^2 = 262,144 cells > 262,080
+    games = 64  # 64 x (64^2 + 1) = 262,208 floats > 262,080
     x = torch.zeros(games * 64 * 7, device="cuda")
     w = torch.zeros(SHAPE.parameter_count(), device="cuda")
     out = torch.zeros(games * 64 * 24, device="cuda")
