@@ -137,14 +137,50 @@ __device__ __forceinline__ void load_cell_weights(const float* __restrict__ w12,
   }
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// tanh for the matrix layers, written from tanh|x| = 2 / (1 + e^(-2|x|)) - 1
+// with one ex2.approx and one rcp.approx (two MUFU operations). For |x| < 1/4,
+// where that form loses relative accuracy to cancellation, the Taylor series
+// x - x^3/3 + 2x^5/15 - 17x^7/315 + 62x^9/2835 - 1382x^11/155925 (the next
+// term is below 6e-11 there). Absolute error a few 1e-7 at most.
+__device__ __forceinline__ float tanh_cell(float x) {
+  const float kLog2e = 1.4426950408889634f;
+  const float ax = fabsf(x);
+  const float x2 = x * x;
+  float p = fmaf(x2, -1382.0f / 155925.0f, 62.0f / 2835.0f);
+  p = fmaf(p, x2, -17.0f / 315.0f);
+  p = fmaf(p, x2, 2.0f / 15.0f);
+  p = fmaf(p, x2, -1.0f / 3.0f);
+  p = fmaf(p * x2, x, x);
+  const float e = ex2_approx(ax * (-2.0f * kLog2e));
+  const float big = copysignf(fmaf(2.0f, rcp_approx(1.0f + e), -1.0f), x);
+  return ax < 0.25f ? p : big;
+}
+
+// logistic sigmoid 1 / (1 + e^-z) for the matrix layers' gate: one ex2.approx and one rcp.approx
+__device__ __forceinline__ float sigmoid_cell(float z) {
+  return rcp_approx(1.0f + ex2_approx(z * -1.4426950408889634f));
+}
+
 // a = (w0,w1,w2,w3) b = (w4,w5,w6,w7) c = (w8,w9,w10,w11)
 __device__ __forceinline__ float matrix_cell_w(float v, const float4 a, const float4 b, const float4 c) {
-  const float ha = tanhf(fmaf(v, a.z, a.w));
-  const float hb = tanhf(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
-  const float g = sigmoid_f(fmaf(v, b.w, c.x));
+  const float ha = tanh_cell(fmaf(v, a.z, a.w));
+  const float hb = tanh_cell(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
+  const float g = sigmoid_cell(fmaf(v, b.w, c.x));
   const float u = fmaf(hb, c.y, fmaf(ha, c.z, c.w));
   const float r = fmaf(v, 1.0f + a.x, a.y);
-  return tanhf(fmaf(g, u, r));
+  return tanh_cell(fmaf(g, u, r));
 }
 
 template <bool VEC>
@@ -190,10 +226,55 @@ __global__ void __launch_bounds__(256) t2_expand_pre(const float* __restrict__ x
   m[static_cast<long long>(r) * L.cells + cell] = v;
 }
 
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
+// ---- collapse (true2d_model.rs:546-647) of one (row, action) by one thread
+// Row stride of the collapse's shared arrays: one float of padding so that
+// lanes reading the same column t of different rows hit different banks.
+constexpr int kRowStride = kMaxRows + 1;
+
+// Stages target_bias and send_bias of a model, times log2 e, into
+// s_bias[2][kTargets][kRowStride] (callers synchronise before reading).
+__device__ __forceinline__ void stage_collapse_bias(const float* __restrict__ w, const T2Dev& L, float* s_bias) {
+  const float kLog2e = 1.4426950408889634f;
+  for (int i = threadIdx.x; i < 2 * static_cast<int>(kTargets) * L.rows; i += blockDim.x) {
+    const int which = i / (static_cast<int>(kTargets) * L.rows), rest = i % (static_cast<int>(kTargets) * L.rows);
+    const int a = rest / L.rows, t = rest % L.rows;
+    const float b = which == 0 ? w[L.tbias + rest] : w[L.sbias + rest];
+    s_bias[(which * kTargets + a) * kRowStride + t] = b * kLog2e;
+  }
+}
+
+// Action a of one row (row values mrow[0..rows), shared memory): the target
+// softmax over rows of m_t * s0 + tb[a][t] gives the expected target index
+// / (rows - 1), clamped to [0, 1] (frac); the send softmax of m_t * s1 + sb[a][t]
+// weights the row values, and sigmoid((weighted * s2 + s4) * s3) is the send
+// fraction before the row's normalisation (send). Scores are formed in log2
+// units (biases staged times log2 e, one FMA each), so each exponential is one
+// ex2.approx; a pass for the two maxima, then one for the four sums.
+__device__ __forceinline__ void collapse_item(const float* mrow, const float* s_bias, int a, int rows,
+                                              const float* __restrict__ sc, float& frac, float& send) {
+  const float kLog2e = 1.4426950408889634f;
+  const float* tb = s_bias + a * kRowStride;
+  const float* sb = s_bias + (kTargets + a) * kRowStride;
+  const float s0 = sc[0] * kLog2e, s1 = sc[1] * kLog2e;
+  float tmax = -INFINITY, smax = -INFINITY;
+  for (int t = 0; t < rows; ++t) {
+    const float v = mrow[t];
+    tmax = fmaxf(tmax, fmaf(v, s0, tb[t]));
+    smax = fmaxf(smax, fmaf(v, s1, sb[t]));
+  }
+  float tden = 0.0f, tnum = 0.0f, sden = 0.0f, snum = 0.0f;
+  for (int t = 0; t < rows; ++t) {
+    const float v = mrow[t];
+    const float et = ex2_approx(fmaf(v, s0, tb[t]) - tmax);
+    tden += et;
+    tnum = fmaf(et, static_cast<float>(t), tnum);
+    const float es = ex2_approx(fmaf(v, s1, sb[t]) - smax);
+    sden += es;
+    snum = fmaf(es, v, snum);
+  }
+  frac = fminf(fmaxf(tnum / (tden * static_cast<float>(rows - 1)), 0.0f), 1.0f);
+  const float logit = fmaf(snum / sden, sc[2], sc[4]);
+  send = sigmoid_f(logit * sc[3]);
 }
 
 // ---- grouped matrix layers: requests of one model processed together
@@ -258,7 +339,8 @@ __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict_
                                                           const float* __restrict__ m, float* __restrict__ out,
                                                           int* err) {
   constexpr int kRows = 4;  // rows of each request per CTA
-  __shared__ float s_m[kGroup][kRows][kMaxRows];
+  __shared__ float s_m[kGroup][kRows][kRowStride];
+  __shared__ float s_bias[2][kTargets][kRowStride];  // target and send biases x log2 e
   __shared__ float s_send[kGroup][kRows][kTargets];
   const int* gr = groups + static_cast<long long>(blockIdx.y) * (kGroup + 1);
   const int row0 = blockIdx.x * kRows;
@@ -272,6 +354,7 @@ __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict_
   for (int i = 0; i < kGroup; ++i) req[i] = gr[1 + i];
   const float* w = all_w + static_cast<long long>(model) * L.total;
   const long long per_layer = static_cast<long long>(L.cells) * kCellWeights;
+  stage_collapse_bias(w, L, &s_bias[0][0][0]);
   for (int i = threadIdx.x; i < kRows * L.rows; i += blockDim.x) {
     const int lr = i / L.rows, t = i % L.rows;
     const int row = row0 + lr;
@@ -292,56 +375,28 @@ __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict_
     for (int g = 0; g < kGroup; ++g) s_m[g][lr][t] = v[g];
   }
   __syncthreads();
-  // warp per (request, row, action): target softmax -> expected index; send softmax -> sigmoid
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  for (int item = warp; item < kGroup * kRows * static_cast<int>(kTargets); item += nwarps) {
+  // thread per (request, row, action)
+  for (int item = threadIdx.x; item < kGroup * kRows * static_cast<int>(kTargets); item += blockDim.x) {
     const int g = item / (kRows * static_cast<int>(kTargets));
     const int rest = item % (kRows * static_cast<int>(kTargets));
     const int lr = rest / kTargets, a = rest % kTargets;
     const int row = row0 + lr;
-    if (row >= L.rows || req[g] < 0) continue;
-    const float* sc = w + L.scalars + a * kOutScalars;
-    const float* tb = w + L.tbias + static_cast<long long>(a) * L.rows;
-    const float* sb = w + L.sbias + static_cast<long long>(a) * L.rows;
-    const float s0 = sc[0], s1 = sc[1];
-    float tmax = -INFINITY, smax = -INFINITY;
-    for (int t = lane; t < L.rows; t += 32) {
-      tmax = fmaxf(tmax, fmaf(s_m[g][lr][t], s0, tb[t]));
-      smax = fmaxf(smax, fmaf(s_m[g][lr][t], s1, sb[t]));
-    }
-    tmax = ow::warp_max(tmax);
-    smax = ow::warp_max(smax);
-    float tden = 0.0f, tnum = 0.0f, sden = 0.0f, snum = 0.0f;
-    const float inv_last = 1.0f / static_cast<float>(L.rows - 1);
-    for (int t = lane; t < L.rows; t += 32) {
-      const float v = s_m[g][lr][t];
-      const float et = expf(fmaf(v, s0, tb[t]) - tmax);
-      tden += et;
-      tnum = fmaf(et, static_cast<float>(t) * inv_last, tnum);
-      const float es = expf(fmaf(v, s1, sb[t]) - smax);
-      sden += es;
-      snum = fmaf(es, v, snum);
-    }
-    tden = ow::warp_sum(tden);
-    tnum = ow::warp_sum(tnum);
-    sden = ow::warp_sum(sden);
-    snum = ow::warp_sum(snum);
-    if (lane == 0) {
-      const float frac = fminf(fmaxf(tnum / tden, 0.0f), 1.0f);
-      const float logit = fmaf(snum / sden, sc[2], sc[4]);
-      s_send[g][lr][a] = sigmoid_f(logit * sc[3]);
-      out[(static_cast<long long>(req[g]) * L.rows + row) * kOutPerRow + a * 2] = frac;
-    }
+    const int rq = gr[1 + g];  // the group table, not req[]: a runtime index would put req[] in local memory
+    if (row >= L.rows || rq < 0) continue;
+    float frac;
+    collapse_item(s_m[g][lr], &s_bias[0][0][0], a, L.rows, w + L.scalars + a * kOutScalars, frac, s_send[g][lr][a]);
+    out[(static_cast<long long>(rq) * L.rows + row) * kOutPerRow + a * 2] = frac;
   }
   __syncthreads();
   if (threadIdx.x < kGroup * kRows) {
     const int g = threadIdx.x / kRows, lr = threadIdx.x % kRows, row = row0 + lr;
-    if (row < L.rows && req[g] >= 0) {
+    const int rq = gr[1 + g];
+    if (row < L.rows && rq >= 0) {
       float sum = 0.0f;
       for (int a = 0; a < static_cast<int>(kTargets); ++a) sum += s_send[g][lr][a];
       const float norm = sum > 1.0f ? 1.0f / sum : 1.0f;
       for (int a = 0; a < static_cast<int>(kTargets); ++a)
-        out[(static_cast<long long>(req[g]) * L.rows + row) * kOutPerRow + a * 2 + 1] = s_send[g][lr][a] * norm;
+        out[(static_cast<long long>(rq) * L.rows + row) * kOutPerRow + a * 2 + 1] = s_send[g][lr][a] * norm;
     }
   }
 }
@@ -720,12 +775,14 @@ template <bool VEC>
 __global__ void __launch_bounds__(512) t2_post_collapse(const size_t* __restrict__ idx, const float* __restrict__ all_w,
                                                         int models, T2Dev L, const float* __restrict__ m,
                                                         float* __restrict__ out, int* err) {
-  __shared__ float s_m[kRowsPerCta][kMaxRows];
+  __shared__ float s_m[kRowsPerCta][kRowStride];
+  __shared__ float s_bias[2][kTargets][kRowStride];  // target and send biases x log2 e
   __shared__ float s_send[kRowsPerCta][kTargets];
   const int r = blockIdx.y;
   const int row0 = blockIdx.x * kRowsPerCta;
   const float* w = model_of(all_w, idx, models, r, L.total, err);
   const long long per_layer = static_cast<long long>(L.cells) * kCellWeights;
+  stage_collapse_bias(w, L, &s_bias[0][0][0]);
   for (int i = threadIdx.x; i < kRowsPerCta * L.rows; i += blockDim.x) {
     const int lr = i / L.rows, t = i % L.rows;
     const int row = row0 + lr;
@@ -737,44 +794,14 @@ __global__ void __launch_bounds__(512) t2_post_collapse(const size_t* __restrict
     s_m[lr][t] = v;
   }
   __syncthreads();
-  // warp per (row, action): target softmax -> expected index; send softmax -> sigmoid
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  for (int item = warp; item < kRowsPerCta * static_cast<int>(kTargets); item += nwarps) {
+  // thread per (row, action)
+  for (int item = threadIdx.x; item < kRowsPerCta * static_cast<int>(kTargets); item += blockDim.x) {
     const int lr = item / kTargets, a = item % kTargets;
     const int row = row0 + lr;
     if (row >= L.rows) continue;
-    const float* sc = w + L.scalars + a * kOutScalars;
-    const float* tb = w + L.tbias + static_cast<long long>(a) * L.rows;
-    const float* sb = w + L.sbias + static_cast<long long>(a) * L.rows;
-    const float s0 = sc[0], s1 = sc[1];
-    float tmax = -INFINITY, smax = -INFINITY;
-    for (int t = lane; t < L.rows; t += 32) {
-      tmax = fmaxf(tmax, fmaf(s_m[lr][t], s0, tb[t]));
-      smax = fmaxf(smax, fmaf(s_m[lr][t], s1, sb[t]));
-    }
-    tmax = ow::warp_max(tmax);
-    smax = ow::warp_max(smax);
-    float tden = 0.0f, tnum = 0.0f, sden = 0.0f, snum = 0.0f;
-    const float inv_last = 1.0f / static_cast<float>(L.rows - 1);
-    for (int t = lane; t < L.rows; t += 32) {
-      const float v = s_m[lr][t];
-      const float et = expf(fmaf(v, s0, tb[t]) - tmax);
-      tden += et;
-      tnum = fmaf(et, static_cast<float>(t) * inv_last, tnum);
-      const float es = expf(fmaf(v, s1, sb[t]) - smax);
-      sden += es;
-      snum = fmaf(es, v, snum);
-    }
-    tden = ow::warp_sum(tden);
-    tnum = ow::warp_sum(tnum);
-    sden = ow::warp_sum(sden);
-    snum = ow::warp_sum(snum);
-    if (lane == 0) {
-      const float frac = fminf(fmaxf(tnum / tden, 0.0f), 1.0f);
-      const float logit = fmaf(snum / sden, sc[2], sc[4]);
-      s_send[lr][a] = sigmoid_f(logit * sc[3]);
-      out[(static_cast<long long>(r) * L.rows + row) * kOutPerRow + a * 2] = frac;
-    }
+    float frac;
+    collapse_item(s_m[lr], &s_bias[0][0][0], a, L.rows, w + L.scalars + a * kOutScalars, frac, s_send[lr][a]);
+    out[(static_cast<long long>(r) * L.rows + row) * kOutPerRow + a * 2] = frac;
   }
   __syncthreads();
   if (threadIdx.x < kRowsPerCta) {
