@@ -26,6 +26,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <condition_variable>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -1031,6 +1032,9 @@ struct Workspace {
   size_t pin_in_cap = 0;
   unsigned char* pin_out = nullptr;
   size_t pin_out_cap = 0;
+  unsigned char* pin_meta = nullptr;  // model indices and the group table of a call
+  size_t pin_meta_cap = 0;
+  std::vector<cudaEvent_t> out_pieces;  // output download pieces (host-buffer forwards)
   // training step: one device arena and the pinned staging of the weights, kept between calls
   unsigned char* train_arena = nullptr;
   size_t train_cap = 0;
@@ -1126,23 +1130,83 @@ OrbitWarsCudaStatus upload(Workspace& W, const float* all_w, size_t models, cons
 }
 
 // memcpy split over up to 8 host threads (pageable <-> pinned staging).
-void par_copy(unsigned char* dst, const unsigned char* src, size_t bytes) {
-  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-  const size_t threads = std::min<size_t>({8, hw, std::max<size_t>(1, bytes >> 20)});
-  if (threads <= 1) {
-    std::memcpy(dst, src, bytes);
-    return;
+// Host copies between pinned staging and the caller's buffers, split over a
+// pool of worker threads started once (thread start-up would otherwise cost
+// more than a few-MB copy). One copy at a time: the pool's own mutex orders
+// callers. The pool is never destroyed; its idle workers end with the process.
+class CopyPool {
+ public:
+  static CopyPool& get() {
+    static CopyPool* pool = new CopyPool();
+    return *pool;
   }
-  const size_t per = (bytes + threads - 1) / threads;
-  std::vector<std::thread> pool;
-  for (size_t k = 1; k < threads; ++k) {
-    const size_t o = k * per;
-    if (o >= bytes) break;
-    pool.emplace_back([=] { std::memcpy(dst + o, src + o, std::min(per, bytes - o)); });
+  void copy(unsigned char* dst, const unsigned char* src, size_t bytes) {
+    const size_t parts = std::min<size_t>(workers_ + 1, std::max<size_t>(1, bytes >> 19));
+    if (parts <= 1) {
+      std::memcpy(dst, src, bytes);
+      return;
+    }
+    std::lock_guard<std::mutex> one(call_mu_);
+    const size_t per = ((bytes + parts - 1) / parts + 63) & ~size_t(63);
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      dst_ = dst;
+      src_ = src;
+      bytes_ = bytes;
+      per_ = per;
+      parts_ = parts;
+      pending_ = parts - 1;
+      ++generation_;
+    }
+    cv_.notify_all();
+    std::memcpy(dst, src, std::min(per, bytes));
+    std::unique_lock<std::mutex> lk(mu_);
+    done_.wait(lk, [&] { return pending_ == 0; });
   }
-  std::memcpy(dst, src, std::min(per, bytes));
-  for (auto& th : pool) th.join();
-}
+
+ private:
+  CopyPool() {
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    workers_ = std::min<size_t>(7, hw > 1 ? hw - 1 : 0);
+    for (size_t k = 1; k <= workers_; ++k) std::thread([this, k] { run(k); }).detach();
+  }
+  void run(size_t k) {
+    uint64_t seen = 0;
+    for (;;) {
+      unsigned char* dst;
+      const unsigned char* src;
+      size_t bytes, per, parts;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return generation_ != seen; });
+        seen = generation_;
+        dst = dst_;
+        src = src_;
+        bytes = bytes_;
+        per = per_;
+        parts = parts_;
+      }
+      if (k < parts) {
+        const size_t o = k * per;
+        if (o < bytes) std::memcpy(dst + o, src + o, std::min(per, bytes - o));
+        std::lock_guard<std::mutex> lk(mu_);
+        if (--pending_ == 0) done_.notify_one();
+      }
+    }
+  }
+  size_t workers_ = 0;
+  std::mutex call_mu_, mu_;
+  std::condition_variable cv_, done_;
+  uint64_t generation_ = 0;
+  unsigned char* dst_ = nullptr;
+  const unsigned char* src_ = nullptr;
+  size_t bytes_ = 0, per_ = 0, parts_ = 0, pending_ = 0;
+};
+
+void par_copy(unsigned char* dst, const unsigned char* src, size_t bytes) { CopyPool::get().copy(dst, src, bytes); }
+
+// Piece size for a staged transfer of `bytes`: four pieces, none under 512 KB.
+size_t copy_piece(size_t bytes) { return std::max<size_t>(size_t(512) << 10, ((bytes + 3) / 4 + 4095) & ~size_t(4095)); }
 
 cudaError_t ensure_pinned(unsigned char*& p, size_t& cap, size_t bytes) {
   if (bytes <= cap && p != nullptr) return cudaSuccess;
@@ -1186,19 +1250,14 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   T2_TRY(ensure(W.out, W.out_cap, out_n));
   T2_TRY(ensure(W.m, W.m_cap, m_n + n));  // cell matrices, then the attention's per-request path flags
   T2_TRY(ensure(W.idx, W.idx_cap, n));
-  if (input_rows != nullptr) {
-    T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
-    // host rows go through pinned memory: host threads copy, then one DMA (the
-    // previous call's copies are done: every host-buffer call ends synchronised)
-    T2_TRY(ensure_pinned(W.pin_in, W.pin_in_cap, in_n * sizeof(float)));
-    par_copy(W.pin_in, reinterpret_cast<const unsigned char*>(input_rows), in_n * sizeof(float));
-    T2_TRY(cudaMemcpyAsync(W.in, W.pin_in, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
-  }
-  const size_t* didx = nullptr;
-  if (model_indices != nullptr) {
-    T2_TRY(cudaMemcpyAsync(W.idx, model_indices, n * sizeof(size_t), cudaMemcpyHostToDevice, W.stream));
-    didx = W.idx;
-  }
+  // device timing (profile_begin / profile_end): copies and kernels, one phase each
+  const bool prof = W.prof_on && W.prof_used + 9 <= W.prof_events.size();
+  auto mark = [&](const char* name) {
+    if (prof) {
+      cudaEventRecord(W.prof_events[W.prof_used], W.stream);
+      W.prof_names[W.prof_used++] = name;
+    }
+  };
   const int models = static_cast<int>(W.models);
   // group the requests by model (counting sort; host-validated indices), kGroup per group
   std::vector<int>& gt = W.host_groups;
@@ -1217,14 +1276,34 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   }
   const size_t n_groups = gt.size() / (kGroup + 1);
   T2_TRY(ensure(W.groups, W.groups_cap, gt.size()));
-  T2_TRY(cudaMemcpyAsync(W.groups, gt.data(), gt.size() * sizeof(int), cudaMemcpyHostToDevice, W.stream));
-  const bool prof = W.prof_on && W.prof_used + (dec != nullptr ? 6 : 4) <= W.prof_events.size();
-  auto mark = [&](const char* name) {
-    if (prof) {
-      cudaEventRecord(W.prof_events[W.prof_used], W.stream);
-      W.prof_names[W.prof_used++] = name;
+  // model indices and the group table go up from pinned memory too (a pageable
+  // source would make each copy wait on the host); the previous call's copies
+  // are done: every call that uses this staging ends synchronised
+  const size_t idx_bytes = model_indices != nullptr ? n * sizeof(size_t) : 0, gt_bytes = gt.size() * sizeof(int);
+  T2_TRY(ensure_pinned(W.pin_meta, W.pin_meta_cap, idx_bytes + gt_bytes));
+  if (idx_bytes) std::memcpy(W.pin_meta, model_indices, idx_bytes);
+  std::memcpy(W.pin_meta + idx_bytes, gt.data(), gt_bytes);
+  mark("copy_rows_h2d");
+  if (input_rows != nullptr) {
+    T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
+    // host rows go through pinned memory in pieces: host threads copy piece k + 1
+    // while piece k's DMA runs
+    const size_t bytes = in_n * sizeof(float);
+    T2_TRY(ensure_pinned(W.pin_in, W.pin_in_cap, bytes));
+    const size_t piece = copy_piece(bytes);
+    for (size_t o = 0; o < bytes; o += piece) {
+      const size_t b = std::min(piece, bytes - o);
+      par_copy(W.pin_in + o, reinterpret_cast<const unsigned char*>(input_rows) + o, b);
+      T2_TRY(cudaMemcpyAsync(reinterpret_cast<unsigned char*>(W.in) + o, W.pin_in + o, b, cudaMemcpyHostToDevice,
+                             W.stream));
     }
-  };
+  }
+  const size_t* didx = nullptr;
+  if (model_indices != nullptr) {
+    T2_TRY(cudaMemcpyAsync(W.idx, W.pin_meta, idx_bytes, cudaMemcpyHostToDevice, W.stream));
+    didx = W.idx;
+  }
+  T2_TRY(cudaMemcpyAsync(W.groups, W.pin_meta + idx_bytes, gt_bytes, cudaMemcpyHostToDevice, W.stream));
   const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(n_groups));
   mark("t2_expand_pre");
   t2_expand_pre_g<<<g1, 256, 0, W.stream>>>(W.in, W.groups, W.weights, models, D, W.m, W.err);
@@ -1259,15 +1338,32 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
       T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
     return ok();
   }
-  // outputs through pinned memory: one DMA, then host threads copy once the stream is done
+  // outputs through pinned memory in pieces, an event after each piece's DMA:
+  // host threads copy piece k out while piece k + 1 downloads
   if (output_rows != nullptr) {
-    T2_TRY(ensure_pinned(W.pin_out, W.pin_out_cap, out_n * sizeof(float)));
-    T2_TRY(cudaMemcpyAsync(W.pin_out, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
+    const size_t bytes = out_n * sizeof(float);
+    T2_TRY(ensure_pinned(W.pin_out, W.pin_out_cap, bytes));
+    const size_t piece = copy_piece(bytes), pieces = (bytes + piece - 1) / piece;
+    while (W.out_pieces.size() < pieces) {
+      cudaEvent_t ev;
+      T2_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+      W.out_pieces.push_back(ev);
+    }
+    mark("copy_out_d2h");
+    for (size_t k = 0; k < pieces; ++k) {
+      const size_t o = k * piece;
+      T2_TRY(cudaMemcpyAsync(W.pin_out + o, reinterpret_cast<const unsigned char*>(W.out) + o,
+                             std::min(piece, bytes - o), cudaMemcpyDeviceToHost, W.stream));
+      T2_TRY(cudaEventRecord(W.out_pieces[k], W.stream));
+    }
+    mark(nullptr);
+    for (size_t k = 0; k < pieces; ++k) {
+      T2_TRY(cudaEventSynchronize(W.out_pieces[k]));
+      const size_t o = k * piece;
+      par_copy(reinterpret_cast<unsigned char*>(output_rows) + o, W.pin_out + o, std::min(piece, bytes - o));
+    }
   }
-  const OrbitWarsCudaStatus st = finish(W);
-  if (output_rows != nullptr && st.code == kOk)
-    par_copy(reinterpret_cast<unsigned char*>(output_rows), W.pin_out, out_n * sizeof(float));
-  return st;
+  return finish(W);
 }
 
 // ---------------------------------------------------------------- device encoder, host side
@@ -1970,7 +2066,7 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_profile_begin(int32_t max_calls) {
   if (max_calls <= 0 || max_calls > 100000) return bad("max_calls must be in [1, 100000]");
   Workspace& W = ws();
   std::lock_guard<std::mutex> lock(W.mu);
-  const size_t need = static_cast<size_t>(max_calls) * 8;  // encode, three forward kernels, decode
+  const size_t need = static_cast<size_t>(max_calls) * 12;  // encode, copies, forward kernels, decode
   while (W.prof_events.size() < need) {
     cudaEvent_t ev;
     T2_TRY(cudaEventCreate(&ev));
