@@ -2,22 +2,24 @@
 // (include/orbit_wars_cuda.h): the True2D self-play policy forward, the
 // legacy TrainableTransformer forward and the identity copy.
 //
-// True2D forward per request (true2d_model.rs:197-283), three kernels:
+// True2D forward per request (true2d_model.rs:197-283), three stages:
 //   1. t2_expand_pre:  thread per (request, cell): expand (true2d_model.rs:321-366)
 //                      then the pre-attention matrix layers (:419-461) with the
 //                      cell value held in a register; weights of request r's
 //                      model streamed from L2/HBM (12 floats per layer per cell,
-//                      three 16-byte loads).
-//   2. t2_attention:   CTA per request: full scalar self-attention over all
-//                      cells (:463-544). Keys/values of the request sit in shared
-//                      memory; the row max is closed-form because scores are
-//                      rank-1 (max_j q*k_j = q*kmax for q >= 0, q*kmin otherwise),
-//                      so softmax and weighted sum take ONE pass over the keys
-//                      (the reference takes two). A quarter of the exponentials
-//                      run as a polynomial on the FMA pipe, the rest on the
-//                      MUFU. Attention FFN fused.
+//                      three 16-byte loads); tanh and sigmoid as one ex2.approx
+//                      and one rcp.approx each.
+//   2. attention (:463-544), CTA per request, attention FFN fused:
+//      t2_attention_moments: the scores are rank one, so each query's softmax-
+//                      weighted mean of the cell values follows from the
+//                      request's Chebyshev moments and the query's modified
+//                      Bessel values (O(cells x P) instead of cells^2 exponentials);
+//      t2_attention:   one pass over keys in shared memory with the exact
+//                      closed-form row max, for the requests the first kernel
+//                      leaves (very large attention weights, over 4,096 cells).
 //   3. t2_post_collapse: CTA per 4 rows of a request: post-attention matrix layers,
-//                      then the 12-action collapse (:546-647) from shared memory.
+//                      then the 12-action collapse (:546-647), a thread per
+//                      (row, action), from shared memory.
 // The model population stays resident in HBM between calls (upload_population);
 // all buffers live in one process-global workspace like the reference's
 // (orbit_wars_cuda.cu:421-441), guarded by a mutex.
