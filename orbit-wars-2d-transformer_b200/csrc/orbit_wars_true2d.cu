@@ -171,6 +171,14 @@ __device__ __forceinline__ float tanh_cell(float x) {
   return ax < 0.25f ? p : big;
 }
 
+// The same form without the series: absolute error a few 1e-7 everywhere, but
+// relative error unbounded as x -> 0. Used for the two hidden activations of a
+// matrix layer, which reach the cell value only through weighted sums.
+__device__ __forceinline__ float tanh_cell_abs(float x) {
+  const float e = ex2_approx(fabsf(x) * (-2.0f * 1.4426950408889634f));
+  return copysignf(fmaf(2.0f, rcp_approx(1.0f + e), -1.0f), x);
+}
+
 // logistic sigmoid 1 / (1 + e^-z) for the matrix layers' gate: one ex2.approx and one rcp.approx
 __device__ __forceinline__ float sigmoid_cell(float z) {
   return rcp_approx(1.0f + ex2_approx(z * -1.4426950408889634f));
@@ -178,8 +186,8 @@ __device__ __forceinline__ float sigmoid_cell(float z) {
 
 // a = (w0,w1,w2,w3) b = (w4,w5,w6,w7) c = (w8,w9,w10,w11)
 __device__ __forceinline__ float matrix_cell_w(float v, const float4 a, const float4 b, const float4 c) {
-  const float ha = tanh_cell(fmaf(v, a.z, a.w));
-  const float hb = tanh_cell(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
+  const float ha = tanh_cell_abs(fmaf(v, a.z, a.w));
+  const float hb = tanh_cell_abs(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
   const float g = sigmoid_cell(fmaf(v, b.w, c.x));
   const float u = fmaf(hb, c.y, fmaf(ha, c.z, c.w));
   const float r = fmaf(v, 1.0f + a.x, a.y);
