@@ -171,12 +171,19 @@ __device__ __forceinline__ float tanh_cell(float x) {
   return ax < 0.25f ? p : big;
 }
 
-// The same form without the series: absolute error a few 1e-7 everywhere, but
-// relative error unbounded as x -> 0. Used for the two hidden activations of a
-// matrix layer, which reach the cell value only through weighted sums.
+// The same form without the series, and with the reciprocal of d = 1 + e^(-2|x|)
+// in [1, 2] on the FMA pipe: a quadratic fitted here by least squares for
+// relative error on [1, 2] (1.2%), then two Newton steps y += y (1 - d y)
+// (1.1e-7). One MUFU operation instead of two. Absolute error a few 1e-7
+// everywhere, but relative error unbounded as x -> 0. Used for the two hidden
+// activations of a matrix layer, which reach the cell value only through
+// weighted sums.
 __device__ __forceinline__ float tanh_cell_abs(float x) {
-  const float e = ex2_approx(fabsf(x) * (-2.0f * 1.4426950408889634f));
-  return copysignf(fmaf(2.0f, rcp_approx(1.0f + e), -1.0f), x);
+  const float d = 1.0f + ex2_approx(fabsf(x) * (-2.0f * 1.4426950408889634f));
+  float y = fmaf(fmaf(0.31368835f, d, -1.4250640f), d, 2.0995536f);
+  y = fmaf(y, fmaf(-d, y, 1.0f), y);
+  y = fmaf(y, fmaf(-d, y, 1.0f), y);
+  return copysignf(fmaf(2.0f, y, -1.0f), x);
 }
 
 // logistic sigmoid 1 / (1 + e^-z) for the matrix layers' gate: one ex2.approx and one rcp.approx
