@@ -33,6 +33,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <pthread.h>
 #include <thread>
 #include <vector>
 
@@ -1151,6 +1152,8 @@ OrbitWarsCudaStatus upload(Workspace& W, const float* all_w, size_t models, cons
 // pool of worker threads started once (thread start-up would otherwise cost
 // more than a few-MB copy). One copy at a time: the pool's own mutex orders
 // callers. The pool is never destroyed; its idle workers end with the process.
+// A child process forked after the pool started has no workers (and may hold
+// a copy of a locked mutex): there every copy runs on the calling thread.
 class CopyPool {
  public:
   static CopyPool& get() {
@@ -1159,7 +1162,7 @@ class CopyPool {
   }
   void copy(unsigned char* dst, const unsigned char* src, size_t bytes) {
     const size_t parts = std::min<size_t>(workers_ + 1, std::max<size_t>(1, bytes >> 19));
-    if (parts <= 1) {
+    if (parts <= 1 || forked_) {
       std::memcpy(dst, src, bytes);
       return;
     }
@@ -1186,6 +1189,7 @@ class CopyPool {
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
     workers_ = std::min<size_t>(7, hw > 1 ? hw - 1 : 0);
     for (size_t k = 1; k <= workers_; ++k) std::thread([this, k] { run(k); }).detach();
+    pthread_atfork(nullptr, nullptr, [] { forked_ = true; });
   }
   void run(size_t k) {
     uint64_t seen = 0;
@@ -1218,6 +1222,7 @@ class CopyPool {
   unsigned char* dst_ = nullptr;
   const unsigned char* src_ = nullptr;
   size_t bytes_ = 0, per_ = 0, parts_ = 0, pending_ = 0;
+  static inline volatile bool forked_ = false;
 };
 
 void par_copy(unsigned char* dst, const unsigned char* src, size_t bytes) { CopyPool::get().copy(dst, src, bytes); }
