@@ -482,15 +482,14 @@ def true2d_workload_name(args, shape) -> str:
 
 
 def true2d_mufu_per_request(shape, part: str) -> float:
-    """MUFU operations per request in a matrix-layer kernel: 6 per cell per layer (the cell's tanh and the
-    gate's sigmoid take one ex2.approx and one rcp.approx each, the two hidden tanh one ex2.approx each,
-    their reciprocals on the FMA pipe); the post-attention kernel adds the collapse's two exponentials per
-    (row, action, target)."""
+    """MUFU operations per request in a matrix-layer kernel: 5 per cell per layer (one ex2.approx for each
+    of the three tanh, their reciprocals on the FMA pipe; ex2.approx and rcp.approx for the gate's sigmoid);
+    the post-attention kernel adds the collapse's two exponentials per (row, action, target)."""
     cells = shape.rows * shape.rows
     mid = shape.layers // 2
     if part == "pre":
-        return 6.0 * cells * mid
-    return 6.0 * cells * (shape.layers - mid) + 2.0 * shape.rows * 12 * shape.rows
+        return 5.0 * cells * mid
+    return 5.0 * cells * (shape.layers - mid) + 2.0 * shape.rows * 12 * shape.rows
 
 
 def true2d_cpu_reference(args, shape, pop, per, x, target_s: float) -> dict | None:
@@ -780,9 +779,8 @@ def run_true2d(args) -> None:
                 "unit": "G MUFU ops/s", "frac": round(ach / peak, 4), "traffic": None,
                 "peak_source": f"computed: 16 MUFU ops/clk/SM x {props.multi_processor_count} SMs x {mhz:.0f} MHz "
                                "(median sampled SM clock); not a measured peak",
-                "work_per_launch": f"{mufu[top]:.0f} MUFU ops per request: 6 per cell per matrix layer (ex2 "
-                                   "and rcp for the cell's tanh and the gate's sigmoid, ex2 for the two hidden "
-                                   "tanh)"
+                "work_per_launch": f"{mufu[top]:.0f} MUFU ops per request: 5 per cell per matrix layer (ex2 "
+                                   "for each of the three tanh, ex2 and rcp for the gate's sigmoid)"
                                    + (" plus two ex2 per (row, action, target) of the collapse" if top ==
                                       "t2_post_collapse" else "")}
     ref_gpu = None

@@ -7,8 +7,9 @@
 //                      then the pre-attention matrix layers (:419-461) with the
 //                      cell value held in a register; weights of request r's
 //                      model streamed from L2/HBM (12 floats per layer per cell,
-//                      three 16-byte loads); tanh and sigmoid as one ex2.approx
-//                      and one rcp.approx each.
+//                      three 16-byte loads); tanh as one ex2.approx with the
+//                      reciprocal on the FMA pipe, the gate's sigmoid as one
+//                      ex2.approx and one rcp.approx.
 //   2. attention (:463-544), CTA per request, attention FFN fused:
 //      t2_attention_moments: the scores are rank one, so each query's softmax-
 //                      weighted mean of the cell values follows from the
@@ -153,33 +154,16 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// tanh for the matrix layers, written from tanh|x| = 2 / (1 + e^(-2|x|)) - 1
-// with one ex2.approx and one rcp.approx (two MUFU operations). For |x| < 1/4,
-// where that form loses relative accuracy to cancellation, the Taylor series
-// x - x^3/3 + 2x^5/15 - 17x^7/315 + 62x^9/2835 - 1382x^11/155925 (the next
-// term is below 6e-11 there). Absolute error a few 1e-7 at most.
+// tanh for the matrix layers, written from tanh|x| = 2 / (1 + e^(-2|x|)) - 1:
+// one ex2.approx, and the reciprocal of d = 1 + e^(-2|x|) in [1, 2] on the FMA
+// pipe, a quadratic fitted here by least squares for relative error on [1, 2]
+// (1.2%) and then two Newton steps y += y (1 - d y) (1.1e-7). Absolute error a
+// few 1e-7 everywhere; relative error grows as x -> 0 (the form cancels), which
+// the matrix layers tolerate: their tanh values enter weighted sums and the
+// next layer's affine maps, where absolute error is what carries. A Taylor
+// branch for |x| < 1/4 on the cell's own tanh measured 5% slower and left the
+// outputs where they were (3.3e-7 from the reference build).
 __device__ __forceinline__ float tanh_cell(float x) {
-  const float kLog2e = 1.4426950408889634f;
-  const float ax = fabsf(x);
-  const float x2 = x * x;
-  float p = fmaf(x2, -1382.0f / 155925.0f, 62.0f / 2835.0f);
-  p = fmaf(p, x2, -17.0f / 315.0f);
-  p = fmaf(p, x2, 2.0f / 15.0f);
-  p = fmaf(p, x2, -1.0f / 3.0f);
-  p = fmaf(p * x2, x, x);
-  const float e = ex2_approx(ax * (-2.0f * kLog2e));
-  const float big = copysignf(fmaf(2.0f, rcp_approx(1.0f + e), -1.0f), x);
-  return ax < 0.25f ? p : big;
-}
-
-// The same form without the series, and with the reciprocal of d = 1 + e^(-2|x|)
-// in [1, 2] on the FMA pipe: a quadratic fitted here by least squares for
-// relative error on [1, 2] (1.2%), then two Newton steps y += y (1 - d y)
-// (1.1e-7). One MUFU operation instead of two. Absolute error a few 1e-7
-// everywhere, but relative error unbounded as x -> 0. Used for the two hidden
-// activations of a matrix layer, which reach the cell value only through
-// weighted sums.
-__device__ __forceinline__ float tanh_cell_abs(float x) {
   const float d = 1.0f + ex2_approx(fabsf(x) * (-2.0f * 1.4426950408889634f));
   float y = fmaf(fmaf(0.31368835f, d, -1.4250640f), d, 2.0995536f);
   y = fmaf(y, fmaf(-d, y, 1.0f), y);
@@ -194,8 +178,8 @@ __device__ __forceinline__ float sigmoid_cell(float z) {
 
 // a = (w0,w1,w2,w3) b = (w4,w5,w6,w7) c = (w8,w9,w10,w11)
 __device__ __forceinline__ float matrix_cell_w(float v, const float4 a, const float4 b, const float4 c) {
-  const float ha = tanh_cell_abs(fmaf(v, a.z, a.w));
-  const float hb = tanh_cell_abs(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
+  const float ha = tanh_cell(fmaf(v, a.z, a.w));
+  const float hb = tanh_cell(fmaf(v, b.x, fmaf(ha, b.y, b.z)));
   const float g = sigmoid_cell(fmaf(v, b.w, c.x));
   const float u = fmaf(hb, c.y, fmaf(ha, c.z, c.w));
   const float r = fmaf(v, 1.0f + a.x, a.y);
