@@ -179,20 +179,24 @@ __global__ void __launch_bounds__(256) layernorm_f32_kernel(const float* __restr
 enum F32Epi : int { kF32Bias = 0, kF32BiasGelu = 1, kF32BiasResid = 2 };
 
 // C[m, n] = A[m, :] . W[n, :] + bias[n]  (+GELU | += into C), fp32 SIMT.
-// 64x64 tile, 256 threads x (4x4), K step 16. Rows >= *m_valid are skipped.
-template <int EPI>
+// TILE x TILE output tile (64: 4x4 per thread, 32: 2x2 per thread), 256
+// threads, K step 16; the small tile gives small batches four times the CTAs.
+// Each output sums its K products in ascending order either way, so both tiles
+// give the same bits. Rows >= *m_valid are skipped.
+template <int EPI, int TILE = 64>
 __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A, const float* __restrict__ W,
                                                        const float* __restrict__ bias, float* __restrict__ C,
                                                        const int* __restrict__ m_valid, int n, int k) {
-  __shared__ float As[16][64 + 4];
-  __shared__ float Ws[16][64 + 4];
+  constexpr int kPer = TILE / 16;  // outputs per thread along each axis
+  __shared__ float As[16][TILE + 4];
+  __shared__ float Ws[16][TILE + 4];
   const int rows = *m_valid;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const int m0 = blockIdx.y * TILE, n0 = blockIdx.x * TILE;
   if (m0 >= rows) return;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  float acc[4][4] = {};
+  float acc[kPer][kPer] = {};
   for (int k0 = 0; k0 < k; k0 += 16) {
-    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+    for (int i = threadIdx.x; i < TILE * 16; i += 256) {
       const int r = i / 16, kk = i % 16;
       const int gm = m0 + r, gn = n0 + r, gk = k0 + kk;
       As[kk][r] = (gm < rows && gk < k) ? A[static_cast<size_t>(gm) * k + gk] : 0.0f;
@@ -201,26 +205,26 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
     __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < 16; ++kk) {
-      float a[4], w[4];
+      float a[kPer], w[kPer];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a[i] = As[kk][ty * 4 + i];
-        w[i] = Ws[kk][tx * 4 + i];
+      for (int i = 0; i < kPer; ++i) {
+        a[i] = As[kk][ty * kPer + i];
+        w[i] = Ws[kk][tx * kPer + i];
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < kPer; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
+        for (int j = 0; j < kPer; ++j) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int gm = m0 + ty * 4 + i;
+  for (int i = 0; i < kPer; ++i) {
+    const int gm = m0 + ty * kPer + i;
     if (gm >= rows) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int gn = n0 + tx * 4 + j;
+    for (int j = 0; j < kPer; ++j) {
+      const int gn = n0 + tx * kPer + j;
       if (gn >= n) continue;
       float v = acc[i][j] + bias[gn];
       float* c = C + static_cast<size_t>(gm) * n + gn;
@@ -232,12 +236,17 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 }
 
 // Masked attention, fp32, one CTA per (state, head), head_dim 32.
-// qkv: [rows, 3d]; out: [rows, d]. Scores of one state live in shared memory.
+// qkv: [rows, 3d]; out: [rows, d]. Keys and values of one state live in shared
+// memory (row pitch 33: lanes reading different rows at one column hit
+// different banks). A warp takes one query at a time: lane j forms score j as
+// a 32-term dot product from shared memory (no shuffles), then a warp max and
+// sum for the softmax, and lane c the output column c.
 template <int NMAX>
 __global__ void __launch_bounds__(128) attention_f32_kernel(const float* __restrict__ qkv, float* __restrict__ out,
                                                             const int* __restrict__ offsets, int d, float scale) {
   __shared__ float sk[NMAX][33];
   __shared__ float sv[NMAX][33];
+  __shared__ float sq[4][32];
   __shared__ float sp[4][NMAX];
   const int b = blockIdx.x, h = blockIdx.y;
   const int row0 = offsets[b];
@@ -252,14 +261,18 @@ __global__ void __launch_bounds__(128) attention_f32_kernel(const float* __restr
   __syncthreads();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   for (int i = w; i < cnt; i += 4) {
-    const float q = qkv[static_cast<size_t>(row0 + i) * ld + h * 32 + lane];
+    sq[w][lane] = qkv[static_cast<size_t>(row0 + i) * ld + h * 32 + lane];
+    __syncwarp();
     float mx = -INFINITY;
-    for (int j = 0; j < cnt; ++j) {
-      const float s = warp_sum(q * sk[j][lane]) * scale;
-      if (lane == 0) sp[w][j] = s;
+    for (int j = lane; j < cnt; j += 32) {
+      float s = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) s = fmaf(sq[w][c], sk[j][c], s);
+      s *= scale;
+      sp[w][j] = s;
       mx = fmaxf(mx, s);
     }
-    __syncwarp();
+    mx = warp_max(mx);
     float den = 0.0f;
     for (int j = lane; j < cnt; j += 32) {
       const float e = expf(sp[w][j] - mx);

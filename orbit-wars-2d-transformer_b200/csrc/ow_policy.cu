@@ -623,7 +623,12 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
   const int d = c.d_model, f = c.ffn;
   if (c.precision == OW_PRECISION_F32) {
     const dim3 blk(256);
-    auto grid_for = [&](int n) { return dim3((n + 63) / 64, static_cast<unsigned>((P.cap_rows + 63) / 64)); };
+    // 32 x 32 tiles when 64 x 64 ones would not give every SM two CTAs (small batches)
+    const bool small = static_cast<long long>((P.cap_rows + 63) / 64) * ((d + 63) / 64) < 2LL * P.num_sms;
+    auto grid_for = [&](int n) {
+      const int t = small ? 32 : 64;
+      return dim3((n + t - 1) / t, static_cast<unsigned>((P.cap_rows + t - 1) / t));
+    };
     float* x = static_cast<float*>(P.x);
     float* ln = static_cast<float*>(P.ln);
     float* qkv = static_cast<float*>(P.qkv);
@@ -631,18 +636,18 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
     float* h = static_cast<float*>(P.h);
     for (int l = 0; l < c.layers; ++l) {
       const auto& W = P.lw[l];
-      OW_STEP("gemm_f32_qkv", (gemm_f32_kernel<kF32Bias><<<grid_for(3 * d), blk, 0, P.stream>>>(
+      OW_STEP("gemm_f32_qkv", ((small ? gemm_f32_kernel<kF32Bias, 32> : gemm_f32_kernel<kF32Bias, 64>)<<<grid_for(3 * d), blk, 0, P.stream>>>(
                    ln, static_cast<const float*>(W.wqkv), W.bqkv, qkv, m_valid, 3 * d, d),
                cudaGetLastError()));
       OW_STEP("attention", launch_attention(P, batch));
-      OW_STEP("gemm_f32_out_resid", (gemm_f32_kernel<kF32BiasResid><<<grid_for(d), blk, 0, P.stream>>>(
+      OW_STEP("gemm_f32_out_resid", ((small ? gemm_f32_kernel<kF32BiasResid, 32> : gemm_f32_kernel<kF32BiasResid, 64>)<<<grid_for(d), blk, 0, P.stream>>>(
                    attn, static_cast<const float*>(W.wo), W.bo, x, m_valid, d, d),
                cudaGetLastError()));
       OW_STEP("layernorm_f32", dispatch_ln_f32(P, m_valid, W.ln2g, W.ln2b));
-      OW_STEP("gemm_f32_ffn_up", (gemm_f32_kernel<kF32BiasGelu><<<grid_for(f), blk, 0, P.stream>>>(
+      OW_STEP("gemm_f32_ffn_up", ((small ? gemm_f32_kernel<kF32BiasGelu, 32> : gemm_f32_kernel<kF32BiasGelu, 64>)<<<grid_for(f), blk, 0, P.stream>>>(
                    ln, static_cast<const float*>(W.w1), W.b1, h, m_valid, f, d),
                cudaGetLastError()));
-      OW_STEP("gemm_f32_ffn_down_resid", (gemm_f32_kernel<kF32BiasResid><<<grid_for(d), blk, 0, P.stream>>>(
+      OW_STEP("gemm_f32_ffn_down_resid", ((small ? gemm_f32_kernel<kF32BiasResid, 32> : gemm_f32_kernel<kF32BiasResid, 64>)<<<grid_for(d), blk, 0, P.stream>>>(
                    h, static_cast<const float*>(W.w2), W.b2, x, m_valid, d, f),
                cudaGetLastError()));
       const bool last = l + 1 == c.layers;
