@@ -179,32 +179,34 @@ __global__ void __launch_bounds__(256) layernorm_f32_kernel(const float* __restr
 enum F32Epi : int { kF32Bias = 0, kF32BiasGelu = 1, kF32BiasResid = 2 };
 
 // C[m, n] = A[m, :] . W[n, :] + bias[n]  (+GELU | += into C), fp32 SIMT.
-// TILE x TILE output tile (64: 4x4 per thread, 32: 2x2 per thread), 256
-// threads, K step 16; the small tile gives small batches four times the CTAs.
-// Each output sums its K products in ascending order either way, so both tiles
-// give the same bits. Rows >= *m_valid are skipped.
+// TILE x TILE output tile (64: 4x4 per thread, K step 16; 32: 2x2 per thread,
+// K step 64), 256 threads; the small tile gives small batches four times the
+// CTAs and a quarter of the K steps (each a load and two barriers). Each output
+// sums its K products in ascending order either way, so both tiles give the
+// same bits. Rows >= *m_valid are skipped.
 template <int EPI, int TILE = 64>
 __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A, const float* __restrict__ W,
                                                        const float* __restrict__ bias, float* __restrict__ C,
                                                        const int* __restrict__ m_valid, int n, int k) {
-  constexpr int kPer = TILE / 16;  // outputs per thread along each axis
-  __shared__ float As[16][TILE + 4];
-  __shared__ float Ws[16][TILE + 4];
+  constexpr int kPer = TILE / 16;           // outputs per thread along each axis
+  constexpr int kStep = TILE == 32 ? 64 : 16;
+  __shared__ float As[kStep][TILE + 4];
+  __shared__ float Ws[kStep][TILE + 4];
   const int rows = *m_valid;
   const int m0 = blockIdx.y * TILE, n0 = blockIdx.x * TILE;
   if (m0 >= rows) return;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   float acc[kPer][kPer] = {};
-  for (int k0 = 0; k0 < k; k0 += 16) {
-    for (int i = threadIdx.x; i < TILE * 16; i += 256) {
-      const int r = i / 16, kk = i % 16;
+  for (int k0 = 0; k0 < k; k0 += kStep) {
+    for (int i = threadIdx.x; i < TILE * kStep; i += 256) {
+      const int r = i / kStep, kk = i % kStep;
       const int gm = m0 + r, gn = n0 + r, gk = k0 + kk;
       As[kk][r] = (gm < rows && gk < k) ? A[static_cast<size_t>(gm) * k + gk] : 0.0f;
       Ws[kk][r] = (gn < n && gk < k) ? W[static_cast<size_t>(gn) * k + gk] : 0.0f;
     }
     __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
+#pragma unroll 16
+    for (int kk = 0; kk < kStep; ++kk) {
       float a[kPer], w[kPer];
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
