@@ -1030,8 +1030,6 @@ struct Workspace {
   size_t enc_err_cap = 0;
   std::vector<int32_t> host_err;
   // pinned staging of the host-buffer forward's input rows and output rows
-  unsigned char* pin_in = nullptr;
-  size_t pin_in_cap = 0;
   unsigned char* pin_out = nullptr;
   size_t pin_out_cap = 0;
   unsigned char* pin_meta = nullptr;  // model indices and the group table of a call
@@ -1292,17 +1290,11 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   mark("copy_rows_h2d");
   if (input_rows != nullptr) {
     T2_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), W.stream));
-    // host rows go through pinned memory in pieces: host threads copy piece k + 1
-    // while piece k's DMA runs
-    const size_t bytes = in_n * sizeof(float);
-    T2_TRY(ensure_pinned(W.pin_in, W.pin_in_cap, bytes));
-    const size_t piece = copy_piece(bytes);
-    for (size_t o = 0; o < bytes; o += piece) {
-      const size_t b = std::min(piece, bytes - o);
-      par_copy(W.pin_in + o, reinterpret_cast<const unsigned char*>(input_rows) + o, b);
-      T2_TRY(cudaMemcpyAsync(reinterpret_cast<unsigned char*>(W.in) + o, W.pin_in + o, b, cudaMemcpyHostToDevice,
-                             W.stream));
-    }
+    // host rows straight from the caller's (pageable) buffer: for the few MB of
+    // rows a call carries, the driver's own staging measured faster than host
+    // threads copying into pinned memory in pieces (129-139 against 155 us for
+    // 1,024 requests)
+    T2_TRY(cudaMemcpyAsync(W.in, input_rows, in_n * sizeof(float), cudaMemcpyHostToDevice, W.stream));
   }
   const size_t* didx = nullptr;
   if (model_indices != nullptr) {
