@@ -49,10 +49,11 @@ L2_FLUSH_BYTES = 256 << 20
 REFERENCE_RUN_S = 120.0  # CPU time budget of one --impl reference run
 
 
-def ncu_traffic(config: int, kernel: str):
+def ncu_traffic(config, kernel: str):
     """DRAM bytes per launch of `kernel` from the committed ncu capture of this
-    config (profiles/ncu_traffic_c<config>.json), or None."""
-    p = REPO / "profiles" / f"ncu_traffic_c{config}.json"
+    config (profiles/ncu_traffic_c<config>.json, or ncu_traffic_true2d.json for
+    config "true2d"), or None."""
+    p = REPO / "profiles" / (f"ncu_traffic_c{config}.json" if config != "true2d" else "ncu_traffic_true2d.json")
     if not p.exists():
         return None, None
     d = json.loads(p.read_text())
@@ -775,8 +776,10 @@ def run_true2d(args) -> None:
         ach = mufu[top] * args.requests / (a["avg_us"] * 1e-6) / 1e9
         mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
         peak = 16.0 * props.multi_processor_count * mhz * 1e6 / 1e9
+        traffic, traffic_src = ncu_traffic("true2d", top) if args.requests == 1024 and args.models == 64 else (None, None)
         roof = {"kernel": top, "bound": "mufu", "achieved": round(ach, 1), "peak": round(peak, 1),
-                "unit": "G MUFU ops/s", "frac": round(ach / peak, 4), "traffic": None,
+                "unit": "G MUFU ops/s", "frac": round(ach / peak, 4), "traffic": traffic,
+                "traffic_unit": "bytes per launch (dram read + write)", "traffic_source": traffic_src,
                 "peak_source": f"computed: 16 MUFU ops/clk/SM x {props.multi_processor_count} SMs x {mhz:.0f} MHz "
                                "(median sampled SM clock); not a measured peak",
                 "work_per_launch": f"{mufu[top]:.0f} MUFU ops per request: 5 per cell per matrix layer (ex2 "
