@@ -809,8 +809,9 @@ def run_true2d(args) -> None:
                        "l2": f"population of {args.models * per * 4 / 1e6:.0f} MB > 126 MB L2, read every step",
                        "parallelism": f"replicas x{world} (the reference ABI is single-device)",
                        "value_timing": "sum of the kernel phases' CUDA events per call (expand and matrix layers, "
-                                       "attention, matrix layers and collapse; row upload and output download "
-                                       "excluded)"},
+                                       "attention, matrix layers and collapse; the row upload excluded; the "
+                                       "collapse writes the outputs into mapped host memory as it runs, so its "
+                                       "time includes their transfer)"},
             "e2e": e2e, "gpu_launches": 4 * args.steps, "roofline": roof, "cpu_baseline": cpu,
             "reference_gpu": ref_gpu, "clocks": clocks, "kernels": kernels, "copies": copies, "turn": turn,
             "train": train,

@@ -345,6 +345,7 @@ __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict_
   __shared__ float s_m[kGroup][kRows][kRowStride];
   __shared__ float s_bias[2][kTargets][kRowStride];  // target and send biases x log2 e
   __shared__ float s_send[kGroup][kRows][kTargets];
+  __shared__ float s_frac[kGroup][kRows][kTargets];
   const int* gr = groups + static_cast<long long>(blockIdx.y) * (kGroup + 1);
   const int row0 = blockIdx.x * kRows;
   const int model = gr[0];
@@ -386,21 +387,28 @@ __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict_
     const int row = row0 + lr;
     const int rq = gr[1 + g];  // the group table, not req[]: a runtime index would put req[] in local memory
     if (row >= L.rows || rq < 0) continue;
-    float frac;
-    collapse_item(s_m[g][lr], &s_bias[0][0][0], a, L.rows, w + L.scalars + a * kOutScalars, frac, s_send[g][lr][a]);
-    out[(static_cast<long long>(rq) * L.rows + row) * kOutPerRow + a * 2] = frac;
+    collapse_item(s_m[g][lr], &s_bias[0][0][0], a, L.rows, w + L.scalars + a * kOutScalars, s_frac[g][lr][a],
+                  s_send[g][lr][a]);
   }
   __syncthreads();
+  // the row's send fractions normalised when they sum above 1
   if (threadIdx.x < kGroup * kRows) {
-    const int g = threadIdx.x / kRows, lr = threadIdx.x % kRows, row = row0 + lr;
+    const int g = threadIdx.x / kRows, lr = threadIdx.x % kRows;
+    float sum = 0.0f;
+    for (int a = 0; a < static_cast<int>(kTargets); ++a) sum += s_send[g][lr][a];
+    const float norm = sum > 1.0f ? 1.0f / sum : 1.0f;
+    for (int a = 0; a < static_cast<int>(kTargets); ++a) s_send[g][lr][a] *= norm;
+  }
+  __syncthreads();
+  // each (request, row) output is 24 contiguous floats: six 16-byte stores of (target, send) pairs
+  for (int item = threadIdx.x; item < kGroup * kRows * 6; item += blockDim.x) {
+    const int g = item / (kRows * 6), lr = (item / 6) % kRows, q = item % 6;
+    const int row = row0 + lr;
     const int rq = gr[1 + g];
-    if (row < L.rows && rq >= 0) {
-      float sum = 0.0f;
-      for (int a = 0; a < static_cast<int>(kTargets); ++a) sum += s_send[g][lr][a];
-      const float norm = sum > 1.0f ? 1.0f / sum : 1.0f;
-      for (int a = 0; a < static_cast<int>(kTargets); ++a)
-        out[(static_cast<long long>(rq) * L.rows + row) * kOutPerRow + a * 2 + 1] = s_send[g][lr][a] * norm;
-    }
+    if (row >= L.rows || rq < 0) continue;
+    const float4 v = make_float4(s_frac[g][lr][2 * q], s_send[g][lr][2 * q], s_frac[g][lr][2 * q + 1],
+                                 s_send[g][lr][2 * q + 1]);
+    reinterpret_cast<float4*>(out + (static_cast<long long>(rq) * L.rows + row) * kOutPerRow)[q] = v;
   }
 }
 
@@ -1032,6 +1040,8 @@ struct Workspace {
   // pinned staging of the host-buffer forward's input rows and output rows
   unsigned char* pin_out = nullptr;
   size_t pin_out_cap = 0;
+  unsigned char* pin_map = nullptr;  // mapped pinned outputs (synchronous host-buffer forwards)
+  size_t pin_map_cap = 0;
   unsigned char* pin_meta = nullptr;  // model indices and the group table of a call
   size_t pin_meta_cap = 0;
   std::vector<cudaEvent_t> out_pieces;  // output download pieces (host-buffer forwards)
@@ -1312,7 +1322,24 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   const dim3 g3((L.rows + kRowsPerCta - 1) / kRowsPerCta, static_cast<unsigned>(n_groups));
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   mark("t2_post_collapse");
-  t2_post_collapse_g<<<g3, threads3, 0, W.stream>>>(W.groups, W.weights, models, D, W.m, W.out, W.err);
+  // synchronous host-buffer forward without decode: the collapse writes the
+  // outputs over PCIe into mapped pinned memory while it runs
+  const bool mapped_out = output_rows != nullptr && dec == nullptr && sync;
+  float* out_target = W.out;
+  if (mapped_out) {
+    const size_t bytes = out_n * sizeof(float);
+    if (bytes > W.pin_map_cap || W.pin_map == nullptr) {
+      if (W.pin_map != nullptr) cudaFreeHost(W.pin_map);
+      W.pin_map = nullptr;
+      W.pin_map_cap = 0;
+      T2_TRY(cudaHostAlloc(reinterpret_cast<void**>(&W.pin_map), bytes, cudaHostAllocMapped));
+      W.pin_map_cap = bytes;
+    }
+    void* dp = nullptr;
+    T2_TRY(cudaHostGetDevicePointer(&dp, W.pin_map, 0));
+    out_target = static_cast<float*>(dp);
+  }
+  t2_post_collapse_g<<<g3, threads3, 0, W.stream>>>(W.groups, W.weights, models, D, W.m, out_target, W.err);
   T2_TRY(cudaGetLastError());
   mark(nullptr);
   if (dec != nullptr) {
@@ -1335,6 +1362,11 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
     if (output_rows != nullptr)
       T2_TRY(cudaMemcpyAsync(output_rows, W.out, out_n * sizeof(float), cudaMemcpyDeviceToHost, W.stream));
     return ok();
+  }
+  if (mapped_out) {
+    const OrbitWarsCudaStatus st = finish(W);
+    if (st.code == kOk) par_copy(reinterpret_cast<unsigned char*>(output_rows), W.pin_map, out_n * sizeof(float));
+    return st;
   }
   // outputs through pinned memory in pieces, an event after each piece's DMA:
   // host threads copy piece k out while piece k + 1 downloads
