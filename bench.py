@@ -242,7 +242,7 @@ def run_reference(args, cfg) -> None:
         "impl": "reference", "metric": METRIC.format(c=args.config), "value": value, "unit": UNIT,
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, SPEC.md section 7)",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded SplitMix/Box-Muller features, Xavier-uniform weights)",
         "config": {"workload": workload_name(cfg), "sample_states_per_step": n},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -439,7 +439,7 @@ def run_ours(args, cfg) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * t_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": {"f32": "f32", "bf16": "bf16", "fp8": "e4m3"}[cfg.precision],
-            "data": "synthetic (seeded SplitMix/Box-Muller, SPEC.md section 7)",
+            "data": "synthetic (seeded SplitMix/Box-Muller features, Xavier-uniform weights)",
             "config": {"workload": workload_name(cfg), "per_gpu_batch": B, "global_batch": B * world,
                        "valid_tokens_per_gpu": m_valid, "l2": "flushed between timed steps (256 MiB write)",
                        "parallelism": f"dp{world} (states sharded, weights broadcast once over NCCL)",

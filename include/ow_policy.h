@@ -4,7 +4,7 @@
  * features plus a per-state valid count, runs through an entity embedding,
  * L pre-LN encoder blocks (masked multi-head attention + GELU FFN), per-entity
  * policy logits, a mean-pooled value head and greedy or Gumbel-max actions.
- * The math and the weight-blob layout are frozen in SPEC.md.
+ * The math and the weight-blob layout are fixed; ow_policy_weight_count gives the blob size.
  *
  * Conventions follow the reference engine's GPU ABI
  * (native/cuda/orbit_wars_cuda.h:9-12, native/cuda/orbit_wars_cuda.cu:12-14):

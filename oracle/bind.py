@@ -4,7 +4,7 @@ TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
 bench.py's CPU-baseline leg, as the checker. The product library never
 loads it.
 
-    policy_forward(cfg, weights, features, counts, f64=True)  encoder policy (SPEC.md)
+    policy_forward(cfg, weights, features, counts, f64=True)  encoder policy (frozen spec)
     true2d_forward(...)                                        True2D (true2d_model.rs restatement)
     encode_batch(batch, request_games, request_players)        state encoder (encoder.rs restatement)
 """

@@ -7,8 +7,8 @@
 // PARITY UNPINNED BY THE REFERENCE: TryDotAtwo/Orbit-Wars-2D-Transformer has
 // no implementation of this network (no LayerNorm, GELU FFN, value head,
 // key-padding mask, FP8 or Gumbel sampling anywhere in it). The math is the
-// frozen spec in SPEC.md; an independent float64 numpy restatement
-// (tests/spec_numpy.py) cross-checks this file. Conventions that do exist in
+// frozen encoder-policy spec restated in this file; an independent float64
+// numpy restatement (tests/spec_numpy.py) cross-checks it. Conventions that do exist in
 // the reference are followed:
 //   - scaled, max-subtracted multi-head softmax attention:
 //     crates/orbit-wars-core/src/model.rs:247-288
@@ -52,7 +52,7 @@ struct Offsets {
   std::vector<Layer> layer;
 };
 
-// Weight-blob layout, SPEC.md section 3.
+// Weight-blob layout: the f32 tensors in the order make_offsets lists them.
 Offsets make_offsets(const OwoShape& s) {
   Offsets o;
   const size_t d = s.d_model, F = s.features, f = s.ffn, P = s.actions;

@@ -48,7 +48,7 @@ const char* device_error_message(int code) {
   }
 }
 
-// ---------------------------------------------------------------- weight layout (SPEC.md section 3)
+// ---------------------------------------------------------------- weight layout
 struct BlobLayout {
   size_t we, be, lnf_g, lnf_b, wp, bp, wv, bv, total;
   struct Layer {

@@ -1,4 +1,4 @@
-"""The five encoder-policy workloads (SPEC.md section 1) as host-side configs.
+"""The five encoder-policy workloads (configs C1-C5) as host-side configs.
 
 Mirrors ow_policy_preset() of the C ABI field for field; a test checks the two
 agree.

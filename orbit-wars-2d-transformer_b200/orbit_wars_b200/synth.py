@@ -1,4 +1,4 @@
-"""Seeded synthetic inputs and weights (SPEC.md section 7).
+"""Seeded synthetic inputs and weights.
 
 Random source: the reference's SplitMix-style mix
 (crates/orbit-wars-core/src/true2d_model.rs:653-663), keyed by
@@ -80,7 +80,7 @@ def make_inputs(cfg: PolicyConfig, batch: int | None = None, seed: int = DEFAULT
 
 
 def tensor_list(cfg: PolicyConfig) -> list[tuple[str, tuple[int, ...], str]]:
-    """(name, shape, kind) of every tensor of the weight blob, in order (SPEC.md section 3).
+    """(name, shape, kind) of every tensor of the weight blob, in order.
 
     kind: 'mat' (Xavier), 'bias', 'ln_g', 'ln_b'.
     """

@@ -1,5 +1,5 @@
-"""Second, independent float64 restatement of the encoder-policy spec (SPEC.md
-sections 3-5) in numpy, used to cross-check the C++ oracle. Test-only."""
+"""Second, independent float64 restatement of the encoder-policy spec (weight layout,
+forward, heads) in numpy, used to cross-check the C++ oracle. Test-only."""
 from __future__ import annotations
 
 import math

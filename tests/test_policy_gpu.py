@@ -1,6 +1,6 @@
 """GPU parity of the encoder-policy forward against the CPU oracle (float64 truth).
 
-Tolerances (SPEC.md section 8): fp32 rel <= 1e-4, bf16 <= 1e-2, fp8 <= 3e-2 on
+Tolerances: fp32 rel <= 1e-4, bf16 <= 1e-2, fp8 <= 3e-2 on
 logits and value; greedy argmax agreement >= 99.9% (ties within the
 precision's noise excluded); masks bit-exact.
 """

@@ -1,4 +1,4 @@
-"""Shared comparison helpers for parity tests (tolerances: SPEC.md section 8)."""
+"""Shared comparison helpers for parity tests (relative error max|a-b| / max|b|; gates fp32 1e-4, bf16 1e-2, fp8 3e-2)."""
 from __future__ import annotations
 
 import numpy as np
