@@ -67,6 +67,15 @@ def load():
     lib.owo_policy_forward.argtypes = [C.POINTER(OwoShape), C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
                                        C.c_int32, C.c_int, C.c_int, C.c_int, C.c_uint64,
                                        C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.owo_policy_forward_emulated.restype = C.c_int
+    lib.owo_policy_forward_emulated.argtypes = [C.POINTER(OwoShape), C.c_void_p, C.c_size_t, C.c_void_p,
+                                                C.c_void_p, C.c_int32, C.c_uint, C.c_int, C.c_void_p, C.c_void_p,
+                                                C.c_void_p]
+    lib.owo_gumbel_argmax.restype = C.c_int
+    lib.owo_gumbel_argmax.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_uint64,
+                                      C.c_uint32, C.c_int, C.c_void_p, C.c_void_p]
+    lib.owo_round_e4m3.restype = C.c_float
+    lib.owo_round_e4m3.argtypes = [C.c_float]
     lib.owo_gumbel.restype = C.c_double
     lib.owo_gumbel.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32]
     lib.owo_philox4x32_10.restype = None
@@ -119,6 +128,59 @@ def policy_forward(cfg, weights, features, counts, f64: bool = True, threads: in
     if rc != 0:
         raise ValueError(f"oracle rejected arguments (rc={rc})")
     return logits, value, actions
+
+
+# rounding points of owo_policy_forward_emulated (ow_policy_oracle.cpp)
+EMU_STORE_BF16, EMU_QUANT_QKV, EMU_QUANT_OUT, EMU_QUANT_UP, EMU_QUANT_DOWN, EMU_VALUE_BF16 = 1, 2, 4, 8, 16, 32
+EMU_QUANT_ALL = EMU_QUANT_QKV | EMU_QUANT_OUT | EMU_QUANT_UP | EMU_QUANT_DOWN
+
+
+def recipe_mode(cfg) -> int:
+    """The full rounding recipe of cfg's precision path (0 for fp32)."""
+    if cfg.precision == "f32":
+        return 0
+    if cfg.precision == "bf16":
+        return EMU_STORE_BF16
+    return EMU_STORE_BF16 | EMU_QUANT_ALL | EMU_VALUE_BF16
+
+
+def policy_forward_emulated(cfg, weights, features, counts, mode: int | None = None, threads: int = 0):
+    """Float64 forward with the precision recipe's rounding points (default: cfg's full recipe).
+    Returns (logits f32 [B,N,P], value f32 [B], greedy actions int32 [B,N])."""
+    lib = load()
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    f = np.ascontiguousarray(features, dtype=np.float32)
+    c = np.ascontiguousarray(counts, dtype=np.int32)
+    B = c.shape[0]
+    logits = np.zeros((B, cfg.n_entities, cfg.actions), dtype=np.float32)
+    value = np.zeros((B,), dtype=np.float32)
+    actions = np.zeros((B, cfg.n_entities), dtype=np.int32)
+    m = recipe_mode(cfg) if mode is None else int(mode)
+    sh = shape_of(cfg)
+    rc = lib.owo_policy_forward_emulated(C.byref(sh), w.ctypes.data, w.size, f.ctypes.data, c.ctypes.data, B, m,
+                                         threads, logits.ctypes.data, value.ctypes.data, actions.ctypes.data)
+    if rc != 0:
+        raise ValueError(f"oracle rejected arguments (rc={rc})")
+    return logits, value, actions
+
+
+def gumbel_argmax(logits, counts, seed: int, state_base: int = 0, threads: int = 0):
+    """Gumbel-max actions of the given logits [B,N,P] under the spec's Philox noise, and the top-two gap
+    per entity (inf for padded entities). Returns (actions int32 [B,N], gap f32 [B,N])."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    c = np.ascontiguousarray(counts, dtype=np.int32)
+    B, N, P = lg.shape
+    actions = np.zeros((B, N), np.int32)
+    gap = np.zeros((B, N), np.float32)
+    rc = load().owo_gumbel_argmax(lg.ctypes.data, c.ctypes.data, B, N, P, C.c_uint64(seed), state_base, threads,
+                                  actions.ctypes.data, gap.ctypes.data)
+    if rc != 0:
+        raise ValueError(f"oracle rejected arguments (rc={rc})")
+    return actions, gap
+
+
+def round_e4m3(v: float) -> float:
+    return float(load().owo_round_e4m3(v))
 
 
 def policy_weight_count(cfg) -> int:

@@ -16,9 +16,13 @@
 //     crates/orbit-wars-trainer/src/cuda_true2d.rs:469-487
 //   - status codes 0/1/2: native/cuda/orbit_wars_cuda.cu:12-14
 //
-// Two numeric modes: T = double is the "truth" used for parity; T = float is
+// Three numeric modes: T = double is the "truth" used for parity; T = float is
 // the plain fp32 CPU forward timed as the CPU baseline (OpenMP over states,
-// weights pre-transposed so the inner loops vectorise).
+// weights pre-transposed so the inner loops vectorise); the recipe emulation
+// (owo_policy_forward_emulated) is float64 with the bf16 / e4m3 rounding
+// points of a precision path applied, which separates what the precision
+// recipe itself loses from what a kernel's arithmetic loses. Padded entities
+// never reach a valid output, so every mode computes the valid rows only.
 
 #include <cmath>
 #include <cstdint>
@@ -200,21 +204,22 @@ void forward_state(const Prepared<T>& p, const float* feat, int count, size_t st
   const size_t N = s.n_entities, F = s.features, d = s.d_model, f = s.ffn, P = s.actions;
   const size_t H = s.heads, hd = d / H;
   const float* w = p.w;
+  // padded entities (j >= count) never reach a valid output: only the valid rows are computed
+  const size_t Nv = static_cast<size_t>(std::max(count, 0));
   // embedding
   std::vector<T> ft(N * F);
   for (size_t i = 0; i < N * F; ++i) ft[i] = static_cast<T>(feat[i]);
-  linear<T>(ft.data(), N, F, p.we_t.data(), d, w + p.off.be, x.data());
+  linear<T>(ft.data(), Nv, F, p.we_t.data(), d, w + p.off.be, x.data());
   const T scale = static_cast<T>(1) / std::sqrt(static_cast<T>(hd));
   for (int l = 0; l < s.layers; ++l) {
     const auto& L = p.off.layer[l];
-    layer_norm<T>(x.data(), N, d, w + L.ln1g, w + L.ln1b, a.data());
-    linear<T>(a.data(), N, d, p.wqkv_t[l].data(), 3 * d, w + L.bqkv, qkv.data());
+    layer_norm<T>(x.data(), Nv, d, w + L.ln1g, w + L.ln1b, a.data());
+    linear<T>(a.data(), Nv, d, p.wqkv_t[l].data(), 3 * d, w + L.bqkv, qkv.data());
     // masked multi-head attention (keys j >= count masked)
     std::fill(o.begin(), o.end(), static_cast<T>(0));
     for (size_t hh = 0; hh < H; ++hh) {
       const size_t qo = hh * hd, ko = d + hh * hd, vo = 2 * d + hh * hd;
-      for (size_t i = 0; i < N; ++i) {
-        if (count <= 0) break;
+      for (size_t i = 0; i < Nv; ++i) {
         T mx = -std::numeric_limits<T>::infinity();
         for (int j = 0; j < count; ++j) {
           T dot = 0;
@@ -234,15 +239,15 @@ void forward_state(const Prepared<T>& p, const float* feat, int count, size_t st
         }
       }
     }
-    linear<T>(o.data(), N, d, p.wo_t[l].data(), d, w + L.bo, t.data());
-    for (size_t i = 0; i < N * d; ++i) x[i] += t[i];
-    layer_norm<T>(x.data(), N, d, w + L.ln2g, w + L.ln2b, a.data());
-    linear<T>(a.data(), N, d, p.w1_t[l].data(), f, w + L.b1, h.data());
-    for (size_t i = 0; i < N * f; ++i) h[i] = gelu<T>(h[i]);
-    linear<T>(h.data(), N, f, p.w2_t[l].data(), d, w + L.b2, t.data());
-    for (size_t i = 0; i < N * d; ++i) x[i] += t[i];
+    linear<T>(o.data(), Nv, d, p.wo_t[l].data(), d, w + L.bo, t.data());
+    for (size_t i = 0; i < Nv * d; ++i) x[i] += t[i];
+    layer_norm<T>(x.data(), Nv, d, w + L.ln2g, w + L.ln2b, a.data());
+    linear<T>(a.data(), Nv, d, p.w1_t[l].data(), f, w + L.b1, h.data());
+    for (size_t i = 0; i < Nv * f; ++i) h[i] = gelu<T>(h[i]);
+    linear<T>(h.data(), Nv, f, p.w2_t[l].data(), d, w + L.b2, t.data());
+    for (size_t i = 0; i < Nv * d; ++i) x[i] += t[i];
   }
-  layer_norm<T>(x.data(), N, d, w + p.off.lnf_g, w + p.off.lnf_b, a.data());
+  layer_norm<T>(x.data(), Nv, d, w + p.off.lnf_g, w + p.off.lnf_b, a.data());
   // policy head on valid entities; padded entities are exactly 0 / -1
   std::vector<T> lg(P);
   for (size_t j = 0; j < N; ++j) {
@@ -277,6 +282,169 @@ void forward_state(const Prepared<T>& p, const float* feat, int count, size_t st
     }
   }
   *value = static_cast<float>(v);
+}
+
+// ---------------------------------------------------------------- recipe emulation
+// Float64 forward that rounds at the points where the bf16 / fp8 paths store
+// a tensor in a narrow type, so that "the recipe's own error" (what any exact
+// implementation of the precision recipe loses against the float64 truth) is
+// measured apart from the kernels' arithmetic error. Rounding points:
+//   kStoreBf16    features, QKV, softmax P, attention output, GELU output,
+//                 bf16 LayerNorm outputs, logits (and value on the fp8 path)
+//   kQuantQkv .. kQuantDown  e4m3 operands of one block GEMM: per-token scale
+//                 s = absmax/448 (1 for an all-zero row), q = e4m3(v/s) RNE
+//                 saturating, the GEMM sums q_a*q_w*s_a*s_w exactly
+// The weight blob is used as given (pass matrices already on the bf16 or
+// per-channel e4m3 grid to exclude weight quantisation).
+enum : unsigned {
+  kStoreBf16 = 1u,
+  kQuantQkv = 2u,
+  kQuantOut = 4u,
+  kQuantUp = 8u,
+  kQuantDown = 16u,
+  kValueBf16 = 32u,
+};
+
+double round_bf16(double v) {
+  float f = static_cast<float>(v);
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u) return f;  // inf / nan unchanged
+  u += 0x7FFFu + ((u >> 16) & 1u);                  // round to nearest even on the upper 16 bits
+  u &= 0xFFFF0000u;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+// e4m3 ("fn": no infinities, max 448, min normal 2^-6, subnormal step 2^-9),
+// round to nearest even, saturating to +-448.
+float round_e4m3(float v) {
+  if (!(v == v)) return v;
+  const float a = std::fabs(v);
+  if (a == 0.0f) return v;
+  float q;
+  if (a >= 448.0f) {
+    q = 448.0f;
+  } else {
+    int e;
+    std::frexp(a, &e);          // a = m * 2^e, m in [0.5, 1): the binade's step is 2^(e-4)
+    const int step_exp = std::max(e - 4, -9);
+    const double scaled = std::ldexp(static_cast<double>(a), -step_exp);
+    q = static_cast<float>(std::ldexp(std::nearbyint(scaled), step_exp));  // FE_TONEAREST: ties to even
+    if (q > 448.0f) q = 448.0f;
+  }
+  return v < 0 ? -q : q;
+}
+
+// Per-token e4m3 operand: v -> q*s with s = absmax/448 computed in f32 like the kernels.
+void quantize_rows(std::vector<double>& v, size_t rows, size_t cols) {
+  for (size_t r = 0; r < rows; ++r) {
+    double* row = v.data() + r * cols;
+    float amax = 0.0f;
+    for (size_t c = 0; c < cols; ++c) amax = std::max(amax, std::fabs(static_cast<float>(row[c])));
+    const float s = amax > 0.0f ? amax * (1.0f / 448.0f) : 1.0f;
+    const float inv = 1.0f / s;
+    for (size_t c = 0; c < cols; ++c)
+      row[c] = static_cast<double>(round_e4m3(static_cast<float>(row[c]) * inv)) * static_cast<double>(s);
+  }
+}
+
+void round_all_bf16(std::vector<double>& v, size_t n) {
+  for (size_t i = 0; i < n; ++i) v[i] = round_bf16(v[i]);
+}
+
+void forward_state_emu(const Prepared<double>& p, unsigned mode, const float* feat, int count, float* logits,
+                       float* value, int32_t* actions) {
+  const OwoShape& s = p.s;
+  const size_t N = s.n_entities, F = s.features, d = s.d_model, f = s.ffn, P = s.actions;
+  const size_t H = s.heads, hd = d / H;
+  const float* w = p.w;
+  const bool bf = (mode & kStoreBf16) != 0;
+  const size_t Nv = static_cast<size_t>(std::max(count, 0));  // padded rows never reach a valid output
+  std::vector<double> x(N * d), a(N * d), qkv(N * 3 * d), o(N * d), t(N * d), h(N * f), scores(N);
+  std::vector<double> ft(N * F);
+  for (size_t i = 0; i < N * F; ++i) ft[i] = bf ? round_bf16(feat[i]) : feat[i];
+  linear<double>(ft.data(), Nv, F, p.we_t.data(), d, w + p.off.be, x.data());
+  // the bf16 / fp8 kernels keep the residual stream x in f32 (mode 0 is the plain float64 forward)
+  auto store_x = [&](double v) { return mode != 0 ? static_cast<double>(static_cast<float>(v)) : v; };
+  for (size_t i = 0; i < Nv * d; ++i) x[i] = store_x(x[i]);
+  auto ln_out = [&](const float* g, const float* b, bool quant) {
+    layer_norm<double>(x.data(), Nv, d, g, b, a.data());
+    if (quant) quantize_rows(a, Nv, d);
+    else if (bf) round_all_bf16(a, Nv * d);
+  };
+  const double scale = 1.0 / std::sqrt(static_cast<double>(hd));
+  for (int l = 0; l < s.layers; ++l) {
+    const auto& L = p.off.layer[l];
+    ln_out(w + L.ln1g, w + L.ln1b, (mode & kQuantQkv) != 0);
+    linear<double>(a.data(), Nv, d, p.wqkv_t[l].data(), 3 * d, w + L.bqkv, qkv.data());
+    if (bf) round_all_bf16(qkv, Nv * 3 * d);
+    std::fill(o.begin(), o.end(), 0.0);
+    for (size_t hh = 0; hh < H && count > 0; ++hh) {
+      const size_t qo = hh * hd, ko = d + hh * hd, vo = 2 * d + hh * hd;
+      for (size_t i = 0; i < Nv; ++i) {
+        double mx = -std::numeric_limits<double>::infinity();
+        for (int j = 0; j < count; ++j) {
+          double dot = 0;
+          for (size_t c = 0; c < hd; ++c) dot += qkv[i * 3 * d + qo + c] * qkv[j * 3 * d + ko + c];
+          scores[j] = dot * scale;
+          mx = std::max(mx, scores[j]);
+        }
+        double den = 0;
+        for (int j = 0; j < count; ++j) {
+          scores[j] = std::exp(scores[j] - mx);
+          den += scores[j];
+          if (bf) scores[j] = round_bf16(scores[j]);  // P enters the PV product as bf16; the sum does not
+        }
+        for (int j = 0; j < count; ++j)
+          for (size_t c = 0; c < hd; ++c) o[i * d + qo + c] += scores[j] * qkv[j * 3 * d + vo + c];
+        for (size_t c = 0; c < hd; ++c) o[i * d + qo + c] /= den;
+      }
+    }
+    if (bf) round_all_bf16(o, Nv * d);
+    if (mode & kQuantOut) quantize_rows(o, Nv, d);
+    linear<double>(o.data(), Nv, d, p.wo_t[l].data(), d, w + L.bo, t.data());
+    for (size_t i = 0; i < Nv * d; ++i) x[i] = store_x(x[i] + t[i]);
+    ln_out(w + L.ln2g, w + L.ln2b, (mode & kQuantUp) != 0);
+    linear<double>(a.data(), Nv, d, p.w1_t[l].data(), f, w + L.b1, h.data());
+    for (size_t i = 0; i < Nv * f; ++i) h[i] = gelu<double>(h[i]);
+    if (bf) round_all_bf16(h, Nv * f);
+    if (mode & kQuantDown) quantize_rows(h, Nv, f);
+    linear<double>(h.data(), Nv, f, p.w2_t[l].data(), d, w + L.b2, t.data());
+    for (size_t i = 0; i < Nv * d; ++i) x[i] = store_x(x[i] + t[i]);
+  }
+  // final LN stays f32 (heads read y in f32)
+  layer_norm<double>(x.data(), Nv, d, w + p.off.lnf_g, w + p.off.lnf_b, a.data());
+  std::vector<double> lg(P);
+  for (size_t j = 0; j < N; ++j) {
+    float* out = logits + j * P;
+    if (static_cast<int>(j) >= count) {
+      for (size_t q = 0; q < P; ++q) out[q] = 0.0f;
+      actions[j] = -1;
+      continue;
+    }
+    linear<double>(a.data() + j * d, 1, d, p.wp_t.data(), P, w + p.off.bp, lg.data());
+    int best = 0;
+    double best_v = -std::numeric_limits<double>::infinity();
+    for (size_t q = 0; q < P; ++q) {
+      const double v = bf ? round_bf16(lg[q]) : lg[q];
+      out[q] = static_cast<float>(v);
+      if (v > best_v) {
+        best_v = v;
+        best = static_cast<int>(q);
+      }
+    }
+    actions[j] = best;
+  }
+  double v = w[p.off.bv];
+  if (count > 0) {
+    for (size_t c = 0; c < d; ++c) {
+      double m = 0;
+      for (int j = 0; j < count; ++j) m += a[j * d + c];
+      v += (m / count) * static_cast<double>(w[p.off.wv + c]);
+    }
+  }
+  *value = static_cast<float>((mode & kValueBf16) ? round_bf16(v) : v);
 }
 
 template <typename T>
@@ -335,6 +503,77 @@ int owo_policy_forward(const OwoShape* shape, const float* weights, size_t n_wei
   return run<float>(shape, weights, n_weights, features, counts, batch, threads, sample, seed,
                     logits, value, actions);
 }
+
+// Float64 forward with the precision recipe's rounding points applied (mode:
+// the kStoreBf16 / kQuant* / kValueBf16 bits above). Greedy actions only.
+// Returns 0 on success, 1 on a bad argument.
+int owo_policy_forward_emulated(const OwoShape* shape, const float* weights, size_t n_weights,
+                                const float* features, const int32_t* counts, int32_t batch, unsigned mode,
+                                int threads, float* logits, float* value, int32_t* actions) {
+  if (shape == nullptr || weights == nullptr || features == nullptr || counts == nullptr ||
+      logits == nullptr || value == nullptr || actions == nullptr || batch < 0 || !shape_ok(*shape))
+    return 1;
+  Prepared<double> p;
+  p.init(*shape, weights);
+  if (n_weights != p.off.total) return 1;
+  for (int32_t b = 0; b < batch; ++b)
+    if (counts[b] < 0 || counts[b] > shape->n_entities) return 1;
+  const size_t N = shape->n_entities, F = shape->features, P = shape->actions;
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel for schedule(dynamic, 1)
+#endif
+  for (int32_t b = 0; b < batch; ++b)
+    forward_state_emu(p, mode, features + static_cast<size_t>(b) * N * F, counts[b],
+                      logits + static_cast<size_t>(b) * N * P, value + b, actions + static_cast<size_t>(b) * N);
+  return 0;
+}
+
+// Gumbel-max actions from given logits (the GPU's own): actions[b,j] =
+// argmax_p(logits[b,j,p] + G(seed, state_base + b, j, p)) for j < counts[b],
+// -1 otherwise; gap[b,j] = the top-two score difference (ties that a rounding
+// may flip have a small gap). Returns 0, or 1 on a bad argument.
+int owo_gumbel_argmax(const float* logits, const int32_t* counts, int32_t batch, int32_t n_entities,
+                      int32_t n_actions, uint64_t seed, uint32_t state_base, int threads, int32_t* actions,
+                      float* gap) {
+  if (logits == nullptr || counts == nullptr || actions == nullptr || gap == nullptr || batch < 0 ||
+      n_entities <= 0 || n_actions <= 0)
+    return 1;
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel for schedule(static)
+#endif
+  for (int32_t b = 0; b < batch; ++b) {
+    for (int32_t j = 0; j < n_entities; ++j) {
+      const size_t row = static_cast<size_t>(b) * n_entities + j;
+      if (j >= counts[b]) {
+        actions[row] = -1;
+        gap[row] = INFINITY;
+        continue;
+      }
+      double best = -INFINITY, second = -INFINITY;
+      int arg = 0;
+      for (int32_t p = 0; p < n_actions; ++p) {
+        const double s = static_cast<double>(logits[row * n_actions + p]) +
+                         gumbel_noise(seed, state_base + static_cast<uint32_t>(b), static_cast<uint32_t>(j),
+                                      static_cast<uint32_t>(p));
+        if (s > best) {
+          second = best;
+          best = s;
+          arg = p;
+        } else if (s > second) {
+          second = s;
+        }
+      }
+      actions[row] = arg;
+      gap[row] = static_cast<float>(best - second);
+    }
+  }
+  return 0;
+}
+
+// e4m3 rounding of one f32 value (for known-answer tests of the emulation).
+float owo_round_e4m3(float v) { return round_e4m3(v); }
 
 // Gumbel noise G for (seed, state, entity, action) as the spec defines it.
 double owo_gumbel(uint64_t seed, uint32_t state, uint32_t entity, uint32_t action) {

@@ -114,6 +114,15 @@ def test_fp8_resid_ln():
     y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
     y = ln_out.view(torch.float8_e4m3fn).float() * ln_scale[:, None]
     close(y, y_ref, 7e-2)
+    # the quantisation point itself follows the recipe: scale absmax/448 per row, and e4m3 codes that equal
+    # RNE(y / scale) except where y sits within f32 rounding of a rounding boundary (then one step away)
+    close(ln_scale, y_ref.abs().amax(dim=1) / 448.0, 1e-5, "scale")
+    q = ln_out.view(torch.float8_e4m3fn).float()
+    q_ref = (y_ref / ln_scale[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).float()
+    off = q != q_ref
+    assert off.float().mean().item() <= 1e-2
+    step = torch.clamp(q_ref.abs(), min=2.0 ** -6) * 2.0 ** -3
+    assert torch.all((q - q_ref).abs()[off] <= step[off] * 1.0001)
 
 
 @pytest.mark.parametrize("epi,n", [(EPI_BIAS, 768), (EPI_GELU, 1024)])

@@ -1,14 +1,16 @@
-"""GPU parity of the encoder-policy forward against the CPU oracle (float64 truth).
+"""GPU parity of the encoder-policy forward against the CPU oracle.
 
-Tolerances: fp32 rel <= 1e-4, bf16 <= 1e-2, fp8 <= 3e-2 on
-logits and value; greedy argmax agreement >= 99.9% (ties within the
-precision's noise excluded); masks bit-exact.
+Tolerances: fp32 rel <= 1e-4 and bf16 <= 1e-2 against the float64 truth, on
+logits and value. fp8: the recipe itself loses about 4.7e-2 against the truth,
+so the fp8 path is held to the recipe's own error on the same inputs (the
+oracle's exact emulation of the recipe; tests/util.py gives the gate). Greedy argmax agreement >= 99.9% (ties within the precision's noise
+excluded); masks bit-exact.
 """
 import numpy as np
 import pytest
 
 import orbit_wars_b200 as ow
-from tests.util import (FP8_MEASURED_GATE, TOL, argmax_agreement, near_tie_mask, rel_err, representable_embedding,
+from tests.util import (TOL, check_fp8_against_recipe, argmax_agreement, near_tie_mask, rel_err, representable_embedding,
                         representable_weights, valid_mask)
 
 pytestmark = pytest.mark.gpu
@@ -36,11 +38,23 @@ def check_parity(cfg, gpu, ref, counts):
     assert np.all(g_lg[~m] == 0.0)
     assert np.all(g_a[~m] == -1)
     assert np.all((g_a[m] >= 0) & (g_a[m] < cfg.actions))
-    tol = TOL[cfg.precision] if cfg.precision != "fp8" else FP8_MEASURED_GATE
+    tol = TOL[cfg.precision]
     e_l = rel_err(g_lg[m], r_lg[m])
     e_v = rel_err(g_v, r_v)
     assert e_l <= tol and e_v <= tol, f"logits rel err {e_l:.3e}, value rel err {e_v:.3e} (tol {tol})"
     return e_l, e_v
+
+
+def check_fp8_parity(cfg, gpu, truth, recipe, counts):
+    """fp8: masks as everywhere; values against the truth within the recipe's own error (tests/util.py)."""
+    m = valid_mask(counts, cfg.n_entities)
+    assert np.all(gpu[0][~m] == 0.0) and np.all(gpu[2][~m] == -1)
+    assert np.all((gpu[2][m] >= 0) & (gpu[2][m] < cfg.actions))
+    r = check_fp8_against_recipe(gpu[0], gpu[1], truth, recipe, m)
+    print(f"{cfg.name}: " + "; ".join(f"{k} vs truth {v['vs_truth']:.2e} (recipe alone {v['recipe']:.2e}, "
+                                       f"rms {v['vs_truth_rms']:.2e} / {v['recipe_rms']:.2e}), "
+                                       f"vs recipe {v['vs_recipe']:.2e}" for k, v in r.items()))
+    return r["logits"]["vs_truth"], r["value"]["vs_truth"]
 
 
 def model_weights(cfg, seed, affine_noise=True):
@@ -59,7 +73,10 @@ def test_policy_matches_oracle(oracle, pid, batch):
     with ow.EncoderPolicy(cfg, w) as pol:
         gpu = pol.forward(feats, counts, seed=5)
     ref = oracle.policy_forward(cfg, w, feats, counts, f64=True, sample=False)
-    e_l, e_v = check_parity(cfg, gpu, ref, counts)
+    if cfg.precision == "fp8":
+        e_l, e_v = check_fp8_parity(cfg, gpu, ref, oracle.policy_forward_emulated(cfg, w, feats, counts), counts)
+    else:
+        e_l, e_v = check_parity(cfg, gpu, ref, counts)
     if not cfg.sample_actions and cfg.precision != "fp8":
         m = valid_mask(counts, cfg.n_entities) & ~near_tie_mask(ref[0], counts, cfg.n_entities,
                                                                  TIE_MARGIN[cfg.precision])

@@ -164,6 +164,34 @@ def test_trainable_legacy_matches_oracle(oracle):
     assert np.abs(out - ref).max() <= 1e-5
 
 
+@pytest.mark.skipif(not REF_LIB.exists(), reason="reference CUDA library not built (make -C oracle ref)")
+@pytest.mark.parametrize("d,heads,layers,games", [(32, 4, 3, 3), (64, 8, 2, 5), (16, 1, 1, 1)])
+def test_trainable_legacy_matches_reference_gpu_build(d, heads, layers, games):
+    """The legacy TrainableTransformer forward against the reference's own kernels
+    (native/cuda/orbit_wars_cuda.cu:2468-2582, built from source for sm_100a).
+
+    The reference writes 2 floats per row packed at the front of its output but copies back
+    rows x 24 floats (.cu:2481, :2570), so its host buffer gets 24 floats per row and only
+    the first games x rows x 2 are compared."""
+    ref = C.CDLL(str(REF_LIB), mode=2)
+    ref.orbit_wars_cuda_trainable_forward.restype = _lib.Status
+    ref.orbit_wars_cuda_trainable_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                                      _lib.TransformerShapeC]
+    lib = _lib.load_library()
+    rows = 64
+    n = 2 * d + d + layers * d + 2 * d
+    w = (np.sin(np.arange(1, n + 1) * 0.37) * 0.3).astype(np.float32)
+    x = np.cos(np.arange(1, games * rows * 2 + 1) * 0.61).astype(np.float32)
+    shape = _lib.TransformerShapeC(layers, d, heads, rows)
+    out_ref = np.zeros(games * rows * 24, np.float32)
+    _lib.check("reference trainable", ref.orbit_wars_cuda_trainable_forward(x.ctypes.data, w.ctypes.data,
+                                                                            out_ref.ctypes.data, games, shape))
+    out = np.zeros(games * rows * 2, np.float32)
+    _lib.check("trainable", lib.orbit_wars_cuda_trainable_forward(x.ctypes.data, w.ctypes.data, out.ctypes.data,
+                                                                  games, shape))
+    assert np.abs(out - out_ref[:games * rows * 2]).max() <= 1e-5
+
+
 def test_identity_copy():
     torch = pytest.importorskip("torch")
     lib = _lib.load_library()

@@ -5,12 +5,44 @@ import numpy as np
 
 TOL = {"f32": 1e-4, "bf16": 1e-2, "fp8": 3e-2}
 
-# The fp8 recipe (per-output-channel weight scales, per-token activation
-# scales absmax/448, e4m3 operands for all 16 block GEMMs) does NOT reach the
-# 3e-2 target on seeded random weights: activation rounding alone leaves
-# ~4.8e-2 on logits and ~2.9e-2 on value at 4 layers (1 layer: ~4e-2). The
-# fp8 parity test gates at this measured level so regressions still fail.
-FP8_MEASURED_GATE = 6e-2
+# The fp8 recipe (per-output-channel e4m3 weights, per-token e4m3 activations
+# with scale absmax/448, for all block GEMMs) loses about 4.7e-2 on logits
+# and 3.4e-2 on value against the float64 truth by itself: the oracle's recipe
+# emulation, exact in everything but the recipe's own rounding, measures that,
+# so no implementation of the recipe meets 3e-2 against the truth. Two exact
+# implementations do not agree with each other much better either: a value
+# within an f32 rounding of an e4m3 rounding boundary (about 1% of them, for
+# the ulp-level differences of accumulation order and of the GELU form) lands
+# one e4m3 step (12.5%) apart, and 16 quantised GEMMs carry that on. So the
+# end-to-end fp8 gate is statistical: against the truth, the kernels' error
+# may exceed the recipe's own error on the same inputs by at most
+# FP8_TRUTH_SLACK (max) and FP8_RMS_SLACK (root mean square). The kernels'
+# arithmetic on identical e4m3 operands is gated tightly per GEMM
+# (tests/test_gemm_gpu.py).
+FP8_TRUTH_SLACK = 1.25
+FP8_RMS_SLACK = 1.15
+
+
+def rms_rel(a, b) -> float:
+    """sqrt(mean (a-b)^2) / sqrt(mean b^2)."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.sqrt(np.mean((a - b) ** 2)) / max(np.sqrt(np.mean(b ** 2)), 1e-12))
+
+
+def check_fp8_against_recipe(gpu_logits, gpu_value, truth, recipe, mask):
+    """Asserts the fp8 gate above; returns the figures (vs truth, the recipe's own, vs the recipe)."""
+    g = {"logits": gpu_logits[mask], "value": gpu_value}
+    t = {"logits": truth[0][mask], "value": truth[1]}
+    r = {"logits": recipe[0][mask], "value": recipe[1]}
+    out = {}
+    for k in ("logits", "value"):
+        e, floor = rel_err(g[k], t[k]), rel_err(r[k], t[k])
+        e_rms, floor_rms = rms_rel(g[k], t[k]), rms_rel(r[k], t[k])
+        out[k] = dict(vs_truth=e, recipe=floor, vs_truth_rms=e_rms, recipe_rms=floor_rms, vs_recipe=rel_err(g[k], r[k]))
+        assert e <= FP8_TRUTH_SLACK * max(floor, 1e-3), (k, out[k])
+        assert e_rms <= FP8_RMS_SLACK * max(floor_rms, 1e-4), (k, out[k])
+    return out
 
 
 def rel_err(a, b) -> float:
