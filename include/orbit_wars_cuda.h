@@ -146,10 +146,15 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_train_full_attention(
  * (NULL: the legacy default stream) and returns without waiting.
  * Scratch is a fixed 1 MiB device array inside the library, held by every GPU
  * that loads it until exit: game_count * (row_count^2 + 1) must be <= 262,080
- * (63 requests at 64 rows), else BAD_ARGUMENT. The first call on a device
- * resolves the array's device address; make that first call before any stream
- * capture. All calls share the array: calls that overlap on the GPU (other
- * streams, other host threads) race and must be serialised by the caller. */
+ * (63 requests at 64 rows), else BAD_ARGUMENT. Every call looks the array's
+ * device address up again (so a device reset leaves nothing stale); the first
+ * call on a device also loads the library's device code, so make that first
+ * call before any stream capture. The three kernels of this path raise no
+ * device-side error (with one model there is no model index to check), so
+ * the returned status, which carries launch errors, is the whole result; a
+ * fault during execution surfaces at the caller's next synchronisation.
+ * All calls share the array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller. */
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(
     const float* input_rows,
     const float* weights,
@@ -321,6 +326,16 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_play_many_resident(
     float* input_rows,
     float* output_rows,
     OrbitWarsCudaTrue2DShape shape);
+
+/* Measured rate of the GPU's special-function (MUFU) pipe -- no counterpart in
+ * the reference ABI; the roofline of the True2D matrix layers, whose tanh and
+ * sigmoid are one ex2.approx and one rcp.approx each. op 0 = ex2.approx,
+ * 1 = rcp.approx. One CTA of 1024 threads per SM runs 8 independent chains
+ * per thread; *ops_per_second is event-timed, *ops_per_clock_per_sm comes
+ * from each CTA's clock64 span, *sm_clock_mhz is their ratio. Allocates and
+ * frees its small buffers (a measurement call, not for a hot loop). */
+OrbitWarsCudaStatus orbit_wars_cuda_mufu_rate(int32_t op, double* ops_per_second, double* ops_per_clock_per_sm,
+                                              double* sm_clock_mhz);
 
 /* Device timing of the True2D forwards -- no counterpart in the reference ABI;
  * for benchmarks. profile_begin arms CUDA events around each kernel of the next

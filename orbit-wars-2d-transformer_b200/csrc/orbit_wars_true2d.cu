@@ -910,21 +910,17 @@ constexpr size_t kNoAllocHeaderFloats = 64;
 constexpr size_t kNoAllocCells = kNoAllocFloats - kNoAllocHeaderFloats;  // 262,080 cells
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
 
-// Device address of g_noalloc_scratch for `dev` (must be the current device).
-// Resolved once per device with cudaGetSymbolAddress: in host code the
-// array's name is only a host-side stand-in, never a device address.
-cudaError_t noalloc_scratch_address(int dev, float** out) {
-  static std::mutex mu;
-  static void* addr[64] = {};
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    addr[dev] = p;
-  }
-  *out = static_cast<float*>(addr[dev]);
+// Device address of g_noalloc_scratch on the current device. In host code
+// the array's name is only a host-side stand-in, never a device address, so
+// every call asks the runtime for it: a cached address would dangle after a
+// device reset reloads the module. Once the module is loaded (the first call
+// on a device, which is why that call must come before any stream capture)
+// the lookup involves no allocation and no synchronisation.
+cudaError_t noalloc_scratch_address(float** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  *out = static_cast<float*>(p);
   return cudaSuccess;
 }
 
@@ -1778,6 +1774,40 @@ OrbitWarsCudaStatus train_step(Workspace& W, const float* input_rows, const floa
 
 }  // namespace
 
+// ---------------------------------------------------------------- MUFU rate probe
+// Throughput of the special-function pipe, the bound of the True2D matrix
+// layers: one CTA of 1024 threads per SM, each thread running 8 independent
+// chains of `op` (0: ex2.approx.ftz.f32 of the negated value, which keeps the
+// chain in (0, 1]; 1: rcp.approx.ftz.f32 of 1 + v, which converges to 0.618:
+// a bare rcp chain would alternate v and 1/v, and the assembler may fold
+// rcp(rcp(v)) away), so the pipe, not a dependency, sets the pace. Each CTA
+// records its clock64 span.
+template <int OP>
+__global__ void __launch_bounds__(1024, 1) mufu_rate_kernel(int iters, float* sink, long long* cycles) {
+  float v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = 0.25f + 0.0625f * k + 1e-6f * threadIdx.x;
+  __syncthreads();
+  const long long c0 = clock64();
+  for (int i = 0; i < iters; ++i) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (OP == 0)
+        asm volatile("{\n\t.reg .f32 t;\n\tneg.f32 t, %1;\n\tex2.approx.ftz.f32 %0, t;\n\t}" : "=f"(v[k]) : "f"(v[k]));
+      else
+        asm volatile("{\n\t.reg .f32 t;\n\tadd.f32 t, %1, 0f3F800000;\n\trcp.approx.ftz.f32 %0, t;\n\t}"
+                     : "=f"(v[k]) : "f"(v[k]));
+    }
+  }
+  __syncthreads();
+  const long long c1 = clock64();
+  float acc = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc += v[k];
+  if (acc == -1.0f) sink[threadIdx.x] = acc;  // never true: keeps the chains live
+  if (threadIdx.x == 0) cycles[blockIdx.x] = c1 - c0;
+}
+
 extern "C" {
 
 OrbitWarsCudaStatus orbit_wars_cuda_status(void) {
@@ -2071,14 +2101,15 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(const float* input_ro
   const T2Layout L = t2_layout(shape.layer_count, shape.row_count, shape.head_count);
   if (game_count > kNoAllocCells / (L.cells + 1))
     return bad("game_count x (row_count^2 + 1) exceeds the allocation-free scratch (262080 floats)");
-  int dev = 0;
-  T2_TRY(cudaGetDevice(&dev));
   float* scratch = nullptr;
-  T2_TRY(noalloc_scratch_address(dev, &scratch));
+  T2_TRY(noalloc_scratch_address(&scratch));
+  // The kernels' error word: with no index array and one model they record
+  // nothing (a model index is the only device-side error of these three
+  // kernels), so launch errors in the returned status are the whole story.
+  // It is still cleared, since the array keeps the previous call's contents.
   int* err = reinterpret_cast<int*>(scratch);
   float* m = scratch + kNoAllocHeaderFloats;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // the array keeps the previous call's contents: clear the error word
   T2_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
   const T2Dev D = ref_layout_dev(L);
   const dim3 g1((L.cells + 255) / 256, static_cast<unsigned>(game_count));
@@ -2090,6 +2121,57 @@ OrbitWarsCudaStatus orbit_wars_cuda_true2d_forward_noalloc(const float* input_ro
   const int threads3 = static_cast<int>(std::min<size_t>(512, std::max<size_t>(128, kRowsPerCta * L.rows)));
   t2_post_collapse<false><<<g3, threads3, 0, s>>>(nullptr, weights, 1, D, m, output_rows, err);
   return from_cuda(cudaGetLastError());
+}
+
+// Measured rate of the special-function pipe (no counterpart in the reference):
+// one launch of mufu_rate_kernel per op on the current device, timed with
+// CUDA events after a warm-up launch.
+OrbitWarsCudaStatus orbit_wars_cuda_mufu_rate(int32_t op, double* ops_per_second, double* ops_per_clock_per_sm,
+                                              double* sm_clock_mhz) {
+  if ((op != 0 && op != 1) || ops_per_second == nullptr || ops_per_clock_per_sm == nullptr ||
+      sm_clock_mhz == nullptr)
+    return bad("op must be 0 (ex2) or 1 (rcp); outputs must not be null");
+  int dev = 0;
+  T2_TRY(cudaGetDevice(&dev));
+  int sms = 0;
+  T2_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  float* sink = nullptr;
+  long long* cyc = nullptr;
+  T2_TRY(cudaMalloc(&sink, 1024 * sizeof(float)));
+  if (cudaMalloc(&cyc, sms * sizeof(long long)) != cudaSuccess) {
+    cudaFree(sink);
+    return rt("cudaMalloc failed");
+  }
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  const int iters = 4096;
+  auto launch = [&]() {
+    if (op == 0) mufu_rate_kernel<0><<<sms, 1024>>>(iters, sink, cyc);
+    else mufu_rate_kernel<1><<<sms, 1024>>>(iters, sink, cyc);
+  };
+  launch();  // warm-up
+  cudaEventRecord(e0);
+  launch();
+  cudaEventRecord(e1);
+  cudaError_t e = cudaEventSynchronize(e1);
+  float ms = 0.0f;
+  std::vector<long long> c(sms);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+  if (e == cudaSuccess) e = cudaMemcpy(c.data(), cyc, sms * sizeof(long long), cudaMemcpyDeviceToHost);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(sink);
+  cudaFree(cyc);
+  if (e != cudaSuccess) return from_cuda(e);
+  const double ops_cta = 1024.0 * iters * 8.0;
+  double mean_cyc = 0.0;
+  for (long long v : c) mean_cyc += static_cast<double>(v);
+  mean_cyc /= sms;
+  *ops_per_second = ops_cta * sms / (ms * 1e-3);
+  *ops_per_clock_per_sm = ops_cta / mean_cyc;
+  *sm_clock_mhz = mean_cyc / (ms * 1e-3) / 1e6;  // cycles of the timed span over its event time (upper bound on launch gaps)
+  return ok();
 }
 
 OrbitWarsCudaStatus orbit_wars_cuda_true2d_profile_begin(int32_t max_calls) {
