@@ -18,10 +18,19 @@ broadcasts them once over NCCL.
          events the library records around each launch in the timed region).
   cpu_baseline  the CPU oracle (fp32, OpenMP, all host threads) on a bounded
          sample of the same workload, rank 0 at N=1 only.
+  weight_broadcast  (N > 1) the library's NCCL broadcast of rank 0's packed
+         device weights into every other rank's handle: bytes, device ms, GB/s.
+  config5  the same measurement, nested, for config 5 (65,536 states per GPU,
+         d=512, 8 blocks): the scale-out workload, so the 1/2/4/8-GPU runs of
+         this command trace its scaling and its weight broadcast too.
+  true2d  (N = 1) the reference ABI drop-in (True2D self-play forward): device
+         and e2e requests/s, the reference's own CUDA build on the same call,
+         the MUFU roofline against the measured MUFU rate, the CPU reference.
 
 --impl reference times the reference-side CPU implementation of this path.
 The reference repository has no implementation of this network, so that arm
-is the repository's CPU port of the spec (oracle, fp32, all host threads).
+is the repository's CPU port of the spec (oracle, fp32, every host core, the
+whole configured batch per step when the run fits its CPU budget).
 """
 from __future__ import annotations
 
@@ -46,7 +55,7 @@ METRIC = "policy-forward states/sec (config {c})"
 UNIT = "states/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
-REFERENCE_RUN_S = 120.0  # CPU time budget of one --impl reference run
+REFERENCE_RUN_S = 150.0  # CPU time budget of one --impl reference run
 
 
 def ncu_traffic(config, kernel: str):
@@ -191,10 +200,19 @@ def gemm_summary(cfg, kernels: dict, m_valid: int, sq_counts: int, batch: int, t
     return res
 
 
+def host_threads() -> int:
+    """Every host core this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks, so the
+    oracle's OpenMP default would be one thread: pass the count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(cfg, weights, feats, counts, target_s: float = 12.0) -> dict:
     """Times the fp32 CPU oracle (OpenMP, all host threads) on a bounded sample of the workload."""
     from oracle import bind
-    threads = bind.max_threads()
+    threads = host_threads()
     n = max(1, min(4, cfg.batch))
     bind.policy_forward(cfg, weights, feats[:n], counts[:n], f64=False, threads=threads)  # warm
     while True:
@@ -206,10 +224,14 @@ def cpu_baseline(cfg, weights, feats, counts, target_s: float = 12.0) -> dict:
         grow = max(2, int(target_s / max(dt, 1e-3)))
         n = min(cfg.batch, n * grow)
     return {"value": n / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} of the {cfg.batch} states of the workload, fp32 CPU oracle, {dt:.1f} s"}
+            "sample": f"{n} of the {cfg.batch} states of the workload, fp32 CPU oracle (valid rows only), "
+                      f"{threads} threads, {dt:.1f} s"}
 
 
 def run_reference(args, cfg) -> None:
+    """The reference-side CPU arm: the fp32 CPU port of the spec on every host core, rank 0 only. Each step
+    is the whole configured batch when warm-up + timed steps fit REFERENCE_RUN_S of CPU work (so the arm
+    runs the same workload as ours), else a bounded sample of it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -217,14 +239,13 @@ def run_reference(args, cfg) -> None:
     from oracle import bind
     weights = ow.make_weights(cfg, seed=args.seed)
     feats, counts = ow.make_inputs(cfg, seed=args.seed)
-    threads = bind.max_threads()
-    # sample size: the whole warm-up + timed run takes about REFERENCE_RUN_S of CPU work
-    n = 4
+    threads = host_threads()
+    n = min(cfg.batch, 16)
     bind.policy_forward(cfg, weights, feats[:n], counts[:n], f64=False, threads=threads)  # warm
     t0 = time.perf_counter()
     bind.policy_forward(cfg, weights, feats[:n], counts[:n], f64=False, threads=threads)
     per_state = (time.perf_counter() - t0) / n
-    step_s = min(3.0, REFERENCE_RUN_S / (args.steps + args.warmup))
+    step_s = REFERENCE_RUN_S / (args.steps + args.warmup)
     n = int(max(1, min(cfg.batch, step_s / max(per_state, 1e-6))))
     for i in range(args.warmup):
         bind.policy_forward(cfg, weights, feats[:n], counts[:n], f64=False, threads=threads)
@@ -236,50 +257,124 @@ def run_reference(args, cfg) -> None:
         times.append(time.perf_counter() - t0)
     total = float(np.sum(times))
     value = n * args.steps / total
-    sample = (f"{n} states per step (of the {cfg.batch}-state workload), fp32 CPU port of the spec, "
-              f"{threads} threads; the reference repository has no implementation of this network")
+    sample = (f"{n} states per step (of the {cfg.batch}-state workload), fp32 CPU port of the spec (valid rows "
+              f"only), {threads} threads; the reference repository has no implementation of this network")
     line = {
         "impl": "reference", "metric": METRIC.format(c=args.config), "value": value, "unit": UNIT,
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded SplitMix/Box-Muller features, Xavier-uniform weights)",
-        "config": {"workload": workload_name(cfg), "sample_states_per_step": n},
+        "config": {"workload": workload_name(cfg), "states_per_step": n, "same_config": n == cfg.batch},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, cfg) -> None:
+class Ctx:
+    """This process's place in the run: rank, device, stream and (N > 1) the library's NCCL communicator."""
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.comm = None
+        self.nccl_log = None
+        self.dev = None
+        self.stream = None
+
+    def start(self):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            # NCCL's init lines (rank counts of every communicator, torch's and the library's) go to a
+            # per-process file and are echoed to stderr at the end: stdout carries one JSON line only
+            self.nccl_log = Path(tempfile.gettempdir()) / f"ow_nccl_{os.getpid()}.log"
+            os.environ.setdefault("NCCL_DEBUG", "INFO")
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ.setdefault("NCCL_DEBUG_FILE", str(self.nccl_log))
+            dist.init_process_group("nccl", device_id=self.dev, timeout=timedelta(seconds=120))
+            # the weight broadcast's communicator: its 128-byte id travels over torch.distributed
+            from orbit_wars_b200.policy import Comm
+            from orbit_wars_b200.shard import share_comm_id
+            uid = share_comm_id(self.rank, Comm.unique_id() if self.rank == 0 else None)
+            self.comm = Comm(uid, self.world, self.rank, self.local)
+        # one non-default stream carries the library's kernels, torch's copies/flushes and the timing events
+        self.stream = torch.cuda.Stream(self.dev)
+        torch.cuda.set_stream(self.stream)
+        return self
+
+    def barrier(self):
+        import torch.distributed as dist
+        if self.world > 1:
+            dist.barrier()
+
+    def max_over_ranks(self, vals):
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor(vals, dtype=torch.float64, device=self.dev)
+        if self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    def finish(self):
+        import torch.distributed as dist
+        if self.world > 1:
+            dist.barrier()
+            if self.comm is not None:
+                self.comm.close()
+            dist.destroy_process_group()
+            if self.nccl_log is not None and self.nccl_log.exists():
+                keep = [ln for ln in self.nccl_log.read_text(errors="replace").splitlines()
+                        if "Init COMPLETE" in ln or "nranks" in ln.lower()]
+                for ln in keep[:16]:
+                    print(ln, file=sys.stderr)
+                self.nccl_log.unlink()
+
+
+def policy_handle(cfg, weights, ctx, io: str, bcast: bool):
+    """A handle on this rank's GPU. Rank 0 converts the seeded f32 blob; every other rank starts with no
+    weights and receives rank 0's packed device arena over NCCL (the library's ncclBroadcast). Returns the
+    handle and, for N > 1 with bcast, the broadcast timing (one warm-up, then three timed broadcasts)."""
+    import orbit_wars_b200 as ow
+    pol = ow.EncoderPolicy(cfg, weights if ctx.rank == 0 else None, device=ctx.local,
+                           stream=ctx.stream.cuda_stream, io=io)
+    if ctx.world == 1:
+        return pol, None
+    pol.broadcast_from(ctx.comm, root=0)
+    if not bcast:
+        return pol, None
+    ms = [pol.broadcast_from(ctx.comm, root=0) for _ in range(3)]
+    _, nbytes = pol.device_weights()
+    worst = ctx.max_over_ranks([float(np.mean(ms))])[0]
+    return pol, {"bytes": int(nbytes), "ms": round(worst, 4), "gbs": round(nbytes / (worst * 1e-3) / 1e9, 1),
+                 "nranks": ctx.world, "timing": "device time of one ncclBroadcast of the packed weight arena "
+                                                "(ow_policy_broadcast_weights_comm), mean of 3 after a warm-up, "
+                                                "max over ranks; in-switch reduction not involved (broadcast)",
+                 "what": "rank 0's converted bf16/e4m3 weights + scales + f32 vectors, as the kernels read them"}
+
+
+def measure_policy(args, cfg, ctx, steps: int, warmup: int, e2e_steps: int, with_cpu: bool,
+                   cpu_target_s: float = 12.0) -> dict:
+    """One workload: device-resident throughput with per-kernel events, the roofline of the dominant
+    kernel, e2e through the host-buffer API, the weight broadcast (N > 1), and the CPU baseline."""
     import torch
-    import torch.distributed as dist
 
     import orbit_wars_b200 as ow
+    from orbit_wars_b200.shard import shard_inputs
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        os.environ["NCCL_DEBUG"] = "WARN"  # NCCL prints its version banner on stdout otherwise: one JSON line only
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-
-    from orbit_wars_b200.shard import broadcast_weights, shard_inputs
-
-    # weights: rank 0 builds them, one NCCL broadcast to every rank
-    weights = broadcast_weights(cfg, args.seed, rank, device=dev)
+    dev, stream = ctx.dev, ctx.stream
+    weights = ow.make_weights(cfg, seed=args.seed) if ctx.rank == 0 else None
     # this rank's shard of the global batch (world * B states)
-    feats, counts = shard_inputs(cfg, args.seed, rank)
+    feats, counts = shard_inputs(cfg, args.seed, ctx.rank)
     B = cfg.batch
     m_valid = int(counts.sum())
     sq_counts = int((counts.astype(np.int64) ** 2).sum())
 
-    # one non-default stream carries the library's kernels, torch's copies/flushes and the timing events
-    stream = torch.cuda.Stream(dev)
-    torch.cuda.set_stream(stream)
-    pol = ow.EncoderPolicy(cfg, weights, device=local, stream=stream.cuda_stream, io="device")
+    pol, bcast = policy_handle(cfg, weights, ctx, "device", bcast=True)
     f_d = torch.from_numpy(feats).to(dev)
     c_d = torch.from_numpy(counts).to(dev)
     ldt = torch.bfloat16 if cfg.logits_dtype == "bf16" else torch.float32
@@ -292,48 +387,42 @@ def run_ours(args, cfg) -> None:
     def step(i):
         pol.forward_device(f_d.data_ptr(), c_d.data_ptr(), B, lg.data_ptr(), vv.data_ptr(), aa.data_ptr(), seed=i)
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         flush.zero_()
         step(i)
     pol.synchronize()
-    if world > 1:
-        dist.barrier()
+    ctx.barrier()
     torch.cuda.synchronize(dev)
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     # per-kernel events on the first timed steps only: an event between two
     # kernels stops the next one from starting early (programmatic dependent
     # launch), so profiled steps run slightly slower than the rest
-    prof_steps = min(args.steps, 20)
+    prof_steps = min(steps, 20)
     pol.profile_begin(prof_steps)
-    with ClockSampler(local) as clk:
+    with ClockSampler(ctx.local) as clk:
         clk.window = (time.time(), None)
-        for i in range(args.steps):
+        for i in range(steps):
             flush.zero_()  # L2 flush outside the step's events
             starts[i].record(stream)
-            step(args.warmup + i)
+            step(warmup + i)
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
         clk.window = (clk.window[0], time.time())
     prof = pol.profile_end()
     pol.synchronize()
-    if world > 1:
-        dist.barrier()
+    ctx.barrier()
     torch.cuda.synchronize(dev)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    t_local = float(np.sum(step_ms)) / 1000.0
-    t = torch.tensor([t_local], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t_max = float(t.item())
-    value = world * B * args.steps / t_max
-    launches = pol.launches_per_forward() * args.steps
+    t_max = ctx.max_over_ranks([float(np.sum(step_ms)) / 1000.0])[0]
+    value = ctx.world * B * steps / t_max
+    launches = pol.launches_per_forward() * steps
     out_ok = bool(torch.isfinite(lg.float()).all().item() and torch.isfinite(vv.float()).all().item())
     # the device-IO handle's workspace goes before the host-IO handle allocates its own
     # (config 5's activations take about 112 GB per workspace)
     pol.close()
-    del f_d, c_d, lg, vv, aa
+    del f_d, c_d, lg, vv, aa, flush
     torch.cuda.empty_cache()
 
     # e2e through the host-buffer API (pinned host buffers): the pipelined
@@ -341,9 +430,8 @@ def run_ours(args, cfg) -> None:
     # download overlap the previous step's forward; every step uploads its
     # features + counts and downloads logits, value and actions
     e2e = None
-    e2e_steps = min(args.steps, 200)
-    if not args.no_e2e:
-        hp = ow.EncoderPolicy(cfg, weights, device=local, stream=stream.cuda_stream, io="host")
+    if e2e_steps > 0:
+        hp, _ = policy_handle(cfg, weights, ctx, "host", bcast=False)
         f_h = torch.from_numpy(feats).pin_memory()
         c_h = torch.from_numpy(counts).pin_memory()
         outs = [(torch.empty((B, cfg.n_entities, cfg.actions), dtype=ldt).pin_memory(),
@@ -355,11 +443,10 @@ def run_ours(args, cfg) -> None:
             return hp.submit_raw(f_h.data_ptr(), c_h.data_ptr(), B, lg_h.data_ptr(), vv_h.data_ptr(),
                                  aa_h.data_ptr(), seed=i)
 
-        for i in range(args.warmup):
+        for i in range(warmup):
             hp.wait(submit(i))
         torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
+        ctx.barrier()
         t0 = time.perf_counter()
         prev = None
         for i in range(e2e_steps):
@@ -370,24 +457,25 @@ def run_ours(args, cfg) -> None:
         hp.wait(prev)
         t_pipe = time.perf_counter() - t0
         # the same calls one at a time (ow_policy_forward: submit + wait)
+        n_sync = min(e2e_steps, 50)
         t0 = time.perf_counter()
-        for i in range(min(e2e_steps, 50)):
+        for i in range(n_sync):
             hp.wait(submit(i))
-        t_sync = (time.perf_counter() - t0) / min(e2e_steps, 50)
-        te = torch.tensor([t_pipe, t_sync], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        t_sync = (time.perf_counter() - t0) / n_sync
+        t_pipe, t_sync = ctx.max_over_ranks([t_pipe, t_sync])
         lg_h, vv_h, aa_h = outs[0]
         h2d = feats.nbytes + counts.nbytes
         d2h = lg_h.numel() * lg_h.element_size() + vv_h.numel() * vv_h.element_size() + aa_h.numel() * 4
-        e2e = {"value": world * B * e2e_steps / float(te[0].item()), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+        e2e = {"value": ctx.world * B * e2e_steps / t_pipe, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
                "timing": "wall clock over the steps, ow_policy_submit / ow_policy_wait with two submissions in "
-                         "flight (pinned host buffers), max over ranks; no L2 flush (each step's working set, "
-                         "about 300 MB at config 2, exceeds the 126 MB L2)",
-               "synchronous_value": world * B / float(te[1].item()),
+                         "flight (pinned host buffers), max over ranks; no L2 flush (each step's working set "
+                         "exceeds the 126 MB L2)",
+               "synchronous_value": ctx.world * B / t_sync,
                "synchronous_timing": "ow_policy_forward-equivalent submit + wait per step, one at a time"}
         hp.close()
+        del f_h, c_h, outs
+        torch.cuda.empty_cache()
 
     # roofline of the dominant kernel: the bound whose roofline time is longer
     # (algorithmic bytes / measured HBM copy rate vs FLOPs / measured bf16 peak)
@@ -419,7 +507,7 @@ def run_ours(args, cfg) -> None:
     if dom_name is not None:
         k = kernels[dom_name]
         peak = tc_peak if k["bound"] == "tensor" else hbm_peak
-        traffic, traffic_src = ncu_traffic(args.config, dom_name)
+        traffic, traffic_src = ncu_traffic(int(cfg.name[1]), dom_name)
         roof = {"kernel": dom_name, "bound": k["bound"], "achieved": k["achieved"], "peak": peak, "unit": k["unit"],
                 "frac": round(k["achieved"] / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
                 "peak_source": peak_src + (" (fp8 peak = 2x measured bf16)" if cfg.precision == "fp8" else ""),
@@ -429,31 +517,52 @@ def run_ours(args, cfg) -> None:
                 "timed_steps_profiled": prof_steps}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(cfg, weights, feats, counts)
+    if with_cpu and ctx.rank == 0 and ctx.world == 1:
+        cpu = cpu_baseline(cfg, weights, feats, counts, target_s=cpu_target_s)
+    tc_sus = (float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
+              * (2.0 if cfg.precision == "fp8" else 1.0)) if tc_peak else None
+    return {
+        "value": value, "ms_per_step": 1000.0 * t_max / steps, "steps": steps, "warmup": warmup,
+        "dtype": {"f32": "f32", "bf16": "bf16", "fp8": "e4m3"}[cfg.precision],
+        "config": {"workload": workload_name(cfg), "per_gpu_batch": B, "global_batch": B * ctx.world,
+                   "valid_tokens_per_gpu": m_valid, "l2": "flushed between timed steps (256 MiB write)",
+                   "parallelism": f"dp{ctx.world} (states sharded; weights broadcast over NCCL by the library)",
+                   "seed": args.seed},
+        "e2e": e2e, "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clk.summary(),
+        "kernels": kernels, "outputs_finite": out_ok, "weight_broadcast": bcast,
+        "gemm": gemm_summary(cfg, kernels, m_valid, sq_counts, B, tc_peak, tc_sus),
+    }
 
-    clocks = clk.summary()
-    if rank == 0:
-        line = {
-            "metric": METRIC.format(c=args.config), "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * t_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": {"f32": "f32", "bf16": "bf16", "fp8": "e4m3"}[cfg.precision],
-            "data": "synthetic (seeded SplitMix/Box-Muller features, Xavier-uniform weights)",
-            "config": {"workload": workload_name(cfg), "per_gpu_batch": B, "global_batch": B * world,
-                       "valid_tokens_per_gpu": m_valid, "l2": "flushed between timed steps (256 MiB write)",
-                       "parallelism": f"dp{world} (states sharded, weights broadcast once over NCCL)",
-                       "seed": args.seed},
-            "e2e": e2e, "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
-            "kernels": kernels, "outputs_finite": out_ok,
-            "gemm": gemm_summary(cfg, kernels, m_valid, sq_counts, B, tc_peak,
-                                 (float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
-                                  * (2.0 if cfg.precision == "fp8" else 1.0)) if tc_peak else None),
-        }
+
+def run_ours(args, cfg) -> None:
+    import orbit_wars_b200 as ow
+
+    ctx = Ctx().start()
+    main = measure_policy(args, cfg, ctx, args.steps, args.warmup, min(args.steps, 200), not args.no_cpu)
+    # config 5 (the scale-out workload: 65,536 states per GPU) rides along as a nested object, so the
+    # 1/2/4/8-GPU runs of this command also trace config 5's scaling and its weight broadcast
+    c5 = None
+    if args.config != 5 and not args.no_c5:
+        c5 = measure_policy(args, ow.preset(5), ctx, steps=5, warmup=3, e2e_steps=3, with_cpu=not args.no_cpu,
+                            cpu_target_s=6.0)
+        c5["metric"] = METRIC.format(c=5)
+        c5["unit"] = UNIT
+    # the True2D drop-in (the reference's own self-play forward, behind its own ABI): one GPU, rank 0
+    t2 = None
+    if ctx.world == 1 and not args.no_true2d:
+        t2 = true2d_measure(args, ctx, steps=50, warmup=5, cpu_target_s=8.0)
+    if ctx.rank == 0:
+        line = {"metric": METRIC.format(c=args.config), "value": main["value"], "unit": UNIT, "n_gpus": ctx.world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": main["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": main["dtype"],
+                "data": "synthetic (seeded SplitMix/Box-Muller features, Xavier-uniform weights)"}
+        for k in ("config", "e2e", "gpu_launches", "roofline", "cpu_baseline", "clocks", "kernels", "outputs_finite",
+                  "weight_broadcast", "gemm"):
+            line[k] = main[k]
+        line["config5"] = c5
+        line["true2d"] = t2
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    ctx.finish()
 
 
 # ---------------------------------------------------------------- True2D drop-in workload
@@ -505,7 +614,7 @@ def true2d_cpu_reference(args, shape, pop, per, x, target_s: float) -> dict | No
     games = int(lib.ref_true2d_smoke_games())
     if int(lib.ref_true2d_smoke_weight_count()) != per or shape.heads != 1:
         return None
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     rows_per_call = games * shape.rows * 7
     calls_avail = max(1, x.size // rows_per_call)
 
@@ -619,7 +728,7 @@ def true2d_turn(args, lib, shape, steps: int) -> dict:
         wall.append(time.perf_counter() - t0)
     prof = lib.profile_end()
     kern = {k: round(ms * 1000.0 / max(c, 1), 2) for k, (c, ms) in prof.items()}
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     bind.encode_batch(batch, rg, rp, threads=threads)
     t0, reps = time.perf_counter(), 0
     while time.perf_counter() - t0 < 2.0:
@@ -698,26 +807,44 @@ def true2d_train(args, lib, shape, samples: int = 64, models: int = 8, steps: in
     return res
 
 
-def run_true2d(args) -> None:
+def mufu_peak(sm_mhz: float | None, cells_ex2: float, cells_rcp: float) -> dict | None:
+    """The special-function pipe's rate, measured on this GPU (orbit_wars_cuda_mufu_rate: ex2.approx and
+    rcp.approx chains, one 1024-thread CTA per SM, clock64 spans), for a kernel that issues ex2 and rcp in
+    the ratio cells_ex2 : cells_rcp; at the SM clock sampled during the timed region."""
+    import ctypes as C
+    from orbit_wars_b200 import _lib
+    lib = _lib.load_library()
+    res = {}
+    for op, name in ((0, "ex2"), (1, "rcp")):
+        ops, per_clk, mhz = C.c_double(), C.c_double(), C.c_double()
+        st = lib.orbit_wars_cuda_mufu_rate(op, C.byref(ops), C.byref(per_clk), C.byref(mhz))
+        if st.code != 0:
+            return None
+        res[name] = {"ops_per_s": ops.value, "per_clock_per_sm": round(per_clk.value, 3),
+                     "probe_sm_mhz": round(mhz.value, 1)}
     import torch
-    import torch.distributed as dist
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    mhz = sm_mhz or res["ex2"]["probe_sm_mhz"]
+    # time per op mix: cells_ex2 / r_ex2 + cells_rcp / r_rcp  ->  effective ops per clock per SM
+    r_e, r_r = res["ex2"]["per_clock_per_sm"], res["rcp"]["per_clock_per_sm"]
+    eff = (cells_ex2 + cells_rcp) / (cells_ex2 / r_e + cells_rcp / r_r)
+    return {"peak_gops": eff * sms * mhz * 1e6 / 1e9, "per_clock_per_sm": round(eff, 3), "sm_mhz": mhz,
+            "probe": res}
 
+
+def true2d_measure(args, ctx, steps: int, warmup: int, cpu_target_s: float = 12.0) -> dict:
+    """The True2D drop-in (reference ABI) on this process's GPU: device kernel phases, e2e through the
+    C-ABI call, the reference's own CUDA build on the same call, the reference's CPU forward, the MUFU
+    roofline against the measured MUFU rate, a device turn and the training step."""
+    import torch
+
+    from orbit_wars_b200 import _lib
     from orbit_wars_b200.true2d import CudaTrue2D
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)  # the reference ABI uses the calling thread's current device
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        os.environ["NCCL_DEBUG"] = "WARN"  # no version banner on stdout
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    dev = ctx.dev
     shape, per, pop, x, idx = true2d_workload(args)  # replicas: every rank runs the same workload
     lib = CudaTrue2D()
     lib.upload_population(pop, args.requests, shape)
-
-    from orbit_wars_b200 import _lib
     out_buf = np.empty(args.requests * shape.rows * 24, np.float32)
     fwd = lib.lib.orbit_wars_cuda_true2d_forward_many_resident
     shape_c = shape.c()
@@ -729,31 +856,26 @@ def run_true2d(args) -> None:
                    fwd(x.ctypes.data, idx.ctypes.data, out_buf.ctypes.data, args.requests, shape_c))
         return out_buf
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         out = step()
-    if world > 1:
-        dist.barrier()
+    ctx.barrier()
     torch.cuda.synchronize(dev)
-    lib.profile_begin(args.steps)
+    lib.profile_begin(steps)
     wall = []
-    with ClockSampler(local) as clk:
+    with ClockSampler(ctx.local) as clk:
         clk.window = (time.time(), None)
-        for _ in range(args.steps):
+        for _ in range(steps):
             t0 = time.perf_counter()
             out = step()
             wall.append(time.perf_counter() - t0)
         clk.window = (clk.window[0], time.time())
     prof = lib.profile_end()
-    if world > 1:
-        dist.barrier()
+    ctx.barrier()
     torch.cuda.synchronize(dev)
     dev_s = sum(v[1] for k, v in prof.items() if k.startswith("t2_")) / 1000.0  # kernels only, not the copies
-    t = torch.tensor([dev_s, float(np.sum(wall))], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t_dev, t_wall = float(t[0].item()), float(t[1].item())
-    value = world * args.requests * args.steps / t_dev
-    e2e = {"value": world * args.requests * args.steps / t_wall, "unit": T2_UNIT,
+    t_dev, t_wall = ctx.max_over_ranks([dev_s, float(np.sum(wall))])
+    value = ctx.world * args.requests * steps / t_dev
+    e2e = {"value": ctx.world * args.requests * steps / t_wall, "unit": T2_UNIT,
            "h2d_bytes_per_step": int(x.nbytes + idx.nbytes),
            "d2h_bytes_per_step": int(args.requests * shape.rows * 24 * 4 + 4),
            "timing": "wall clock per synchronous forward_many_resident C-ABI call (host buffers, output buffer reused "
@@ -766,7 +888,6 @@ def run_true2d(args) -> None:
     for k in kernels.values():
         k["share"] = round(k["total_ms"] / total, 4)
     clocks = clk.summary()
-    props = torch.cuda.get_device_properties(dev)
     roof = None
     mufu = {"t2_expand_pre": true2d_mufu_per_request(shape, "pre"),
             "t2_post_collapse": true2d_mufu_per_request(shape, "post")}
@@ -774,53 +895,62 @@ def run_true2d(args) -> None:
     if top is not None:
         a = kernels[top]
         ach = mufu[top] * args.requests / (a["avg_us"] * 1e-6) / 1e9
-        mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
-        peak = 16.0 * props.multi_processor_count * mhz * 1e6 / 1e9
+        # per cell and layer 4 ex2 (three tanh, the gate) and 1 rcp (the gate); the collapse adds ex2 only
+        cells = shape.rows * shape.rows
+        n_layers = shape.layers // 2 if top == "t2_expand_pre" else shape.layers - shape.layers // 2
+        ex2 = 4.0 * cells * n_layers + (2.0 * shape.rows * 12 * shape.rows if top == "t2_post_collapse" else 0.0)
+        rcp = 1.0 * cells * n_layers
+        pk = mufu_peak(clocks.get("sm_mhz"), ex2, rcp)
         traffic, traffic_src = ncu_traffic("true2d", top) if args.requests == 1024 and args.models == 64 else (None, None)
-        roof = {"kernel": top, "bound": "mufu", "achieved": round(ach, 1), "peak": round(peak, 1),
-                "unit": "G MUFU ops/s", "frac": round(ach / peak, 4), "traffic": traffic,
-                "traffic_unit": "bytes per launch (dram read + write)", "traffic_source": traffic_src,
-                "peak_source": f"computed: 16 MUFU ops/clk/SM x {props.multi_processor_count} SMs x {mhz:.0f} MHz "
-                               "(median sampled SM clock); not a measured peak",
-                "work_per_launch": f"{mufu[top]:.0f} MUFU ops per request: 5 per cell per matrix layer (ex2 "
-                                   "for each of the three tanh, ex2 and rcp for the gate's sigmoid)"
-                                   + (" plus two ex2 per (row, action, target) of the collapse" if top ==
-                                      "t2_post_collapse" else "")}
+        if pk is not None:
+            roof = {"kernel": top, "bound": "mufu", "achieved": round(ach, 1), "peak": round(pk["peak_gops"], 1),
+                    "unit": "G MUFU ops/s", "frac": round(ach / pk["peak_gops"], 4), "traffic": traffic,
+                    "traffic_unit": "bytes per launch (dram read + write)", "traffic_source": traffic_src,
+                    "peak_source": f"measured: ex2/rcp probe {pk['per_clock_per_sm']} ops/clk/SM for this kernel's "
+                                   f"ex2:rcp mix x SMs x {pk['sm_mhz']:.0f} MHz (median SM clock sampled during the "
+                                   "timed region)", "mufu_probe": pk["probe"],
+                    "work_per_launch": f"{mufu[top]:.0f} MUFU ops per request: 5 per cell per matrix layer (ex2 "
+                                       "for each of the three tanh, ex2 and rcp for the gate's sigmoid)"
+                                       + (" plus two ex2 per (row, action, target) of the collapse" if top ==
+                                          "t2_post_collapse" else "")}
     ref_gpu = None
-    if rank == 0 and world == 1:
-        ref_gpu = reference_gpu_true2d(args, shape, pop, x, idx, steps=min(args.steps, 50))
+    if ctx.rank == 0 and ctx.world == 1:
+        ref_gpu = reference_gpu_true2d(args, shape, pop, x, idx, steps=min(steps, 50))
         if ref_gpu is not None:
             ro = ref_gpu.pop("output")
             ref_gpu["max_abs_diff_vs_ours"] = float(np.abs(ro - out.reshape(-1)).max())
             ref_gpu["ours_e2e_over_reference"] = round(e2e["value"] / ref_gpu["value"], 3)
-    turn = true2d_turn(args, lib, shape, steps=min(args.steps, 20)) if rank == 0 and world == 1 else None
-    train = true2d_train(args, lib, shape) if rank == 0 and world == 1 else None
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = true2d_cpu_reference(args, shape, pop, per, x, target_s=12.0)
-    if rank == 0:
-        line = {
-            "metric": T2_METRIC, "value": value, "unit": T2_UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * t_dev / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            ref_gpu["ours_device_over_reference"] = round(value / ref_gpu["value"], 3)
+    solo = ctx.rank == 0 and ctx.world == 1
+    turn = true2d_turn(args, lib, shape, steps=min(steps, 20)) if solo else None
+    train = true2d_train(args, lib, shape) if solo else None
+    cpu = true2d_cpu_reference(args, shape, pop, per, x, target_s=cpu_target_s) if solo and not args.no_cpu else None
+    return {"metric": T2_METRIC, "value": value, "unit": T2_UNIT, "steps": steps, "warmup": warmup,
+            "ms_per_step": 1000.0 * t_dev / steps, "dtype": "f32",
             "data": "synthetic (seeded True2DTransformer::seeded models, N(0,1)/2 request rows)",
             "config": {"workload": true2d_workload_name(args, shape), "requests_per_gpu": args.requests,
                        "models": args.models,
                        "l2": f"population of {args.models * per * 4 / 1e6:.0f} MB > 126 MB L2, read every step",
-                       "parallelism": f"replicas x{world} (the reference ABI is single-device)",
+                       "parallelism": f"replicas x{ctx.world} (the reference ABI is single-device)",
                        "value_timing": "sum of the kernel phases' CUDA events per call (expand and matrix layers, "
                                        "attention, matrix layers and collapse; the row upload excluded; the "
                                        "collapse writes the outputs into mapped host memory as it runs, so its "
                                        "time includes their transfer)"},
-            "e2e": e2e, "gpu_launches": 4 * args.steps, "roofline": roof, "cpu_baseline": cpu,
+            "e2e": e2e, "gpu_launches": 4 * steps, "roofline": roof, "cpu_baseline": cpu,
             "reference_gpu": ref_gpu, "clocks": clocks, "kernels": kernels, "copies": copies, "turn": turn,
-            "train": train,
-            "outputs_finite": bool(np.isfinite(out).all()),
-        }
+            "train": train, "outputs_finite": bool(np.isfinite(out).all())}
+
+
+def run_true2d(args) -> None:
+    ctx = Ctx().start()
+    res = true2d_measure(args, ctx, args.steps, args.warmup)
+    if ctx.rank == 0:
+        line = {"metric": res["metric"], "value": res["value"], "unit": T2_UNIT, "n_gpus": ctx.world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None}
+        line.update({k: v for k, v in res.items() if k not in line and k != "metric"})
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    ctx.finish()
 
 
 def main() -> None:
@@ -834,6 +964,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=None, help="override the config's per-GPU batch")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-c5", action="store_true", help="skip the nested config-5 (scale-out) measurement")
+    ap.add_argument("--no-true2d", action="store_true", help="skip the nested True2D drop-in measurement")
     ap.add_argument("--workload", default="policy", choices=["policy", "true2d"],
                     help="policy: the encoder-policy forward (default); true2d: the reference ABI drop-in")
     ap.add_argument("--requests", type=int, default=1024, help="true2d: requests per step")

@@ -65,7 +65,9 @@ OwStatus ow_policy_weight_count(const OwPolicyConfig* config, size_t* count);
 /* Creates a handle on `device`: validates the config, converts and uploads
  * the f32 weight blob (to bf16 / e4m3 + per-channel scales as the precision
  * asks), allocates the batch_capacity workspace. `stream` may be NULL (a
- * handle-owned stream is created). */
+ * handle-owned stream is created). `weights` may be NULL (weight_count still
+ * the config's count): the handle then holds zero weights, for a receiver of
+ * ow_policy_broadcast_weights*. */
 OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, size_t weight_count, int device,
                           void* stream, OwPolicy** out);
 
@@ -107,6 +109,49 @@ OwStatus ow_policy_synchronize(OwPolicy* policy);
 /* Device pointer and byte size of the handle's packed device weights (the
  * tensor a weight broadcast moves), for callers that run their own NCCL. */
 OwStatus ow_policy_device_weights(OwPolicy* policy, void** ptr, size_t* bytes);
+
+/* ---- Weight broadcast over NCCL (NVLink / NVSwitch).
+ * A data-parallel run shards states across GPUs with no exchange on the data
+ * path; the one exchange is the model. These calls move a handle's packed
+ * device weight arena (the bf16 / e4m3 matrices with their scales and the f32
+ * vectors the kernels read, ow_policy_device_weights) from the root rank's
+ * handle into every other rank's, as one ncclBroadcast: no host round trip and
+ * no re-conversion on the receivers. All ranks' handles must have the same
+ * config (the arena layout is a function of the config). A receiver can be
+ * created with weights == NULL (ow_policy_create): it holds zero weights
+ * until the broadcast fills them. Reference counterpart: none in the ABI; the
+ * nearest operation is the population upload (native/cuda/orbit_wars_cuda.cu:
+ * 2772-2800), which copies weights from host memory on one device.
+ * NCCL is loaded at run time: the libnccl.so.2 already in the process, else
+ * $ORBIT_WARS_NCCL_LIB, else libnccl.so.2 from the loader path; without it
+ * these calls return RUNTIME_ERROR. Every wait is bounded by
+ * $ORBIT_WARS_COMM_TIMEOUT_S (default 120 s): a rank that does not join makes
+ * the others return RUNTIME_ERROR with their communicator aborted. */
+typedef struct OwComm OwComm;
+
+/* One process per GPU: one rank calls ow_comm_unique_id (128 bytes into
+ * `id`), the caller shares those bytes over its own channel, then every rank
+ * calls ow_comm_init_rank with them, its rank and its device. */
+OwStatus ow_comm_unique_id(void* id, size_t id_bytes);
+OwStatus ow_comm_init_rank(const void* id, size_t id_bytes, int nranks, int rank, int device, OwComm** out);
+/* One process driving n GPUs (distinct devices): comms[i] is rank i on devices[i]. */
+OwStatus ow_comm_init_all(const int* devices, int n, OwComm** comms);
+OwStatus ow_comm_info(const OwComm* comm, int* rank, int* nranks, int* device);
+void ow_comm_destroy(OwComm* comm);
+
+/* Every rank calls this with its own handle (on the communicator's device):
+ * the root's weights replace the others'. Waits for the handle's forwards in
+ * flight first and returns after the copy completed; *elapsed_ms (may be
+ * NULL) is the broadcast's device time on this rank. */
+OwStatus ow_policy_broadcast_weights_comm(OwPolicy* policy, OwComm* comm, int root, float* elapsed_ms);
+
+/* One process, handles[i] on distinct devices: handles[0]'s weights go to
+ * every other handle (a communicator over those devices is created for the
+ * call and released after it). */
+OwStatus ow_policy_broadcast_weights(OwPolicy** handles, int n_gpus);
+
+/* NCCL version code of the loaded library (e.g. 22809 for 2.28.9). */
+OwStatus ow_nccl_version(int* version);
 
 /* Per-kernel device timing. ow_policy_profile_begin arms CUDA events around
  * every launch of the next `max_forwards` forwards (events only, no host

@@ -23,7 +23,7 @@ REPO = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_DIR = PKG_DIR / "orbit_wars_b200" / "lib"
 LIB = LIB_DIR / "liborbit_wars_cuda.so"
-SOURCES = ["ow_policy.cu", "orbit_wars_true2d.cu"]
+SOURCES = ["ow_policy.cu", "orbit_wars_true2d.cu", "ow_comm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -51,7 +51,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     cmd = [
         nvcc(), "-std=c++17", "-O3", *ARCH, "-lineinfo", "-shared", "-Xcompiler", "-fPIC",
         "-I", str(REPO / "include"), "-I", str(CSRC),
-        "--expt-relaxed-constexpr", *srcs, "-o", str(LIB) + ".tmp",
+        "--expt-relaxed-constexpr", *srcs, "-ldl", "-o", str(LIB) + ".tmp",
     ]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")

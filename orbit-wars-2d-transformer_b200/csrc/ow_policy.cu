@@ -1150,11 +1150,17 @@ OwStatus ow_policy_weight_count(const OwPolicyConfig* config, size_t* count) {
 
 OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, size_t weight_count, int device,
                           void* stream, OwPolicy** out) {
-  if (config == nullptr || weights == nullptr || out == nullptr) return st_bad("null argument");
+  if (config == nullptr || out == nullptr) return st_bad("null argument");
   *out = nullptr;
   if (const char* m = validate_config(*config)) return st_bad(m);
   const BlobLayout lay = blob_layout(*config);
   if (weight_count != lay.total) return st_bad("weight_count does not match the config");
+  // weights == NULL: zero weights, to be filled by a broadcast from another rank
+  std::vector<float> zeros;
+  if (weights == nullptr) {
+    zeros.assign(lay.total, 0.0f);
+    weights = zeros.data();
+  }
   for (size_t i = 0; i < weight_count; ++i)
     if (!std::isfinite(weights[i])) return st_bad("non-finite weight");
   int ndev = 0;

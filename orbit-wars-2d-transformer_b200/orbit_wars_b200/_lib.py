@@ -90,6 +90,14 @@ SIGNATURES = {
     "ow_policy_profile_begin": (Status, [P, C.c_int32]),
     "ow_policy_profile_end": (Status, [P, C.POINTER(KernelTimingC), C.c_int32, C.POINTER(C.c_int32)]),
     "ow_policy_destroy": (None, [P]),
+    "ow_comm_unique_id": (Status, [P, SZ]),
+    "ow_comm_init_rank": (Status, [P, SZ, C.c_int, C.c_int, C.c_int, C.POINTER(P)]),
+    "ow_comm_init_all": (Status, [P, C.c_int, P]),
+    "ow_comm_info": (Status, [P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "ow_comm_destroy": (None, [P]),
+    "ow_policy_broadcast_weights_comm": (Status, [P, P, C.c_int, FP]),
+    "ow_policy_broadcast_weights": (Status, [P, C.c_int]),
+    "ow_nccl_version": (Status, [C.POINTER(C.c_int)]),
     "ow_selftest_gemm": (Status, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, C.c_int, P, P,
                                   P, P]),
     "ow_selftest_ffn": (Status, [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, P, C.c_int, P]),
@@ -110,6 +118,8 @@ SIGNATURES = {
     "orbit_wars_cuda_true2d_play_many_resident": (
         Status, [C.POINTER(GameBatchC), P, P, P, SZ, C.POINTER(EncoderConfigC), P, P, P, P, P, P, True2DShapeC]),
     "orbit_wars_cuda_true2d_profile_begin": (Status, [C.c_int32]),
+    "orbit_wars_cuda_mufu_rate": (Status, [C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                           C.POINTER(C.c_double)]),
     "orbit_wars_cuda_true2d_profile_end": (Status, [C.POINTER(KernelTimingC), C.c_int32, C.POINTER(C.c_int32)]),
     "orbit_wars_cuda_true2d_train_full_attention": (
         Status, [P, P, P, P, P, P, SZ, SZ, True2DShapeC, TrainingConfigC]),

@@ -34,17 +34,33 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
 
 
 class EncoderPolicy:
-    def __init__(self, cfg: PolicyConfig, weights: np.ndarray, device: int = 0, stream: int | None = None,
+    def __init__(self, cfg: PolicyConfig, weights: np.ndarray | None, device: int = 0, stream: int | None = None,
                  io: str = "host", batch_capacity: int | None = None):
+        """weights None: the handle holds zero weights until broadcast_from() fills them."""
         self.lib = _lib.load_library()
         self.cfg = cfg
         self.io = io
+        self.device = device
         self.ccfg = to_config_c(cfg, io, batch_capacity)
-        w = np.ascontiguousarray(weights, dtype=np.float32)
         h = C.c_void_p()
-        _lib.check("ow_policy_create", self.lib.ow_policy_create(
-            C.byref(self.ccfg), w.ctypes.data_as(_lib.FP), w.size, device, stream, C.byref(h)))
+        if weights is None:
+            n = C.c_size_t()
+            _lib.check("ow_policy_weight_count", self.lib.ow_policy_weight_count(C.byref(self.ccfg), C.byref(n)))
+            _lib.check("ow_policy_create", self.lib.ow_policy_create(
+                C.byref(self.ccfg), None, n.value, device, stream, C.byref(h)))
+        else:
+            w = np.ascontiguousarray(weights, dtype=np.float32)
+            _lib.check("ow_policy_create", self.lib.ow_policy_create(
+                C.byref(self.ccfg), w.ctypes.data_as(_lib.FP), w.size, device, stream, C.byref(h)))
         self.handle = h
+
+    def broadcast_from(self, comm: "Comm", root: int = 0) -> float:
+        """Every rank calls this: the root's device weights replace this handle's (one ncclBroadcast of the
+        packed weight arena). Returns this rank's broadcast device time in ms."""
+        ms = C.c_float()
+        _lib.check("ow_policy_broadcast_weights_comm", self.lib.ow_policy_broadcast_weights_comm(
+            self.handle, comm.handle, int(root), C.byref(ms)))
+        return float(ms.value)
 
     def set_weights(self, weights: np.ndarray) -> None:
         w = np.ascontiguousarray(weights, dtype=np.float32)
@@ -134,3 +150,53 @@ class EncoderPolicy:
 
     def __exit__(self, *a):
         self.close()
+
+
+class Comm:
+    """NCCL communicator for the weight broadcast (include/ow_policy.h, "Weight broadcast over NCCL").
+
+        uid = Comm.unique_id()                  # on one rank; share the 128 bytes over any channel
+        comm = Comm(uid, nranks, rank, device)  # on every rank
+        pol.broadcast_from(comm, root=0)
+    """
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int):
+        self.lib = _lib.load_library()
+        buf = C.create_string_buffer(bytes(uid), 128)
+        h = C.c_void_p()
+        _lib.check("ow_comm_init_rank", self.lib.ow_comm_init_rank(buf, 128, int(nranks), int(rank), int(device),
+                                                                    C.byref(h)))
+        self.handle = h
+        self.rank, self.nranks, self.device = int(rank), int(nranks), int(device)
+
+    @staticmethod
+    def unique_id() -> bytes:
+        lib = _lib.load_library()
+        buf = C.create_string_buffer(128)
+        _lib.check("ow_comm_unique_id", lib.ow_comm_unique_id(buf, 128))
+        return buf.raw
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.ow_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def broadcast_weights_all(policies: list["EncoderPolicy"]) -> None:
+    """One process, one handle per GPU: policies[0]'s weights go to the others (ow_policy_broadcast_weights)."""
+    lib = _lib.load_library()
+    arr = (C.c_void_p * len(policies))(*[p.handle.value for p in policies])
+    _lib.check("ow_policy_broadcast_weights", lib.ow_policy_broadcast_weights(arr, len(policies)))
+
+
+def nccl_version() -> int:
+    lib = _lib.load_library()
+    v = C.c_int()
+    _lib.check("ow_nccl_version", lib.ow_nccl_version(C.byref(v)))
+    return v.value

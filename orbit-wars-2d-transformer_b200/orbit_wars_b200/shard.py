@@ -2,7 +2,11 @@
 
 States are independent, so a global batch of world * B states splits into
 contiguous shards with no collective on the data path. The only exchange is
-the weight broadcast from rank 0 (NCCL on GPUs, gloo on CPU test ranks).
+the weight broadcast from rank 0. On GPUs the library does it: one
+ncclBroadcast of the packed device weight arena (EncoderPolicy.broadcast_from),
+over a communicator whose 128-byte id travels through torch.distributed
+(share_comm_id). broadcast_weights moves the f32 blob itself, for CPU ranks
+(gloo) and tests.
 """
 from __future__ import annotations
 
@@ -41,3 +45,16 @@ def broadcast_weights(cfg: PolicyConfig, seed: int, rank: int, device=None) -> n
     if dist.is_initialized() and dist.get_world_size() > 1:
         dist.broadcast(t, src=0)
     return t.cpu().numpy()
+
+
+def share_comm_id(rank: int, uid: bytes | None = None) -> bytes:
+    """The NCCL id (ow_comm_unique_id on rank 0) handed to every rank over the
+    initialised torch.distributed group: host plumbing only, 128 bytes once."""
+    import torch.distributed as dist
+
+    obj = [uid if rank == 0 else None]
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.broadcast_object_list(obj, src=0)
+    if obj[0] is None or len(obj[0]) != 128:
+        raise RuntimeError("communicator id did not arrive")
+    return obj[0]

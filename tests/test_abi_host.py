@@ -19,7 +19,7 @@ def declared_symbols():
     names = set()
     for h in (REPO / "include").glob("*.h"):
         txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
-        names |= set(re.findall(r"\b((?:ow_policy|ow_selftest|orbit_wars)_\w+)\s*\(", txt))
+        names |= set(re.findall(r"\b((?:ow_policy|ow_selftest|ow_comm|ow_nccl|orbit_wars)_\w+)\s*\(", txt))
     return sorted(names)
 
 
@@ -105,3 +105,23 @@ def test_true2d_abi_validates_arguments(lib):
     assert st.code == 1
     st = lib.orbit_wars_cuda_encode_identity_batch(None, None, 1, 1, 1)
     assert st.code == 1
+
+
+def test_nccl_resolves_at_run_time(lib):
+    """The weight broadcast's NCCL is found without linking it (no GPU needed to load it)."""
+    import ctypes as C
+    v = C.c_int()
+    st = lib.ow_nccl_version(C.byref(v))
+    assert st.code == 0, st.message
+    assert v.value >= 21800
+
+
+def test_broadcast_validates_arguments(lib):
+    import ctypes as C
+    assert lib.ow_policy_broadcast_weights(None, 2).code == 1
+    assert lib.ow_policy_broadcast_weights_comm(None, None, 0, None).code == 1
+    h = C.c_void_p()
+    assert lib.ow_comm_init_rank(None, 128, 2, 0, 0, C.byref(h)).code == 1
+    uid = C.create_string_buffer(128)
+    assert lib.ow_comm_init_rank(uid, 128, 2, 2, 0, C.byref(h)).code == 1  # rank outside [0, nranks)
+    assert lib.ow_comm_unique_id(uid, 16).code == 1  # id buffer too short

@@ -39,9 +39,13 @@ def _rank_main(rank, world, port, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     cfg = ow.preset(1)
     w = broadcast_weights(cfg, seed=17, rank=rank)
+    # the communicator id of the library's NCCL weight broadcast travels over the same group
+    from orbit_wars_b200.shard import share_comm_id
+    uid = share_comm_id(rank, bytes(range(128)) if rank == 0 else None)
     feats, counts = shard_inputs(cfg, 17, rank, PER_RANK)
     lg, v, a = bind.policy_forward(cfg, w, feats, counts, f64=False, threads=1)
-    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), w=w, lg=lg, v=v, a=a, counts=counts)
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), w=w, lg=lg, v=v, a=a, counts=counts,
+             uid=np.frombuffer(uid, np.uint8))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -52,6 +56,7 @@ def test_sharded_forward_equals_unsharded(tmp_path, oracle):
     cfg = ow.preset(1)
     ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(WORLD)]
     assert np.array_equal(ranks[0]["w"], ranks[1]["w"])
+    assert all(np.array_equal(r["uid"], np.arange(128, dtype=np.uint8)) for r in ranks)
     assert np.array_equal(ranks[0]["w"], ow.make_weights(cfg, seed=17))
     feats, counts = ow.make_inputs(cfg, batch=WORLD * PER_RANK, seed=17)
     lg, v, a = oracle.policy_forward(cfg, ranks[0]["w"], feats, counts, f64=False, threads=1)
