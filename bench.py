@@ -152,21 +152,22 @@ def kernel_work(cfg, name: str, m_valid: int, sq_counts: int, batch: int) -> tup
     a8 = 1 if cfg.precision == "fp8" else act         # GEMM A operands (e4m3 on the fp8 path)
     ln_out = (act * (L - 1) + 4) / L                  # LN output of the block's last GEMM: f32 after the last layer
     wb = 1 if cfg.precision == "fp8" else act
+    xb = 2 if (cfg.precision != "f32" and d == 256) else 4  # the residual stream: bf16 at d = 256, else f32
     M = float(m_valid)
     if name in ("gemm_qkv", "gemm_f32_qkv"):
         return 2.0 * M * 3 * d * d, M * (d * a8 + 3 * d * act) + 3 * d * d * wb
     if name in ("gemm_out_resid_ln", "gemm_f32_out_resid"):
-        return 2.0 * M * d * d, M * (d * a8 + 8 * d + d * a8) + d * d * wb
+        return 2.0 * M * d * d, M * (d * a8 + 2 * xb * d + d * a8) + d * d * wb
     if name in ("gemm_ffn_up_gelu", "gemm_f32_ffn_up"):
         return 2.0 * M * f * d, M * (d * a8 + f * act) + f * d * wb
     if name in ("gemm_ffn_down_resid_ln", "gemm_f32_ffn_down_resid"):
-        return 2.0 * M * d * f, M * (f * a8 + 8 * d + d * ln_out) + d * f * wb
+        return 2.0 * M * d * f, M * (f * a8 + 2 * xb * d + d * ln_out) + d * f * wb
     if name == "ffn_fused":
         return 4.0 * M * d * f, M * (d * a8 + 8 * d + d * ln_out) + 2 * d * f * wb
     if name == "attention":
         return 4.0 * sq_counts * d, M * (3 * d * act + d * act)
     if name == "embed_ln":
-        return 2.0 * M * F * d, M * (F * 4 + 4 * d + d * a8)
+        return 2.0 * M * F * d, M * (F * 4 + xb * d + d * a8)
     if name == "heads":
         lb = 4 if cfg.logits_dtype == "f32" else 2
         return 2.0 * M * d * (P + 1), M * (4 * d + 4) + batch * N * (P * lb + 4)
@@ -293,9 +294,9 @@ class Ctx:
             # NCCL's init lines (rank counts of every communicator, torch's and the library's) go to a
             # per-process file and are echoed to stderr at the end: stdout carries one JSON line only
             self.nccl_log = Path(tempfile.gettempdir()) / f"ow_nccl_{os.getpid()}.log"
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-            os.environ.setdefault("NCCL_DEBUG_FILE", str(self.nccl_log))
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+            os.environ["NCCL_DEBUG_FILE"] = str(self.nccl_log)
             dist.init_process_group("nccl", device_id=self.dev, timeout=timedelta(seconds=120))
             # the weight broadcast's communicator: its 128-byte id travels over torch.distributed
             from orbit_wars_b200.policy import Comm

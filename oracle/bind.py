@@ -132,6 +132,7 @@ def policy_forward(cfg, weights, features, counts, f64: bool = True, threads: in
 
 # rounding points of owo_policy_forward_emulated (ow_policy_oracle.cpp)
 EMU_STORE_BF16, EMU_QUANT_QKV, EMU_QUANT_OUT, EMU_QUANT_UP, EMU_QUANT_DOWN, EMU_VALUE_BF16 = 1, 2, 4, 8, 16, 32
+EMU_RESID_BF16 = 64
 EMU_QUANT_ALL = EMU_QUANT_QKV | EMU_QUANT_OUT | EMU_QUANT_UP | EMU_QUANT_DOWN
 
 
@@ -139,9 +140,10 @@ def recipe_mode(cfg) -> int:
     """The full rounding recipe of cfg's precision path (0 for fp32)."""
     if cfg.precision == "f32":
         return 0
+    resid = EMU_RESID_BF16 if cfg.d_model == 256 else 0  # the d = 256 tensor-core paths keep x in bf16
     if cfg.precision == "bf16":
-        return EMU_STORE_BF16
-    return EMU_STORE_BF16 | EMU_QUANT_ALL | EMU_VALUE_BF16
+        return EMU_STORE_BF16 | resid
+    return EMU_STORE_BF16 | EMU_QUANT_ALL | EMU_VALUE_BF16 | resid
 
 
 def policy_forward_emulated(cfg, weights, features, counts, mode: int | None = None, threads: int = 0):

@@ -291,6 +291,8 @@ void forward_state(const Prepared<T>& p, const float* feat, int count, size_t st
 // measured apart from the kernels' arithmetic error. Rounding points:
 //   kStoreBf16    features, QKV, softmax P, attention output, GELU output,
 //                 bf16 LayerNorm outputs, logits (and value on the fp8 path)
+//   kResidBf16    the residual stream between residual adds (the d = 256
+//                 tensor-core paths keep it in bf16)
 //   kQuantQkv .. kQuantDown  e4m3 operands of one block GEMM: per-token scale
 //                 s = absmax/448 (1 for an all-zero row), q = e4m3(v/s) RNE
 //                 saturating, the GEMM sums q_a*q_w*s_a*s_w exactly
@@ -303,6 +305,7 @@ enum : unsigned {
   kQuantUp = 8u,
   kQuantDown = 16u,
   kValueBf16 = 32u,
+  kResidBf16 = 64u,  // the residual stream is kept in bf16 between the residual adds
 };
 
 double round_bf16(double v) {
@@ -365,18 +368,26 @@ void forward_state_emu(const Prepared<double>& p, unsigned mode, const float* fe
   std::vector<double> ft(N * F);
   for (size_t i = 0; i < N * F; ++i) ft[i] = bf ? round_bf16(feat[i]) : feat[i];
   linear<double>(ft.data(), Nv, F, p.we_t.data(), d, w + p.off.be, x.data());
-  // the bf16 / fp8 kernels keep the residual stream x in f32 (mode 0 is the plain float64 forward)
-  auto store_x = [&](double v) { return mode != 0 ? static_cast<double>(static_cast<float>(v)) : v; };
-  for (size_t i = 0; i < Nv * d; ++i) x[i] = store_x(x[i]);
+  // The kernels form each residual sum in f32 (mode 0 is the plain float64
+  // forward) and take its LayerNorm from that sum; the stream then keeps it in
+  // f32, or in bf16 (kResidBf16), for the next residual add.
+  auto sum_x = [&](double v) { return mode != 0 ? static_cast<double>(static_cast<float>(v)) : v; };
+  auto keep_x = [&]() {
+    if (mode & kResidBf16) round_all_bf16(x, Nv * d);
+  };
+  for (size_t i = 0; i < Nv * d; ++i) x[i] = sum_x(x[i]);
   auto ln_out = [&](const float* g, const float* b, bool quant) {
     layer_norm<double>(x.data(), Nv, d, g, b, a.data());
     if (quant) quantize_rows(a, Nv, d);
     else if (bf) round_all_bf16(a, Nv * d);
   };
   const double scale = 1.0 / std::sqrt(static_cast<double>(hd));
+  if (s.layers > 0) {
+    ln_out(w + p.off.layer[0].ln1g, w + p.off.layer[0].ln1b, (mode & kQuantQkv) != 0);
+    keep_x();
+  }
   for (int l = 0; l < s.layers; ++l) {
     const auto& L = p.off.layer[l];
-    ln_out(w + L.ln1g, w + L.ln1b, (mode & kQuantQkv) != 0);
     linear<double>(a.data(), Nv, d, p.wqkv_t[l].data(), 3 * d, w + L.bqkv, qkv.data());
     if (bf) round_all_bf16(qkv, Nv * 3 * d);
     std::fill(o.begin(), o.end(), 0.0);
@@ -404,17 +415,24 @@ void forward_state_emu(const Prepared<double>& p, unsigned mode, const float* fe
     if (bf) round_all_bf16(o, Nv * d);
     if (mode & kQuantOut) quantize_rows(o, Nv, d);
     linear<double>(o.data(), Nv, d, p.wo_t[l].data(), d, w + L.bo, t.data());
-    for (size_t i = 0; i < Nv * d; ++i) x[i] = store_x(x[i] + t[i]);
+    for (size_t i = 0; i < Nv * d; ++i) x[i] = sum_x(x[i] + t[i]);
     ln_out(w + L.ln2g, w + L.ln2b, (mode & kQuantUp) != 0);
+    keep_x();
     linear<double>(a.data(), Nv, d, p.w1_t[l].data(), f, w + L.b1, h.data());
     for (size_t i = 0; i < Nv * f; ++i) h[i] = gelu<double>(h[i]);
     if (bf) round_all_bf16(h, Nv * f);
     if (mode & kQuantDown) quantize_rows(h, Nv, f);
     linear<double>(h.data(), Nv, f, p.w2_t[l].data(), d, w + L.b2, t.data());
-    for (size_t i = 0; i < Nv * d; ++i) x[i] = store_x(x[i] + t[i]);
+    for (size_t i = 0; i < Nv * d; ++i) x[i] = sum_x(x[i] + t[i]);
+    if (l + 1 < s.layers) {
+      ln_out(w + p.off.layer[l + 1].ln1g, w + p.off.layer[l + 1].ln1b, (mode & kQuantQkv) != 0);
+      keep_x();
+    } else {
+      // final LN stays f32 (heads read y in f32)
+      layer_norm<double>(x.data(), Nv, d, w + p.off.lnf_g, w + p.off.lnf_b, a.data());
+    }
   }
-  // final LN stays f32 (heads read y in f32)
-  layer_norm<double>(x.data(), Nv, d, w + p.off.lnf_g, w + p.off.lnf_b, a.data());
+  if (s.layers == 0) layer_norm<double>(x.data(), Nv, d, w + p.off.lnf_g, w + p.off.lnf_b, a.data());
   std::vector<double> lg(P);
   for (size_t j = 0; j < N; ++j) {
     float* out = logits + j * P;

@@ -493,13 +493,14 @@ constexpr int kHeadsMinBlocks = 6;
 // its columns shifted by its first value; the four lanes of a quad, which
 // share a row, merge mean and M2 exactly, Chan et al.), [pass 2 e4m3 row
 // absmax], last pass writes x (f32) and the LN output.
-template <int D, int LN_MODE>  // LN_MODE 1: bf16 out; 2: e4m3 out + per-row scale
+// XB: the residual stream x is stored as bf16 (else f32).
+template <int D, int LN_MODE, bool XB>  // LN_MODE 1: bf16 out; 2: e4m3 out + per-row scale
 __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const float* __restrict__ feats, const int* __restrict__ offsets,
                                                         int batch, int n_entities, int n_feat,
                                                         const __nv_bfloat16* __restrict__ w_e16,  // [D][32] bf16
                                                         const float* __restrict__ b_e,
                                                         const float* __restrict__ g, const float* __restrict__ beta,
-                                                        float* __restrict__ x, void* __restrict__ ln_out,
+                                                        void* __restrict__ x, void* __restrict__ ln_out,
                                                         float* __restrict__ ln_scale, int* __restrict__ row_slot) {
   constexpr int WP = 40;  // bf16 pitch of staged rows (32 features + pad: conflict-free ldmatrix)
   constexpr int kGW = kEmbedGroupCols;  // output columns per MMA pass (accumulators: kGW / 2 registers)
@@ -636,7 +637,11 @@ __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const f
               a1 = fmaxf(a1, fmaxf(fabsf(y10), fabsf(y11)));
             } else {
               if (ra < M) {
-                *reinterpret_cast<float2*>(x + static_cast<size_t>(ra) * D + col) = make_float2(v00, v01);
+                if (XB)
+                  *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(x) + static_cast<size_t>(ra) * D + col) =
+                      pack_bf16x2(v00, v01);
+                else
+                  *reinterpret_cast<float2*>(reinterpret_cast<float*>(x) + static_cast<size_t>(ra) * D + col) = make_float2(v00, v01);
                 if (LN_MODE == 1)
                   *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(ln_out) + static_cast<size_t>(ra) * D + col) =
                       pack_bf16x2(y00, y01);
@@ -645,7 +650,11 @@ __global__ void __launch_bounds__(128, kEmbedMinBlocks) embed_mma_kernel(const f
                       __nv_cvt_float2_to_fp8x2(make_float2(y00 * inv0, y01 * inv0), __NV_SATFINITE, __NV_E4M3);
               }
               if (rb < M) {
-                *reinterpret_cast<float2*>(x + static_cast<size_t>(rb) * D + col) = make_float2(v10, v11);
+                if (XB)
+                  *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(x) + static_cast<size_t>(rb) * D + col) =
+                      pack_bf16x2(v10, v11);
+                else
+                  *reinterpret_cast<float2*>(reinterpret_cast<float*>(x) + static_cast<size_t>(rb) * D + col) = make_float2(v10, v11);
                 if (LN_MODE == 1)
                   *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(ln_out) + static_cast<size_t>(rb) * D + col) =
                       pack_bf16x2(y10, y11);

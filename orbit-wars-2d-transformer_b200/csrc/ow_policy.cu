@@ -232,7 +232,10 @@ struct OwPolicy {
   CUtensorMap e_ln, e_y;               // LayerNorm outputs: ln (bf16 or e4m3), y (f32, final LN)
   int qkv_block_n = 256;
   bool pdl = false;       // tensor-core path: programmatic dependent launches (ORBIT_WARS_PDL=0 turns them off)
-  bool fuse_ffn = false;  // ORBIT_WARS_FFN_FUSED=1 at create selects the fused FFN kernel (d = 256, bf16)
+  bool fuse_ffn = false;  // ORBIT_WARS_FFN_FUSED=1 at create selects the fused FFN kernel (d = 256, bf16, f32 x)
+  // bf16 residual stream x (the spec's bf16 storage) with the 16-warp LayerNorm
+  // epilogue: the tensor-core paths at d = 256 (ORBIT_WARS_X_F32=1 keeps f32)
+  bool x16 = false;
   int launches = 0;
   // host-IO submissions (ow_policy_submit / ow_policy_wait): two slots, each
   // with its own device inputs, outputs and error word. Uploads run on
@@ -338,7 +341,8 @@ cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensor
   using S = TcGemmShape<BN, EPI>;
   const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM) * (prm.n / BN);
   const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
-  if (prm.n * ((FP8 ? 2 : 1) + (EPI == kEpiResidLn ? 2 : 0)) > S::kParamFloats) return cudaErrorInvalidValue;
+  if (prm.n * ((FP8 ? 2 : 1) + ((EPI == kEpiResidLn || EPI == kEpiResidLn16) ? 2 : 0)) > S::kParamFloats)
+    return cudaErrorInvalidValue;
   return launch_k(P, tc_gemm_kernel<BN, EPI, FP8>, grid, EpiWarps<EPI>::kThreads, S::kSmemBytes, ma, mw, mo, ml, prm);
 }
 
@@ -346,6 +350,10 @@ cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensor
 cudaError_t launch_gemm_resid_ln(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw,
                                  const CUtensorMap& mx, const CUtensorMap& ml, const TcGemmParams& prm, bool fp8) {
   const int d = P.cfg.d_model;
+  if (P.x16) {
+    if (fp8) return launch_gemm<256, kEpiResidLn16, true>(P, ma, mw, mx, ml, prm);
+    return launch_gemm<256, kEpiResidLn16, false>(P, ma, mw, mx, ml, prm);
+  }
   if (fp8) return launch_gemm<256, kEpiResidLn, true>(P, ma, mw, mx, ml, prm);
   switch (d) {
     case 128: return launch_gemm<128, kEpiResidLn, false>(P, ma, mw, mx, ml, prm);
@@ -359,7 +367,7 @@ cudaError_t launch_gemm_resid_ln(const OwPolicy& P, const CUtensorMap& ma, const
 // multiple of 128 with b1, b2, gamma and beta staged in shared memory.
 bool ffn_fused(const OwPolicy& P) {
   const auto& c = P.cfg;
-  return P.fuse_ffn && c.precision == OW_PRECISION_BF16 && c.d_model == 256 && c.ffn % 128 == 0 &&
+  return P.fuse_ffn && !P.x16 && c.precision == OW_PRECISION_BF16 && c.d_model == 256 && c.ffn % 128 == 0 &&
          c.ffn + 3 * c.d_model <= TcFfnShape<256>::kParamFloats;
 }
 
@@ -386,6 +394,8 @@ cudaError_t set_all_gemm_attrs() {
   upd(set_gemm_attr<256, kEpiBias, true>());
   upd(set_gemm_attr<256, kEpiBiasGelu, true>());
   upd(set_gemm_attr<256, kEpiResidLn, true>());
+  upd(set_gemm_attr<256, kEpiResidLn16, false>());
+  upd(set_gemm_attr<256, kEpiResidLn16, true>());
   upd(cudaFuncSetAttribute(tc_ffn_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            TcFfnShape<256>::kSmemBytes));
   return e;
@@ -410,19 +420,33 @@ cudaError_t launch_embed(const OwPolicy& P, int batch) {
     // a warp takes 16 packed rows at a time; one wave of resident CTAs, each staging W_e once
     const int eg = static_cast<int>(std::max<size_t>(1, std::min<size_t>((P.cap_rows + 63) / 64,
                                                                           static_cast<size_t>(P.num_sms) * kEmbedMinBlocks)));
-    if (c.precision == OW_PRECISION_BF16) {
-      auto k = embed_mma_kernel<D, 1>;
+    if (c.precision == OW_PRECISION_BF16 && P.x16) {
+      auto k = embed_mma_kernel<D, 1, true>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
       return launch_k(P, k, eg, 128, esmem, static_cast<const float*>(P.feats), static_cast<const int*>(P.offsets),
                       batch, c.n_entities, c.features, static_cast<const __nv_bfloat16*>(P.we16),
-                      static_cast<const float*>(P.be), g, b, static_cast<float*>(P.x), static_cast<void*>(P.ln),
+                      static_cast<const float*>(P.be), g, b, P.x, static_cast<void*>(P.ln),
                       static_cast<float*>(nullptr), P.row_slot);
-    } else {
-      auto k = embed_mma_kernel<D, 2>;
+    } else if (c.precision == OW_PRECISION_BF16) {
+      auto k = embed_mma_kernel<D, 1, false>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
       return launch_k(P, k, eg, 128, esmem, static_cast<const float*>(P.feats), static_cast<const int*>(P.offsets),
                       batch, c.n_entities, c.features, static_cast<const __nv_bfloat16*>(P.we16),
-                      static_cast<const float*>(P.be), g, b, static_cast<float*>(P.x), static_cast<void*>(P.ln8),
+                      static_cast<const float*>(P.be), g, b, P.x, static_cast<void*>(P.ln),
+                      static_cast<float*>(nullptr), P.row_slot);
+    } else if (P.x16) {
+      auto k = embed_mma_kernel<D, 2, true>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
+      return launch_k(P, k, eg, 128, esmem, static_cast<const float*>(P.feats), static_cast<const int*>(P.offsets),
+                      batch, c.n_entities, c.features, static_cast<const __nv_bfloat16*>(P.we16),
+                      static_cast<const float*>(P.be), g, b, P.x, static_cast<void*>(P.ln8),
+                      P.ln_scale, P.row_slot);
+    } else {
+      auto k = embed_mma_kernel<D, 2, false>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(esmem));
+      return launch_k(P, k, eg, 128, esmem, static_cast<const float*>(P.feats), static_cast<const int*>(P.offsets),
+                      batch, c.n_entities, c.features, static_cast<const __nv_bfloat16*>(P.we16),
+                      static_cast<const float*>(P.be), g, b, P.x, static_cast<void*>(P.ln8),
                       P.ln_scale, P.row_slot);
     }
   }
@@ -992,9 +1016,13 @@ OwStatus alloc_workspace(OwPolicy& P, int cap_states) {
            make_kmajor_map(&P.m_h, P.h, false, f, rows, 128);
     ok = ok && make_out_map(&P.e_qkv, P.qkv, 3 * d, rows, ow::EpiWarps<ow::kEpiBias>::kChunkCols) &&
          make_out_map(&P.e_h, P.h, f, rows, ow::EpiWarps<ow::kEpiBiasGelu>::kChunkCols) &&
-         make_map_128b(&P.e_x, P.x, kMapF32, d, rows, 32) &&
-         make_ln_map(&P.e_y, P.y, kMapF32, d, rows) &&
-         (e4 ? make_ln_map(&P.e_ln, P.ln8, kMapU8, d, rows) : make_ln_map(&P.e_ln, P.ln, kMapBf16, d, rows));
+         make_ln_map(&P.e_y, P.y, kMapF32, d, rows);
+    if (P.x16)  // 64-column boxes: x (bf16, 128 B rows), LN out (bf16 128 B rows or e4m3 64 B rows)
+      ok = ok && make_map_128b(&P.e_x, P.x, kMapBf16, d, rows, 32) &&
+           (e4 ? make_map_box(&P.e_ln, P.ln8, kMapU8, d, rows, 64, 32) : make_map_128b(&P.e_ln, P.ln, kMapBf16, d, rows, 32));
+    else
+      ok = ok && make_map_128b(&P.e_x, P.x, kMapF32, d, rows, 32) &&
+           (e4 ? make_ln_map(&P.e_ln, P.ln8, kMapU8, d, rows) : make_ln_map(&P.e_ln, P.ln, kMapBf16, d, rows));
     if (!ok) return st_rt("cuTensorMapEncodeTiled failed for an activation buffer");
   }
   OW_TRY(cudaStreamSynchronize(P.stream));
@@ -1182,6 +1210,8 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
     P->fuse_ffn = e != nullptr && e[0] == '1';
     const char* q = std::getenv("ORBIT_WARS_PDL");
     P->pdl = config->precision != OW_PRECISION_F32 && !(q != nullptr && q[0] == '0');
+    const char* xf = std::getenv("ORBIT_WARS_X_F32");
+    P->x16 = config->precision != OW_PRECISION_F32 && config->d_model == 256 && !(xf != nullptr && xf[0] == '1');
   }
   if (stream != nullptr) {
     P->stream = static_cast<cudaStream_t>(stream);
@@ -1432,7 +1462,11 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || w == nullptr || bias == nullptr) return st_bad("bad selftest args");
   if (k % (fp8 ? 128 : 64) != 0) return st_bad("k must be a multiple of 128 bytes");
   int bn = 0;
-  if (epilogue == kEpiResidLn) {
+  if (epilogue == kEpiResidLn16) {  // bf16 residual stream (resid points at bf16 values)
+    if (resid == nullptr || ln_g == nullptr || ln_b == nullptr || ln_out == nullptr) return st_bad("bad ln args");
+    if (n != 256) return st_bad("the bf16-residual LayerNorm epilogue needs n = 256");
+    bn = n;
+  } else if (epilogue == kEpiResidLn) {
     if (resid == nullptr || ln_g == nullptr || ln_b == nullptr || ln_out == nullptr) return st_bad("bad ln args");
     if (!(n == 128 || n == 256 || n == 384 || n == 512) || (fp8 && n != 256)) return st_bad("unsupported ln width");
     bn = n;
@@ -1459,7 +1493,12 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   if (!make_kmajor_map(&ma, a, fp8, k, m, 128) || !make_kmajor_map(&mw, w, fp8, k, n, box_rows))
     return st_rt("cuTensorMapEncodeTiled failed");
   bool mok;
-  if (epilogue == kEpiResidLn) {
+  if (epilogue == kEpiResidLn16) {
+    mok = make_map_128b(&mo, resid, kMapBf16, n, m, 32) &&
+          (ln_mode == kLnF32 ? make_ln_map(&ml, ln_out, kMapF32, n, m)
+                             : (ln_mode == kLnE4m3 ? make_map_box(&ml, ln_out, kMapU8, n, m, 64, 32)
+                                                   : make_map_128b(&ml, ln_out, kMapBf16, n, m, 32)));
+  } else if (epilogue == kEpiResidLn) {
     const MapType lt = ln_mode == kLnF32 ? kMapF32 : (ln_mode == kLnE4m3 ? kMapU8 : kMapBf16);
     mok = make_map_128b(&mo, resid, kMapF32, n, m, 32) && make_ln_map(&ml, ln_out, lt, n, m);
   } else {
@@ -1491,7 +1530,11 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   q.a_scale = a_scale;
   q.b_scale = b_scale;
   if (e == cudaSuccess) {
-    if (epilogue == kEpiResidLn) {
+    if (epilogue == kEpiResidLn16) {
+      P.cfg.d_model = n;
+      P.x16 = true;
+      e = launch_gemm_resid_ln(P, ma, mw, mo, ml, q, fp8);
+    } else if (epilogue == kEpiResidLn) {
       P.cfg.d_model = n;
       e = launch_gemm_resid_ln(P, ma, mw, mo, ml, q, fp8);
     } else if (epilogue == kEpiBias) {

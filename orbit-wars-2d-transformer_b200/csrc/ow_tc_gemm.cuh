@@ -43,7 +43,7 @@
 
 namespace ow {
 
-enum EpiMode : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidLn = 2 };
+enum EpiMode : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidLn = 2, kEpiResidLn16 = 3 };
 enum LnMode : int { kLnBf16 = 0, kLnE4m3 = 1, kLnF32 = 2 };
 
 struct TcGemmParams {
@@ -85,7 +85,9 @@ constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 // output chunk (one TMA store box of 32 rows: 32 columns = 64 B rows, 64 = 128 B).
 template <int EPI>
 struct EpiWarps {
-  static constexpr int kCount = EPI == kEpiResidLn ? 8 : (EPI == kEpiBias ? OW_BIAS_EPI_WARPS : OW_GELU_EPI_WARPS);
+  static constexpr int kCount = EPI == kEpiResidLn ? 8
+                                : EPI == kEpiResidLn16 ? 16
+                                : (EPI == kEpiBias ? OW_BIAS_EPI_WARPS : OW_GELU_EPI_WARPS);
   static constexpr int kThreads = 64 + 32 * kCount;
   static constexpr int kChunkCols = EPI == kEpiBias ? OW_BIAS_CHUNK_COLS : OW_GELU_CHUNK_COLS;
   static_assert(kChunkCols == 32 || kChunkCols == 64, "output chunks of 64 B or 128 B rows");
@@ -109,17 +111,20 @@ struct TcGemmShape {
                                    : kTmemColsNeeded <= 128 ? 128
                                    : kTmemColsNeeded <= 256 ? 256 : 512;
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kParamFloats = EPI == kEpiResidLn ? 2048 : 4096;  // staged bias/scale/g/b vectors
+  static constexpr int kParamFloats = EPI == kEpiResidLn ? 2048 : (EPI == kEpiResidLn16 ? 1024 : 4096);  // staged bias/scale/g/b vectors
   static constexpr int kParamBytes = kParamFloats * 4;
   // staging tiles (4 KB) per epilogue warp, used by the TMA loads of the
   // residual and the TMA stores of the outputs: 2, or 1 at d = 512 (budget)
-  static constexpr int kTilesPerWarp = (EPI == kEpiResidLn && BLOCK_N > 384) ? 1 : 2;
+  // (the bf16-residual LayerNorm epilogue keeps one tile per warp: its 32 rows x
+  // 64 columns of the residual, rewritten in place by x and then the LN output)
+  static constexpr int kTilesPerWarp = ((EPI == kEpiResidLn && BLOCK_N > 384) || EPI == kEpiResidLn16) ? 1 : 2;
   // bias/GELU epilogues stage 32 rows x kChunkCols bf16 columns; LayerNorm 32 x 128 B
-  static constexpr int kTileBytes = EPI == kEpiResidLn ? 4096 : 32 * EpiWarps<EPI>::kChunkCols * 2;
+  static constexpr int kTileBytes = (EPI == kEpiResidLn || EPI == kEpiResidLn16) ? 4096 : 32 * EpiWarps<EPI>::kChunkCols * 2;
   static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * kTilesPerWarp * kTileBytes;
   // LayerNorm: per-row partial statistics exchanged between the two warps of a
   // lane quadrant: [2 parities][8 warps][32 lanes] x (mean, M2, amax, pad)
-  static constexpr int kStatsBytes = EPI == kEpiResidLn ? 2 * 8 * 32 * 16 : 0;
+  // bf16-residual LayerNorm: (mean, M2) float2 and amax per [2 parities][16 warps][32 lanes]
+  static constexpr int kStatsBytes = EPI == kEpiResidLn ? 2 * 8 * 32 * 16 : (EPI == kEpiResidLn16 ? 2 * 16 * 32 * 12 : 0);
   static constexpr int kFixedBytes = kBarrierBytes + kParamBytes + kXposeBytes + kStatsBytes + 1024;  // + align slack
   static constexpr int kStagesFit = (kSmemLimit - kFixedBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
@@ -130,6 +135,7 @@ struct TcGemmShape {
   static_assert(kTmemColsNeeded <= 512, "TMEM has 512 columns");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory per CTA");
   static_assert(kStageBytes % 1024 == 0 && kXposeBytes % 1024 == 0, "swizzled tiles stay 1024 B aligned");
+  static_assert(EPI != kEpiResidLn16 || BLOCK_N == 256, "bf16-residual LayerNorm epilogue: d = 256 (64 columns per warp)");
 };
 
 // 16 B chunk j of row r of a 32 x 128 B staging tile (128 B swizzle).
@@ -153,6 +159,12 @@ __device__ __forceinline__ void pair_sync(uint64_t* bar, uint32_t& phase, volati
   mbar_arrive(bar);
   mbar_wait(bar, phase, abort, err);
   phase ^= 1u;
+}
+__device__ __forceinline__ bool pair_sync_ok(uint64_t* bar, uint32_t& phase, volatile int* abort, int* err) {
+  mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase, abort, err);
+  phase ^= 1u;
+  return ok;
 }
 
 // Residual add + LayerNorm over a full row (BLOCK_N == n == d) for one
@@ -375,6 +387,201 @@ __device__ __forceinline__ void resid_ln_epilogue(uint32_t tbase, uint8_t* tiles
   }
 }
 
+// Residual add + LayerNorm with a bf16 residual stream, 16 epilogue warps
+// (kEpiResidLn16, d = 256). Warp ew owns TMEM lane quadrant `quad` (32 rows,
+// thread `lane` = row row_base + lane) and columns [64*(ew/4), +64) of them.
+// Its staging tile receives those 32 rows x 64 bf16 columns of the residual
+// (128 B rows, 128 B swizzle) by TMA when the tile starts, so they land while
+// the MMAs run. Then
+//   pass 1: v = x + acc*s + bias in packed f32x2 arithmetic, written back to
+//           TMEM; shifted sums of the warp's 64 values per row;
+//   merge:  the quadrant's four (mean, M2) partials meet in shared memory
+//           (parity-double-buffered) at a 128-arrival mbarrier, and every warp
+//           merges them in the same order (Chan et al., equal counts);
+//   [fp8:   an absmax pass and a second rendezvous give the row's e4m3 scale;]
+//   pass 2: x = bf16(v) into the staging tile in place of the residual (each
+//           thread rewrites only its own row) and a TMA store; the LayerNorm
+//           output is computed while that store reads the tile, then leaves
+//           through the same tile (bf16: one 64-column box; e4m3: a 64 B-row
+//           box; f32, the final LayerNorm: two 32-column boxes in turn).
+// Row-per-thread global stores instead of the staging tile measured slower
+// (each warp store touches 32 cache lines). The epilogue is issue-bound (the
+// tensor cores run the next tile's MMAs on the other TMEM accumulator
+// meanwhile), hence the packed arithmetic. The caller has issued the
+// residual load on *xbar (phase parity xpar).
+template <bool FP8>
+__device__ __forceinline__ void resid_ln16_epilogue(uint32_t tbase, uint8_t* tile, uint64_t* xbar, uint32_t& xpar,
+                                                    float2* st, float* st_amax, const float* s_bias,
+                                                    const float* s_bscale, const float* s_g, const float* s_b,
+                                                    const CUtensorMap* map_x, const CUtensorMap* map_l,
+                                                    const TcGemmParams& p, volatile int* abort_flag,
+                                                    uint64_t* quad_bar, uint32_t& quad_phase, int ew, int lane,
+                                                    int row_base, int m, bool live, float a_s) {
+  constexpr int kCols = 64;  // per warp
+  constexpr int kChunks = kCols / 32;
+  constexpr int kD = 256;
+  const int cbase = (ew >> 2) * kCols;
+  const int q0 = ew & 3;  // this quadrant's warps are q0, q0+4, q0+8, q0+12
+  bool ok = mbar_wait(xbar, xpar, abort_flag, p.err);
+  xpar ^= 1u;
+  float2 shift = make_float2(0.0f, 0.0f);
+  float2 s1 = make_float2(0.0f, 0.0f), s2 = make_float2(0.0f, 0.0f);
+  uint32_t ra[32], rb[32];
+  tmem_ld32(tbase + cbase, ra);
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    uint32_t(&r)[32] = (c & 1) ? rb : ra;
+    uint32_t(&rn)[32] = (c & 1) ? ra : rb;
+    tmem_ld_wait_dep(r);
+    if (c + 1 < kChunks) tmem_ld32(tbase + cbase + (c + 1) * 32, rn);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 16-byte chunk 4c+q of this thread's row: 8 bf16 residual values
+      const uint4 u = *xpose_slot(tile, lane, 4 * c + q);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {  // 4 columns at a time
+        const int i = 8 * q + 4 * h;
+        const int col = cbase + c * 32 + i;
+        const float4 bv = *reinterpret_cast<const float4*>(s_bias + col);
+        float2 v0 = make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+        float2 v1 = make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+        if (FP8) {
+          const float4 sv = *reinterpret_cast<const float4*>(s_bscale + col);
+          v0 = mul_f2(v0, make_float2(a_s * sv.x, a_s * sv.y));
+          v1 = mul_f2(v1, make_float2(a_s * sv.z, a_s * sv.w));
+        }
+        v0 = add_f2(add_f2(v0, make_float2(bv.x, bv.y)), bf16x2_to_f2(uw[2 * h]));
+        v1 = add_f2(add_f2(v1, make_float2(bv.z, bv.w)), bf16x2_to_f2(uw[2 * h + 1]));
+        if (c == 0 && i == 0) shift = make_float2(v0.x, v0.x);
+        const float2 d0 = sub_f2(v0, shift), d1 = sub_f2(v1, shift);
+        s1 = add_f2(s1, add_f2(d0, d1));
+        s2 = fma_f2(d0, d0, fma_f2(d1, d1, s2));
+        r[i] = __float_as_uint(v0.x);
+        r[i + 1] = __float_as_uint(v0.y);
+        r[i + 2] = __float_as_uint(v1.x);
+        r[i + 3] = __float_as_uint(v1.y);
+      }
+    }
+    tmem_st32(tbase + cbase + c * 32, r);
+  }
+  {
+    const float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+    st[ew * 32 + lane] = make_float2(shift.x + t1 * (1.0f / kCols), fmaxf(t2 - t1 * t1 * (1.0f / kCols), 0.0f));
+  }
+  tmem_st_wait();
+  if (!pair_sync_ok(quad_bar, quad_phase, abort_flag, p.err)) ok = false;
+  // merge the four equal-count partials: (0,1), (2,3), then the two pairs
+  const float2 w0 = st[(q0 + 0) * 32 + lane], w1 = st[(q0 + 4) * 32 + lane];
+  const float2 w2 = st[(q0 + 8) * 32 + lane], w3 = st[(q0 + 12) * 32 + lane];
+  const float d01 = w1.x - w0.x, d23 = w3.x - w2.x;
+  const float m01 = 0.5f * (w0.x + w1.x), m23 = 0.5f * (w2.x + w3.x);
+  const float M01 = w0.y + w1.y + d01 * d01 * (0.5f * kCols);
+  const float M23 = w2.y + w3.y + d23 * d23 * (0.5f * kCols);
+  const float dd = m23 - m01;
+  const float mean = 0.5f * (m01 + m23);
+  const float var = (M01 + M23 + dd * dd * kCols) * (1.0f / kD);
+  const float rstd = rsqrtf(var + 1e-5f);
+  const float2 mean2 = make_float2(mean, mean), rstd2 = make_float2(rstd, rstd);
+  float inv_scale = 1.0f;
+  if (p.ln_mode == kLnE4m3) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tbase + cbase + c * 32, r);
+      tmem_ld_wait_dep(r);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int col = cbase + c * 32 + i;
+        const float2 y = fma_f2(mul_f2(sub_f2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), mean2), rstd2),
+                                *reinterpret_cast<const float2*>(s_g + col), *reinterpret_cast<const float2*>(s_b + col));
+        amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
+      }
+    }
+    st_amax[ew * 32 + lane] = amax;
+    if (!pair_sync_ok(quad_bar, quad_phase, abort_flag, p.err)) ok = false;
+    amax = fmaxf(fmaxf(st_amax[(q0 + 0) * 32 + lane], st_amax[(q0 + 4) * 32 + lane]),
+                 fmaxf(st_amax[(q0 + 8) * 32 + lane], st_amax[(q0 + 12) * 32 + lane]));
+    const float scale = amax > 0.0f ? amax * (1.0f / 448.0f) : 1.0f;
+    inv_scale = 1.0f / scale;
+    if (live && ew < 4) p.ln_scale[m] = scale;
+  }
+  // pass 2a: the new residual row, bf16, in place of the residual just read
+  // (each thread rewrites only its own row), then one TMA store of the tile
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tbase + cbase + c * 32, r);
+    tmem_ld_wait_dep(r);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *xpose_slot(tile, lane, 4 * c + q) =
+          make_uint4(pack_bf16x2(__uint_as_float(r[8 * q]), __uint_as_float(r[8 * q + 1])),
+                     pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
+                     pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
+                     pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && ok) {
+    tma_store_2d_hint(map_x, tile, cbase, row_base, l2_evict_last());
+    bulk_commit();
+  }
+  // pass 2b: the LayerNorm output through the same tile once that store has
+  // read it (the first chunk is computed while it does); bf16: one 64-column
+  // box, e4m3: one 64 B-row box, f32 (the final LayerNorm): one 32-column box
+  // per chunk, in turn
+  const bool f32_out = p.ln_mode == kLnF32;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tbase + cbase + c * 32, r);
+    tmem_ld_wait_dep(r);
+    float2 y[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const int col = cbase + c * 32 + i;
+      y[i / 2] = fma_f2(mul_f2(sub_f2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), mean2), rstd2),
+                        *reinterpret_cast<const float2*>(s_g + col), *reinterpret_cast<const float2*>(s_b + col));
+    }
+    if (c == 0 || f32_out) {
+      if (lane == 0) bulk_wait_read<0>();  // the previous store has read the tile
+      __syncwarp();
+    }
+    if (f32_out) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *xpose_slot(tile, lane, q) = make_uint4(__float_as_uint(y[2 * q].x), __float_as_uint(y[2 * q].y),
+                                                __float_as_uint(y[2 * q + 1].x), __float_as_uint(y[2 * q + 1].y));
+    } else if (p.ln_mode == kLnE4m3) {  // 32 rows x 64 B, 64 B swizzle: chunks 2c, 2c+1
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t q8[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 u = y[8 * h + 2 * i], v = y[8 * h + 2 * i + 1];
+          q8[i] = pack_e4m3x4(u.x * inv_scale, u.y * inv_scale, v.x * inv_scale, v.y * inv_scale);
+        }
+        *xpose_slot64(tile, lane, 2 * c + h) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *xpose_slot(tile, lane, 4 * c + q) =
+            make_uint4(pack_bf16x2(y[4 * q].x, y[4 * q].y), pack_bf16x2(y[4 * q + 1].x, y[4 * q + 1].y),
+                       pack_bf16x2(y[4 * q + 2].x, y[4 * q + 2].y), pack_bf16x2(y[4 * q + 3].x, y[4 * q + 3].y));
+    }
+    if (f32_out || c + 1 == kChunks) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && ok) {
+        tma_store_2d(map_l, tile, cbase + (f32_out ? 32 * c : 0), row_base);
+        bulk_commit();
+      }
+    }
+  }
+}
+
 template <int BLOCK_N, int EPI, bool FP8>
 __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
@@ -420,14 +627,14 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       mbar_init(&tempty[a], kEpiWarps);
     }
     for (int i = 0; i < S::kTilesPerWarp * kEpiWarps; ++i) mbar_init(&xbar[i], 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], EPI == kEpiResidLn16 ? 128 : 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
     s_bias[i] = p.bias[i];
     if (FP8) s_bscale[i] = p.b_scale[i];
-    if (EPI == kEpiResidLn) {
+    if (EPI == kEpiResidLn || EPI == kEpiResidLn16) {
       s_g[i] = p.ln_g[i];
       s_b[i] = p.ln_b[i];
     }
@@ -450,7 +657,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       tma_prefetch_desc(&map_a);
       tma_prefetch_desc(&map_w);
       tma_prefetch_desc(&map_o);
-      if (EPI == kEpiResidLn) tma_prefetch_desc(&map_l);
+      if (EPI == kEpiResidLn || EPI == kEpiResidLn16) tma_prefetch_desc(&map_l);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -556,6 +763,15 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           }
         }
         __syncwarp();
+      } else if (EPI == kEpiResidLn16) {
+        // this warp's 32 rows x 64 columns of the bf16 residual, landing while the MMAs run
+        const int rb = (tile / n_tiles) * S::kBlockM + quad * 32;
+        if (lane == 0 && rb < m_valid) {
+          bulk_wait_read<0>();  // the staging tile is free: the previous tile's stores have read it
+          mbar_arrive_expect_tx(&my_xbar[0], 4096);
+          tma_load_2d_hint(tiles, &map_o, &my_xbar[0], (ew >> 2) * 64, rb, l2_evict_last());
+        }
+        __syncwarp();
       }
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
@@ -623,6 +839,15 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
             bulk_commit();
           }
           ++out_k;
+        }
+      } else if (EPI == kEpiResidLn16) {
+        if (any) {
+          float2* st16 = reinterpret_cast<float2*>(s_stats);
+          float* amax16 = reinterpret_cast<float*>(st16 + 2 * 16 * 32);
+          resid_ln16_epilogue<FP8>(tbase, tiles, &my_xbar[0], xbits, st16 + stat_par * 16 * 32,
+                                   amax16 + stat_par * 16 * 32, s_bias, s_bscale, s_g, s_b, &map_o, &map_l, p,
+                                   abort_flag, &pair_bar[quad], pair_phase, ew, lane, row_base, m, live, a_s);
+          stat_par ^= 1;
         }
       } else if (any) {
         resid_ln_epilogue<BLOCK_N, FP8, S::kTilesPerWarp>(tbase, tiles, my_xbar, xbits, s_stats + (stat_par * 8) * 32,

@@ -9,7 +9,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 BF16, FP8 = 1, 2
-EPI_BIAS, EPI_GELU, EPI_LN = 0, 1, 2
+EPI_BIAS, EPI_GELU, EPI_LN, EPI_LN16 = 0, 1, 2, 3
 LN_BF16, LN_E4M3, LN_F32 = 0, 1, 2
 
 
@@ -159,6 +159,57 @@ def test_bf16_resid_ln_repeatable_many_tiles():
     x_ref = resid0 + a.float() @ w.float().T + bias
     close(outs[0][0], x_ref, 1e-4, "x")
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("m,k", [(333, 1024), (1000, 256), (40271, 1024)])
+@pytest.mark.parametrize("ln_mode", [LN_BF16, LN_F32])
+def test_bf16_resid16_ln(m, k, ln_mode):
+    """bf16 residual stream, 16-warp LayerNorm epilogue (d = 256): x += a.w^T + bias in place (bf16), the
+    LayerNorm of the f32 sum -> ln_out; repeated launches are bit-identical."""
+    n = 256
+    g = torch.Generator(device="cuda").manual_seed(m + k + ln_mode)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).bfloat16()
+    bias = torch.randn(n, device="cuda", generator=g) * 0.1
+    resid0 = torch.randn(m, n, device="cuda", generator=g).bfloat16()
+    gam = 1 + 0.1 * torch.randn(n, device="cuda", generator=g)
+    bet = 0.1 * torch.randn(n, device="cuda", generator=g)
+    outs = []
+    for _ in range(2):
+        resid = resid0.clone()
+        ln_out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16 if ln_mode == LN_BF16 else torch.float32)
+        call(BF16, EPI_LN16, m, n, k, a, w, bias, resid=resid, g=gam, b=bet, ln_out=ln_out, ln_mode=ln_mode)
+        outs.append((resid, ln_out))
+    x_ref = resid0.float() + a.float() @ w.float().T + bias
+    close(outs[0][0], x_ref, 8e-3, "x")
+    y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
+    close(outs[0][1], y_ref, 8e-3 if ln_mode == LN_BF16 else 1e-4, "ln")
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_fp8_resid16_ln():
+    m, n, k = 700, 256, 1024
+    a, sa = quant_rows(torch.randn(m, k, device="cuda"))
+    w, sw = quant_rows(torch.randn(n, k, device="cuda") / 32)
+    bias = torch.randn(n, device="cuda") * 0.1
+    resid0 = torch.randn(m, n, device="cuda").bfloat16()
+    resid = resid0.clone()
+    gam = torch.ones(n, device="cuda")
+    bet = torch.zeros(n, device="cuda")
+    ln_out = torch.empty(m, n, device="cuda", dtype=torch.uint8)
+    ln_scale = torch.empty(m, device="cuda")
+    call(FP8, EPI_LN16, m, n, k, a, w, bias, resid=resid, g=gam, b=bet, ln_out=ln_out, ln_mode=LN_E4M3,
+         ln_scale=ln_scale, a_scale=sa, b_scale=sw)
+    x_ref = resid0.float() + (a.float() * sa[:, None]) @ (w.float() * sw[:, None]).T + bias
+    close(resid, x_ref, 8e-3, "x")
+    y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
+    close(ln_scale, y_ref.abs().amax(dim=1) / 448.0, 1e-5, "scale")
+    q = ln_out.view(torch.float8_e4m3fn).float()
+    q_ref = (y_ref / ln_scale[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).float()
+    off = q != q_ref
+    assert off.float().mean().item() <= 1e-2
+    step = torch.clamp(q_ref.abs(), min=2.0 ** -6) * 2.0 ** -3
+    assert torch.all((q - q_ref).abs()[off] <= step[off] * 1.0001)
 
 
 def ffn_call(m, f, ln, w1, b1, w2, b2, x, g, b, ln_out, ln_mode):

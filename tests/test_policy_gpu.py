@@ -192,14 +192,15 @@ def test_device_side_bad_count_reports_runtime_error():
 
 
 def test_fused_ffn_matches_two_kernel_path(monkeypatch):
-    """Config-2 full batch (315 row tiles, several per CTA): the fused FFN kernel
-    (ORBIT_WARS_FFN_FUSED=1) against the default up-projection + down-projection
-    kernels. Each CTA starts the hidden-chunk walk at its own chunk, so the
+    """Config-2 full batch (315 row tiles, several per CTA), f32 residual stream
+    (ORBIT_WARS_X_F32=1): the fused FFN kernel (ORBIT_WARS_FFN_FUSED=1) against the
+    up-projection + down-projection kernels. Each CTA starts the hidden-chunk walk at its own chunk, so the
     down-projection sums the same terms in another order: outputs agree to f32
     rounding, far inside the bf16 tolerance, and each path repeats bit for bit."""
     cfg = ow.preset(2)
     w = ow.make_weights(cfg, seed=17)
     feats, counts = ow.make_inputs(cfg, seed=17)
+    monkeypatch.setenv("ORBIT_WARS_X_F32", "1")  # the fused FFN kernel keeps the residual stream in f32
     with ow.EncoderPolicy(cfg, w) as pol:
         two = pol.forward(feats, counts)
         assert pol.launches_per_forward() == 3 + 5 * cfg.layers + 1
@@ -213,6 +214,26 @@ def test_fused_ffn_matches_two_kernel_path(monkeypatch):
     m = valid_mask(counts, cfg.n_entities)
     assert rel_err(fused[0][m], two[0][m]) <= 1e-2 and rel_err(fused[1], two[1]) <= 1e-2
     assert float((fused[2][m] == two[2][m]).mean()) >= 0.99
+
+
+def test_bf16_and_f32_residual_streams_agree(monkeypatch):
+    """Config 2: the default bf16 residual stream (16-warp LayerNorm epilogue) and the f32 one
+    (ORBIT_WARS_X_F32=1) agree within the bf16 tolerance, and both repeat bit for bit."""
+    cfg = ow.preset(2).with_(batch=256)
+    w = ow.make_weights(cfg, seed=19)
+    feats, counts = ow.make_inputs(cfg, batch=256, seed=19)
+    outs = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("ORBIT_WARS_X_F32", mode)
+        with ow.EncoderPolicy(cfg, w) as pol:
+            a = pol.forward(feats, counts)
+            b = pol.forward(feats, counts)
+        for u, v in zip(a, b):
+            assert np.array_equal(u, v)
+        outs[mode] = a
+    m = valid_mask(counts, cfg.n_entities)
+    assert rel_err(outs["0"][0][m], outs["1"][0][m]) <= 1e-2
+    assert rel_err(outs["0"][1], outs["1"][1]) <= 1e-2
 
 
 def test_submit_wait_pipeline():
