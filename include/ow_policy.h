@@ -176,7 +176,10 @@ void ow_policy_destroy(OwPolicy* policy);
  * issues it. precision OW_PRECISION_BF16 or _FP8 (then a_scale[m], b_scale[n]
  * dequantise); epilogue 0 bias -> bf16 out, 1 bias + GELU -> bf16 out,
  * 2 residual (f32 resid, in place) + LayerNorm -> ln_out (ln_mode 0 bf16,
- * 1 e4m3 + ln_scale, 2 f32). Synchronous on `stream`. */
+ * 1 e4m3 + ln_scale, 2 f32); 3 the same with a bf16 residual (resid points at
+ * bf16 values; n = 256). epilogue + 16 runs the CTA-pair kernel (cta_group::2,
+ * 256-row tiles; n a multiple of 256; epilogue 0, 1 or 3). Synchronous on
+ * `stream`. */
 OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, const void* a, const void* w,
                           const float* bias, void* out, float* resid, const float* ln_g, const float* ln_b,
                           void* ln_out, int ln_mode, float* ln_scale, const float* a_scale, const float* b_scale,

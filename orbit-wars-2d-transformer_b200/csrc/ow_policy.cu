@@ -22,6 +22,7 @@
 #include "ow_common.cuh"
 #include "ow_kernels.cuh"
 #include "ow_tc_gemm.cuh"
+#include "ow_tc_gemm2.cuh"
 #include "ow_tc_ffn.cuh"
 
 namespace {
@@ -210,6 +211,7 @@ struct OwPolicy {
     float *sqkv, *so, *s1, *s2;     // e4m3 per-output-channel scales
     CUtensorMap mqkv, mo, m1, m2;
     CUtensorMap m1f, m2f;           // fused FFN: W1 / W2 in 128-row boxes
+    CUtensorMap mqkv2, mo2, m12, m22;  // CTA-pair GEMMs: each CTA's half of a 256-row box
   };
   std::vector<LayerW> lw;
   float *we = nullptr, *be = nullptr, *lnfg = nullptr, *lnfb = nullptr, *wp = nullptr, *bp = nullptr,
@@ -236,6 +238,14 @@ struct OwPolicy {
   // bf16 residual stream x (the spec's bf16 storage) with the 16-warp LayerNorm
   // epilogue: the tensor-core paths at d = 256 (ORBIT_WARS_X_F32=1 keeps f32)
   bool x16 = false;
+  // block GEMMs on CTA pairs (tc_gemm2_kernel, cta_group::2) where x16 holds,
+  // opt-in with ORBIT_WARS_PAIR=1: the pair mainloop is faster, but at config
+  // 2 the epilogues bound the QKV, up-projection and out-projection GEMMs and
+  // the pair couples the two CTAs' epilogues, so the forward measured slower
+  // (1.41M -> 1.33M states/s); pair_clusters = the clusters of two that fit on
+  // the device at once (the persistent grid)
+  bool pair = false;
+  int pair_clusters = 0;
   int launches = 0;
   // host-IO submissions (ow_policy_submit / ow_policy_wait): two slots, each
   // with its own device inputs, outputs and error word. Uploads run on
@@ -335,6 +345,46 @@ cudaError_t set_gemm_attr() {
                               TcGemmShape<BN, EPI>::kSmemBytes);
 }
 
+template <int EPI, bool FP8>
+cudaError_t set_gemm2_attr() {
+  return cudaFuncSetAttribute(tc_gemm2_kernel<256, EPI, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              TcGemm2Shape<256, EPI>::kSmemBytes);
+}
+
+// Clusters of two CTAs of the pair GEMM that can be resident at once (the
+// persistent grid is twice this, at most).
+int pair_cluster_capacity(int num_sms) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(num_sms & ~1));
+  cfg.blockDim = dim3(EpiWarps<kEpiResidLn16>::kThreads);
+  cfg.dynamicSmemBytes = TcGemm2Shape<256, kEpiResidLn16>::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, tc_gemm2_kernel<256, kEpiResidLn16, false>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+// CTA-pair GEMM launch: a persistent grid of at most P.pair_clusters clusters.
+template <int EPI, bool FP8>
+cudaError_t launch_gemm2(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo,
+                         const CUtensorMap& ml, const TcGemmParams& prm) {
+  using S = TcGemm2Shape<256, EPI>;
+  const long long pair_tiles = static_cast<long long>((P.cap_rows + 255) / 256) * (prm.n / 256);
+  const int clusters = static_cast<int>(std::max<long long>(1, std::min<long long>(P.pair_clusters, pair_tiles)));
+  if (prm.n * ((FP8 ? 2 : 1) + (EPI == kEpiResidLn16 ? 2 : 0)) > S::E::kParamFloats) return cudaErrorInvalidValue;
+  return launch_k(P, tc_gemm2_kernel<256, EPI, FP8>, 2 * clusters, EpiWarps<EPI>::kThreads, S::kSmemBytes, ma, mw, mo,
+                  ml, prm);
+}
+
 template <int BN, int EPI, bool FP8>
 cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo,
                         const CUtensorMap& ml, const TcGemmParams& prm) {
@@ -350,6 +400,10 @@ cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensor
 cudaError_t launch_gemm_resid_ln(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw,
                                  const CUtensorMap& mx, const CUtensorMap& ml, const TcGemmParams& prm, bool fp8) {
   const int d = P.cfg.d_model;
+  if (P.x16 && P.pair) {
+    if (fp8) return launch_gemm2<kEpiResidLn16, true>(P, ma, mw, mx, ml, prm);
+    return launch_gemm2<kEpiResidLn16, false>(P, ma, mw, mx, ml, prm);
+  }
   if (P.x16) {
     if (fp8) return launch_gemm<256, kEpiResidLn16, true>(P, ma, mw, mx, ml, prm);
     return launch_gemm<256, kEpiResidLn16, false>(P, ma, mw, mx, ml, prm);
@@ -396,6 +450,12 @@ cudaError_t set_all_gemm_attrs() {
   upd(set_gemm_attr<256, kEpiResidLn, true>());
   upd(set_gemm_attr<256, kEpiResidLn16, false>());
   upd(set_gemm_attr<256, kEpiResidLn16, true>());
+  upd(set_gemm2_attr<kEpiBias, false>());
+  upd(set_gemm2_attr<kEpiBiasGelu, false>());
+  upd(set_gemm2_attr<kEpiResidLn16, false>());
+  upd(set_gemm2_attr<kEpiBias, true>());
+  upd(set_gemm2_attr<kEpiBiasGelu, true>());
+  upd(set_gemm2_attr<kEpiResidLn16, true>());
   upd(cudaFuncSetAttribute(tc_ffn_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            TcFfnShape<256>::kSmemBytes));
   return e;
@@ -693,7 +753,9 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       q.ld_out = 3 * d;
       q.a_scale = P.ln_scale;
       q.b_scale = W.sqkv;
-      if (fp8) OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, true>(P, P.m_ln, W.mqkv, P.e_qkv, P.e_qkv, q)));
+      if (P.pair && fp8) OW_STEP("gemm_qkv", (launch_gemm2<kEpiBias, true>(P, P.m_ln, W.mqkv2, P.e_qkv, P.e_qkv, q)));
+      else if (P.pair) OW_STEP("gemm_qkv", (launch_gemm2<kEpiBias, false>(P, P.m_ln, W.mqkv2, P.e_qkv, P.e_qkv, q)));
+      else if (fp8) OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, true>(P, P.m_ln, W.mqkv, P.e_qkv, P.e_qkv, q)));
       else if (P.qkv_block_n == 256)
         OW_STEP("gemm_qkv", (launch_gemm<256, kEpiBias, false>(P, P.m_ln, W.mqkv, P.e_qkv, P.e_qkv, q)));
       else OW_STEP("gemm_qkv", (launch_gemm<128, kEpiBias, false>(P, P.m_ln, W.mqkv, P.e_qkv, P.e_qkv, q)));
@@ -715,7 +777,7 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       o.ln_scale = P.ln_scale;
       o.a_scale = P.attn_scale;
       o.b_scale = W.so;
-      OW_STEP("gemm_out_resid_ln", launch_gemm_resid_ln(P, P.m_attn, W.mo, P.e_x, P.e_ln, o, fp8));
+      OW_STEP("gemm_out_resid_ln", launch_gemm_resid_ln(P, P.m_attn, P.pair ? W.mo2 : W.mo, P.e_x, P.e_ln, o, fp8));
       if (ffn_fused(P)) {
         // FFN up + GELU + down + residual + next LN in one kernel
         TcGemmParams w{};
@@ -743,7 +805,9 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       u.ld_out = f;
       u.a_scale = P.ln_scale;
       u.b_scale = W.s1;
-      if (fp8) OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, true>(P, P.m_ln, W.m1, P.e_h, P.e_h, u)));
+      if (P.pair && fp8) OW_STEP("gemm_ffn_up_gelu", (launch_gemm2<kEpiBiasGelu, true>(P, P.m_ln, W.m12, P.e_h, P.e_h, u)));
+      else if (P.pair) OW_STEP("gemm_ffn_up_gelu", (launch_gemm2<kEpiBiasGelu, false>(P, P.m_ln, W.m12, P.e_h, P.e_h, u)));
+      else if (fp8) OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, true>(P, P.m_ln, W.m1, P.e_h, P.e_h, u)));
       else OW_STEP("gemm_ffn_up_gelu", (launch_gemm<256, kEpiBiasGelu, false>(P, P.m_ln, W.m1, P.e_h, P.e_h, u)));
       if (fp8) OW_STEP("quantize_e4m3", launch_quantize(P, m_valid, P.h, f, P.h8, P.h_scale));
       // FFN down + residual + next LN (LN1 of the next block, or the final LN)
@@ -763,7 +827,7 @@ cudaError_t run_blocks(OwPolicy& P, int batch, uint64_t seed, void* logits, void
       w.b_scale = W.s2;
       w.a_stream = 1;  // h is read once here
       OW_STEP("gemm_ffn_down_resid_ln",
-              launch_gemm_resid_ln(P, P.m_h, W.m2, P.e_x, last ? P.e_y : P.e_ln, w, fp8));
+              launch_gemm_resid_ln(P, P.m_h, P.pair ? W.m22 : W.m2, P.e_x, last ? P.e_y : P.e_ln, w, fp8));
     }
   }
   if (c.precision == OW_PRECISION_F32) {
@@ -910,6 +974,10 @@ OwStatus upload_weights(OwPolicy& P, const float* w) {
           !make_kmajor_map(&W.mo, W.wo, e4, d, d, d_rows) || !make_kmajor_map(&W.m1, W.w1, e4, d, f, 256u) ||
           !make_kmajor_map(&W.m2, W.w2, e4, f, d, d_rows))
         return st_rt("cuTensorMapEncodeTiled failed for a weight matrix");
+      if (P.pair && (!make_kmajor_map(&W.mqkv2, W.wqkv, e4, d, 3 * d, 128u) ||
+                     !make_kmajor_map(&W.mo2, W.wo, e4, d, d, 128u) || !make_kmajor_map(&W.m12, W.w1, e4, d, f, 128u) ||
+                     !make_kmajor_map(&W.m22, W.w2, e4, f, d, 128u)))
+        return st_rt("cuTensorMapEncodeTiled failed for a CTA-pair weight map");
       if (ffn_fused(P) && (!make_kmajor_map(&W.m1f, W.w1, false, d, f, 128u) ||
                            !make_kmajor_map(&W.m2f, W.w2, false, f, d, 128u)))
         return st_rt("cuTensorMapEncodeTiled failed for an FFN weight matrix");
@@ -1212,6 +1280,8 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
     P->pdl = config->precision != OW_PRECISION_F32 && !(q != nullptr && q[0] == '0');
     const char* xf = std::getenv("ORBIT_WARS_X_F32");
     P->x16 = config->precision != OW_PRECISION_F32 && config->d_model == 256 && !(xf != nullptr && xf[0] == '1');
+    const char* pr = std::getenv("ORBIT_WARS_PAIR");
+    P->pair = P->x16 && pr != nullptr && pr[0] == '1';
   }
   if (stream != nullptr) {
     P->stream = static_cast<cudaStream_t>(stream);
@@ -1223,6 +1293,10 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
     P->own_stream = true;
   }
   OwStatus s = st_cuda(set_all_gemm_attrs());
+  if (s.code == OW_STATUS_OK && P->pair) {
+    P->pair_clusters = pair_cluster_capacity(P->num_sms);
+    if (P->pair_clusters <= 0) P->pair = false;
+  }
   if (s.code == OW_STATUS_OK) s = alloc_workspace(*P, config->batch_capacity);
   if (s.code == OW_STATUS_OK) s = add_second_lane(*P);
   if (s.code == OW_STATUS_OK) s = upload_weights(*P, weights);
@@ -1458,6 +1532,10 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
                           void* ln_out, int ln_mode, float* ln_scale, const float* a_scale, const float* b_scale,
                           void* stream) {
   const bool fp8 = precision == OW_PRECISION_FP8;
+  const bool pair = (epilogue & 16) != 0;  // the CTA-pair kernel (n a multiple of 256; bias, GELU or epilogue 3)
+  epilogue &= 15;
+  if (pair && (n % 256 != 0 || !(epilogue == kEpiBias || epilogue == kEpiBiasGelu || epilogue == kEpiResidLn16)))
+    return st_bad("the CTA-pair GEMM takes n a multiple of 256 and epilogue 0, 1 or 3");
   if (precision != OW_PRECISION_BF16 && !fp8) return st_bad("selftest precision must be bf16 or fp8");
   if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || w == nullptr || bias == nullptr) return st_bad("bad selftest args");
   if (k % (fp8 ? 128 : 64) != 0) return st_bad("k must be a multiple of 128 bytes");
@@ -1488,7 +1566,13 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   OW_TRY(cudaGetDeviceProperties(&prop, dev));
   P.num_sms = prop.multiProcessorCount;
   OW_TRY(set_all_gemm_attrs());
-  const uint32_t box_rows = bn <= 256 ? static_cast<uint32_t>(bn) : static_cast<uint32_t>(bn / 2);
+  uint32_t box_rows = bn <= 256 ? static_cast<uint32_t>(bn) : static_cast<uint32_t>(bn / 2);
+  if (pair) {
+    box_rows = 128;
+    P.pair = true;
+    P.pair_clusters = pair_cluster_capacity(P.num_sms);
+    if (P.pair_clusters <= 0) return st_rt("no CTA-pair cluster fits on this device");
+  }
   CUtensorMap ma, mw, mo, ml;
   if (!make_kmajor_map(&ma, a, fp8, k, m, 128) || !make_kmajor_map(&mw, w, fp8, k, n, box_rows))
     return st_rt("cuTensorMapEncodeTiled failed");
@@ -1537,6 +1621,11 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
     } else if (epilogue == kEpiResidLn) {
       P.cfg.d_model = n;
       e = launch_gemm_resid_ln(P, ma, mw, mo, ml, q, fp8);
+    } else if (pair) {
+      if (epilogue == kEpiBias) e = fp8 ? launch_gemm2<kEpiBias, true>(P, ma, mw, mo, ml, q)
+                                        : launch_gemm2<kEpiBias, false>(P, ma, mw, mo, ml, q);
+      else e = fp8 ? launch_gemm2<kEpiBiasGelu, true>(P, ma, mw, mo, ml, q)
+                   : launch_gemm2<kEpiBiasGelu, false>(P, ma, mw, mo, ml, q);
     } else if (epilogue == kEpiBias) {
       if (fp8) e = launch_gemm<256, kEpiBias, true>(P, ma, mw, mo, ml, q);
       else if (bn == 256) e = launch_gemm<256, kEpiBias, false>(P, ma, mw, mo, ml, q);

@@ -10,6 +10,7 @@ torch = pytest.importorskip("torch")
 
 BF16, FP8 = 1, 2
 EPI_BIAS, EPI_GELU, EPI_LN, EPI_LN16 = 0, 1, 2, 3
+PAIR = 16  # epilogue flag: the CTA-pair (cta_group::2) kernel
 LN_BF16, LN_E4M3, LN_F32 = 0, 1, 2
 
 
@@ -210,6 +211,70 @@ def test_fp8_resid16_ln():
     assert off.float().mean().item() <= 1e-2
     step = torch.clamp(q_ref.abs(), min=2.0 ** -6) * 2.0 ** -3
     assert torch.all((q - q_ref).abs()[off] <= step[off] * 1.0001)
+
+
+@pytest.mark.parametrize("m", [77, 333, 40271])
+@pytest.mark.parametrize("epi,n,k", [(EPI_BIAS, 768, 256), (EPI_GELU, 1024, 256), (EPI_BIAS, 256, 1024)])
+def test_pair_bias_gelu(m, epi, n, k):
+    """CTA-pair kernel (256-row tiles over two SMs) against torch fp32 and the single-CTA kernel."""
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).bfloat16()
+    bias = torch.randn(n, device="cuda", generator=g)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    one = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    call(BF16, epi | PAIR, m, n, k, a, w, bias, out=out)
+    call(BF16, epi, m, n, k, a, w, bias, out=one)
+    ref = a.float() @ w.float().T + bias
+    if epi == EPI_GELU:
+        ref = torch.nn.functional.gelu(ref)
+    close(out, ref, 8e-3)
+    close(out, one.float(), 8e-3, "vs single-CTA")
+
+
+@pytest.mark.parametrize("m,k", [(200, 256), (40271, 1024)])
+@pytest.mark.parametrize("ln_mode", [LN_BF16, LN_F32])
+def test_pair_resid16_ln(m, k, ln_mode):
+    n = 256
+    g = torch.Generator(device="cuda").manual_seed(m + k + 11 * ln_mode)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).bfloat16()
+    bias = torch.randn(n, device="cuda", generator=g) * 0.1
+    resid0 = torch.randn(m, n, device="cuda", generator=g).bfloat16()
+    gam = 1 + 0.1 * torch.randn(n, device="cuda", generator=g)
+    bet = 0.1 * torch.randn(n, device="cuda", generator=g)
+    outs = []
+    for _ in range(2):
+        resid = resid0.clone()
+        ln_out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16 if ln_mode == LN_BF16 else torch.float32)
+        call(BF16, EPI_LN16 | PAIR, m, n, k, a, w, bias, resid=resid, g=gam, b=bet, ln_out=ln_out, ln_mode=ln_mode)
+        outs.append((resid, ln_out))
+    x_ref = resid0.float() + a.float() @ w.float().T + bias
+    close(outs[0][0], x_ref, 8e-3, "x")
+    y_ref = torch.nn.functional.layer_norm(x_ref, (n,), gam, bet, eps=1e-5)
+    close(outs[0][1], y_ref, 8e-3 if ln_mode == LN_BF16 else 1e-4, "ln")
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_pair_fp8():
+    m, n, k = 700, 256, 1024
+    a, sa = quant_rows(torch.randn(m, k, device="cuda"))
+    w, sw = quant_rows(torch.randn(n, k, device="cuda") / 32)
+    bias = torch.randn(n, device="cuda") * 0.1
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    call(FP8, EPI_BIAS | PAIR, m, n, k, a, w, bias, out=out, a_scale=sa, b_scale=sw)
+    ref = (a.float() * sa[:, None]) @ (w.float() * sw[:, None]).T + bias
+    close(out, ref, 8e-3)
+    resid0 = torch.randn(m, n, device="cuda").bfloat16()
+    resid = resid0.clone()
+    ln_out = torch.empty(m, n, device="cuda", dtype=torch.uint8)
+    ln_scale = torch.empty(m, device="cuda")
+    call(FP8, EPI_LN16 | PAIR, m, n, k, a, w, bias, resid=resid, g=torch.ones(n, device="cuda"),
+         b=torch.zeros(n, device="cuda"), ln_out=ln_out, ln_mode=LN_E4M3, ln_scale=ln_scale, a_scale=sa, b_scale=sw)
+    x_ref = resid0.float() + ref
+    close(resid, x_ref, 8e-3, "x")
+    y_ref = torch.nn.functional.layer_norm(x_ref, (n,), eps=1e-5)
+    close(ln_scale, y_ref.abs().amax(dim=1) / 448.0, 1e-5, "scale")
 
 
 def ffn_call(m, f, ln, w1, b1, w2, b2, x, g, b, ln_out, ln_mode):
