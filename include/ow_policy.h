@@ -195,6 +195,16 @@ OwStatus ow_selftest_ffn(int m, int d, int f, const void* ln, const void* w1, co
                          const float* b2, float* x, const float* ln_g, const float* ln_b, void* ln_out, int ln_mode,
                          void* stream);
 
+/* Test hook, not part of the forward: one launch of the bf16 masked attention
+ * on device buffers, as the forward issues it. counts[batch] (device) are the
+ * valid entities per state (<= n_entities); qkv is [Σcounts rows, 3 * 32 *
+ * heads] bf16 in the packed layout (rows of state b after those of states < b;
+ * the buffer holds batch * n_entities rows); out [rows, 32 * heads] bf16.
+ * kernel 0 runs the tcgen05 kernel (S and P in tensor memory), 1 the
+ * mma.sync kernel. Synchronous on `stream`. */
+OwStatus ow_selftest_attention(int kernel, int batch, int n_entities, int heads, const int32_t* counts,
+                               const void* qkv, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

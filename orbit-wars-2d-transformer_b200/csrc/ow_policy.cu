@@ -24,6 +24,7 @@
 #include "ow_tc_gemm.cuh"
 #include "ow_tc_gemm2.cuh"
 #include "ow_tc_ffn.cuh"
+#include "ow_tc_attn.cuh"
 
 namespace {
 
@@ -169,6 +170,9 @@ bool make_ln_map(CUtensorMap* map, const void* base, MapType t, uint64_t inner, 
 bool make_out_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, int chunk_cols) {
   return make_map_box(map, base, kMapBf16, inner, rows, static_cast<uint32_t>(chunk_cols) * 2, 32);
 }
+// The tcgen05 attention's block: the smallest of 32, 64, 128 rows holding N entities.
+uint32_t attn_block_rows(int n_entities) { return n_entities <= 32 ? 32u : (n_entities <= 64 ? 64u : 128u); }
+
 // K-major GEMM operand map (bf16 or e4m3), box = 128 bytes x box_rows.
 bool make_kmajor_map(CUtensorMap* map, const void* base, bool e4m3, uint64_t inner, uint64_t rows, uint32_t box_rows) {
   return make_map_128b(map, base, e4m3 ? kMapU8 : kMapBf16, inner, rows, box_rows);
@@ -232,6 +236,7 @@ struct OwPolicy {
   CUtensorMap m_ln, m_attn, m_h;       // GEMM A operands
   CUtensorMap e_qkv, e_h, e_x;         // epilogue outputs: qkv / h (bf16, 32-row boxes), x (f32)
   CUtensorMap e_ln, e_y;               // LayerNorm outputs: ln (bf16 or e4m3), y (f32, final LN)
+  CUtensorMap a_qkv;                   // attention: qkv in 64-column (two heads) x block-row boxes, 128 B swizzle
   int qkv_block_n = 256;
   bool pdl = false;       // tensor-core path: programmatic dependent launches (ORBIT_WARS_PDL=0 turns them off)
   bool fuse_ffn = false;  // ORBIT_WARS_FFN_FUSED=1 at create selects the fused FFN kernel (d = 256, bf16, f32 x)
@@ -246,6 +251,12 @@ struct OwPolicy {
   // the device at once (the persistent grid)
   bool pair = false;
   int pair_clusters = 0;
+  // masked attention on tcgen05 with S and P in TMEM (tc_attention_kernel);
+  // ORBIT_WARS_ATTN_MMA=1 selects the mma.sync kernel with S and P in
+  // registers (attention_bf16_kernel), measured faster at config 2 (30.8 us
+  // against 34.8 us per layer): at head_dim 32 every tcgen05.mma is small and
+  // costs its issuing thread about 100 cycles, and TMEM holds eight heads
+  bool attn_tc = true;
   int launches = 0;
   // host-IO submissions (ow_policy_submit / ow_policy_wait): two slots, each
   // with its own device inputs, outputs and error word. Uploads run on
@@ -284,7 +295,7 @@ struct OwPolicy {
     void *x = nullptr, *ln = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr;
     uint8_t *ln8 = nullptr, *attn8 = nullptr, *h8 = nullptr;
     float *ln_scale = nullptr, *attn_scale = nullptr, *h_scale = nullptr;
-    CUtensorMap m_ln, m_attn, m_h, e_qkv, e_h, e_x, e_ln, e_y;
+    CUtensorMap m_ln, m_attn, m_h, e_qkv, e_h, e_x, e_ln, e_y, a_qkv;
   };
   Lane lanes[2];
   int n_lanes = 1;
@@ -433,6 +444,15 @@ cudaError_t launch_ffn(const OwPolicy& P, const CUtensorMap& ma, const CUtensorM
   return launch_k(P, tc_ffn_kernel<256>, grid, S::kThreads, S::kSmemBytes, ma, m1, m2, mx, ml, prm);
 }
 
+// Test hook support: packed row -> state * n + entity (the embedding kernel
+// writes the same map in the forward).
+__global__ void fill_row_slot_kernel(const int* offsets, int batch, int n, int* row_slot) {
+  for (int b = blockIdx.x; b < batch; b += gridDim.x) {
+    const int r0 = offsets[b], c = offsets[b + 1] - r0;
+    for (int j = threadIdx.x; j < c; j += blockDim.x) row_slot[r0 + j] = b * n + j;
+  }
+}
+
 cudaError_t set_all_gemm_attrs() {
   cudaError_t e = cudaSuccess;
   auto upd = [&e](cudaError_t r) {
@@ -458,6 +478,12 @@ cudaError_t set_all_gemm_attrs() {
   upd(set_gemm2_attr<kEpiResidLn16, true>());
   upd(cudaFuncSetAttribute(tc_ffn_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            TcFfnShape<256>::kSmemBytes));
+  upd(cudaFuncSetAttribute(tc_attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TcAttnShape<32>::kSmemBytes));
+  upd(cudaFuncSetAttribute(tc_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TcAttnShape<64>::kSmemBytes));
+  upd(cudaFuncSetAttribute(tc_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TcAttnShape<128>::kSmemBytes));
   return e;
 }
 
@@ -631,6 +657,39 @@ cudaError_t dispatch_ln_f32(const OwPolicy& P, const int* m_valid, const float* 
   }
 }
 
+// tcgen05 attention: persistent, one CTA per SM; a work unit is a tile of
+// 128 / BS states (BS = the power-of-two block >= N) and two heads.
+template <int BS>
+cudaError_t launch_attention_tc_bs(const OwPolicy& P, int batch, float scale_log2) {
+  using S = TcAttnShape<BS>;
+  const auto& c = P.cfg;
+  TcAttnParams a{};
+  a.offsets = P.offsets;
+  a.out = static_cast<__nv_bfloat16*>(P.attn);
+  a.err = P.err;
+  a.batch = batch;
+  a.d = c.d_model;
+  a.heads = c.heads;
+  a.scale_log2 = scale_log2;
+  const long long units = static_cast<long long>((batch + S::kStatesPerTile - 1) / S::kStatesPerTile) *
+                          (c.heads / S::kGroup);
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, units)));
+  return launch_k(P, tc_attention_kernel<BS>, grid, S::kThreads, S::kSmemBytes, P.a_qkv, a);
+}
+
+// The tcgen05 attention serves head_dim 32 with an even head count.
+bool attention_tc(const OwPolicy& P) {
+  const auto& c = P.cfg;
+  return P.attn_tc && c.precision != OW_PRECISION_F32 && c.d_model == 32 * c.heads && c.heads % 2 == 0 &&
+         c.n_entities <= 128;
+}
+
+cudaError_t launch_attention_tc(const OwPolicy& P, int batch, float scale_log2) {
+  if (P.cfg.n_entities <= 32) return launch_attention_tc_bs<32>(P, batch, scale_log2);
+  if (P.cfg.n_entities <= 64) return launch_attention_tc_bs<64>(P, batch, scale_log2);
+  return launch_attention_tc_bs<128>(P, batch, scale_log2);
+}
+
 cudaError_t launch_attention(const OwPolicy& P, int batch) {
   const auto& c = P.cfg;
   const dim3 grid(batch, c.heads);
@@ -641,6 +700,8 @@ cudaError_t launch_attention(const OwPolicy& P, int batch) {
     if (c.n_entities <= 32) attention_f32_kernel<32><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, scale);
     else if (c.n_entities <= 64) attention_f32_kernel<64><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, scale);
     else attention_f32_kernel<128><<<grid, 128, 0, P.stream>>>(q, o, P.offsets, c.d_model, scale);
+  } else if (attention_tc(P)) {
+    return launch_attention_tc(P, batch, scale * 1.4426950408889634f);
   } else {
     const auto* q = static_cast<const __nv_bfloat16*>(P.qkv);
     auto* o = static_cast<__nv_bfloat16*>(P.attn);
@@ -1084,7 +1145,7 @@ OwStatus alloc_workspace(OwPolicy& P, int cap_states) {
            make_kmajor_map(&P.m_h, P.h, false, f, rows, 128);
     ok = ok && make_out_map(&P.e_qkv, P.qkv, 3 * d, rows, ow::EpiWarps<ow::kEpiBias>::kChunkCols) &&
          make_out_map(&P.e_h, P.h, f, rows, ow::EpiWarps<ow::kEpiBiasGelu>::kChunkCols) &&
-         make_ln_map(&P.e_y, P.y, kMapF32, d, rows);
+         make_ln_map(&P.e_y, P.y, kMapF32, d, rows) && make_map_box(&P.a_qkv, P.qkv, kMapBf16, 3 * d, rows, 128, attn_block_rows(c.n_entities));
     if (P.x16)  // 64-column boxes: x (bf16, 128 B rows), LN out (bf16 128 B rows or e4m3 64 B rows)
       ok = ok && make_map_128b(&P.e_x, P.x, kMapBf16, d, rows, 32) &&
            (e4 ? make_map_box(&P.e_ln, P.ln8, kMapU8, d, rows, 64, 32) : make_map_128b(&P.e_ln, P.ln, kMapBf16, d, rows, 32));
@@ -1110,7 +1171,7 @@ void save_lane(const OwPolicy& P, OwPolicy::Lane& L) {
   L.ln8 = P.ln8; L.attn8 = P.attn8; L.h8 = P.h8;
   L.ln_scale = P.ln_scale; L.attn_scale = P.attn_scale; L.h_scale = P.h_scale;
   L.m_ln = P.m_ln; L.m_attn = P.m_attn; L.m_h = P.m_h;
-  L.e_qkv = P.e_qkv; L.e_h = P.e_h; L.e_x = P.e_x; L.e_ln = P.e_ln; L.e_y = P.e_y;
+  L.e_qkv = P.e_qkv; L.e_h = P.e_h; L.e_x = P.e_x; L.e_ln = P.e_ln; L.e_y = P.e_y; L.a_qkv = P.a_qkv;
 }
 
 void load_lane(OwPolicy& P, const OwPolicy::Lane& L) {
@@ -1126,7 +1187,7 @@ void load_lane(OwPolicy& P, const OwPolicy::Lane& L) {
   P.ln8 = L.ln8; P.attn8 = L.attn8; P.h8 = L.h8;
   P.ln_scale = L.ln_scale; P.attn_scale = L.attn_scale; P.h_scale = L.h_scale;
   P.m_ln = L.m_ln; P.m_attn = L.m_attn; P.m_h = L.m_h;
-  P.e_qkv = L.e_qkv; P.e_h = L.e_h; P.e_x = L.e_x; P.e_ln = L.e_ln; P.e_y = L.e_y;
+  P.e_qkv = L.e_qkv; P.e_h = L.e_h; P.e_x = L.e_x; P.e_ln = L.e_ln; P.e_y = L.e_y; P.a_qkv = L.a_qkv;
 }
 
 // Lane 0 is the handle's stream and workspace. On the tensor-core path a
@@ -1282,6 +1343,8 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
     P->x16 = config->precision != OW_PRECISION_F32 && config->d_model == 256 && !(xf != nullptr && xf[0] == '1');
     const char* pr = std::getenv("ORBIT_WARS_PAIR");
     P->pair = P->x16 && pr != nullptr && pr[0] == '1';
+    const char* am = std::getenv("ORBIT_WARS_ATTN_MMA");
+    P->attn_tc = !(am != nullptr && am[0] == '1');
   }
   if (stream != nullptr) {
     P->stream = static_cast<cudaStream_t>(stream);
@@ -1688,6 +1751,55 @@ OwStatus ow_selftest_ffn(int m, int d, int f, const void* ln, const void* w1, co
   if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost, P.stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(P.stream);
   cudaFree(d_m);
+  if (e != cudaSuccess) return st_cuda(e);
+  if (herr != 0) return st_rt(device_error_message(herr));
+  return st_ok();
+}
+
+OwStatus ow_selftest_attention(int kernel, int batch, int n_entities, int heads, const int32_t* counts,
+                               const void* qkv, void* out, void* stream) {
+  if ((kernel != 0 && kernel != 1) || batch <= 0 || n_entities <= 0 || n_entities > 128 || heads <= 0 ||
+      heads > 16 || counts == nullptr || qkv == nullptr || out == nullptr)
+    return st_bad("bad attention selftest args");
+  int dev = 0;
+  OW_TRY(cudaGetDevice(&dev));
+  OwPolicy P;
+  P.device = dev;
+  P.stream = static_cast<cudaStream_t>(stream);
+  P.cap_rows = static_cast<size_t>(batch) * n_entities;
+  cudaDeviceProp prop{};
+  OW_TRY(cudaGetDeviceProperties(&prop, dev));
+  P.num_sms = prop.multiProcessorCount;
+  P.cfg.precision = OW_PRECISION_BF16;
+  P.cfg.n_entities = n_entities;
+  P.cfg.heads = heads;
+  P.cfg.d_model = 32 * heads;
+  P.attn_tc = kernel == 0;
+  OW_TRY(set_all_gemm_attrs());
+  if (kernel == 0 && heads % 2 != 0) return st_bad("the tcgen05 attention needs an even head count");
+  if (!make_map_box(&P.a_qkv, qkv, kMapBf16, 3 * P.cfg.d_model, P.cap_rows, 128, attn_block_rows(n_entities)))
+    return st_rt("cuTensorMapEncodeTiled failed");
+  // device scratch: error word, offsets, row -> slot map
+  int* buf = nullptr;
+  OW_TRY(cudaMalloc(&buf, (static_cast<size_t>(batch) + 2 + P.cap_rows) * sizeof(int)));
+  P.err = buf;
+  P.offsets = buf + 1;
+  P.row_slot = buf + 2 + batch;
+  P.qkv = const_cast<void*>(qkv);
+  P.attn = out;
+  cudaError_t e = cudaMemsetAsync(P.err, 0, sizeof(int), P.stream);
+  if (e == cudaSuccess) {
+    scan_counts_kernel<<<1, 1024, 0, P.stream>>>(counts, batch, n_entities, P.offsets, P.err);
+    fill_row_slot_kernel<<<std::min(batch, 4 * P.num_sms), 128, 0, P.stream>>>(P.offsets, batch, n_entities,
+                                                                                P.row_slot);
+    e = cudaGetLastError();
+  }
+
+  if (e == cudaSuccess) e = launch_attention(P, batch);
+  int herr = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, P.err, sizeof(int), cudaMemcpyDeviceToHost, P.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(P.stream);
+  cudaFree(buf);
   if (e != cudaSuccess) return st_cuda(e);
   if (herr != 0) return st_rt(device_error_message(herr));
   return st_ok();

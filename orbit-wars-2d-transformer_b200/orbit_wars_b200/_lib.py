@@ -101,6 +101,7 @@ SIGNATURES = {
     "ow_selftest_gemm": (Status, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, C.c_int, P, P,
                                   P, P]),
     "ow_selftest_ffn": (Status, [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, P, C.c_int, P]),
+    "ow_selftest_attention": (Status, [C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P]),
     # include/orbit_wars_cuda.h
     "orbit_wars_cuda_status": (Status, []),
     "orbit_wars_cuda_encode_identity_batch": (Status, [P, P, SZ, SZ, SZ]),
