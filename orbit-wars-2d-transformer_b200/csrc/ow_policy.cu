@@ -257,6 +257,9 @@ struct OwPolicy {
   // against 34.8 us per layer): at head_dim 32 every tcgen05.mma is small and
   // costs its issuing thread about 100 cycles, and TMEM holds eight heads
   bool attn_tc = true;
+  // bias / GELU GEMMs at BLOCK_N = 256 and K <= 4 k-blocks keep the CTA's slice
+  // of W in shared memory (TcGemmWsShape); ORBIT_WARS_GEMM_WS=0 streams it
+  bool gemm_ws = true;
   int launches = 0;
   // host-IO submissions (ow_policy_submit / ow_policy_wait): two slots, each
   // with its own device inputs, outputs and error word. Uploads run on
@@ -355,6 +358,11 @@ cudaError_t set_gemm_attr() {
   return cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               TcGemmShape<BN, EPI>::kSmemBytes);
 }
+template <int EPI, bool FP8>
+cudaError_t set_gemm_ws_attr() {
+  return cudaFuncSetAttribute(tc_gemm_kernel<256, EPI, FP8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              TcGemmWsShape<EPI>::kSmemBytes);
+}
 
 template <int EPI, bool FP8>
 cudaError_t set_gemm2_attr() {
@@ -399,6 +407,19 @@ cudaError_t launch_gemm2(const OwPolicy& P, const CUtensorMap& ma, const CUtenso
 template <int BN, int EPI, bool FP8>
 cudaError_t launch_gemm(const OwPolicy& P, const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo,
                         const CUtensorMap& ml, const TcGemmParams& prm) {
+  if constexpr (BN == 256 && (EPI == kEpiBias || EPI == kEpiBiasGelu)) {
+    // weight-stationary: a multiple of the column tiles as the persistent grid,
+    // so each CTA keeps one 256-row slice of W in shared memory
+    using W = TcGemmWsShape<EPI>;
+    const int n_tiles = prm.n / BN;
+    if (P.gemm_ws && prm.k_blocks <= W::kMaxKBlocks && n_tiles <= P.num_sms &&
+        prm.n * (FP8 ? 2 : 1) <= W::kParamFloats) {
+      const long long m_tiles = static_cast<long long>((P.cap_rows + W::kBlockM - 1) / W::kBlockM);
+      const int per = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms / n_tiles, m_tiles)));
+      return launch_k(P, tc_gemm_kernel<BN, EPI, FP8, true>, per * n_tiles, EpiWarps<EPI>::kThreads, W::kSmemBytes,
+                      ma, mw, mo, ml, prm);
+    }
+  }
   using S = TcGemmShape<BN, EPI>;
   const long long cap_tiles = static_cast<long long>((P.cap_rows + S::kBlockM - 1) / S::kBlockM) * (prm.n / BN);
   const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(P.num_sms, cap_tiles)));
@@ -470,6 +491,10 @@ cudaError_t set_all_gemm_attrs() {
   upd(set_gemm_attr<256, kEpiResidLn, true>());
   upd(set_gemm_attr<256, kEpiResidLn16, false>());
   upd(set_gemm_attr<256, kEpiResidLn16, true>());
+  upd(set_gemm_ws_attr<kEpiBias, false>());
+  upd(set_gemm_ws_attr<kEpiBiasGelu, false>());
+  upd(set_gemm_ws_attr<kEpiBias, true>());
+  upd(set_gemm_ws_attr<kEpiBiasGelu, true>());
   upd(set_gemm2_attr<kEpiBias, false>());
   upd(set_gemm2_attr<kEpiBiasGelu, false>());
   upd(set_gemm2_attr<kEpiResidLn16, false>());
@@ -1345,6 +1370,8 @@ OwStatus ow_policy_create(const OwPolicyConfig* config, const float* weights, si
     P->pair = P->x16 && pr != nullptr && pr[0] == '1';
     const char* am = std::getenv("ORBIT_WARS_ATTN_MMA");
     P->attn_tc = !(am != nullptr && am[0] == '1');
+    const char* ws = std::getenv("ORBIT_WARS_GEMM_WS");
+    P->gemm_ws = !(ws != nullptr && ws[0] == '0');
   }
   if (stream != nullptr) {
     P->stream = static_cast<cudaStream_t>(stream);
@@ -1623,6 +1650,10 @@ OwStatus ow_selftest_gemm(int precision, int epilogue, int m, int n, int k, cons
   OW_TRY(cudaGetDevice(&dev));
   OwPolicy P;
   P.device = dev;
+  {
+    const char* ws = std::getenv("ORBIT_WARS_GEMM_WS");
+    P.gemm_ws = !(ws != nullptr && ws[0] == '0');
+  }
   P.stream = static_cast<cudaStream_t>(stream);
   P.cap_rows = static_cast<size_t>(m);
   cudaDeviceProp prop{};

@@ -125,6 +125,7 @@ struct TcGemmShape {
   // lane quadrant: [2 parities][8 warps][32 lanes] x (mean, M2, amax, pad)
   // bf16-residual LayerNorm: (mean, M2) float2 and amax per [2 parities][16 warps][32 lanes]
   static constexpr int kStatsBytes = EPI == kEpiResidLn ? 2 * 8 * 32 * 16 : (EPI == kEpiResidLn16 ? 2 * 16 * 32 * 12 : 0);
+  static constexpr int kWBytes = 0;  // resident weight slice (weight-stationary shape only)
   static constexpr int kFixedBytes = kBarrierBytes + kParamBytes + kXposeBytes + kStatsBytes + 1024;  // + align slack
   static constexpr int kStagesFit = (kSmemLimit - kFixedBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
@@ -136,6 +137,42 @@ struct TcGemmShape {
   static_assert(kSmemBytes <= kSmemLimit, "shared memory per CTA");
   static_assert(kStageBytes % 1024 == 0 && kXposeBytes % 1024 == 0, "swizzled tiles stay 1024 B aligned");
   static_assert(EPI != kEpiResidLn16 || BLOCK_N == 256, "bf16-residual LayerNorm epilogue: d = 256 (64 columns per warp)");
+};
+
+// Weight-stationary shape for the bias / GELU epilogues at BLOCK_N = 256 and
+// K of at most 4 k-blocks (bf16 K <= 256, e4m3 K <= 512): the CTA's 256-row
+// slice of W (up to 128 KB) is loaded once and stays in shared memory for all
+// of the CTA's row tiles (the persistent grid is a multiple of the column
+// tiles, so tile = blockIdx.x + k * gridDim.x keeps one slice per CTA); only
+// A streams through the stages, 16 KB per k-block instead of 48 KB, so three
+// stages cover three k-blocks of MMAs where the streaming shape fits three of
+// 48 KB. One staging tile per epilogue warp.
+template <int EPI>
+struct TcGemmWsShape : TcGemmShape<256, EPI> {
+  using Base = TcGemmShape<256, EPI>;
+  static constexpr int kMaxKBlocks = 4;
+  static constexpr int kStageBytes = Base::kATileBytes;
+  static constexpr int kWBytes = kMaxKBlocks * Base::kBTileBytes;
+  static constexpr int kTilesPerWarp = 1;
+  static constexpr int kXposeBytes = EpiWarps<EPI>::kCount * kTilesPerWarp * Base::kTileBytes;
+  static constexpr int kParamFloats = 2048;
+  static constexpr int kParamBytes = kParamFloats * 4;
+  static constexpr int kFixedBytes = Base::kBarrierBytes + kParamBytes + kXposeBytes + kWBytes + 1024;
+  static constexpr int kStagesFit = (kSmemLimit - kFixedBytes) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kFixedBytes;
+  static_assert(EPI == kEpiBias || EPI == kEpiBiasGelu, "weight-stationary shape: bias / GELU epilogues");
+  static_assert(kStages >= 2, "at least double-buffered A stages");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory per CTA");
+  static_assert(kWBytes % 1024 == 0 && kXposeBytes % 1024 == 0, "swizzled tiles stay 1024 B aligned");
+};
+template <int BLOCK_N, int EPI, bool WS>
+struct GemmShapeSel {
+  using T = TcGemmShape<BLOCK_N, EPI>;
+};
+template <int EPI>
+struct GemmShapeSel<256, EPI, true> {
+  using T = TcGemmWsShape<EPI>;
 };
 
 // 16 B chunk j of row r of a 32 x 128 B staging tile (128 B swizzle).
@@ -582,27 +619,29 @@ __device__ __forceinline__ void resid_ln16_epilogue(uint32_t tbase, uint8_t* til
   }
 }
 
-template <int BLOCK_N, int EPI, bool FP8>
+template <int BLOCK_N, int EPI, bool FP8, bool WS = false>
 __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                    const __grid_constant__ CUtensorMap map_o, const __grid_constant__ CUtensorMap map_l,
                    const TcGemmParams p) {
-  using S = TcGemmShape<BLOCK_N, EPI>;
+  using S = typename GemmShapeSel<BLOCK_N, EPI, WS>::T;
+  static_assert(!WS || BLOCK_N == 256, "weight-stationary: BLOCK_N = 256");
   constexpr int kEpiWarps = EpiWarps<EPI>::kCount;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
-  uint8_t* sb = smem + S::kStages * S::kATileBytes;
-  // layout: [operand stages][staging tiles (1024 B aligned: the swizzle phase
-  // is taken from address bits)][barriers][epilogue vectors]
-  uint8_t* s_xpose = smem + S::kStages * S::kStageBytes;
+  uint8_t* sb = smem + S::kStages * S::kATileBytes;  // B stages, or (WS) the resident slice of W
+  // layout: [operand stages][(WS) W slice][staging tiles (1024 B aligned: the
+  // swizzle phase is taken from address bits)][barriers][epilogue vectors]
+  uint8_t* s_xpose = smem + S::kStages * S::kStageBytes + S::kWBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_xpose + S::kXposeBytes);
   uint64_t* empty = full + S::kStages;
   uint64_t* tfull = empty + S::kStages;
   uint64_t* tempty = tfull + S::kAcc;
   uint64_t* xbar = tempty + S::kAcc;  // residual loads: one barrier per staging tile of each epilogue warp
   uint64_t* pair_bar = xbar + S::kTilesPerWarp * kEpiWarps;  // LayerNorm: one per lane quadrant (64 arrivals)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pair_bar + 4);
+  uint64_t* w_full = pair_bar + 4;  // WS: the slice of W has landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(w_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* s_par = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + S::kBarrierBytes);
   float4* s_stats = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(s_par) + S::kParamBytes);
@@ -628,6 +667,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
     }
     for (int i = 0; i < S::kTilesPerWarp * kEpiWarps; ++i) mbar_init(&xbar[i], 1);
     for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], EPI == kEpiResidLn16 ? 128 : 64);
+    mbar_init(w_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -662,6 +702,12 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       const uint64_t a_policy = l2_evict_first();
+      if (WS) {  // this CTA's slice of W, once (gridDim.x is a multiple of n_tiles)
+        const int n0 = (static_cast<int>(blockIdx.x) % n_tiles) * BLOCK_N;
+        mbar_arrive_expect_tx(w_full, p.k_blocks * S::kBTileBytes);
+        for (int kb = 0; kb < p.k_blocks; ++kb)
+          tma_load_2d(sb + kb * S::kBTileBytes, &map_w, w_full, kb * (FP8 ? 128 : 64), n0);
+      }
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * S::kBlockM;
         const int n0 = (tile % n_tiles) * BLOCK_N;
@@ -677,7 +723,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           else
             tma_load_2d(sa + stage * S::kATileBytes, &map_a, &full[stage], kx, m0);
 #pragma unroll
-          for (int c = 0; c < S::kBoxCount; ++c)
+          for (int c = 0; c < S::kBoxCount && !WS; ++c)
             tma_load_2d(sb + stage * S::kBTileBytes + c * S::kBoxRows * S::kRowBytes, &map_w, &full[stage], kx,
                         n0 + c * S::kBoxRows);
           if (++stage == S::kStages) {
@@ -693,7 +739,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      bool ok = true;
+      bool ok = !WS || mbar_wait(w_full, 0, abort_flag, p.err);
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
         tc_fence_after();
@@ -705,7 +751,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           }
           tc_fence_after();
           const uint32_t a_base = smem_u32(sa + stage * S::kATileBytes);
-          const uint32_t b_base = smem_u32(sb + stage * S::kBTileBytes);
+          const uint32_t b_base = smem_u32(sb + (WS ? kb : stage) * S::kBTileBytes);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 4 x 32 bytes of K per 128-byte row
             const uint64_t adesc = sdesc_k_sw128(a_base + k * 32);
@@ -791,7 +837,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
           uint32_t r[CW];
 #pragma unroll
           for (int h = 0; h < CW / 32; ++h) tmem_ld32(tbase + c + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
-          if (lane == 0) bulk_wait_read<1>();  // the store that last used this tile has read it
+          if (lane == 0) bulk_wait_read<S::kTilesPerWarp - 1>();  // the store that last used this tile has read it
           tmem_ld_wait();
           uint32_t packed[CW / 2];
 #pragma unroll
@@ -819,7 +865,7 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
             packed[i / 2] = pack_bf16x2(v0, v1);
             packed[i / 2 + 1] = pack_bf16x2(v2, v3);
           }
-          uint8_t* ot = tiles + (out_k & 1) * S::kTileBytes;
+          uint8_t* ot = tiles + (out_k % S::kTilesPerWarp) * S::kTileBytes;
           __syncwarp();
 #pragma unroll
           for (int q = 0; q < CW / 8; ++q) {

@@ -47,6 +47,28 @@ def test_bf16_bias(m, n, k):
     close(out, ref, 8e-3)
 
 
+@pytest.mark.parametrize("epi,n,m", [(EPI_BIAS, 768, 5000), (EPI_GELU, 1024, 4111), (EPI_BIAS, 256, 129)])
+def test_weight_stationary_matches_streaming(monkeypatch, epi, n, m):
+    """K = 256 bias / GELU GEMMs keep each CTA's slice of W in shared memory;
+    the same MMAs in the same order as the streaming kernel, so the same bits."""
+    k = 256
+    g = torch.Generator(device="cuda").manual_seed(n + m)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) / 16).bfloat16()
+    bias = torch.randn(n, device="cuda", generator=g)
+    outs = []
+    for ws in ("1", "0"):
+        monkeypatch.setenv("ORBIT_WARS_GEMM_WS", ws)
+        out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        call(BF16, epi, m, n, k, a, w, bias, out=out)
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    ref = a.float() @ w.float().T + bias
+    if epi == EPI_GELU:
+        ref = torch.nn.functional.gelu(ref)
+    close(outs[0], ref, 8e-3)
+
+
 def test_bf16_gelu():
     m, n, k = 513, 1024, 256
     a = torch.randn(m, k, device="cuda").bfloat16()
