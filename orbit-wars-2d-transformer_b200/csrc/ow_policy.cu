@@ -254,8 +254,8 @@ struct OwPolicy {
   // masked attention on tcgen05 with S and P in TMEM (tc_attention_kernel);
   // ORBIT_WARS_ATTN_MMA=1 selects the mma.sync kernel with S and P in
   // registers (attention_bf16_kernel), measured faster at config 2 (30.8 us
-  // against 34.8 us per layer): at head_dim 32 every tcgen05.mma is small and
-  // costs its issuing thread about 100 cycles, and TMEM holds eight heads
+  // against 33.5 us per layer): two softmax warpgroups per SM take the heads
+  // one at a time, against the mma.sync kernel's many resident CTAs
   bool attn_tc = true;
   // bias / GELU GEMMs at BLOCK_N = 256 and K <= 4 k-blocks keep the CTA's slice
   // of W in shared memory (TcGemmWsShape); ORBIT_WARS_GEMM_WS=0 streams it

@@ -31,10 +31,10 @@
 // Roles: warp 0 issues the TMA loads; two warpgroups of four warps run the
 // softmax and output of alternate heads (warpgroup g: head g of every unit);
 // one MMA warp per warpgroup polls that warpgroup's barriers and issues
-// whichever of its QK^T or PV is ready. A thread issues one tcgen05.mma about
-// every 100 cycles whatever N is, and a head takes twelve (QK^T: 2 per state,
-// PV: BS / 16 per state), so the two issuers run in parallel and off the
-// softmax path. Each warpgroup owns half of the TMEM buffers: while it works on
+// whichever of its QK^T or PV is ready. A head takes twelve tcgen05.mma
+// (QK^T: 2 per state, PV: BS / 16 per state), each of M = 128 and K = 16,
+// issued every ~50 cycles at N = 64 from one thread with its descriptors
+// precomputed, so the two issuers run in parallel and off the softmax path. Each warpgroup owns half of the TMEM buffers: while it works on
 // one head, the tensor cores fill its other buffers with the next heads' scores.
 #pragma once
 
@@ -374,6 +374,11 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
       constexpr uint32_t kIdescS = idesc_bf16(128, BS);
       constexpr uint32_t kIdescPV = idesc_bf16(128, 32) | (1u << 16);  // B (V) MN-major
       int nq = 0, np = 0;  // next QK / PV head
+      // Descriptors of stage 0, built once: a stage, state or k-step offset is
+      // an add to the start-address field (address >> 4, below 2^14 for any
+      // shared-memory address, so the field never carries into the next one).
+      const uint64_t q_desc0 = sdesc_k_sw128(smem_u32(stages) + g * 64);
+      const uint64_t v_desc0 = sdesc_mn_sw128(smem_u32(stages) + 2 * S::kTileBytes + g * 64);
       unsigned long long t0 = 0;
       uint32_t idle = 0;
       while (np < my_units) {
@@ -382,15 +387,15 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
           tc_fence_after();
           const int b = g + 2 * (np % S::kPerWg), s = np % S::kStages;
           const uint32_t ta = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
-          const uint32_t sv = smem_u32(stages + s * S::kStageBytes + 2 * S::kTileBytes) + g * 64;
+          const uint64_t vd = v_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
 #pragma unroll
           for (int j = 0; j < K; ++j) {
             uint32_t m[4];
             state_lanes<BS>(j, m);
 #pragma unroll
             for (int kk = 0; kk < BS / 16; ++kk)
-              umma_f16_ts_lanes(ta + S::kOCol, ta + 8 * kk, sdesc_mn_sw128(sv + (j * BS + 16 * kk) * 128), kIdescPV,
-                                kk > 0 ? 1u : 0u, m);
+              umma_f16_ts_lanes(ta + S::kOCol, ta + 8 * kk, vd + static_cast<uint64_t>((j * BS + 16 * kk) * 8),
+                                kIdescPV, kk > 0 ? 1u : 0u, m);
           }
           umma_commit(&o_full[b]);
           umma_commit(&empty[s]);
@@ -403,15 +408,15 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
               (nq < S::kPerWg || mbar_test(&t_empty[b], ((nq / S::kPerWg) - 1) & 1u))) {
             tc_fence_after();
             const uint32_t dt = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
-            const uint32_t sq = smem_u32(stages + s * S::kStageBytes) + g * 64;
-            const uint32_t sk = sq + S::kTileBytes;
+            const uint64_t qd = q_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
+            const uint64_t kd = qd + static_cast<uint64_t>(S::kTileBytes >> 4);
 #pragma unroll
             for (int j = 0; j < K; ++j) {
               uint32_t m[4];
               state_lanes<BS>(j, m);
-              const uint32_t skj = sk + j * BS * 128;
-              umma_f16_lanes(dt, sdesc_k_sw128(sq), sdesc_k_sw128(skj), kIdescS, 0u, m);
-              umma_f16_lanes(dt, sdesc_k_sw128(sq + 32), sdesc_k_sw128(skj + 32), kIdescS, 1u, m);
+              const uint64_t kdj = kd + static_cast<uint64_t>(j * BS * 8);  // key rows of state j
+              umma_f16_lanes(dt, qd, kdj, kIdescS, 0u, m);
+              umma_f16_lanes(dt, qd + 2u, kdj + 2u, kIdescS, 1u, m);  // + 32 bytes of K
             }
             umma_commit(&s_full[b]);
             ++nq;

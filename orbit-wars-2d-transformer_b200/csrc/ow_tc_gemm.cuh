@@ -740,6 +740,11 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = !WS || mbar_wait(w_full, 0, abort_flag, p.err);
+      // Descriptors of stage 0 / k-step 0, built once: a stage or k-step
+      // offset is an add to the start-address field (address >> 4, below 2^14
+      // for any shared-memory address, so the field never carries).
+      const uint64_t a_desc0 = sdesc_k_sw128(smem_u32(sa));
+      const uint64_t b_desc0 = sdesc_k_sw128(smem_u32(sb));
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
         tc_fence_after();
@@ -750,15 +755,16 @@ __global__ void __launch_bounds__(EpiWarps<EPI>::kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sa + stage * S::kATileBytes);
-          const uint32_t b_base = smem_u32(sb + (WS ? kb : stage) * S::kBTileBytes);
+          const uint64_t a_desc = a_desc0 + static_cast<uint64_t>((stage * S::kATileBytes) >> 4);
+          const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(((WS ? kb : stage) * S::kBTileBytes) >> 4);
+          const uint32_t acc_first = kb > 0 ? 1u : 0u;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 4 x 32 bytes of K per 128-byte row
-            const uint64_t adesc = sdesc_k_sw128(a_base + k * 32);
 #pragma unroll
             for (int c = 0; c < S::kInstCount; ++c) {
-              const uint64_t bdesc = sdesc_k_sw128(b_base + c * S::kInstN * S::kRowBytes + k * 32);
-              const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+              const uint64_t adesc = a_desc + static_cast<uint64_t>(k * 2);
+              const uint64_t bdesc = b_desc + static_cast<uint64_t>((c * S::kInstN * S::kRowBytes + k * 32) >> 4);
+              const uint32_t accumulate = k > 0 ? 1u : acc_first;
               if (FP8)
                 umma_f8(d_tmem + c * S::kInstN, adesc, bdesc, kIdesc, accumulate);
               else
