@@ -186,6 +186,43 @@ __device__ __forceinline__ float matrix_cell_w(float v, const float4 a, const fl
   return tanh_cell(fmaf(g, u, r));
 }
 
+// The same cell for two requests of one model at once (the grouped kernels'
+// request pairs): every FP32 step of tanh_cell, sigmoid_cell and
+// matrix_cell_w as one packed f32x2 instruction, whose lanes round exactly as
+// the scalar instruction does, so each lane's result is bit-identical to
+// matrix_cell_w and a pair takes about half the issue slots (the MUFU
+// operations stay scalar). The tanh keeps -d = -(1 + e) instead of d: round to
+// nearest is symmetric, so -(1 + e) rounds to exactly the negated sum, and the
+// quadratic's and the Newton steps' signs are turned to match, product for
+// product.
+__device__ __forceinline__ float2 f2s(float s) { return make_float2(s, s); }
+
+__device__ __forceinline__ float2 tanh_cell2(float2 x) {
+  const float2 t = ow::mul_f2(x, f2s(2.0f * 1.4426950408889634f));
+  const float2 e = make_float2(ex2_approx(-fabsf(t.x)), ex2_approx(-fabsf(t.y)));
+  const float2 nd = ow::sub_f2(f2s(-1.0f), e);
+  float2 y = ow::fma_f2(ow::fma_f2(f2s(0.31368835f), nd, f2s(1.4250640f)), nd, f2s(2.0995536f));
+  y = ow::fma_f2(y, ow::fma_f2(nd, y, f2s(1.0f)), y);
+  y = ow::fma_f2(y, ow::fma_f2(nd, y, f2s(1.0f)), y);
+  const float2 r = ow::fma_f2(f2s(2.0f), y, f2s(-1.0f));
+  return make_float2(copysignf(r.x, x.x), copysignf(r.y, x.y));
+}
+
+__device__ __forceinline__ float2 sigmoid_cell2(float2 z) {
+  const float2 t = ow::mul_f2(z, f2s(-1.4426950408889634f));
+  const float2 d = ow::add_f2(f2s(1.0f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
+  return make_float2(rcp_approx(d.x), rcp_approx(d.y));
+}
+
+__device__ __forceinline__ float2 matrix_cell_w2(float2 v, const float4 a, const float4 b, const float4 c) {
+  const float2 ha = tanh_cell2(ow::fma_f2(v, f2s(a.z), f2s(a.w)));
+  const float2 hb = tanh_cell2(ow::fma_f2(v, f2s(b.x), ow::fma_f2(ha, f2s(b.y), f2s(b.z))));
+  const float2 g = sigmoid_cell2(ow::fma_f2(v, f2s(b.w), f2s(c.x)));
+  const float2 u = ow::fma_f2(hb, f2s(c.y), ow::fma_f2(ha, f2s(c.z), f2s(c.w)));
+  const float2 r = ow::fma_f2(v, f2s(1.0f + a.x), f2s(a.y));
+  return tanh_cell2(ow::fma_f2(g, u, r));
+}
+
 template <bool VEC>
 __device__ __forceinline__ float matrix_cell(float v, const float* __restrict__ w12) {
   float4 a, b, c;
@@ -288,6 +325,7 @@ __device__ __forceinline__ void collapse_item(const float* mrow, const float* s_
 // traffic drops by the group size; the arithmetic per request is that of
 // matrix_cell, in the same order, so the results are unchanged.
 constexpr int kGroup = 8;
+static_assert(kGroup % 2 == 0, "request pairs");
 
 // 1g. expand + matrix layers [0, mid) for one group; thread per cell.
 __global__ void __launch_bounds__(256) t2_expand_pre_g(const float* __restrict__ x, const int* __restrict__ groups,
@@ -328,7 +366,11 @@ __global__ void __launch_bounds__(256) t2_expand_pre_g(const float* __restrict__
     float4 a, b, c;
     load_cell_weights<true>(mw + l * per_layer, a, b, c);
 #pragma unroll
-    for (int i = 0; i < kGroup; ++i) v[i] = matrix_cell_w(v[i], a, b, c);
+    for (int i = 0; i < kGroup; i += 2) {
+      const float2 o = matrix_cell_w2(make_float2(v[i], v[i + 1]), a, b, c);
+      v[i] = o.x;
+      v[i + 1] = o.y;
+    }
   }
 #pragma unroll
   for (int i = 0; i < kGroup; ++i)
@@ -373,7 +415,11 @@ __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict_
       float4 a, b, c;
       load_cell_weights<true>(mw + l * per_layer, a, b, c);
 #pragma unroll
-      for (int g = 0; g < kGroup; ++g) v[g] = matrix_cell_w(v[g], a, b, c);
+      for (int g = 0; g < kGroup; g += 2) {
+        const float2 o = matrix_cell_w2(make_float2(v[g], v[g + 1]), a, b, c);
+        v[g] = o.x;
+        v[g + 1] = o.y;
+      }
     }
 #pragma unroll
     for (int g = 0; g < kGroup; ++g) s_m[g][lr][t] = v[g];

@@ -28,14 +28,15 @@
 // stages start zeroed and TMA only brings finite rows), so their P of exactly
 // 0 keeps O = P V exact.
 //
-// Roles: warp 0 issues the TMA loads; two warpgroups of four warps run the
-// softmax and output of alternate heads (warpgroup g: head g of every unit);
-// one MMA warp per warpgroup polls that warpgroup's barriers and issues
-// whichever of its QK^T or PV is ready. A head takes twelve tcgen05.mma
+// Roles: warp 0 issues the TMA loads; four warpgroups of four warps (two at
+// BS = 128) run the softmax and output, warpgroup w taking head w % 2 of every
+// other unit; MMA warp g issues head g's products for the warpgroups of that
+// head, polling each one's barriers and issuing whichever QK^T or PV is ready. A head takes twelve tcgen05.mma
 // (QK^T: 2 per state, PV: BS / 16 per state), each of M = 128 and K = 16,
 // issued every ~50 cycles at N = 64 from one thread with its descriptors
-// precomputed, so the two issuers run in parallel and off the softmax path. Each warpgroup owns half of the TMEM buffers: while it works on
-// one head, the tensor cores fill its other buffers with the next heads' scores.
+// precomputed, so the two issuers run in parallel and off the softmax path.
+// Each warpgroup owns kBuffers / kWgs TMEM buffers: while it works on one
+// head, the tensor cores fill its other buffer with its next head's scores.
 #pragma once
 
 #include "ow_common.cuh"
@@ -60,21 +61,27 @@ struct TcAttnShape {
   static constexpr int kGroup = 2;                  // heads per work unit
   static constexpr int kBufCols = BS == 128 ? 128 : 64;  // TMEM columns of one head
   static constexpr int kBuffers = 512 / kBufCols;   // heads in flight
-  static constexpr int kPerWg = kBuffers / 2;       // buffers per softmax warpgroup
+  // softmax warpgroups: four (two TMEM buffers each) up to BS = 64; two at
+  // BS = 128, where a head holds 128 columns and only four fit
+  static constexpr int kWgs = BS == 128 ? 2 : 4;
+  static constexpr int kWgPerHead = kWgs / kGroup;  // warpgroups taking alternate units' head h
+  static constexpr int kPerWg = kBuffers / kWgs;    // buffers per softmax warpgroup
   static constexpr int kOCol = BS == 128 ? 64 : BS / 2;  // O columns of a buffer (P uses BS / 2 columns)
   static constexpr int kBoxBytes = BS * 128;       // one state's rows of one matrix, both heads (128 B per row)
   static constexpr int kTileBytes = 128 * 128;      // Q, K or V of a unit
   static constexpr int kStageBytes = 3 * kTileBytes;  // one unit
   static constexpr int kStages = 4;
-  static constexpr int kThreads = 96 + 256;
+  static constexpr int kThreads = 96 + 128 * kWgs;
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kOutBytes = 8 * 32 * 64;     // per softmax warp: 32 rows x 64 B of output
+  static constexpr int kOutBytes = 4 * kWgs * 32 * 64;  // per softmax warp: 32 rows x 64 B of output
   static constexpr int kTmemCols = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kOutBytes + kBarrierBytes;
-  // Registers per thread: an SM sub-partition holds every fourth warp (three of
-  // the eleven) in its 16,384 registers.
-  static constexpr int kMaxRegs = 168;
+  // Registers per thread: an SM sub-partition holds every fourth warp (five of
+  // nineteen, three of eleven) in its 16,384 registers.
+  static constexpr int kMaxRegs = kWgs == 4 ? 96 : 168;
   static_assert(kStageBytes % 1024 == 0, "1024 B aligned stages");
+  static_assert(kSmemBytes <= 232448, "227 KB of shared memory per CTA");
+  static_assert(8 * (2 * kStages + 4 * kBuffers) + 8 <= kBarrierBytes, "barrier area");
 };
 
 // MN-major operand in the 128-byte swizzle (V: rows = keys = K, 64 contiguous
@@ -205,7 +212,22 @@ template <int CHUNKS>
 __device__ __forceinline__ float2 attn_softmax_rows(uint32_t tb, int c0, int c, float2 sc, float scale_log2) {
   const int nch = (c + 31) >> 5;
   float2 sum2 = make_float2(0.0f, 0.0f);
-  if (nch <= 2) {
+  if constexpr (CHUNKS <= 2) {
+    // one TMEM round trip: both chunks in registers for the max and the
+    // exponentials (the four-warpgroup kernel's 96 registers hold them; the
+    // wider-state path below is compiled only for BS = 128)
+    uint32_t r0[32], r1[32];
+    tmem_ld32(tb + 32 * c0, r0);
+    if (CHUNKS == 2 && nch == 2) tmem_ld32(tb + 32 * (c0 + 1), r1);
+    tmem_ld_wait_dep(r0);
+    if (CHUNKS == 2 && nch == 2) tmem_ld_wait_dep(r1);
+    float mx = attn_max_any(r0, c, -INFINITY);
+    if (CHUNKS == 2 && nch == 2) mx = attn_max_any(r1, c - 32, mx);
+    const float2 off = make_float2(-mx * scale_log2, -mx * scale_log2);
+    attn_exp_any(r0, c, sc, off, sum2, tb + 16 * c0);
+    // P of chunk 0 goes to S chunk 0's columns, already read
+    if (CHUNKS == 2 && nch == 2) attn_exp_any(r1, c - 32, sc, off, sum2, tb + 16 * (c0 + 1));
+  } else if (nch <= 2) {
     // one TMEM round trip: both chunks in registers for the max and the exponentials
     uint32_t r0[32], r1[32];
     tmem_ld32(tb + 32 * c0, r0);
@@ -363,17 +385,27 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
       }
     }
   } else if (warp <= 2) {
-    // ---------------------------------------------------------------- MMA issue (one thread per warpgroup)
-    // MMA warp g serves warpgroup g: its k-th head is head g of this CTA's
-    // k-th unit (stage k % kStages, the 64-byte half g of the rows, TMEM
-    // buffer g + 2 (k % kPerWg)). QK(k) needs the stage's loads and the buffer
-    // free (the output of head k - kPerWg read); PV(k) needs P(k). The thread
-    // polls both and issues whichever is ready (a sleeping wait wakes too late here).
+    // ---------------------------------------------------------------- MMA issue
+    // MMA warp g issues head g of every unit. The CTA's unit i goes to
+    // warpgroup w = g + 2 (i % kWgPerHead) as that warpgroup's k-th head,
+    // k = i / kWgPerHead, in TMEM buffer w + kWgs (k % kPerWg); stage i %
+    // kStages, the 64-byte half g of its rows. QK(i) needs the stage's loads
+    // and the buffer free (the output of the warpgroup's head k - kPerWg read);
+    // PV(i) needs P. The thread keeps one QK / PV position per warpgroup it
+    // serves, polls them all and issues whatever is ready, so a slow warpgroup
+    // does not hold up the other (a sleeping wait wakes too late here).
     if (lane == 0) {
       const int g = warp - 1;
+      constexpr int H = S::kWgPerHead;
       constexpr uint32_t kIdescS = idesc_bf16(128, BS);
       constexpr uint32_t kIdescPV = idesc_bf16(128, 32) | (1u << 16);  // B (V) MN-major
-      int nq = 0, np = 0;  // next QK / PV head
+      int nq[H], np[H], cnt[H];  // per served warpgroup: next QK / PV head, heads in all
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        nq[h] = 0;
+        np[h] = 0;
+        cnt[h] = my_units > h ? (my_units - h + H - 1) / H : 0;
+      }
       // Descriptors of stage 0, built once: a stage, state or k-step offset is
       // an add to the start-address field (address >> 4, below 2^14 for any
       // shared-memory address, so the field never carries into the next one).
@@ -381,46 +413,58 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
       const uint64_t v_desc0 = sdesc_mn_sw128(smem_u32(stages) + 2 * S::kTileBytes + g * 64);
       unsigned long long t0 = 0;
       uint32_t idle = 0;
-      while (np < my_units) {
+      int left = 0;
+#pragma unroll
+      for (int h = 0; h < H; ++h) left += cnt[h];
+      while (left > 0) {
         bool progressed = false;
-        if (np < nq && mbar_test(&p_full[g + 2 * (np % S::kPerWg)], (np / S::kPerWg) & 1u)) {
-          tc_fence_after();
-          const int b = g + 2 * (np % S::kPerWg), s = np % S::kStages;
-          const uint32_t ta = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
-          const uint64_t vd = v_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
 #pragma unroll
-          for (int j = 0; j < K; ++j) {
-            uint32_t m[4];
-            state_lanes<BS>(j, m);
+        for (int h = 0; h < H; ++h) {
+          const int w = g + 2 * h;
+          if (np[h] < nq[h]) {
+            const int b = w + S::kWgs * (np[h] % S::kPerWg);
+            if (mbar_test(&p_full[b], (np[h] / S::kPerWg) & 1u)) {
+              tc_fence_after();
+              const int s = (h + H * np[h]) % S::kStages;
+              const uint32_t ta = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
+              const uint64_t vd = v_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
 #pragma unroll
-            for (int kk = 0; kk < BS / 16; ++kk)
-              umma_f16_ts_lanes(ta + S::kOCol, ta + 8 * kk, vd + static_cast<uint64_t>((j * BS + 16 * kk) * 8),
-                                kIdescPV, kk > 0 ? 1u : 0u, m);
-          }
-          umma_commit(&o_full[b]);
-          umma_commit(&empty[s]);
-          ++np;
-          progressed = true;
-        }
-        if (nq < my_units) {
-          const int s = nq % S::kStages, b = g + 2 * (nq % S::kPerWg);
-          if (mbar_test(&full[s], (nq / S::kStages) & 1u) &&
-              (nq < S::kPerWg || mbar_test(&t_empty[b], ((nq / S::kPerWg) - 1) & 1u))) {
-            tc_fence_after();
-            const uint32_t dt = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
-            const uint64_t qd = q_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
-            const uint64_t kd = qd + static_cast<uint64_t>(S::kTileBytes >> 4);
+              for (int j = 0; j < K; ++j) {
+                uint32_t m[4];
+                state_lanes<BS>(j, m);
 #pragma unroll
-            for (int j = 0; j < K; ++j) {
-              uint32_t m[4];
-              state_lanes<BS>(j, m);
-              const uint64_t kdj = kd + static_cast<uint64_t>(j * BS * 8);  // key rows of state j
-              umma_f16_lanes(dt, qd, kdj, kIdescS, 0u, m);
-              umma_f16_lanes(dt, qd + 2u, kdj + 2u, kIdescS, 1u, m);  // + 32 bytes of K
+                for (int kk = 0; kk < BS / 16; ++kk)
+                  umma_f16_ts_lanes(ta + S::kOCol, ta + 8 * kk, vd + static_cast<uint64_t>((j * BS + 16 * kk) * 8),
+                                    kIdescPV, kk > 0 ? 1u : 0u, m);
+              }
+              umma_commit(&o_full[b]);
+              umma_commit(&empty[s]);
+              ++np[h];
+              --left;
+              progressed = true;
             }
-            umma_commit(&s_full[b]);
-            ++nq;
-            progressed = true;
+          }
+          if (nq[h] < cnt[h]) {
+            const int i = h + H * nq[h];
+            const int s = i % S::kStages, b = w + S::kWgs * (nq[h] % S::kPerWg);
+            if (mbar_test(&full[s], (i / S::kStages) & 1u) &&
+                (nq[h] < S::kPerWg || mbar_test(&t_empty[b], ((nq[h] / S::kPerWg) - 1) & 1u))) {
+              tc_fence_after();
+              const uint32_t dt = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
+              const uint64_t qd = q_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
+              const uint64_t kd = qd + static_cast<uint64_t>(S::kTileBytes >> 4);
+#pragma unroll
+              for (int j = 0; j < K; ++j) {
+                uint32_t m[4];
+                state_lanes<BS>(j, m);
+                const uint64_t kdj = kd + static_cast<uint64_t>(j * BS * 8);  // key rows of state j
+                umma_f16_lanes(dt, qd, kdj, kIdescS, 0u, m);
+                umma_f16_lanes(dt, qd + 2u, kdj + 2u, kIdescS, 1u, m);  // + 32 bytes of K
+              }
+              umma_commit(&s_full[b]);
+              ++nq[h];
+              progressed = true;
+            }
           }
         }
         if (progressed) {
@@ -440,9 +484,11 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
     }
   } else {
     // ---------------------------------------------------------------- softmax + output
-    // Warpgroup wg takes head wg of each unit, its k-th head in TMEM buffer
-    // wg + 2 (k % kPerWg).
+    // Warpgroup wg takes head wg % 2 of the CTA's units i with i % kWgPerHead
+    // = wg / 2, its k-th head in TMEM buffer wg + kWgs (k % kPerWg).
     const int wg = (warp - 3) >> 2;
+    const int par = wg >> 1;
+    const int ustep = S::kWgPerHead * static_cast<int>(gridDim.x);
     const int quad = warp & 3;                    // TMEM lane quadrant: tile rows quad*32 .. +31
     const int blk = (quad * 32) / BS;             // the tile block (state) of this warp's rows
     const int rib = quad * 32 - blk * BS + lane;  // this thread's row within its block
@@ -452,8 +498,8 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
     int prev_r = 0, prev_c = 0, prev_col = 0;  // the head whose output is pending
     float2 prev_sum = make_float2(0.0f, 0.0f);
     int nxt_r = 0, nxt_c = 0;  // this warp's state (first row, count) in the next unit
-    if (my_units > 0) {
-      const int st = (static_cast<int>(blockIdx.x) / hgs) * K + blk;
+    if (my_units > par) {
+      const int st = ((static_cast<int>(blockIdx.x) + par * static_cast<int>(gridDim.x)) / hgs) * K + blk;
       nxt_r = p.offsets[min(st, p.batch)];
       nxt_c = p.offsets[min(st + 1, p.batch)] - nxt_r;
     }
@@ -463,7 +509,7 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
     // rows x 64 contiguous bytes per store instruction.
     uint8_t* ostage = out_stage + (warp - 3) * 32 * 64;
     auto output = [&](int k) -> bool {
-      const int b = wg + 2 * (k % S::kPerWg);
+      const int b = wg + S::kWgs * (k % S::kPerWg);
       if (!mbar_wait(&o_full[b], (k / S::kPerWg) & 1u, abort_flag, p.err)) return false;
       tc_fence_after();
       const int first = rib - lane;  // the warp's first row within its block
@@ -498,15 +544,15 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
     // Iteration k: softmax(k), then the output of head k - 1 (whose PV ran
     // during this softmax); the MMA warp then reuses that buffer for QK(k + 1).
     int k = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++k) {
-      const int col = ((u % hgs) * S::kGroup + wg) * 32;
+    for (int u = blockIdx.x + par * static_cast<int>(gridDim.x); u < n_units; u += ustep, ++k) {
+      const int col = ((u % hgs) * S::kGroup + (wg & 1)) * 32;
       const int r0 = nxt_r, c = nxt_c;
-      if (u + static_cast<int>(gridDim.x) < n_units) {
-        const int st = ((u + static_cast<int>(gridDim.x)) / hgs) * K + blk;
+      if (u + ustep < n_units) {
+        const int st = ((u + ustep) / hgs) * K + blk;
         nxt_r = p.offsets[min(st, p.batch)];
         nxt_c = p.offsets[min(st + 1, p.batch)] - nxt_r;
       }
-      const int b = wg + 2 * (k % S::kPerWg);
+      const int b = wg + S::kWgs * (k % S::kPerWg);
       if (!mbar_wait(&s_full[b], (k / S::kPerWg) & 1u, abort_flag, p.err)) {
         ok = false;
         break;
