@@ -193,14 +193,21 @@ __global__ void __launch_bounds__(TcFfnShape<D>::kThreads, 1)
       // per-buffer phase parities as bits (bit b = buffer b), kept in registers
       uint32_t h_bits = 0u, hs_bits = 0u;
       bool ok = true;
-      // takes the next weight box of the ring (false once a wait expired)
-      auto take = [&]() -> uint32_t {
+      // Descriptors of the first weight box, the A tile and the first hidden
+      // tile, built once: a box, k-block or k-step offset is an add to the
+      // start-address field (address >> 4, below 2^14 for any shared-memory
+      // address, so the field never carries into the next one).
+      const uint64_t w_desc0 = sdesc_k_sw128(smem_u32(sW));
+      const uint64_t a_desc0 = sdesc_k_sw128(smem_u32(sA));
+      const uint64_t h_desc0 = sdesc_k_sw128(smem_u32(sH));
+      // takes the next weight box of the ring: its descriptor (ok = false once a wait expired)
+      auto take = [&]() -> uint64_t {
         if (!ok || !mbar_wait(&full[stage], phase, abort_flag, p.err)) {
           ok = false;
           return 0u;
         }
         tc_fence_after();
-        return smem_u32(sW + stage * S::kStageBytes);
+        return w_desc0 + static_cast<uint64_t>(stage * (S::kStageBytes >> 4));
       };
       auto release = [&]() {
         umma_commit(&empty[stage]);  // the box is reusable once these MMAs retire
@@ -223,13 +230,14 @@ __global__ void __launch_bounds__(TcFfnShape<D>::kThreads, 1)
           h_bits ^= 1u << b;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(D + b * S::kChunk);
+#pragma unroll
           for (int kb = 0; kb < S::kDk; ++kb) {
-            const uint32_t wb = take();
+            const uint64_t wd = take();
             if (!ok) return;
-            const uint32_t ab = smem_u32(sA + kb * S::kTile);
+            const uint64_t ad = a_desc0 + static_cast<uint64_t>(kb * (S::kTile >> 4));
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              umma_f16(d_tmem, sdesc_k_sw128(ab + k * 32), sdesc_k_sw128(wb + k * 32), kIdesc,
+              umma_f16(d_tmem, ad + static_cast<uint64_t>(2 * k), wd + static_cast<uint64_t>(2 * k), kIdesc,
                        (kb > 0 || k > 0) ? 1u : 0u);
             release();
           }
@@ -250,15 +258,17 @@ __global__ void __launch_bounds__(TcFfnShape<D>::kThreads, 1)
             return;
           }
           tc_fence_after();
+#pragma unroll
           for (int kb = 0; kb < S::kHk; ++kb) {
-            const uint32_t hb = smem_u32(sH + (b * S::kHk + kb) * S::kTile);
+            const uint64_t hd = h_desc0 + static_cast<uint64_t>((b * S::kHk + kb) * (S::kTile >> 4));
+#pragma unroll
             for (int nh = 0; nh < S::kNh; ++nh) {
-              const uint32_t wb = take();
+              const uint64_t wd = take();
               if (!ok) return;
 #pragma unroll
               for (int k = 0; k < 4; ++k)
-                umma_f16(tmem_base + static_cast<uint32_t>(nh * 128), sdesc_k_sw128(hb + k * 32),
-                         sdesc_k_sw128(wb + k * 32), kIdesc, (c > 0 || kb > 0 || k > 0) ? 1u : 0u);
+                umma_f16(tmem_base + static_cast<uint32_t>(nh * 128), hd + static_cast<uint64_t>(2 * k),
+                         wd + static_cast<uint64_t>(2 * k), kIdesc, (c > 0 || kb > 0 || k > 0) ? 1u : 0u);
               release();
             }
           }
