@@ -12,17 +12,19 @@
 // half of the rows. Per head, with the tile's states sharing TMEM columns
 // (each MMA writes only its state's lanes: the disable-output-lane mask):
 //   S = Q K^T        per state j: tcgen05.mma, M = 128, N = BS, K = 32, into
-//                    TMEM columns 0 .. BS-1 of lanes j*BS .. j*BS+BS-1;
+//                    the warpgroup's score region (BS columns) at lanes
+//                    j*BS .. j*BS+BS-1;
 //   P = softmax(S)   one thread per query row reads its state's keys (at
 //                    most BS / 32 chunks of 32 columns) from TMEM and writes P
 //                    as bf16 into the same TMEM columns (two values per 32-bit
 //                    column), 0 past the state's count;
 //   O = P V          per state j: tcgen05.mma with A = P straight from TMEM
 //                    and B = the state's V rows from shared memory
-//                    (MN-major), into the columns after P of its lanes;
+//                    (MN-major), into one of the warpgroup's two 32-column
+//                    O buffers;
 //   out = O / rowsum bf16, written by the same threads.
-// A head thus holds 64 TMEM columns (128 when BS = 128), so eight heads (four)
-// are in flight. Every warp's 32 rows lie in one state, so the key range (and
+// A warpgroup thus holds a 64-column score region (128 when BS = 128) and two
+// O buffers. Every warp's 32 rows lie in one state, so the key range (and
 // the mask of the last partial chunk) is the same for all its lanes. Key
 // positions past a state's count hold whatever the stage held before (finite:
 // stages start zeroed and TMA only brings finite rows), so their P of exactly
@@ -31,12 +33,13 @@
 // Roles: warp 0 issues the TMA loads; four warpgroups of four warps (two at
 // BS = 128) run the softmax and output, warpgroup w taking head w % 2 of every
 // other unit; MMA warp g issues head g's products for the warpgroups of that
-// head, polling each one's barriers and issuing whichever QK^T or PV is ready. A head takes twelve tcgen05.mma
-// (QK^T: 2 per state, PV: BS / 16 per state), each of M = 128 and K = 16,
-// issued every ~50 cycles at N = 64 from one thread with its descriptors
-// precomputed, so the two issuers run in parallel and off the softmax path.
-// Each warpgroup owns kBuffers / kWgs TMEM buffers: while it works on one
-// head, the tensor cores fill its other buffer with its next head's scores.
+// head, polling each one's barriers and issuing whichever QK^T or PV is ready.
+// A head takes twelve tcgen05.mma (QK^T: 2 per state, PV: BS / 16 per state),
+// each of M = 128 and K = 16, issued every ~50 cycles at N = 64 from one
+// thread with its descriptors precomputed, so the two issuers run in parallel
+// and off the softmax path. A warpgroup's next scores go into its score region
+// right behind the PV product that reads its P, so they are computed while the
+// warpgroup writes the previous head's output.
 #pragma once
 
 #include "ow_common.cuh"
@@ -59,14 +62,13 @@ struct TcAttnShape {
   static constexpr int kStatesPerTile = 128 / BS;
   static constexpr int kChunks = BS / 32;           // key chunks of a block
   static constexpr int kGroup = 2;                  // heads per work unit
-  static constexpr int kBufCols = BS == 128 ? 128 : 64;  // TMEM columns of one head
-  static constexpr int kBuffers = 512 / kBufCols;   // heads in flight
+  static constexpr int kSCols = BS == 128 ? 128 : 64;  // TMEM columns of a score region (P over its first BS / 2)
   // softmax warpgroups: four (two TMEM buffers each) up to BS = 64; two at
   // BS = 128, where a head holds 128 columns and only four fit
   static constexpr int kWgs = BS == 128 ? 2 : 4;
   static constexpr int kWgPerHead = kWgs / kGroup;  // warpgroups taking alternate units' head h
-  static constexpr int kPerWg = kBuffers / kWgs;    // buffers per softmax warpgroup
-  static constexpr int kOCol = BS == 128 ? 64 : BS / 2;  // O columns of a buffer (P uses BS / 2 columns)
+  // a warpgroup's TMEM: one score region and two 32-column O buffers
+  static constexpr int kWgCols = kSCols + 64;
   static constexpr int kBoxBytes = BS * 128;       // one state's rows of one matrix, both heads (128 B per row)
   static constexpr int kTileBytes = 128 * 128;      // Q, K or V of a unit
   static constexpr int kStageBytes = 3 * kTileBytes;  // one unit
@@ -81,7 +83,8 @@ struct TcAttnShape {
   static constexpr int kMaxRegs = kWgs == 4 ? 96 : 168;
   static_assert(kStageBytes % 1024 == 0, "1024 B aligned stages");
   static_assert(kSmemBytes <= 232448, "227 KB of shared memory per CTA");
-  static_assert(8 * (2 * kStages + 4 * kBuffers) + 8 <= kBarrierBytes, "barrier area");
+  static_assert(kWgs * kWgCols <= kTmemCols, "TMEM columns");
+  static_assert(8 * (2 * kStages + 6 * kWgs) + 8 <= kBarrierBytes, "barrier area");
 };
 
 // MN-major operand in the 128-byte swizzle (V: rows = keys = K, 64 contiguous
@@ -298,11 +301,11 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
   uint8_t* out_stage = smem + S::kStages * S::kStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(out_stage + S::kOutBytes);
   uint64_t* empty = full + S::kStages;
-  uint64_t* s_full = empty + S::kStages;
-  uint64_t* p_full = s_full + S::kBuffers;
-  uint64_t* o_full = p_full + S::kBuffers;
-  uint64_t* t_empty = o_full + S::kBuffers;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(t_empty + S::kBuffers);
+  uint64_t* s_full = empty + S::kStages;    // [kWgs] scores of the warpgroup's head in its region
+  uint64_t* p_full = s_full + S::kWgs;      // [kWgs] P written (the region's scores read)
+  uint64_t* o_full = p_full + S::kWgs;      // [kWgs][2] O buffer written
+  uint64_t* t_empty = o_full + 2 * S::kWgs; // [kWgs][2] O buffer read
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(t_empty + 2 * S::kWgs);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -312,9 +315,11 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 2);  // both MMA warps' PV products have read the stage
     }
-    for (int b = 0; b < S::kBuffers; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 4);
+    for (int w = 0; w < S::kWgs; ++w) {
+      mbar_init(&s_full[w], 1);
+      mbar_init(&p_full[w], 4);
+    }
+    for (int b = 0; b < 2 * S::kWgs; ++b) {
       mbar_init(&o_full[b], 1);
       mbar_init(&t_empty[b], 4);
     }
@@ -388,12 +393,15 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
     // ---------------------------------------------------------------- MMA issue
     // MMA warp g issues head g of every unit. The CTA's unit i goes to
     // warpgroup w = g + 2 (i % kWgPerHead) as that warpgroup's k-th head,
-    // k = i / kWgPerHead, in TMEM buffer w + kWgs (k % kPerWg); stage i %
-    // kStages, the 64-byte half g of its rows. QK(i) needs the stage's loads
-    // and the buffer free (the output of the warpgroup's head k - kPerWg read);
-    // PV(i) needs P. The thread keeps one QK / PV position per warpgroup it
-    // serves, polls them all and issues whatever is ready, so a slow warpgroup
-    // does not hold up the other (a sleeping wait wakes too late here).
+    // k = i / kWgPerHead: stage i % kStages, the 64-byte half g of its rows.
+    // PV(k) reads P from the warpgroup's score region and accumulates into its
+    // O buffer k % 2 (free once the output of head k - 2 is read); QK(k + 1)
+    // then goes straight into the same score region. tcgen05.mma operations
+    // of one thread run in issue order, so it overwrites P only after PV(k)
+    // has read it, and it runs while the warpgroup writes head k - 1's output.
+    // The thread keeps one QK / PV position per warpgroup it serves, polls them
+    // all and issues whatever is ready, so a slow warpgroup does not hold up
+    // the other (a sleeping wait wakes too late here).
     if (lane == 0) {
       const int g = warp - 1;
       constexpr int H = S::kWgPerHead;
@@ -422,11 +430,12 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
         for (int h = 0; h < H; ++h) {
           const int w = g + 2 * h;
           if (np[h] < nq[h]) {
-            const int b = w + S::kWgs * (np[h] % S::kPerWg);
-            if (mbar_test(&p_full[b], (np[h] / S::kPerWg) & 1u)) {
+            const int k = np[h], ob = 2 * w + (k & 1);
+            if (mbar_test(&p_full[w], k & 1u) && (k < 2 || mbar_test(&t_empty[ob], ((k >> 1) - 1) & 1u))) {
               tc_fence_after();
-              const int s = (h + H * np[h]) % S::kStages;
-              const uint32_t ta = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
+              const int s = (h + H * k) % S::kStages;
+              const uint32_t ta = tmem_base + static_cast<uint32_t>(w * S::kWgCols);
+              const uint32_t to = ta + static_cast<uint32_t>(S::kSCols + 32 * (k & 1));
               const uint64_t vd = v_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
 #pragma unroll
               for (int j = 0; j < K; ++j) {
@@ -434,23 +443,23 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
                 state_lanes<BS>(j, m);
 #pragma unroll
                 for (int kk = 0; kk < BS / 16; ++kk)
-                  umma_f16_ts_lanes(ta + S::kOCol, ta + 8 * kk, vd + static_cast<uint64_t>((j * BS + 16 * kk) * 8),
+                  umma_f16_ts_lanes(to, ta + 8 * kk, vd + static_cast<uint64_t>((j * BS + 16 * kk) * 8),
                                     kIdescPV, kk > 0 ? 1u : 0u, m);
               }
-              umma_commit(&o_full[b]);
+              umma_commit(&o_full[ob]);
               umma_commit(&empty[s]);
               ++np[h];
               --left;
               progressed = true;
             }
           }
-          if (nq[h] < cnt[h]) {
+          // QK(k) once PV(k - 1) is issued: the score region is the warpgroup's only one
+          if (nq[h] < cnt[h] && nq[h] == np[h]) {
             const int i = h + H * nq[h];
-            const int s = i % S::kStages, b = w + S::kWgs * (nq[h] % S::kPerWg);
-            if (mbar_test(&full[s], (i / S::kStages) & 1u) &&
-                (nq[h] < S::kPerWg || mbar_test(&t_empty[b], ((nq[h] / S::kPerWg) - 1) & 1u))) {
+            const int s = i % S::kStages;
+            if (mbar_test(&full[s], (i / S::kStages) & 1u)) {
               tc_fence_after();
-              const uint32_t dt = tmem_base + static_cast<uint32_t>(b * S::kBufCols);
+              const uint32_t dt = tmem_base + static_cast<uint32_t>(w * S::kWgCols);
               const uint64_t qd = q_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
               const uint64_t kd = qd + static_cast<uint64_t>(S::kTileBytes >> 4);
 #pragma unroll
@@ -461,7 +470,7 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
                 umma_f16_lanes(dt, qd, kdj, kIdescS, 0u, m);
                 umma_f16_lanes(dt, qd + 2u, kdj + 2u, kIdescS, 1u, m);  // + 32 bytes of K
               }
-              umma_commit(&s_full[b]);
+              umma_commit(&s_full[w]);
               ++nq[h];
               progressed = true;
             }
@@ -485,7 +494,8 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
   } else {
     // ---------------------------------------------------------------- softmax + output
     // Warpgroup wg takes head wg % 2 of the CTA's units i with i % kWgPerHead
-    // = wg / 2, its k-th head in TMEM buffer wg + kWgs (k % kPerWg).
+    // = wg / 2: its k-th head's scores and P in the warpgroup's score region,
+    // its O in the warpgroup's O buffer k % 2.
     const int wg = (warp - 3) >> 2;
     const int par = wg >> 1;
     const int ustep = S::kWgPerHead * static_cast<int>(gridDim.x);
@@ -509,13 +519,13 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
     // rows x 64 contiguous bytes per store instruction.
     uint8_t* ostage = out_stage + (warp - 3) * 32 * 64;
     auto output = [&](int k) -> bool {
-      const int b = wg + S::kWgs * (k % S::kPerWg);
-      if (!mbar_wait(&o_full[b], (k / S::kPerWg) & 1u, abort_flag, p.err)) return false;
+      const int b = 2 * wg + (k & 1);
+      if (!mbar_wait(&o_full[b], (k >> 1) & 1u, abort_flag, p.err)) return false;
       tc_fence_after();
       const int first = rib - lane;  // the warp's first row within its block
       if (first < prev_c) {          // the warp has rows of its state
         uint32_t r[32];
-        tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(b * S::kBufCols) + S::kOCol, r);
+        tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(wg * S::kWgCols + S::kSCols + 32 * (k & 1)), r);
         tmem_ld_wait_dep(r);
         const float inv = 1.0f / (prev_sum.x + prev_sum.y);
 #pragma unroll
@@ -552,21 +562,20 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
         nxt_r = p.offsets[min(st, p.batch)];
         nxt_c = p.offsets[min(st + 1, p.batch)] - nxt_r;
       }
-      const int b = wg + S::kWgs * (k % S::kPerWg);
-      if (!mbar_wait(&s_full[b], (k / S::kPerWg) & 1u, abort_flag, p.err)) {
+      if (!mbar_wait(&s_full[wg], k & 1u, abort_flag, p.err)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float2 sum2 = make_float2(0.0f, 0.0f);
       if (rib - lane < c) {  // the warp has rows of its state
-        sum2 = attn_softmax_rows<S::kChunks>(tmem_base + lane_off + static_cast<uint32_t>(b * S::kBufCols), 0, c,
+        sum2 = attn_softmax_rows<S::kChunks>(tmem_base + lane_off + static_cast<uint32_t>(wg * S::kWgCols), 0, c,
                                              sc, p.scale_log2);
         tmem_st_wait();
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(&p_full[wg]);
       if (k > 0 && !output(k - 1)) {
         ok = false;
         break;
