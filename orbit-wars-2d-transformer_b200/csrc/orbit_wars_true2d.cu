@@ -28,6 +28,8 @@
 #include "orbit_wars_cuda.h"
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <condition_variable>
 #include <cstdint>
@@ -379,10 +381,13 @@ __global__ void __launch_bounds__(256) t2_expand_pre_g(const float* __restrict__
 
 // 3g. matrix layers [mid, layers) + collapse for one group: CTA = 4 rows of
 // every request of the group (blockDim = 4 * rows, at most 512 threads).
+// done (or nullptr): one word per CTA in mapped host memory, set to `epoch`
+// once the CTA's outputs are visible to the host, so host threads can copy a
+// group's requests while later groups still run.
 __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict__ groups,
                                                           const float* __restrict__ all_w, int models, T2Dev L,
                                                           const float* __restrict__ m, float* __restrict__ out,
-                                                          int* err) {
+                                                          int* err, unsigned* done, unsigned epoch) {
   constexpr int kRows = 4;  // rows of each request per CTA
   __shared__ float s_m[kGroup][kRows][kRowStride];
   __shared__ float s_bias[2][kTargets][kRowStride];  // target and send biases x log2 e
@@ -455,6 +460,13 @@ __global__ void __launch_bounds__(512) t2_post_collapse_g(const int* __restrict_
     const float4 v = make_float4(s_frac[g][lr][2 * q], s_send[g][lr][2 * q], s_frac[g][lr][2 * q + 1],
                                  s_send[g][lr][2 * q + 1]);
     reinterpret_cast<float4*>(out + (static_cast<long long>(rq) * L.rows + row) * kOutPerRow)[q] = v;
+  }
+  if (done != nullptr) {
+    // every thread orders its own output stores before the barrier, then one
+    // thread publishes the CTA's done word
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(done + blockIdx.y * gridDim.x + blockIdx.x) = epoch;
   }
 }
 
@@ -1084,6 +1096,9 @@ struct Workspace {
   size_t pin_out_cap = 0;
   unsigned char* pin_map = nullptr;  // mapped pinned outputs (synchronous host-buffer forwards)
   size_t pin_map_cap = 0;
+  unsigned* done_map = nullptr;  // mapped done words of the collapse CTAs, one per CTA
+  size_t done_cap = 0;
+  unsigned done_epoch = 0;       // the value this call's CTAs write (0 never)
   unsigned char* pin_meta = nullptr;  // model indices and the group table of a call
   size_t pin_meta_cap = 0;
   std::vector<cudaEvent_t> out_pieces;  // output download pieces (host-buffer forwards)
@@ -1200,23 +1215,43 @@ class CopyPool {
       std::memcpy(dst, src, bytes);
       return;
     }
+    struct Job {
+      unsigned char* dst;
+      const unsigned char* src;
+      size_t bytes, per;
+    } job{dst, src, bytes, ((bytes + parts - 1) / parts + 63) & ~size_t(63)};
+    run_parts(
+        [](void* c, size_t k) {
+          const Job* j = static_cast<const Job*>(c);
+          const size_t o = k * j->per;
+          if (o < j->bytes) std::memcpy(j->dst + o, j->src + o, std::min(j->per, j->bytes - o));
+        },
+        &job, parts);
+  }
+  // fn(ctx, k) for k = 0 .. parts - 1 (at most the workers + 1): k = 0 on the
+  // calling thread, the rest on workers; returns when all have returned. In a
+  // forked child every part runs on the calling thread, in order.
+  void run_parts(void (*fn)(void*, size_t), void* ctx, size_t parts) {
+    parts = std::max<size_t>(1, std::min<size_t>(parts, workers_ + 1));
+    if (parts == 1 || forked_) {
+      for (size_t k = 0; k < parts; ++k) fn(ctx, k);
+      return;
+    }
     std::lock_guard<std::mutex> one(call_mu_);
-    const size_t per = ((bytes + parts - 1) / parts + 63) & ~size_t(63);
     {
       std::lock_guard<std::mutex> lk(mu_);
-      dst_ = dst;
-      src_ = src;
-      bytes_ = bytes;
-      per_ = per;
+      fn_ = fn;
+      ctx_ = ctx;
       parts_ = parts;
       pending_ = parts - 1;
       ++generation_;
     }
     cv_.notify_all();
-    std::memcpy(dst, src, std::min(per, bytes));
+    fn(ctx, 0);
     std::unique_lock<std::mutex> lk(mu_);
     done_.wait(lk, [&] { return pending_ == 0; });
   }
+  size_t threads() const { return forked_ ? 1 : workers_ + 1; }
 
  private:
   CopyPool() {
@@ -1228,22 +1263,19 @@ class CopyPool {
   void run(size_t k) {
     uint64_t seen = 0;
     for (;;) {
-      unsigned char* dst;
-      const unsigned char* src;
-      size_t bytes, per, parts;
+      void (*fn)(void*, size_t);
+      void* ctx;
+      size_t parts;
       {
         std::unique_lock<std::mutex> lk(mu_);
         cv_.wait(lk, [&] { return generation_ != seen; });
         seen = generation_;
-        dst = dst_;
-        src = src_;
-        bytes = bytes_;
-        per = per_;
+        fn = fn_;
+        ctx = ctx_;
         parts = parts_;
       }
       if (k < parts) {
-        const size_t o = k * per;
-        if (o < bytes) std::memcpy(dst + o, src + o, std::min(per, bytes - o));
+        fn(ctx, k);
         std::lock_guard<std::mutex> lk(mu_);
         if (--pending_ == 0) done_.notify_one();
       }
@@ -1253,13 +1285,63 @@ class CopyPool {
   std::mutex call_mu_, mu_;
   std::condition_variable cv_, done_;
   uint64_t generation_ = 0;
-  unsigned char* dst_ = nullptr;
-  const unsigned char* src_ = nullptr;
-  size_t bytes_ = 0, per_ = 0, parts_ = 0, pending_ = 0;
+  void (*fn_)(void*, size_t) = nullptr;
+  void* ctx_ = nullptr;
+  size_t parts_ = 0, pending_ = 0;
   static inline volatile bool forked_ = false;
 };
 
 void par_copy(unsigned char* dst, const unsigned char* src, size_t bytes) { CopyPool::get().copy(dst, src, bytes); }
+
+// Host side of a streamed output copy. The collapse CTAs publish one done word
+// each (set to the call's epoch) in mapped memory after their outputs; the pool
+// threads take the model groups in launch order, wait for a group's words and
+// copy its requests' rows to the caller's buffer while later groups still run.
+struct GroupCopy {
+  const volatile unsigned* done;
+  unsigned epoch;
+  size_t per_group;          // collapse CTAs per group
+  const int* table;          // kGroup + 1 ints per group: the model, then request indices (-1: none)
+  size_t n_groups;
+  const unsigned char* src;  // the mapped outputs
+  unsigned char* dst;        // the caller's outputs
+  size_t req_bytes;
+  cudaStream_t stream;
+  std::chrono::steady_clock::time_point deadline;
+  std::atomic<size_t> next{0};
+  std::atomic<int> stream_done{0};  // set by the calling thread once the stream has drained
+  std::atomic<int> gave_up{0};      // some group's words never came: the caller copies everything
+};
+
+void group_copy(void* c, size_t k) {
+  GroupCopy* j = static_cast<GroupCopy*>(c);
+  for (;;) {
+    const size_t g = j->next.fetch_add(1);
+    if (g >= j->n_groups) return;
+    for (size_t b = 0; b < j->per_group; ++b) {
+      const volatile unsigned* w = j->done + g * j->per_group + b;
+      for (unsigned spins = 1; *w != j->epoch; ++spins) {
+        if (j->gave_up.load(std::memory_order_relaxed) != 0) return;
+        if ((spins & 1023u) != 0) continue;
+        // the calling thread watches the stream: once it has drained, a word
+        // still unset belongs to a CTA that returned early (a device error)
+        if (k == 0 && j->stream_done.load() == 0 && cudaStreamQuery(j->stream) != cudaErrorNotReady)
+          j->stream_done.store(1);
+        if ((j->stream_done.load() != 0 && *w != j->epoch) || std::chrono::steady_clock::now() > j->deadline) {
+          j->gave_up.store(1);
+          return;
+        }
+      }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    const int* t = j->table + g * (kGroup + 1);
+    for (int i = 1; i <= kGroup; ++i)
+      if (t[i] >= 0) {
+        const size_t o = static_cast<size_t>(t[i]) * j->req_bytes;
+        std::memcpy(j->dst + o, j->src + o, j->req_bytes);
+      }
+  }
+}
 
 // Piece size for a staged transfer of `bytes`: four pieces, none under 512 KB.
 size_t copy_piece(size_t bytes) { return std::max<size_t>(size_t(512) << 10, ((bytes + 3) / 4 + 4095) & ~size_t(4095)); }
@@ -1368,6 +1450,7 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
   // outputs over PCIe into mapped pinned memory while it runs
   const bool mapped_out = output_rows != nullptr && dec == nullptr && sync;
   float* out_target = W.out;
+  unsigned* done_dev = nullptr;
   if (mapped_out) {
     const size_t bytes = out_n * sizeof(float);
     if (bytes > W.pin_map_cap || W.pin_map == nullptr) {
@@ -1380,8 +1463,25 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
     void* dp = nullptr;
     T2_TRY(cudaHostGetDevicePointer(&dp, W.pin_map, 0));
     out_target = static_cast<float*>(dp);
+    const size_t words = static_cast<size_t>(g3.x) * g3.y;
+    if (words > W.done_cap || W.done_map == nullptr) {
+      if (W.done_map != nullptr) cudaFreeHost(W.done_map);
+      W.done_map = nullptr;
+      W.done_cap = 0;
+      T2_TRY(cudaHostAlloc(reinterpret_cast<void**>(&W.done_map), words * sizeof(unsigned), cudaHostAllocMapped));
+      std::memset(W.done_map, 0, words * sizeof(unsigned));
+      W.done_cap = words;
+    }
+    if (++W.done_epoch == 0) {  // wrapped: clear the words so no stale one matches
+      std::memset(W.done_map, 0, W.done_cap * sizeof(unsigned));
+      W.done_epoch = 1;
+    }
+    void* dd = nullptr;
+    T2_TRY(cudaHostGetDevicePointer(&dd, W.done_map, 0));
+    done_dev = static_cast<unsigned*>(dd);
   }
-  t2_post_collapse_g<<<g3, threads3, 0, W.stream>>>(W.groups, W.weights, models, D, W.m, out_target, W.err);
+  t2_post_collapse_g<<<g3, threads3, 0, W.stream>>>(W.groups, W.weights, models, D, W.m, out_target, W.err,
+                                                    done_dev, W.done_epoch);
   T2_TRY(cudaGetLastError());
   mark(nullptr);
   if (dec != nullptr) {
@@ -1406,8 +1506,25 @@ OrbitWarsCudaStatus run_forward(Workspace& W, const float* input_rows, const siz
     return ok();
   }
   if (mapped_out) {
+    // each group's rows go to the caller as soon as its CTAs are done; if a
+    // wait ends without them (a device error, or a minute after the launches),
+    // everything is copied once the stream has finished
+    GroupCopy job;
+    job.done = W.done_map;
+    job.epoch = W.done_epoch;
+    job.per_group = g3.x;
+    job.table = gt.data();
+    job.n_groups = n_groups;
+    job.src = W.pin_map;
+    job.dst = reinterpret_cast<unsigned char*>(output_rows);
+    job.req_bytes = static_cast<size_t>(L.rows) * kOutPerRow * sizeof(float);
+    job.stream = W.stream;
+    job.deadline = std::chrono::steady_clock::now() + std::chrono::seconds(60);
+    CopyPool& pool = CopyPool::get();
+    pool.run_parts(group_copy, &job, pool.threads());
     const OrbitWarsCudaStatus st = finish(W);
-    if (st.code == kOk) par_copy(reinterpret_cast<unsigned char*>(output_rows), W.pin_map, out_n * sizeof(float));
+    if (st.code == kOk && job.gave_up.load() != 0)
+      par_copy(reinterpret_cast<unsigned char*>(output_rows), W.pin_map, out_n * sizeof(float));
     return st;
   }
   // outputs through pinned memory in pieces, an event after each piece's DMA:
