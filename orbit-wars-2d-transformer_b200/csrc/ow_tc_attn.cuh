@@ -23,16 +23,15 @@
 //                    (MN-major), into one of the warpgroup's two 32-column
 //                    O buffers;
 //   out = O / rowsum bf16, written by the same threads.
-// A warpgroup thus holds a 64-column score region (128 when BS = 128) and two
-// O buffers. Every warp's 32 rows lie in one state, so the key range (and
+// A warpgroup thus holds a 64-column score region and two O buffers (at
+// BS = 128 a 128-column region with O in its columns 64 .. 95). Every warp's 32 rows lie in one state, so the key range (and
 // the mask of the last partial chunk) is the same for all its lanes. Key
 // positions past a state's count hold whatever the stage held before (finite:
 // stages start zeroed and TMA only brings finite rows), so their P of exactly
 // 0 keeps O = P V exact.
 //
-// Roles: warp 0 issues the TMA loads; four warpgroups of four warps (two at
-// BS = 128) run the softmax and output, warpgroup w taking head w % 2 of every
-// other unit; MMA warp g issues head g's products for the warpgroups of that
+// Roles: warp 0 issues the TMA loads; four warpgroups of four warps run the
+// softmax and output, warpgroup w taking head w % 2 of every other unit; MMA warp g issues head g's products for the warpgroups of that
 // head, polling each one's barriers and issuing whichever QK^T or PV is ready.
 // A head takes twelve tcgen05.mma (QK^T: 2 per state, PV: BS / 16 per state),
 // each of M = 128 and K = 16, issued every ~50 cycles at N = 64 from one
@@ -65,10 +64,13 @@ struct TcAttnShape {
   static constexpr int kSCols = BS == 128 ? 128 : 64;  // TMEM columns of a score region (P over its first BS / 2)
   // softmax warpgroups: four (two TMEM buffers each) up to BS = 64; two at
   // BS = 128, where a head holds 128 columns and only four fit
-  static constexpr int kWgs = BS == 128 ? 2 : 4;
+  static constexpr int kWgs = 4;
   static constexpr int kWgPerHead = kWgs / kGroup;  // warpgroups taking alternate units' head h
-  // a warpgroup's TMEM: one score region and two 32-column O buffers
-  static constexpr int kWgCols = kSCols + 64;
+  // a warpgroup's TMEM: one score region and two 32-column O buffers; at
+  // BS = 128 (four 128-column regions fill TMEM) O goes into the region's
+  // columns 64 .. 95, free once P (columns 0 .. 63) is written
+  static constexpr bool kInRegionO = BS == 128;
+  static constexpr int kWgCols = kInRegionO ? kSCols : kSCols + 64;
   static constexpr int kBoxBytes = BS * 128;       // one state's rows of one matrix, both heads (128 B per row)
   static constexpr int kTileBytes = 128 * 128;      // Q, K or V of a unit
   static constexpr int kStageBytes = 3 * kTileBytes;  // one unit
@@ -80,7 +82,7 @@ struct TcAttnShape {
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kOutBytes + kBarrierBytes;
   // Registers per thread: an SM sub-partition holds every fourth warp (five of
   // nineteen, three of eleven) in its 16,384 registers.
-  static constexpr int kMaxRegs = kWgs == 4 ? 96 : 168;
+  static constexpr int kMaxRegs = 96;
   static_assert(kStageBytes % 1024 == 0, "1024 B aligned stages");
   static_assert(kSmemBytes <= 232448, "227 KB of shared memory per CTA");
   static_assert(kWgs * kWgCols <= kTmemCols, "TMEM columns");
@@ -230,29 +232,10 @@ __device__ __forceinline__ float2 attn_softmax_rows(uint32_t tb, int c0, int c, 
     attn_exp_any(r0, c, sc, off, sum2, tb + 16 * c0);
     // P of chunk 0 goes to S chunk 0's columns, already read
     if (CHUNKS == 2 && nch == 2) attn_exp_any(r1, c - 32, sc, off, sum2, tb + 16 * (c0 + 1));
-  } else if (nch <= 2) {
-    // one TMEM round trip: both chunks in registers for the max and the exponentials
-    uint32_t r0[32], r1[32];
-    tmem_ld32(tb + 32 * c0, r0);
-    if (nch == 2) tmem_ld32(tb + 32 * (c0 + 1), r1);
-    tmem_ld_wait_dep(r0);
-    if (nch == 2) tmem_ld_wait_dep(r1);
-    float mx;
-    if (nch == 2) {
-      mx = attn_chunk_max<true>(r0, 32, -INFINITY);
-      mx = attn_max_any(r1, c - 32, mx);
-    } else {
-      mx = attn_max_any(r0, c, -INFINITY);
-    }
-    const float2 off = make_float2(-mx * scale_log2, -mx * scale_log2);
-    if (nch == 2) {
-      attn_exp_chunk<true>(r0, 32, sc, off, sum2, tb + 16 * c0);
-      attn_exp_any(r1, c - 32, sc, off, sum2, tb + 16 * (c0 + 1));
-    } else {
-      attn_exp_any(r0, c, sc, off, sum2, tb + 16 * c0);
-    }
   } else {
-    // wider states: two passes, the next chunk's load in flight
+    // wide states (BS = 128, 96 registers): the max with the next chunk's
+    // load in flight, then each chunk read again for its exponentials (P
+    // column 16 (c0 + k) lies in S chunk (c0 + k) / 2 <= c0 + k, already read)
     uint32_t ra[32], rb[32];
     float mx = -INFINITY;
     tmem_ld32(tb + 32 * c0, ra);
@@ -266,18 +249,11 @@ __device__ __forceinline__ float2 attn_softmax_rows(uint32_t tb, int c0, int c, 
         mx = attn_max_any(rb, c - 32 * (k + 1), mx);
       }
     }
-    // P column 16 (c0 + k) lies in S chunk (c0 + k) / 2 <= c0 + k, already read
     const float2 off = make_float2(-mx * scale_log2, -mx * scale_log2);
-    tmem_ld32(tb + 32 * c0, ra);
-    for (int k = 0; k < nch; k += 2) {
+    for (int k = 0; k < nch; ++k) {
+      tmem_ld32(tb + 32 * (c0 + k), ra);
       tmem_ld_wait_dep(ra);
-      if (k + 1 < nch) tmem_ld32(tb + 32 * (c0 + k + 1), rb);
       attn_exp_any(ra, c - 32 * k, sc, off, sum2, tb + 16 * (c0 + k));
-      if (k + 1 < nch) {
-        tmem_ld_wait_dep(rb);
-        if (k + 2 < nch) tmem_ld32(tb + 32 * (c0 + k + 2), ra);
-        attn_exp_any(rb, c - 32 * (k + 1), sc, off, sum2, tb + 16 * (c0 + k + 1));
-      }
     }
   }
   // P = 0 for the key chunks past the state's count (after the reads above)
@@ -431,11 +407,12 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
           const int w = g + 2 * h;
           if (np[h] < nq[h]) {
             const int k = np[h], ob = 2 * w + (k & 1);
-            if (mbar_test(&p_full[w], k & 1u) && (k < 2 || mbar_test(&t_empty[ob], ((k >> 1) - 1) & 1u))) {
+            if (mbar_test(&p_full[w], k & 1u) &&
+                (S::kInRegionO || k < 2 || mbar_test(&t_empty[ob], ((k >> 1) - 1) & 1u))) {
               tc_fence_after();
               const int s = (h + H * k) % S::kStages;
               const uint32_t ta = tmem_base + static_cast<uint32_t>(w * S::kWgCols);
-              const uint32_t to = ta + static_cast<uint32_t>(S::kSCols + 32 * (k & 1));
+              const uint32_t to = ta + static_cast<uint32_t>(S::kInRegionO ? 64 : S::kSCols + 32 * (k & 1));
               const uint64_t vd = v_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
 #pragma unroll
               for (int j = 0; j < K; ++j) {
@@ -454,10 +431,12 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
             }
           }
           // QK(k) once PV(k - 1) is issued: the score region is the warpgroup's only one
+          // (O in the region: also once the output of head k - 1 has left it)
           if (nq[h] < cnt[h] && nq[h] == np[h]) {
-            const int i = h + H * nq[h];
+            const int k = nq[h], i = h + H * k;
             const int s = i % S::kStages;
-            if (mbar_test(&full[s], (i / S::kStages) & 1u)) {
+            if (mbar_test(&full[s], (i / S::kStages) & 1u) &&
+                (!S::kInRegionO || k == 0 || mbar_test(&t_empty[2 * w + ((k - 1) & 1)], ((k - 1) >> 1) & 1u))) {
               tc_fence_after();
               const uint32_t dt = tmem_base + static_cast<uint32_t>(w * S::kWgCols);
               const uint64_t qd = q_desc0 + static_cast<uint64_t>(s * (S::kStageBytes >> 4));
@@ -525,7 +504,9 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
       const int first = rib - lane;  // the warp's first row within its block
       if (first < prev_c) {          // the warp has rows of its state
         uint32_t r[32];
-        tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(wg * S::kWgCols + S::kSCols + 32 * (k & 1)), r);
+        tmem_ld32(tmem_base + lane_off +
+                      static_cast<uint32_t>(wg * S::kWgCols + (S::kInRegionO ? 64 : S::kSCols + 32 * (k & 1))),
+                  r);
         tmem_ld_wait_dep(r);
         const float inv = 1.0f / (prev_sum.x + prev_sum.y);
 #pragma unroll
@@ -552,7 +533,8 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
       return true;
     };
     // Iteration k: softmax(k), then the output of head k - 1 (whose PV ran
-    // during this softmax); the MMA warp then reuses that buffer for QK(k + 1).
+    // during this softmax), or at BS = 128 (O in the score region) the output
+    // of head k itself, after which the region takes QK(k + 1).
     int k = 0;
     for (int u = blockIdx.x + par * static_cast<int>(gridDim.x); u < n_units; u += ustep, ++k) {
       const int col = ((u % hgs) * S::kGroup + (wg & 1)) * 32;
@@ -576,16 +558,29 @@ __global__ void __launch_bounds__(TcAttnShape<BS>::kThreads) __maxnreg__(TcAttnS
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[wg]);
-      if (k > 0 && !output(k - 1)) {
-        ok = false;
-        break;
+      if constexpr (S::kInRegionO) {
+        // O shares the score region: write this head's output now, which
+        // frees the region for the next head's scores
+        prev_r = r0;
+        prev_c = c;
+        prev_col = col;
+        prev_sum = sum2;
+        if (!output(k)) {
+          ok = false;
+          break;
+        }
+      } else {
+        if (k > 0 && !output(k - 1)) {
+          ok = false;
+          break;
+        }
+        prev_r = r0;
+        prev_c = c;
+        prev_col = col;
+        prev_sum = sum2;
       }
-      prev_r = r0;
-      prev_c = c;
-      prev_col = col;
-      prev_sum = sum2;
     }
-    if (ok && k > 0) output(k - 1);
+    if (!S::kInRegionO && ok && k > 0) output(k - 1);
   }
 
   __syncthreads();
